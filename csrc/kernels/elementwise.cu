@@ -1,0 +1,286 @@
+// Memory-bound per-token kernels of the decoder: embedding gather, RMSNorm
+// (optionally fused with a residual add), q/k-norm + RoPE + paged KV-cache
+// write, and greedy argmax over logits.
+//
+// Reference semantics: RMSNorm computes the variance in fp32 and multiplies
+// the bf16-rounded normalised value by the weight (HF Llama/Qwen3 RMSNorm as
+// used through si/model/qwen3.py:517-546 and si/microsharding/dense.py:146-166);
+// RoPE is the rotate-half form with a host-built fp32 cos/sin table
+// (si/microsharding/dense.py:169-219); greedy argmax breaks ties toward the
+// lowest token id (si/model/qwen3_sampling.py:79-96, si/microsharding/dense.py:825-838).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "sil/host.h"
+#include "sil/ptx.cuh"
+
+namespace sil {
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float s = lane < nw ? red[lane] : 0.f;
+  s = warp_sum(s);
+  __syncthreads();
+  return s;
+}
+
+// y = rmsnorm(x (+ r)) * w;  when `res_out` is given, it receives x + r (bf16).
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                               const __nv_bfloat16* __restrict__ r, long long ldr,
+                               __nv_bfloat16* __restrict__ res_out, long long ldro,
+                               const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                               long long ldy, int H, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  extern __shared__ float vals[];  // H floats
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    uint4 q = *reinterpret_cast<const uint4*>(xr + i);
+    float v[8] = {bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y),
+                  bf16_lo(q.z), bf16_hi(q.z), bf16_lo(q.w), bf16_hi(q.w)};
+    if (r != nullptr) {
+      uint4 p = *reinterpret_cast<const uint4*>(r + row * ldr + i);
+      float u[8] = {bf16_lo(p.x), bf16_hi(p.x), bf16_lo(p.y), bf16_hi(p.y),
+                    bf16_lo(p.z), bf16_hi(p.z), bf16_lo(p.w), bf16_hi(p.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j] + u[j]));
+      uint4 o;
+      o.x = pack_bf16x2(v[0], v[1]); o.y = pack_bf16x2(v[2], v[3]);
+      o.z = pack_bf16x2(v[4], v[5]); o.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(res_out + row * ldro + i) = o;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      vals[i + j] = v[j];
+      ss += v[j] * v[j];
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float rstd = rsqrtf(tot / H + eps);
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    uint4 wq = *reinterpret_cast<const uint4*>(w + i);
+    float wv[8] = {bf16_lo(wq.x), bf16_hi(wq.x), bf16_lo(wq.y), bf16_hi(wq.y),
+                   bf16_lo(wq.z), bf16_hi(wq.z), bf16_lo(wq.w), bf16_hi(wq.w)};
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float nrm = __bfloat162float(__float2bfloat16_rn(vals[i + j] * rstd));
+      o[j] = wv[j] * nrm;
+    }
+    uint4 q;
+    q.x = pack_bf16x2(o[0], o[1]); q.y = pack_bf16x2(o[2], o[3]);
+    q.z = pack_bf16x2(o[4], o[5]); q.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(y + row * ldy + i) = q;
+  }
+}
+
+// One warp per (token, head).  qkv: [T, (Hq + 2*Hkv) * 128]; q heads are
+// rotated in place; k heads are normalised/rotated and written with v into
+// the paged cache at `slots[t]` (= page * 64 + offset; negative = skip).
+__global__ void rope_kv_write_kernel(__nv_bfloat16* __restrict__ qkv, long long ld,
+                                     const int* __restrict__ positions,
+                                     const int* __restrict__ slots,
+                                     const float* __restrict__ cos_sin,  // [max_pos, 128]
+                                     const __nv_bfloat16* __restrict__ q_norm_w,
+                                     const __nv_bfloat16* __restrict__ k_norm_w, float eps,
+                                     __nv_bfloat16* __restrict__ k_cache,
+                                     __nv_bfloat16* __restrict__ v_cache, int T, int Hq, int Hkv) {
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int tok = warp_global / heads;
+  const int hh = warp_global % heads;
+  if (tok >= T) return;
+  __nv_bfloat16* row = qkv + tok * ld + hh * 128;
+  const int d0 = 2 * lane;  // this lane owns dims d0, d0+1, d0+64, d0+65
+  uint32_t lo = *reinterpret_cast<const uint32_t*>(row + d0);
+  uint32_t hi = *reinterpret_cast<const uint32_t*>(row + d0 + 64);
+  float x0 = bf16_lo(lo), x1 = bf16_hi(lo), x2 = bf16_lo(hi), x3 = bf16_hi(hi);
+  const int slot = slots[tok];
+  if (hh >= Hq + Hkv) {  // value head: copy into the cache
+    if (slot >= 0) {
+      const int kvh = hh - Hq - Hkv;
+      const long long base = ((long long)(slot >> 6) * Hkv + kvh) * 64 * 128 + (slot & 63) * 128;
+      *reinterpret_cast<uint32_t*>(v_cache + base + d0) = lo;
+      *reinterpret_cast<uint32_t*>(v_cache + base + d0 + 64) = hi;
+    }
+    return;
+  }
+  const bool is_q = hh < Hq;
+  const __nv_bfloat16* nw = is_q ? q_norm_w : k_norm_w;
+  if (nw != nullptr) {
+    const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+    const float rstd = rsqrtf(ss / 128.f + eps);
+    x0 = __bfloat162float(nw[d0]) * __bfloat162float(__float2bfloat16_rn(x0 * rstd));
+    x1 = __bfloat162float(nw[d0 + 1]) * __bfloat162float(__float2bfloat16_rn(x1 * rstd));
+    x2 = __bfloat162float(nw[d0 + 64]) * __bfloat162float(__float2bfloat16_rn(x2 * rstd));
+    x3 = __bfloat162float(nw[d0 + 65]) * __bfloat162float(__float2bfloat16_rn(x3 * rstd));
+    x0 = __bfloat162float(__float2bfloat16_rn(x0));
+    x1 = __bfloat162float(__float2bfloat16_rn(x1));
+    x2 = __bfloat162float(__float2bfloat16_rn(x2));
+    x3 = __bfloat162float(__float2bfloat16_rn(x3));
+  }
+  const float* cs = cos_sin + (long long)positions[tok] * 128;
+  const float c0 = cs[d0], c1 = cs[d0 + 1], s0 = cs[64 + d0], s1 = cs[64 + d0 + 1];
+  const float y0 = x0 * c0 - x2 * s0;
+  const float y1 = x1 * c1 - x3 * s1;
+  const float y2 = x2 * c0 + x0 * s0;
+  const float y3 = x3 * c1 + x1 * s1;
+  const uint32_t olo = pack_bf16x2(y0, y1), ohi = pack_bf16x2(y2, y3);
+  if (is_q) {
+    *reinterpret_cast<uint32_t*>(row + d0) = olo;
+    *reinterpret_cast<uint32_t*>(row + d0 + 64) = ohi;
+  } else if (slot >= 0) {
+    const int kvh = hh - Hq;
+    const long long base = ((long long)(slot >> 6) * Hkv + kvh) * 64 * 128 + (slot & 63) * 128;
+    *reinterpret_cast<uint32_t*>(k_cache + base + d0) = olo;
+    *reinterpret_cast<uint32_t*>(k_cache + base + d0 + 64) = ohi;
+  }
+}
+
+__global__ void embedding_kernel(const long long* __restrict__ ids,
+                                 const __nv_bfloat16* __restrict__ table, int H,
+                                 __nv_bfloat16* __restrict__ out, long long ldo, long long vocab) {
+  const int row = blockIdx.x;
+  long long id = ids[row];
+  if (id < 0 || id >= vocab) id = 0;  // out-of-range ids map to token 0 (checked on host in tests)
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + row * ldo);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// Greedy argmax per row of fp32 logits; ties resolve to the lowest index.
+__global__ void argmax_kernel(const float* __restrict__ logits, long long ld, int V,
+                              long long* __restrict__ out) {
+  const float* row = logits + blockIdx.x * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const bool vec = (ld % 4 == 0) && (V % 4 == 0);
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < V; i += blockDim.x * 4) {
+      float4 q = *reinterpret_cast<const float4*>(row + i);
+      if (q.x > best) { best = q.x; bi = i; }
+      if (q.y > best) { best = q.y; bi = i + 1; }
+      if (q.z > best) { best = q.z; bi = i + 2; }
+      if (q.w > best) { best = q.w; bi = i + 3; }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = row[i];
+      if (v > best) { best = v; bi = i; }
+    }
+  }
+  // Reduce (value desc, index asc).
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+}  // namespace
+
+void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
+             const c10::optional<at::Tensor>& residual_out, const at::Tensor& w, at::Tensor& y,
+             double eps) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "rmsnorm: x must be 2-D bf16 with contiguous rows");
+  const int T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm: H must be a multiple of 8");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  const __nv_bfloat16* rp = nullptr;
+  __nv_bfloat16* rop = nullptr;
+  long long ldr = 0, ldro = 0;
+  if (residual.has_value()) {
+    TORCH_CHECK(residual_out.has_value(), "rmsnorm: residual_out required with residual");
+    rp = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+    rop = reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr());
+    ldro = residual_out->stride(0);
+  }
+  const int threads = std::min(1024, std::max(32, ((H / 8 + 31) / 32) * 32));
+  rmsnorm_kernel<<<T, threads, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), rp, ldr, rop, ldro,
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), H, static_cast<float>(eps));
+  check_cuda(cudaGetLastError(), "rmsnorm launch");
+}
+
+void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,
+                   const at::Tensor& cos_sin, const c10::optional<at::Tensor>& q_norm_w,
+                   const c10::optional<at::Tensor>& k_norm_w, double eps, at::Tensor& k_cache,
+                   at::Tensor& v_cache, int64_t Hq, int64_t Hkv) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1, "rope_kv_write: qkv");
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * 128, "rope_kv_write: head_dim must be 128");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt,
+              "rope_kv_write: int32 positions/slots");
+  const int T = qkv.size(0);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const long long warps = (long long)T * (Hq + 2 * Hkv);
+  const int threads = 256;
+  const long long blocks = (warps * 32 + threads - 1) / threads;
+  rope_kv_write_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int>(),
+      slots.data_ptr<int>(), cos_sin.data_ptr<float>(),
+      q_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm_w->data_ptr()) : nullptr,
+      k_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm_w->data_ptr()) : nullptr,
+      static_cast<float>(eps), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, Hq, Hkv);
+  check_cuda(cudaGetLastError(), "rope_kv_write launch");
+}
+
+void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && table.scalar_type() == at::kBFloat16,
+              "embedding: int64 ids, bf16 table");
+  const int T = ids.numel(), H = table.size(1);
+  TORCH_CHECK(H % 8 == 0, "embedding: H % 8");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(ids.device());
+  embedding_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>() ? reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()) : nullptr,
+      reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), H,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), table.size(0));
+  check_cuda(cudaGetLastError(), "embedding launch");
+}
+
+void argmax(const at::Tensor& logits, at::Tensor& out) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "argmax: fp32 [T, V]");
+  TORCH_CHECK(out.scalar_type() == at::kLong, "argmax: int64 output");
+  const int T = logits.size(0);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(logits.device());
+  argmax_kernel<<<T, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), logits.size(1),
+      reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
+  check_cuda(cudaGetLastError(), "argmax launch");
+}
+
+}  // namespace sil

@@ -1,0 +1,68 @@
+"""Paged GQA attention kernels (``csrc/kernels/attention.cu``).
+
+KV cache per layer: ``[num_pages, num_kv_heads, 64, 128]`` bf16 for K and V.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import ext
+from .workspace import get_workspace
+
+PAGE_SIZE = 64
+
+
+def decode_splits(batch: int, kv_heads: int, max_pages: int, sm_count: int = 148) -> int:
+    """Split-KV factor: enough CTAs for ~2 waves, at least 2 pages per split."""
+    base = max(1, batch * kv_heads)
+    want = max(1, (2 * sm_count + base - 1) // base)
+    return int(max(1, min(want, max(1, max_pages // 2), 32)))
+
+
+def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 block_table: torch.Tensor, seq_lens: torch.Tensor, *, out: torch.Tensor | None = None,
+                 num_splits: int = 1, scale: float | None = None) -> torch.Tensor:
+    """q: [B, Hq, 128] (one new token per sequence) -> out [B, Hq*128]."""
+    B, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((B, Hq * D), dtype=q.dtype, device=q.device)
+    ws = get_workspace(q.device)
+    ext().paged_decode(q, k_cache, v_cache, block_table, seq_lens, out,
+                       scale if scale is not None else 1.0 / math.sqrt(D), int(num_splits),
+                       ws.attn_ws, ws.attn_counters, ws.status)
+    return out
+
+
+def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  block_table: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor,
+                  max_q_len: int, *, out: torch.Tensor | None = None,
+                  scale: float | None = None) -> torch.Tensor:
+    """q: packed [T, Hq, 128]; cu_q: [B+1] int32 query offsets -> out [T, Hq*128]."""
+    T, Hq, D = q.shape
+    if out is None:
+        out = torch.empty((T, Hq * D), dtype=q.dtype, device=q.device)
+    ws = get_workspace(q.device)
+    ext().paged_prefill(q, k_cache, v_cache, block_table, seq_lens, cu_q, out,
+                        scale if scale is not None else 1.0 / math.sqrt(D), int(max_q_len),
+                        ws.status)
+    return out
+
+
+def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal_offset: int,
+                        scale: float | None = None) -> torch.Tensor:
+    """Dense GQA attention in fp32.  q: [Tq, Hq, D], k/v: [Tk, Hkv, D]; query i sits at
+    absolute position ``causal_offset + i`` and sees keys ``<=`` that position."""
+    Tq, Hq, D = q.shape
+    Tk, Hkv, _ = k.shape
+    g = Hq // Hkv
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    kf = k.float().repeat_interleave(g, dim=1)
+    vf = v.float().repeat_interleave(g, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), kf) * scale
+    qpos = torch.arange(Tq, device=q.device)[:, None] + causal_offset
+    kpos = torch.arange(Tk, device=q.device)[None, :]
+    s = s.masked_fill((kpos > qpos)[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hqk,khd->qhd", p, vf)

@@ -1,0 +1,52 @@
+"""Tensor-parallel communicators.
+
+``NcclComm`` wraps a ``torch.distributed`` NCCL process group (one process per
+GPU).  It is the unfused baseline: GEMM, then ``all_reduce``.  The fused
+path (``parallel/fused_tp.py``) exposes the same interface plus
+``fused_gemm_allreduce`` which performs the row-parallel GEMM and the
+reduction over NVLink peer memory in one kernel.
+
+``LocalComm`` is the single-rank identity used at TP=1.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class LocalComm:
+    rank = 0
+    size = 1
+    fused_gemm_allreduce = None
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        return x[None]
+
+    def barrier(self) -> None:
+        pass
+
+
+class NcclComm:
+    """All-reduce / all-gather over an NCCL group (the baseline TP path)."""
+
+    fused_gemm_allreduce = None
+
+    def __init__(self, group: dist.ProcessGroup | None = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        dist.all_reduce(x, group=self.group)
+        return x
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        return out
+
+    def barrier(self) -> None:
+        dist.barrier(group=self.group)
