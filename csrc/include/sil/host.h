@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -77,6 +78,34 @@ inline int device_sm_count() {
              "cudaDeviceGetAttribute(SM count)");
   if (dev < 64) cached[dev] = n;
   return n;
+}
+
+// Programmatic dependent launch is on unless SIL_PDL=0.
+inline bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("SIL_PDL");
+    v = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// Launch `kern` with the programmatic-stream-serialization attribute so its
+// pre-`griddepcontrol.wait` prologue may overlap the previous kernel's tail.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
 }
 
 }  // namespace sil

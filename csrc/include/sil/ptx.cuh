@@ -288,6 +288,14 @@ __host__ __device__ constexpr uint32_t umma_idesc_e4m3(int M, int N) {
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Programmatic dependent launch: wait until the preceding kernel in the stream has
+// completed and flushed its memory (no-op when launched without the attribute),
+// and allow the next kernel to be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier over a subset of warps.
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(128)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   int* sflag = reinterpret_cast<int*>(full + kStages);
 
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -308,6 +310,8 @@ __global__ void __launch_bounds__(128)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   int* sflag = reinterpret_cast<int*>(full + kStages);
 
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int hq = blockIdx.y, b = blockIdx.z;
@@ -536,8 +540,8 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
     configured = true;
   }
   dim3 grid(S, Hkv, B);
-  paged_decode_kernel<<<grid, 128, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(tk, tv, a);
-  check_cuda(cudaGetLastError(), "paged_decode launch");
+  launch_pdl(paged_decode_kernel, grid, dim3(128), kSmemBytes, at::cuda::getCurrentCUDAStream(),
+             "paged_decode launch", tk, tv, a);
 }
 
 // q: packed [T, Hq, 128]; cu_q: [B+1]; seq_lens: [B] (context after append); out: [T, Hq*128].
@@ -577,8 +581,8 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
     configured = true;
   }
   dim3 grid((max_q_len + 63) / 64, Hq, B);
-  paged_prefill_kernel<<<grid, 128, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(tk, tv, a);
-  check_cuda(cudaGetLastError(), "paged_prefill launch");
+  launch_pdl(paged_prefill_kernel, grid, dim3(128), kSmemBytes, at::cuda::getCurrentCUDAStream(),
+             "paged_prefill launch", tk, tv, a);
 }
 
 }  // namespace sil

@@ -37,6 +37,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                long long ldy, int H, float eps) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * ldx;
   extern __shared__ float vals[];  // H floats
@@ -92,6 +94,8 @@ __global__ void rope_kv_write_kernel(__nv_bfloat16* __restrict__ qkv, long long 
                                      const __nv_bfloat16* __restrict__ k_norm_w, float eps,
                                      __nv_bfloat16* __restrict__ k_cache,
                                      __nv_bfloat16* __restrict__ v_cache, int T, int Hq, int Hkv) {
+  pdl_trigger();
+  pdl_wait();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
@@ -148,6 +152,8 @@ __global__ void rope_kv_write_kernel(__nv_bfloat16* __restrict__ qkv, long long 
 __global__ void embedding_kernel(const long long* __restrict__ ids,
                                  const __nv_bfloat16* __restrict__ table, int H,
                                  __nv_bfloat16* __restrict__ out, long long ldo, long long vocab) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   long long id = ids[row];
   if (id < 0 || id >= vocab) id = 0;  // out-of-range ids map to token 0 (checked on host in tests)
@@ -159,6 +165,8 @@ __global__ void embedding_kernel(const long long* __restrict__ ids,
 // Greedy argmax per row of fp32 logits; ties resolve to the lowest index.
 __global__ void argmax_kernel(const float* __restrict__ logits, long long ld, int V,
                               long long* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const float* row = logits + blockIdx.x * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -225,11 +233,12 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
     ldro = residual_out->stride(0);
   }
   const int threads = std::min(1024, std::max(32, ((H / 8 + 31) / 32) * 32));
-  rmsnorm_kernel<<<T, threads, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), rp, ldr, rop, ldro,
-      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), H, static_cast<float>(eps));
-  check_cuda(cudaGetLastError(), "rmsnorm launch");
+  launch_pdl(rmsnorm_kernel, dim3(T), dim3(threads), H * sizeof(float),
+             at::cuda::getCurrentCUDAStream(), "rmsnorm launch",
+             reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0), rp, ldr,
+             rop, ldro, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), (long long)y.stride(0), H,
+             static_cast<float>(eps));
 }
 
 void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,
@@ -246,14 +255,17 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
   const long long warps = (long long)T * (Hq + 2 * Hkv);
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;
-  rope_kv_write_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int>(),
-      slots.data_ptr<int>(), cos_sin.data_ptr<float>(),
-      q_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm_w->data_ptr()) : nullptr,
-      k_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm_w->data_ptr()) : nullptr,
-      static_cast<float>(eps), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, Hq, Hkv);
-  check_cuda(cudaGetLastError(), "rope_kv_write launch");
+  const __nv_bfloat16* qn =
+      q_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm_w->data_ptr()) : nullptr;
+  const __nv_bfloat16* kn =
+      k_norm_w.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm_w->data_ptr()) : nullptr;
+  launch_pdl(rope_kv_write_kernel, dim3(blocks), dim3(threads), 0,
+             at::cuda::getCurrentCUDAStream(), "rope_kv_write launch",
+             reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), (long long)qkv.stride(0),
+             (const int*)positions.data_ptr<int>(), (const int*)slots.data_ptr<int>(),
+             (const float*)cos_sin.data_ptr<float>(), qn, kn, static_cast<float>(eps),
+             reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, (int)Hq, (int)Hkv);
 }
 
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
@@ -263,11 +275,11 @@ void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) 
   TORCH_CHECK(H % 8 == 0, "embedding: H % 8");
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(ids.device());
-  embedding_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int64_t>() ? reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()) : nullptr,
-      reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), H,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), table.size(0));
-  check_cuda(cudaGetLastError(), "embedding launch");
+  launch_pdl(embedding_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             "embedding launch", reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
+             reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), H,
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0),
+             (long long)table.size(0));
 }
 
 void argmax(const at::Tensor& logits, at::Tensor& out) {
@@ -277,10 +289,9 @@ void argmax(const at::Tensor& logits, at::Tensor& out) {
   const int T = logits.size(0);
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(logits.device());
-  argmax_kernel<<<T, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), logits.stride(0), logits.size(1),
-      reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
-  check_cuda(cudaGetLastError(), "argmax launch");
+  launch_pdl(argmax_kernel, dim3(T), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
+             "argmax launch", (const float*)logits.data_ptr<float>(), (long long)logits.stride(0),
+             (int)logits.size(1), reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
 }
 
 }  // namespace sil

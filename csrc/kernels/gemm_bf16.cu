@@ -60,64 +60,67 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
   const int sms = device_sm_count();
-
+  int bn;
+  CUtensorMap ta, tb;
   if (swap) {
     TORCH_CHECK(T <= 128, "gemm_bf16: swapped mode supports at most 128 tokens");
-    const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
     a.M = swiglu ? inter : Nw;
     a.N = T;
-    const int m_tiles = (a.M + BM - 1) / BM;
-    const int n_tiles = 1;
-    const int tiles = m_tiles * n_tiles;
-    const int stage = smem_stage_bytes(bn, swiglu);
-    const int ctas_per_sm = stage * 4 <= 110 * 1024 ? 2 : 1;
-    int splits = 1;
-    if (force_splits > 0) {
-      splits = force_splits;
-    } else if (tiles < sms * ctas_per_sm) {
-      splits = (sms * ctas_per_sm + tiles - 1) / tiles;
-      splits = std::min(splits, std::max(1, a.num_kb / 4));
-    }
-    const long long acc_cols = (swiglu ? 2 : 1) * bn;
-    while (splits > 1 && (long long)tiles * splits * acc_cols * BM > ws.numel()) --splits;
-    splits = std::max(1, std::min(splits, a.num_kb));
-    TORCH_CHECK(splits == 1 || tiles <= counters.numel(), "gemm_bf16: counter array too small");
-    a.splits = splits;
-    CUtensorMap ta = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Nw, K,
-                                  w.stride(0), BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tb = make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K,
-                                  x.stride(0), bn, BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    switch (epi) {
-      case kEpiBf16: dispatch_swap<kEpiBf16>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiResAdd: dispatch_swap<kEpiResAdd>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiSwiGLU: dispatch_swap<kEpiSwiGLU>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiF32: dispatch_swap<kEpiF32>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue");
-    }
+    a.m_tiles = (a.M + BM - 1) / BM;
+    a.n_tiles = 1;
+    ta = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Nw, K, w.stride(0), BM,
+                      BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    tb = make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K, x.stride(0), bn,
+                      BK, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
-    const int bn = (Nout >= 2048 || swiglu) ? 256 : 128;
+    bn = (Nout >= 2048 || swiglu) ? 256 : 128;
     const int out_cols = swiglu ? bn / 2 : bn;
     a.M = T;
     a.N = Nout;
-    const int m_tiles = (T + BM - 1) / BM;
-    const int n_tiles = (Nout + out_cols - 1) / out_cols;
-    int splits = force_splits > 0 ? (int)force_splits : 1;
-    const long long acc_cols = bn;
-    while (splits > 1 && (long long)m_tiles * n_tiles * splits * acc_cols * BM > ws.numel()) --splits;
-    splits = std::max(1, std::min(splits, a.num_kb));
-    TORCH_CHECK(splits == 1 || m_tiles * n_tiles <= counters.numel(),
-                "gemm_bf16: counter array too small");
-    a.splits = splits;
-    CUtensorMap ta = make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K,
-                                  x.stride(0), BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tb = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Nw, K,
-                                  w.stride(0), swiglu ? bn / 2 : bn, BK,
-                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    a.m_tiles = (T + BM - 1) / BM;
+    a.n_tiles = (Nout + out_cols - 1) / out_cols;
+    ta = make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K, x.stride(0), BM, BK,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tb = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Nw, K, w.stride(0),
+                      swiglu ? bn / 2 : bn, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  const long long tiles = (long long)a.m_tiles * a.n_tiles;
+  a.units = tiles * a.num_kb;
+  // Persistent grid: one CTA per SM, fewer when the problem has little work per CTA.
+  // force_splits > 0 caps the grid at tiles * force_splits (tests of the fix-up path).
+  // Stream-K when the tiles alone cannot fill the SMs (decode shapes); otherwise whole
+  // tiles in grouped raster order, which keeps the concurrently active tiles' operands
+  // L2-resident.
+  a.stream_k = (swap || tiles < 2LL * sms || force_splits > 0) ? 1 : 0;
+  a.group_m = 16;
+  long long g;
+  if (a.stream_k) {
+    g = std::min<long long>(sms, a.units);
+    const long long min_units = 4;
+    g = std::max<long long>(1, std::min<long long>(g, (a.units + min_units - 1) / min_units));
+    if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
+  } else {
+    g = std::min<long long>(sms, tiles);
+  }
+  const long long acc_cols = (swap && swiglu ? 2 : 1) * bn;
+  TORCH_CHECK(g * 2 * acc_cols * BM <= ws.numel(), "gemm_bf16: workspace too small");
+  TORCH_CHECK(tiles <= counters.numel(), "gemm_bf16: counter array too small");
+  a.grid = static_cast<int>(g);
+  if (swap) {
     switch (epi) {
-      case kEpiBf16: dispatch_normal<kEpiBf16>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiResAdd: dispatch_normal<kEpiResAdd>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiSwiGLU: dispatch_normal<kEpiSwiGLU>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
-      case kEpiF32: dispatch_normal<kEpiF32>(bn, ta, tb, a, m_tiles, n_tiles, stream); break;
+      case kEpiBf16: dispatch_swap<kEpiBf16>(bn, ta, tb, a, stream); break;
+      case kEpiResAdd: dispatch_swap<kEpiResAdd>(bn, ta, tb, a, stream); break;
+      case kEpiSwiGLU: dispatch_swap<kEpiSwiGLU>(bn, ta, tb, a, stream); break;
+      case kEpiF32: dispatch_swap<kEpiF32>(bn, ta, tb, a, stream); break;
+      default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue");
+    }
+  } else {
+    switch (epi) {
+      case kEpiBf16: dispatch_normal<kEpiBf16>(bn, ta, tb, a, stream); break;
+      case kEpiResAdd: dispatch_normal<kEpiResAdd>(bn, ta, tb, a, stream); break;
+      case kEpiSwiGLU: dispatch_normal<kEpiSwiGLU>(bn, ta, tb, a, stream); break;
+      case kEpiF32: dispatch_normal<kEpiF32>(bn, ta, tb, a, stream); break;
       default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue");
     }
   }

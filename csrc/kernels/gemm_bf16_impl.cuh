@@ -1,22 +1,30 @@
 #pragma once
-// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) with
-// TMA-fed, mbarrier-pipelined shared-memory stages and fused epilogues.
+// Persistent stream-K bf16 GEMM on the 5th-generation tensor cores
+// (tcgen05 + TMEM), TMA-fed through an mbarrier ring of shared-memory stages.
 //
 //   y[T, Nout] = epilogue( x[T, K] . W[Nw, K]^T )
 //
-// Two operand orders share one kernel template:
-//  * normal  (prefill, T > 128): A = x (M = tokens), B = W (N = features),
-//    BN = 128/256.  The accumulator row is a token, columns are features.
+// Operand orders:
+//  * normal  (prefill, T > 128): A = x (M = tokens), B = W (N = features).
 //  * swapped (decode, T <= 128):  A = W (M = features), B = x (N = tokens,
-//    padded to 16/32/64/128).  Weight streaming is the bound here, so the
-//    kernel splits K across CTAs (split-K) until the grid covers every SM;
-//    partial tiles go to an fp32 workspace and the last CTA of a tile sums
-//    them in split order (deterministic) before the epilogue.
+//    padded to 16/32/64/128).
 //
-// Epilogues: plain bf16 store, residual add (y = acc + r, in place allowed),
-// SwiGLU (y = silu(gate) * up from a fused [gate; up] weight) and fp32 store
-// (LM-head logits).  Warp roles: warp 0 issues TMA, warp 1 issues tcgen05.mma
-// (single elected thread) and owns the TMEM allocation, warps 2-5 drain TMEM.
+// Work decomposition (stream-K): the (tile, k-block) units of the problem
+// are cut into G equal contiguous ranges, one per persistent CTA (G <= SMs).
+// A CTA streams its range without draining the pipeline between tiles; a
+// tile covered by one CTA is stored directly, a tile shared by several CTAs
+// has each contributor write an fp32 partial and the last contributor to
+// arrive sums the partials in contributor order (deterministic) before the
+// epilogue.  Two TMEM accumulators let the epilogue of one tile overlap the
+// main loop of the next.
+//
+// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (one thread) and
+// TMEM owner, warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4)...).
+//
+// Programmatic dependent launch: the producer starts streaming the weight
+// operand before `griddepcontrol.wait`, so weight traffic overlaps the tail
+// of the previous kernel; activations, residuals and the shared workspace
+// are touched only after the wait.
 //
 // Replaces the per-layer F.linear / cuBLAS calls of the reference's decoder
 // layers (si/microsharding/dense.py:320-412, HF layers via si/model/qwen3.py:517-546).
@@ -37,17 +45,22 @@ constexpr int kThreads = 192;
 enum EpiKind : int { kEpiBf16 = 0, kEpiResAdd = 1, kEpiSwiGLU = 2, kEpiF32 = 3 };
 
 struct GemmArgs {
-  int M;       // rows of A that are valid (features in swapped mode, tokens otherwise)
-  int N;       // valid output columns of the accumulator space (tokens / features)
-  int num_kb;  // number of 64-wide K blocks
-  int splits;  // split-K factor (grid.z)
-  int inter;   // SwiGLU: row offset of the 'up' half inside the fused weight
+  int M;          // valid rows of A (features when swapped, tokens otherwise)
+  int N;          // valid output columns (tokens when swapped, features otherwise)
+  int num_kb;     // 64-wide K blocks per tile
+  int m_tiles;
+  int n_tiles;
+  int grid;       // G: persistent CTAs
+  long long units;  // m_tiles * n_tiles * num_kb
+  int stream_k;   // 1: contiguous (tile, k-block) ranges per CTA; 0: whole tiles, strided
+  int group_m;    // tile mode: m-tiles per raster group (L2 reuse of the B operand)
+  int inter;      // SwiGLU: row offset of the 'up' half inside the fused weight
   void* out;
   long long ldo;
   const __nv_bfloat16* res;
   long long ldr;
-  float* ws;
-  int* counters;
+  float* ws;      // [G][2][ACC_COLS][128] partial tiles
+  int* counters;  // per tile arrivals
   int* status;
 };
 
@@ -59,14 +72,22 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = NUM_A * A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = NUM_A * BN;
-  // Output columns produced per tile (SwiGLU in normal order halves them).
   static constexpr int OUT_COLS = (kSwiGLU && !SWAP) ? BN / 2 : BN;
-  static constexpr int TMEM_COLS =
-      ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS <= 32    ? 32
+                                   : 2 * ACC_COLS <= 64  ? 64
+                                   : 2 * ACC_COLS <= 128 ? 128
+                                   : 2 * ACC_COLS <= 256 ? 256
+                                                         : 512;
+  static constexpr int CW = (OUT_COLS >= 32 && BN >= 32) ? 32 : 16;  // columns per TMEM load
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N constraint for M=128");
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(2 * ACC_COLS <= 512, "two accumulators must fit in TMEM");
 };
+
+__device__ __forceinline__ long long unit_begin(int c, long long U, int G) {
+  return (U * c) / G;
+}
 
 // Store CW consecutive accumulator columns [n0, n0+CW) of accumulator row `m_glob`.
 template <int EPI, bool SWAP, int CW>
@@ -74,7 +95,6 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int m_glob, int n
                                             const float (&v)[CW], const float (&u)[CW]) {
   if (m_glob >= a.M) return;
   if constexpr (SWAP) {
-    // Accumulator row = output feature m_glob, column = token n.
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
       const int n = n0 + j;
@@ -91,7 +111,6 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int m_glob, int n
       }
     }
   } else {
-    // Accumulator row = token m_glob, columns = output features n0 + j.
     if constexpr (EPI == kEpiF32) {
       float* o = reinterpret_cast<float*>(a.out) + (long long)m_glob * a.ldo;
       if (n0 + CW <= a.N && (a.ldo & 3) == 0) {
@@ -154,11 +173,69 @@ __device__ __forceinline__ void tmem_load(uint32_t taddr, uint32_t (&r)[CW]) {
   } else {
     tmem_ld16(taddr, r);
     tmem_ld_wait();
-    // Register dependency: keep uses of r after the wait.
 #pragma unroll
     for (int j = 0; j < CW; ++j) asm volatile("" : "+r"(r[j]));
   }
 }
+
+// Segment of a CTA's work that lies in one tile.
+struct Segment {
+  int tile;
+  int kb0;
+  int kb1;
+  bool first;  // first segment of this CTA (stream-K partial slot 0)
+};
+
+// Walks the segments of one CTA.  Stream-K: the contiguous unit range
+// [U*c/G, U*(c+1)/G).  Tile mode: whole tiles c, c+G, c+2G, ... in grouped
+// raster order (group_m m-tiles sweep all n-tiles before the next group).
+struct Sched {
+  long long u, u_end, u_begin;
+  int t, tiles;
+  __device__ __forceinline__ Sched(const GemmArgs& a, int cta) {
+    u_begin = (a.units * cta) / a.grid;
+    u_end = (a.units * (cta + 1)) / a.grid;
+    u = u_begin;
+    t = cta;
+    tiles = a.m_tiles * a.n_tiles;
+  }
+  __device__ __forceinline__ bool next(const GemmArgs& a, Segment& s) {
+    if (a.stream_k) {
+      if (u >= u_end) return false;
+      s.tile = static_cast<int>(u / a.num_kb);
+      s.kb0 = static_cast<int>(u % a.num_kb);
+      const long long want = s.kb0 + (u_end - u);
+      s.kb1 = want < a.num_kb ? static_cast<int>(want) : a.num_kb;
+      s.first = u == u_begin;
+      u += s.kb1 - s.kb0;
+      return true;
+    }
+    if (t >= tiles) return false;
+    s.tile = t;
+    s.kb0 = 0;
+    s.kb1 = a.num_kb;
+    s.first = t < a.grid;
+    t += a.grid;
+    return true;
+  }
+};
+
+// (m-tile, n-tile) of a tile index.  Stream-K: m fastest.  Tile mode: grouped raster.
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mt, int& nt) {
+  if (a.stream_k) {
+    mt = tile % a.m_tiles;
+    nt = tile / a.m_tiles;
+    return;
+  }
+  const int per_group = a.group_m * a.n_tiles;
+  const int g = tile / per_group;
+  const int first_m = g * a.group_m;
+  const int gm = min(a.m_tiles - first_m, a.group_m);
+  const int in = tile % per_group;
+  mt = first_m + in % gm;
+  nt = in / gm;
+}
+
 
 template <int BN, int STAGES, int EPI, bool SWAP>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -170,31 +247,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] skip, [1] last split
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] skip, [1] last contributor
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x;
-  const int n_tile = blockIdx.y;
-  const int split = blockIdx.z;
-  const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
-  const int kb_per = args.num_kb / args.splits;
-  const int kb_rem = args.num_kb % args.splits;
-  const int kb0 = split * kb_per + min(split, kb_rem);
-  const int nkb = kb_per + (split < kb_rem ? 1 : 0);
+  const int cta = blockIdx.x;
+  const int nkb = args.num_kb;
+  const long long U = args.units;
+  const int G = args.grid;
 
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    flags[0] = load_status(args.status) != 0 || nkb <= 0;
+    flags[0] = load_status(args.status) != 0;
     flags[1] = 0;
   }
   if (warp == 1) {
@@ -210,122 +288,213 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!skip) {
     if (warp == 0) {
       if (lane == 0) {
-        // Weights are streamed once per step: evict them first so activations stay in L2.
         const uint64_t pol_w = l2_policy_evict_first();
         const uint64_t pol_x = l2_policy_evict_last();
-        const uint64_t pol_a = SWAP ? pol_w : pol_x;
-        const uint64_t pol_b = SWAP ? pol_x : pol_w;
-        for (int i = 0; i < nkb; ++i) {
-          const int s = i % STAGES;
-          const uint32_t r = i / STAGES;
-          if (!mbar_wait(&empty[s], (r & 1) ^ 1, args.status, kStatusTimeoutEmpty)) break;
-          uint8_t* sa = smem + s * C::STAGE_BYTES;
-          uint8_t* sb = sa + C::NUM_A * C::A_BYTES;
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-          const int kx = (kb0 + i) * BK;
-          tma_load_2d_hint(sa, &tmA, &full[s], kx, m_tile * BM, pol_a);
-          if constexpr (C::NUM_A == 2)
-            tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[s], kx, m_tile * BM + args.inter, pol_a);
-          if constexpr (C::kSwiGLU && !SWAP) {
-            tma_load_2d_hint(sb, &tmB, &full[s], kx, n_tile * (BN / 2), pol_b);
-            tma_load_2d_hint(sb + (BN / 2) * 128, &tmB, &full[s], kx,
-                             n_tile * (BN / 2) + args.inter, pol_b);
-          } else {
-            tma_load_2d_hint(sb, &tmB, &full[s], kx, n_tile * BN, pol_b);
+        // Weight operand: A when swapped, B otherwise.  Issue the weight halves of the
+        // first stages before waiting on the previous kernel.
+        int i = 0;
+        bool waited = false;
+        // Pre-issue weights for up to STAGES k-blocks.
+        {
+          Sched pre(args, cta);
+          Segment sg;
+          int pi = 0;
+          while (pi < STAGES && pre.next(args, sg)) {
+            int mt, nt;
+            tile_coords(args, sg.tile, mt, nt);
+            for (int kb = sg.kb0; kb < sg.kb1 && pi < STAGES; ++kb, ++pi) {
+              uint8_t* sa = smem + pi * C::STAGE_BYTES;
+              uint8_t* sb = sa + C::NUM_A * C::A_BYTES;
+              mbar_arrive_expect_tx(&full[pi], C::STAGE_BYTES);
+              const int kx = kb * BK;
+              if constexpr (SWAP) {
+                tma_load_2d_hint(sa, &tmA, &full[pi], kx, mt * BM, pol_w);
+                if constexpr (C::NUM_A == 2)
+                  tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[pi], kx, mt * BM + args.inter, pol_w);
+              } else {
+                if constexpr (C::kSwiGLU) {
+                  tma_load_2d_hint(sb, &tmB, &full[pi], kx, nt * (BN / 2), pol_w);
+                  tma_load_2d_hint(sb + (BN / 2) * 128, &tmB, &full[pi], kx,
+                                   nt * (BN / 2) + args.inter, pol_w);
+                } else {
+                  tma_load_2d_hint(sb, &tmB, &full[pi], kx, nt * BN, pol_w);
+                }
+              }
+            }
           }
+        }
+        Sched sch(args, cta);
+        Segment sg;
+        while (sch.next(args, sg)) {
+          int mt, nt;
+          tile_coords(args, sg.tile, mt, nt);
+          bool ok = true;
+          for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
+            const int s = i % STAGES;
+            const uint32_t r = i / STAGES;
+            uint8_t* sa = smem + s * C::STAGE_BYTES;
+            uint8_t* sb = sa + C::NUM_A * C::A_BYTES;
+            const int kx = kb * BK;
+            if (i < STAGES) {
+              // Weight half already in flight; activations need the previous kernel.
+              if (!waited) {
+                pdl_wait();
+                waited = true;
+              }
+              if constexpr (SWAP) {
+                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_x);
+              } else {
+                tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_x);
+              }
+              continue;
+            }
+            if (!mbar_wait(&empty[s], (r & 1) ^ 1, args.status, kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            if constexpr (SWAP) {
+              tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_w);
+              if constexpr (C::NUM_A == 2)
+                tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[s], kx, mt * BM + args.inter, pol_w);
+              tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_x);
+            } else {
+              tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_x);
+              if constexpr (C::kSwiGLU) {
+                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * (BN / 2), pol_w);
+                tma_load_2d_hint(sb + (BN / 2) * 128, &tmB, &full[s], kx,
+                                 nt * (BN / 2) + args.inter, pol_w);
+              } else {
+                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_w);
+              }
+            }
+          }
+          if (!ok) break;
         }
       }
     } else if (warp == 1) {
       if (lane == 0) {
         constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+        int i = 0, j = 0;
         bool ok = true;
-        for (int i = 0; i < nkb; ++i) {
-          const int s = i % STAGES;
-          const uint32_t r = i / STAGES;
-          if (!mbar_wait(&full[s], r & 1, args.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
-          }
+        Sched sch(args, cta);
+        Segment sg;
+        while (ok && sch.next(args, sg)) {
+          const int b = j & 1;
+          if (!mbar_wait(&acc_empty[b], ((j >> 1) & 1) ^ 1, args.status, kStatusTimeoutAccum)) break;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + C::NUM_A * C::A_BYTES;
+          const uint32_t acc = tmem_base + b * C::ACC_COLS;
+          for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
+            const int s = i % STAGES;
+            if (!mbar_wait(&full[s], (i / STAGES) & 1, args.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t b_addr = a_addr + C::NUM_A * C::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t bd = umma_desc_sw128(b_addr + k * 32);
-            umma_f16(tmem_base, umma_desc_sw128(a_addr + k * 32), bd, idesc, (i | k) != 0);
-            if constexpr (C::NUM_A == 2)
-              umma_f16(tmem_base + BN, umma_desc_sw128(a_addr + C::A_BYTES + k * 32), bd, idesc,
-                       (i | k) != 0);
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint32_t accum = (kb > sg.kb0 || k > 0) ? 1u : 0u;
+              const uint64_t bd = umma_desc_sw128(b_addr + k * 32);
+              umma_f16(acc, umma_desc_sw128(a_addr + k * 32), bd, idesc, accum);
+              if constexpr (C::NUM_A == 2)
+                umma_f16(acc + BN, umma_desc_sw128(a_addr + C::A_BYTES + k * 32), bd, idesc, accum);
+            }
+            umma_commit(&empty[s]);
           }
-          umma_commit(&empty[s]);
+          if (!ok) break;
+          umma_commit(&acc_full[b]);
+          ++j;
         }
-        if (ok) umma_commit(accum_full);
       }
     } else {
-      // Epilogue warps 2..5: warp w may only touch TMEM lanes [32*(w%4), 32*(w%4)+32).
+      // Epilogue warps 2..5.
+      constexpr int CW = C::CW;
+      constexpr int UOFF = SWAP ? BN : BN / 2;
       const int q = warp & 3;
       const int row = q * 32 + lane;
-      const int m_glob = m_tile * BM + row;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-      bool ok = mbar_wait(accum_full, 0, args.status, kStatusTimeoutAccum);
-      if (ok) tc_fence_after();
-      bool do_final = ok;
-      constexpr int CW = (C::OUT_COLS >= 32 && BN >= 32) ? 32 : 16;  // columns per TMEM load
-      if (ok && args.splits > 1) {
-        float* mine = args.ws + ((long long)tile_id * args.splits + split) * C::ACC_COLS * BM;
+      pdl_wait();  // residual, output and workspace belong to the previous kernel until now
+      int j = 0;
+      Sched sch(args, cta);
+      Segment sg;
+      while (sch.next(args, sg)) {
+        const int b = j & 1;
+        int mt, nt;
+        tile_coords(args, sg.tile, mt, nt);
+        const int m_glob = mt * BM + row;
+        if (!mbar_wait(&acc_full[b], (j >> 1) & 1, args.status, kStatusTimeoutAccum)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + b * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+        const bool whole = sg.kb0 == 0 && sg.kb1 == nkb;
+        if (whole) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::ACC_COLS; c0 += CW) {
-          uint32_t v[CW];
-          tmem_load<CW>(taddr + c0, v);
-#pragma unroll
-          for (int j = 0; j < CW; ++j) __stcg(&mine[(c0 + j) * BM + row], __uint_as_float(v[j]));
-        }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64) {
-          const int old = atomicAdd(&args.counters[tile_id], 1);
-          flags[1] = (old == args.splits - 1);
-        }
-        named_bar_sync(1, 128);
-        do_final = flags[1] != 0;
-        if (do_final) __threadfence();
-      }
-      if (do_final) {
-        const float* base = args.ws + (long long)tile_id * args.splits * C::ACC_COLS * BM;
-        constexpr int UOFF = SWAP ? BN : BN / 2;  // column offset of the SwiGLU 'up' half
-#pragma unroll 1
-        for (int c0 = 0; c0 < C::OUT_COLS; c0 += CW) {
-          float v[CW], u[CW];
-          if (args.splits == 1) {
+          for (int c0 = 0; c0 < C::OUT_COLS; c0 += CW) {
+            float v[CW], uu[CW];
             uint32_t rv[CW];
             tmem_load<CW>(taddr + c0, rv);
 #pragma unroll
-            for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(rv[j]);
+            for (int t = 0; t < CW; ++t) v[t] = __uint_as_float(rv[t]);
             if constexpr (C::kSwiGLU) {
               tmem_load<CW>(taddr + c0 + UOFF, rv);
 #pragma unroll
-              for (int j = 0; j < CW; ++j) u[j] = __uint_as_float(rv[j]);
+              for (int t = 0; t < CW; ++t) uu[t] = __uint_as_float(rv[t]);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < CW; ++j) { v[j] = 0.f; u[j] = 0.f; }
-            for (int s = 0; s < args.splits; ++s) {
-              const float* p = base + (long long)s * C::ACC_COLS * BM;
-#pragma unroll
-              for (int j = 0; j < CW; ++j) v[j] += __ldcg(&p[(c0 + j) * BM + row]);
-              if constexpr (C::kSwiGLU) {
-#pragma unroll
-                for (int j = 0; j < CW; ++j) u[j] += __ldcg(&p[(c0 + UOFF + j) * BM + row]);
-              }
+            if (c0 + CW >= C::OUT_COLS) {
+              tc_fence_before();
+              mbar_arrive(&acc_empty[b]);
             }
+            store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
           }
-          const int n0 = n_tile * C::OUT_COLS + c0;
-          store_chunk<EPI, SWAP, CW>(args, m_glob, n0, v, u);
-        }
-        if (args.splits > 1) {
+        } else {
+          // Partial tile: slot 0 = this CTA's first segment, slot 1 = its last.
+          const int slot = sg.first ? 0 : 1;
+          float* mine = args.ws + ((long long)cta * 2 + slot) * C::ACC_COLS * BM;
+#pragma unroll 1
+          for (int c0 = 0; c0 < C::ACC_COLS; c0 += CW) {
+            uint32_t rv[CW];
+            tmem_load<CW>(taddr + c0, rv);
+#pragma unroll
+            for (int t = 0; t < CW; ++t) __stcg(&mine[(c0 + t) * BM + row], __uint_as_float(rv[t]));
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[b]);
+          // Contributors of this tile: CTAs whose unit ranges intersect it.
+          const long long t0 = (long long)sg.tile * nkb;
+          const int c_first = static_cast<int>(((t0 + 1) * G - 1) / U);
+          const int c_last = min(G - 1, static_cast<int>(((t0 + nkb) * (long long)G - 1) / U));
+          __threadfence();
           named_bar_sync(1, 128);
-          if (threadIdx.x == 64) args.counters[tile_id] = 0;  // re-arm for the next launch
+          if (threadIdx.x == 64) {
+            const int old = atomicAdd(&args.counters[sg.tile], 1);
+            flags[1] = (old == c_last - c_first);
+          }
+          named_bar_sync(1, 128);
+          const bool last = flags[1] != 0;
+          named_bar_sync(1, 128);  // flags[1] is reused by the next partial segment
+          if (last) {
+            __threadfence();
+#pragma unroll 1
+            for (int c0 = 0; c0 < C::OUT_COLS; c0 += CW) {
+              float v[CW], uu[CW];
+#pragma unroll
+              for (int t = 0; t < CW; ++t) { v[t] = 0.f; uu[t] = 0.f; }
+              for (int c = c_first; c <= c_last; ++c) {
+                const int sl = unit_begin(c, U, G) >= t0 ? 0 : 1;
+                const float* p = args.ws + ((long long)c * 2 + sl) * C::ACC_COLS * BM;
+#pragma unroll
+                for (int t = 0; t < CW; ++t) v[t] += __ldcg(&p[(c0 + t) * BM + row]);
+                if constexpr (C::kSwiGLU) {
+#pragma unroll
+                  for (int t = 0; t < CW; ++t) uu[t] += __ldcg(&p[(c0 + UOFF + t) * BM + row]);
+                }
+              }
+              store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
+            }
+            if (threadIdx.x == 64) args.counters[sg.tile] = 0;  // re-arm for the next launch
+          }
         }
+        ++j;
       }
     }
   }
@@ -338,32 +507,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int STAGES, int EPI, bool SWAP>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int m_tiles,
-            int n_tiles, cudaStream_t stream) {
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+            cudaStream_t stream) {
   using C = Cfg<BN, STAGES, EPI, SWAP>;
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, SWAP>;
-  static bool configured = false;  // per instantiation; attribute is per-function
+  static bool configured = false;
   if (!configured) {
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::SMEM_BYTES),
                "cudaFuncSetAttribute(gemm smem)");
     configured = true;
   }
-  dim3 grid(m_tiles, n_tiles, args.splits);
-  kern<<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, args);
-  check_cuda(cudaGetLastError(), "gemm_bf16_kernel launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(args.grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "gemm_bf16_kernel launch");
 }
 
 template <int EPI>
 void dispatch_swap(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                   int mt, int nt, cudaStream_t st);
+                   cudaStream_t st);
 template <int EPI>
 void dispatch_normal(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                     int mt, int nt, cudaStream_t st);
-
-inline int smem_stage_bytes(int bn, bool swiglu_swap) {
-  return (swiglu_swap ? 2 : 1) * BM * BK * 2 + bn * BK * 2;
-}
+                     cudaStream_t st);
 
 }  // namespace gemm_detail
 }  // namespace sil

@@ -1,0 +1,181 @@
+"""Coordinator-side session control over a stage ring, with restart-and-replay.
+
+Per request: open the session on the ring (stage 0 forwards it down),
+prefill the prompt, then drive one DECODE per output token into stage 0 and
+accept the TOKEN_RESULT it relays back.  Hidden states only flow stage to
+stage; the coordinator sees token ids (and, in verification mode, the last
+stage's logits).
+
+On a transport failure the controller asks its ``recover`` callback for a
+(possibly new) route generation, opens a fresh session, replays the prompt
+and every accepted token exactly as they were first computed, checks that
+the replay reproduces each accepted token (any divergence fails closed with
+:class:`IntegrityError`), and resumes at the first unaccepted position.
+
+Reference: si/coordinator/session_controller.py:99-1289 (token loop :236-263,
+_recover :926, replay :1006-1035).
+"""
+from __future__ import annotations
+
+import time
+import uuid
+from dataclasses import dataclass, field
+from typing import Awaitable, Callable
+
+import torch
+
+from ..protocol import stage_ring as sr
+from ..transport.stage_ring_net import ConnectionPool, TransportError
+from ..transport.tensor_codec import pack_tensor, unpack_tensor
+
+
+class IntegrityError(RuntimeError):
+    """A replay produced a token different from one already accepted."""
+
+
+class StageError(RuntimeError):
+    """A stage answered with an ERROR frame."""
+
+
+@dataclass
+class Route:
+    stage0: tuple[str, int]
+    generation: int
+    topology_id: str
+    model_revision: str
+    stage0_layers: tuple[int, int]
+    tokenizer_revision: str = "none"
+
+
+@dataclass
+class SessionResult:
+    request_id: str
+    tokens: list[int]
+    logits: list[torch.Tensor] = field(default_factory=list)
+    recoveries: int = 0
+    generations: list[int] = field(default_factory=list)
+    ttft_ms: float = 0.0
+    total_ms: float = 0.0
+
+    @property
+    def tpot_ms(self) -> float:
+        n = len(self.tokens)
+        return (self.total_ms - self.ttft_ms) / max(1, n - 1)
+
+
+Recover = Callable[[Route, Exception], Awaitable[Route]]
+
+
+class SessionController:
+    def __init__(self, route: Route, *, pool: ConnectionPool | None = None,
+                 recover: Recover | None = None, max_recoveries: int = 3,
+                 return_logits: bool = False):
+        self.route = route
+        self.pool = pool or ConnectionPool()
+        self.recover_cb = recover
+        self.max_recoveries = max_recoveries
+        self.return_logits = return_logits
+        self.seq = sr.SequenceAllocator()
+        self.events: list[dict] = []
+
+    def _msg(self, op, session_id, request_id, position, payload=b"", attrs=None, shape=(),
+             dtype="none") -> sr.StageMessage:
+        r = self.route
+        a = dict(attrs or {})
+        a["generation"] = r.generation
+        return sr.StageMessage(
+            operation=op, model_revision=r.model_revision, tokenizer_revision=r.tokenizer_revision,
+            topology_id=r.topology_id, stage_id=0, layer_start=r.stage0_layers[0],
+            layer_end=r.stage0_layers[1], session_id=session_id, request_id=request_id,
+            sequence_number=self.seq.next(session_id, sr.COORDINATOR, 0)
+            if op not in (sr.Operation.OPEN_SESSION, sr.Operation.HEALTH) else 0,
+            token_position=position, source_stage=sr.COORDINATOR, destination_stage=0,
+            tensor_shape=tuple(shape), tensor_dtype=dtype, payload=payload, attributes=a)
+
+    async def _call(self, msg) -> sr.StageMessage:
+        rep = await self.pool.send(*self.route.stage0, msg)
+        if rep.operation == sr.Operation.ERROR:
+            raise StageError(f"{rep.attributes.get('error')}: {rep.attributes.get('detail')}")
+        return rep
+
+    async def _run_tokens(self, session_id, request_id, ids: list[int], position: int,
+                          op: sr.Operation, replay: bool) -> tuple[int, torch.Tensor | None]:
+        pk = pack_tensor(torch.tensor(ids, dtype=torch.int64))
+        attrs = {"tensor": pk.attributes, "replay": replay}
+        if self.return_logits:
+            attrs["return_logits"] = True
+        rep = await self._call(self._msg(op, session_id, request_id, position, pk.payload, attrs,
+                                         pk.shape, "int64"))
+        logits = None
+        if rep.payload and "tensor" in rep.attributes:
+            logits = unpack_tensor(rep.payload, rep.attributes["tensor"])
+        return int(rep.attributes["token"]), logits
+
+    async def _open(self, session_id, request_id):
+        await self._call(self._msg(sr.Operation.OPEN_SESSION, session_id, request_id, -1))
+
+    async def _close(self, session_id, request_id, cancel=False):
+        op = sr.Operation.CANCEL_SESSION if cancel else sr.Operation.CLOSE_SESSION
+        try:
+            await self._call(self._msg(op, session_id, request_id, -1))
+        except (TransportError, StageError):
+            pass
+        self.seq.reset_session(session_id)
+
+    async def generate(self, prompt: list[int], max_new_tokens: int,
+                       request_id: str | None = None) -> SessionResult:
+        request_id = request_id or uuid.uuid4().hex[:12]
+        res = SessionResult(request_id, [])
+        t_start = time.perf_counter()
+        recoveries = 0
+        session_id = f"{request_id}:g{self.route.generation}"
+        res.generations.append(self.route.generation)
+        need_open = True
+        while True:
+            try:
+                if need_open:
+                    await self._open(session_id, request_id)
+                    need_open = False
+                    # (Re)build the session: prompt, then each accepted token one by one.
+                    tok, lg = await self._run_tokens(session_id, request_id, prompt, 0,
+                                                     sr.Operation.PREFILL, replay=bool(res.tokens))
+                    if not res.tokens:
+                        res.tokens.append(tok)
+                        res.logits.append(lg)
+                        res.ttft_ms = (time.perf_counter() - t_start) * 1e3
+                        self.events.append({"event": "first_token", "request": request_id})
+                    else:
+                        if tok != res.tokens[0]:
+                            raise IntegrityError(f"replay diverged at output 0: {tok} != {res.tokens[0]}")
+                        for i in range(len(res.tokens) - 1):
+                            t2, _ = await self._run_tokens(session_id, request_id, [res.tokens[i]],
+                                                           len(prompt) + i, sr.Operation.DECODE, True)
+                            if t2 != res.tokens[i + 1]:
+                                raise IntegrityError(
+                                    f"replay diverged at output {i + 1}: {t2} != {res.tokens[i + 1]}")
+                        self.events.append({"event": "replay_complete", "request": request_id,
+                                            "tokens": len(res.tokens)})
+                while len(res.tokens) < max_new_tokens:
+                    pos = len(prompt) + len(res.tokens) - 1
+                    tok, lg = await self._run_tokens(session_id, request_id, [res.tokens[-1]], pos,
+                                                     sr.Operation.DECODE, False)
+                    res.tokens.append(tok)
+                    res.logits.append(lg)
+                break
+            except (TransportError, StageError) as exc:
+                if isinstance(exc, StageError) and "IntegrityError" in str(exc):
+                    raise
+                recoveries += 1
+                self.events.append({"event": "recovery_started", "request": request_id,
+                                    "error": str(exc), "accepted": len(res.tokens)})
+                if recoveries > self.max_recoveries or self.recover_cb is None:
+                    raise
+                await self._close(session_id, request_id, cancel=True)
+                self.route = await self.recover_cb(self.route, exc)
+                res.generations.append(self.route.generation)
+                session_id = f"{request_id}:g{self.route.generation}:r{recoveries}"
+                need_open = True
+        await self._close(session_id, request_id)
+        res.recoveries = recoveries
+        res.total_ms = (time.perf_counter() - t_start) * 1e3
+        return res

@@ -1,0 +1,210 @@
+"""Persistent stage owner: loads its layer interval once and serves many sessions.
+
+Message flow per generated token (the ring):
+
+    coordinator --PREFILL/DECODE--> stage 0 --> stage 1 --> ... --> last stage
+    coordinator <--TOKEN_RESULT---- stage 0 <-- stage 1 <-- ... <-- (greedy token)
+
+Each stage validates the frame (model revision, topology, route generation,
+session, strict per-edge sequence numbers), runs its executor, and either
+forwards the boundary activation to the next stage and relays the
+TOKEN_RESULT back, or (last stage) selects the token and answers.  Sessions
+are opened on every stage by forwarding OPEN_SESSION down the ring, so the
+coordinator talks to stage 0 only and never relays hidden states.
+
+Reference: si/worker/stage_runtime.py:213 (``PersistentStageRuntime``):
+:1391 open_session, :1960 handle_message, :2137 _execute_message,
+:2221 forward, :2276 token result, :2428 relay.
+"""
+from __future__ import annotations
+
+import asyncio
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..protocol import stage_ring as sr
+from ..transport.stage_ring_net import ConnectionPool, TransportError
+from ..transport.tensor_codec import pack_tensor, unpack_tensor
+from .executors import StageExecutor
+
+
+@dataclass
+class RouteInfo:
+    topology_id: str
+    generation: int
+    model_revision: str
+    tokenizer_revision: str = "none"
+    next_hop: tuple[str, int] | None = None
+    next_stage: int | None = None
+
+
+@dataclass
+class OwnerStats:
+    sessions_opened: int = 0
+    sessions_closed: int = 0
+    frames: int = 0
+    rejected: int = 0
+    forward_ms: float = 0.0
+    tokens: int = 0
+    relayed: int = 0
+    errors: list = field(default_factory=list)
+
+
+class StageOwner:
+    def __init__(self, executor: StageExecutor, route: RouteInfo, *, max_queue: int = 64,
+                 compression: str = "none", pool: ConnectionPool | None = None):
+        self.ex = executor
+        self.spec = executor.spec
+        self.route = route
+        self.pool = pool or ConnectionPool()
+        self.seq_in = sr.SequenceValidator()
+        self.seq_out = sr.SequenceAllocator()
+        self.sessions = sr.SessionValidator(sr.SessionPin(
+            model_revision=route.model_revision, topology_id=route.topology_id,
+            stage_id=self.spec.stage_id, layer_range=(self.spec.layer_start, self.spec.layer_end)))
+        self.stats = OwnerStats()
+        self.compression = compression
+        self._sem = asyncio.Semaphore(max_queue)
+        self._lock = asyncio.Lock()  # executor calls are serialised per owner
+
+    # ------------------------------------------------------------ helpers
+    def _reply(self, req: sr.StageMessage, op: sr.Operation, *, status="OK", payload=b"",
+               attrs=None, shape=(), dtype="none") -> sr.StageMessage:
+        return sr.StageMessage(
+            operation=op, model_revision=req.model_revision, tokenizer_revision=req.tokenizer_revision,
+            topology_id=req.topology_id, stage_id=self.spec.stage_id,
+            layer_start=self.spec.layer_start, layer_end=self.spec.layer_end,
+            session_id=req.session_id, request_id=req.request_id,
+            sequence_number=req.sequence_number, token_position=req.token_position,
+            source_stage=self.spec.stage_id, destination_stage=req.source_stage,
+            tensor_shape=tuple(shape), tensor_dtype=dtype, payload=payload, status=status,
+            attributes=attrs or {})
+
+    def _error(self, req: sr.StageMessage, exc: Exception) -> list[sr.StageMessage]:
+        self.stats.rejected += 1
+        self.stats.errors.append(f"{type(exc).__name__}: {exc}")
+        return [self._reply(req, sr.Operation.ERROR, status="ERROR",
+                            attrs={"error": type(exc).__name__, "detail": str(exc)})]
+
+    def _downstream(self, req: sr.StageMessage, op: sr.Operation, *, payload=b"", attrs=None,
+                    shape=(), dtype="none") -> sr.StageMessage:
+        nxt = self.route.next_stage
+        return sr.StageMessage(
+            operation=op, model_revision=req.model_revision, tokenizer_revision=req.tokenizer_revision,
+            topology_id=req.topology_id, stage_id=nxt, layer_start=self._next_range[0],
+            layer_end=self._next_range[1], session_id=req.session_id, request_id=req.request_id,
+            sequence_number=self.seq_out.next(req.session_id, self.spec.stage_id, nxt),
+            token_position=req.token_position, source_stage=self.spec.stage_id,
+            destination_stage=nxt, tensor_shape=tuple(shape), tensor_dtype=dtype,
+            compression_mode=attrs.get("codec", "none") if attrs else "none", payload=payload,
+            attributes=dict(attrs or {}, generation=self.route.generation))
+
+    _next_range: tuple[int, int] = (0, 0)
+
+    def set_next_range(self, start: int, end: int) -> None:
+        self._next_range = (start, end)
+
+    async def _send_next(self, msg: sr.StageMessage) -> sr.StageMessage:
+        host, port = self.route.next_hop
+        return await self.pool.send(host, port, msg)
+
+    # ------------------------------------------------------------ dispatch
+    async def handle(self, msg: sr.StageMessage) -> list[sr.StageMessage]:
+        self.stats.frames += 1
+        op = msg.operation
+        try:
+            if op == sr.Operation.HEALTH:
+                return [self._reply(msg, sr.Operation.HEALTH, attrs=self.health())]
+            if op == sr.Operation.HELLO:
+                return [self._reply(msg, sr.Operation.HELLO, attrs={
+                    "stage_id": self.spec.stage_id, "generation": self.route.generation})]
+            gen = msg.attributes.get("generation", self.route.generation)
+            if gen != self.route.generation:
+                raise sr.SessionError(f"stale route generation {gen} (installed "
+                                      f"{self.route.generation})")
+            self.sessions.check(msg)
+            if op in (sr.Operation.PREFILL, sr.Operation.DECODE, sr.Operation.CLOSE_SESSION,
+                      sr.Operation.CANCEL_SESSION):
+                self.seq_in.check(msg)
+        except (sr.SessionError, sr.SequenceError) as exc:
+            return self._error(msg, exc)
+        async with self._sem:
+            try:
+                if op == sr.Operation.OPEN_SESSION:
+                    return await self._open(msg)
+                if op in (sr.Operation.CLOSE_SESSION, sr.Operation.CANCEL_SESSION):
+                    return await self._close(msg)
+                if op in (sr.Operation.PREFILL, sr.Operation.DECODE):
+                    return await self._execute(msg)
+                if op == sr.Operation.VERIFY_CANDIDATES:
+                    raise NotImplementedError("speculative verification is not enabled on stage owners")
+                raise sr.FrameError(f"unexpected operation {op.name}")
+            except TransportError:
+                raise
+            except Exception as exc:  # noqa: BLE001 - reported back as an ERROR frame
+                return self._error(msg, exc)
+
+    async def _open(self, msg):
+        async with self._lock:
+            self.ex.open(msg.session_id)
+        self.stats.sessions_opened += 1
+        if not self.spec.is_last:
+            rep = await self._send_next(self._downstream(msg, sr.Operation.OPEN_SESSION))
+            if rep.status != "OK":
+                return [self._reply(msg, sr.Operation.ERROR, status="ERROR", attrs=rep.attributes)]
+        return [self._reply(msg, sr.Operation.OPEN_SESSION)]
+
+    async def _close(self, msg):
+        async with self._lock:
+            self.ex.close(msg.session_id)
+        self.seq_in.reset_session(msg.session_id)
+        self.seq_out.reset_session(msg.session_id)
+        self.stats.sessions_closed += 1
+        if not self.spec.is_last:
+            try:
+                await self._send_next(self._downstream(msg, msg.operation))
+            except TransportError:
+                pass  # the downstream session dies with its connection
+        return [self._reply(msg, msg.operation)]
+
+    async def _execute(self, msg):
+        attrs = msg.attributes
+        x = unpack_tensor(msg.payload, attrs["tensor"])
+        t0 = time.perf_counter()
+        async with self._lock:
+            y = await asyncio.to_thread(self.ex.forward, msg.session_id, x, msg.token_position)
+        self.stats.forward_ms += (time.perf_counter() - t0) * 1e3
+        if self.spec.is_last:
+            last = y[-1].float()
+            token = int(torch.argmax(last))  # lowest id on ties
+            self.stats.tokens += 1
+            out_attrs = {"token": token, "replay": bool(attrs.get("replay", False))}
+            payload, shape, dtype = b"", (), "none"
+            if attrs.get("return_logits"):
+                pk = pack_tensor(last.cpu())
+                out_attrs["tensor"] = pk.attributes
+                payload, shape, dtype = pk.payload, pk.shape, "float32"
+            return [self._reply(msg, sr.Operation.TOKEN_RESULT, attrs=out_attrs, payload=payload,
+                                shape=shape, dtype=dtype)]
+        pk = pack_tensor(y, compression=self.compression)
+        fwd_attrs = {"tensor": pk.attributes, "codec": pk.attributes["codec"]}
+        for k in ("return_logits", "replay"):
+            if k in attrs:
+                fwd_attrs[k] = attrs[k]
+        rep = await self._send_next(self._downstream(msg, msg.operation, payload=pk.payload,
+                                                     attrs=fwd_attrs, shape=pk.shape,
+                                                     dtype=pk.attributes["dtype"]))
+        self.stats.relayed += 1
+        if rep.operation == sr.Operation.ERROR:
+            return [self._reply(msg, sr.Operation.ERROR, status="ERROR", attrs=rep.attributes)]
+        return [self._reply(msg, sr.Operation.TOKEN_RESULT, attrs=rep.attributes,
+                            payload=rep.payload, shape=rep.tensor_shape, dtype=rep.tensor_dtype)]
+
+    def health(self) -> dict:
+        s = self.stats
+        return {"stage_id": self.spec.stage_id, "layers": [self.spec.layer_start, self.spec.layer_end],
+                "generation": self.route.generation, "sessions_active": len(self.sessions.active),
+                "sessions_opened": s.sessions_opened, "frames": s.frames, "rejected": s.rejected,
+                "tokens": s.tokens, "forward_ms": round(s.forward_ms, 3)}

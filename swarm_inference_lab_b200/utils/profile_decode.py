@@ -1,0 +1,133 @@
+"""Decode-step and single-kernel timing harness (CUDA events, no profiler).
+
+    python -m swarm_inference_lab_b200.utils.profile_decode --batch 32 --ctx 2048 [--steps 5]
+    python -m swarm_inference_lab_b200.utils.profile_decode --op gemm --m 28672 --n 32 --k 4096 --swiglu
+    python -m swarm_inference_lab_b200.utils.profile_decode --op decode_attn --batch 32 --ctx 2048
+
+The decode mode builds the Llama-3-8B-shaped model with random weights and
+a KV cache whose pages hold random values (attention cost depends only on
+the context length), then runs eager decode steps: suitable for a kernel
+launch list under ``ncu`` (each step issues the same launch sequence).
+The op modes time one kernel on a small case and report achieved bytes/s
+and FLOP/s against the measured box peaks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+PEAKS = {"hbm_gbs": 6534.1, "bf16_tflops": 1649.5}
+
+
+def _peaks():
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"]}
+    except (OSError, KeyError, ValueError):
+        return PEAKS
+
+
+def time_fn(fn, iters: int = 20, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def op_gemm(a):
+    from ..ops import gemm
+    T, N, K = a.n, a.m, a.k
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    rows = 2 * N if a.swiglu else N
+    w = (torch.randn(rows, K, device="cuda") * 0.02).bfloat16()
+    ms = time_fn(lambda: gemm.linear(x, w, swiglu=a.swiglu), a.iters)
+    bytes_ = rows * K * 2 + T * K * 2 + T * N * 2
+    flops = 2 * T * rows * K
+    pk = _peaks()
+    return {"op": "gemm", "tokens": T, "out_features": N, "k": K, "swiglu": a.swiglu, "ms": ms,
+            "GBps": bytes_ / ms / 1e6, "TFLOPs": flops / ms / 1e9,
+            "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"],
+            "frac_bf16_of_measured": flops / ms / 1e9 / pk["bf16_tflops"]}
+
+
+def op_decode_attn(a):
+    from ..ops import attention as A
+    B, ctx, hq, hkv = a.batch, a.ctx, 32, 8
+    pages_per = (ctx + 63) // 64
+    P = B * pages_per
+    kc = torch.randn(P, hkv, 64, 128, device="cuda").bfloat16()
+    vc = torch.randn_like(kc)
+    bt = torch.arange(P, dtype=torch.int32, device="cuda").view(B, pages_per)
+    sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq, 128, device="cuda").bfloat16()
+    splits = A.decode_splits(B, hkv, pages_per)
+    ms = time_fn(lambda: A.paged_decode(q, kc, vc, bt, sl, num_splits=splits), a.iters)
+    bytes_ = 2 * B * ctx * hkv * 128 * 2
+    pk = _peaks()
+    return {"op": "paged_decode", "batch": B, "ctx": ctx, "splits": splits, "ms": ms,
+            "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"]}
+
+
+def decode_steps(a):
+    from ..engine.kv_cache import PagedKVCache
+    from ..models.config import preset
+    from ..models.dense import DenseModel, DenseWeights, ForwardBatch, TPInfo
+    from ..ops import attention as A
+    cfg = preset(a.model)
+    if a.layers:
+        cfg = cfg.replace(num_layers=a.layers)
+    w = DenseWeights.random(cfg, TPInfo(), "cuda", seed=0)
+    model = DenseModel(w, "cuda", max_positions=a.ctx + 64)
+    B = a.batch
+    pages_per = (a.ctx + 1 + 63) // 64
+    kv = PagedKVCache(cfg.num_layers, cfg.num_kv_heads, B * pages_per, "cuda")
+    kv.k.normal_()
+    kv.v.normal_()
+    bt = torch.arange(B * pages_per, dtype=torch.int32, device="cuda").view(B, pages_per)
+    pos = torch.full((B,), a.ctx, dtype=torch.int32, device="cuda")
+    slots = bt[:, a.ctx // 64] * 64 + a.ctx % 64
+    fb = ForwardBatch(ids=torch.randint(0, cfg.vocab_size, (B,), device="cuda"), positions=pos,
+                      slots=slots.int(), seq_lens=pos + 1, block_table=bt,
+                      last_idx=torch.arange(B, device="cuda"), is_decode=True,
+                      decode_splits=A.decode_splits(B, cfg.num_kv_heads, pages_per))
+    ms = time_fn(lambda: model.forward(fb, kv), a.steps, warmup=2)
+    wbytes = w.nbytes()
+    kvbytes = 2 * B * (a.ctx + 1) * cfg.num_layers * cfg.num_kv_heads * 128 * 2
+    pk = _peaks()
+    return {"mode": "decode_step_eager", "model": cfg.name, "batch": B, "ctx": a.ctx, "ms": ms,
+            "weight_bytes": wbytes, "kv_bytes": kvbytes,
+            "roofline_ms": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6,
+            "frac_of_roofline": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6 / ms}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", choices=["step", "gemm", "decode_attn"], default="step")
+    ap.add_argument("--model", default="llama-3-8b-shape")
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--m", type=int, default=4096)
+    ap.add_argument("--n", type=int, default=32)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--swiglu", action="store_true")
+    a = ap.parse_args()
+    out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn}[a.op](a)
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()
