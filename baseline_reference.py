@@ -1,0 +1,169 @@
+"""Reference arm of ``bench.py``: the UNMODIFIED reference engine, through its public API.
+
+The reference (installed under ``baseline/_ref``) runs dense decoders only
+through its Qwen3 fast engine (``swarm_inference.model.qwen3_engine.
+load_qwen3_fast_engine`` + ``Qwen3FastEngine.generate_batch``): there is no
+Llama path.  The arm therefore serves a Qwen3-architecture checkpoint with
+the Llama-3-8B dimensions (hidden 4096, 32 layers, 32 query / 8 KV heads of
+128, FFN 14336, vocab 128256, RoPE theta 500000), random N(0, 0.02) weights
+written as safetensors, synthetic uniform-random prompts of the benchmark
+shape, its fastest stock options (``qwen3_fast`` profile, static cache, SDPA
+attention, manual CUDA graphs) and reports the engine's own CUDA-event
+decode throughput.  The reference has no multi-GPU tensor parallelism (its
+TP is logical, on one device), so on N GPUs every rank serves an
+independent replica of the model on batch/N sequences: the reference's
+replica data-parallel strategy; the box value is the sum over ranks.
+"""
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import statistics
+import tempfile
+import time
+
+
+def _write_checkpoint(path: str, seed: int, device: str) -> None:
+    import torch
+    from safetensors.torch import save_file
+
+    H, L, NH, KV, D, FF, V = 4096, 32, 32, 8, 128, 14336, 128256
+    cfg = {
+        "architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": H,
+        "intermediate_size": FF, "num_hidden_layers": L, "num_attention_heads": NH,
+        "num_key_value_heads": KV, "head_dim": D, "vocab_size": V, "rope_theta": 500000.0,
+        "rms_norm_eps": 1e-5, "max_position_embeddings": 8192, "tie_word_embeddings": False,
+        "torch_dtype": "bfloat16", "hidden_act": "silu", "attention_bias": False,
+        "attention_dropout": 0.0, "bos_token_id": 0, "eos_token_id": 1,
+        "use_sliding_window": False, "sliding_window": None, "max_window_layers": L,
+        "initializer_range": 0.02, "use_cache": True,
+    }
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def rnd(*shape):
+        return torch.empty(shape, device=device, dtype=torch.bfloat16).normal_(0.0, 0.02, generator=gen).cpu()
+
+    index = {"metadata": {"total_size": 0}, "weight_map": {}}
+    total = 0
+
+    def flush(tensors, name):
+        nonlocal total
+        save_file(tensors, os.path.join(path, name), metadata={"format": "pt"})
+        for k, t in tensors.items():
+            index["weight_map"][k] = name
+            total += t.numel() * t.element_size()
+
+    flush({"model.embed_tokens.weight": rnd(V, H)}, "model-embed.safetensors")
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16)  # noqa: E731
+    for i in range(L):
+        p = f"model.layers.{i}."
+        flush({
+            p + "input_layernorm.weight": ones(H), p + "post_attention_layernorm.weight": ones(H),
+            p + "self_attn.q_proj.weight": rnd(NH * D, H), p + "self_attn.k_proj.weight": rnd(KV * D, H),
+            p + "self_attn.v_proj.weight": rnd(KV * D, H), p + "self_attn.o_proj.weight": rnd(H, NH * D),
+            p + "self_attn.q_norm.weight": ones(D), p + "self_attn.k_norm.weight": ones(D),
+            p + "mlp.gate_proj.weight": rnd(FF, H), p + "mlp.up_proj.weight": rnd(FF, H),
+            p + "mlp.down_proj.weight": rnd(H, FF),
+        }, f"model-layer{i:02d}.safetensors")
+    flush({"model.norm.weight": ones(H), "lm_head.weight": rnd(V, H)}, "model-head.safetensors")
+    index["metadata"]["total_size"] = total
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump(index, f)
+
+
+def run_reference_arm(args, rank, world, local, metric):
+    import torch
+    import torch.distributed as dist
+
+    try:
+        from swarm_inference.model.qwen3_engine import load_qwen3_fast_engine
+        from swarm_inference.model.qwen3_runtime import Qwen3EngineOptions
+    except Exception as exc:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"reference import failed: {exc}"[:300]}
+    from pathlib import Path
+
+    B_total, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
+    if B_total % world:
+        return {"impl": "reference", "unavailable": "batch not divisible by the replica count"}
+    B = B_total // world
+    root = os.environ.get("SIL_REF_CKPT_DIR") or tempfile.mkdtemp(prefix=f"ref_ckpt_r{rank}_")
+    ckpt = os.path.join(root, "qwen3-arch-llama3-8b-dims")
+    device = f"cuda:{local}"
+    try:
+        if not os.path.exists(os.path.join(ckpt, "model.safetensors.index.json")):
+            _write_checkpoint(ckpt, seed=0, device=device)
+        # The reference's fastest stock options first; its static cache needs a
+        # transformers<5 cache API, so fall back to its dynamic-cache path.
+        attempts = [("static", "manual_cuda_graph"), ("dynamic_reference", "eager")]
+        loaded, errors, used = None, [], None
+        for cache, compile_mode in attempts:
+            try:
+                opts = Qwen3EngineOptions.from_values(
+                    profile="qwen3_fast", attention_backend="sdpa", cache_backend=cache,
+                    max_sequence_length=P + K + W + 16, max_batch_size=B, compile_mode=compile_mode,
+                    cuda_graph_batch_sizes=(B,), final_worker_sampling=True,
+                    diagnostic_full_logits=False, boundary_diagnostics=False)
+                loaded = load_qwen3_fast_engine(
+                    model_id="synthetic/qwen3-arch-llama-3-8b-dims", model_revision="random-seed-0",
+                    model_path=Path(ckpt), options=opts, device=device)
+                g0 = torch.Generator().manual_seed(rank)
+                probe = torch.randint(0, 128256, (B, 8), generator=g0, dtype=torch.long)
+                loaded.engine.generate_batch(probe, request_ids=tuple(f"p{i}" for i in range(B)),
+                                             output_tokens=2, scheduler_policy="throughput")
+                used = f"{cache}+{compile_mode}"
+                break
+            except Exception as exc:  # noqa: BLE001
+                errors.append(f"{cache}+{compile_mode}: {type(exc).__name__}: {exc}"[:200])
+                loaded = None
+                torch.cuda.empty_cache()
+        if loaded is None:
+            return {"impl": "reference", "unavailable": " | ".join(errors)[:500]}
+        eng = loaded.engine
+        g = torch.Generator().manual_seed(rank)
+        inputs = torch.randint(0, 128256, (B, P), generator=g, dtype=torch.long)
+        eng.generate_batch(inputs, request_ids=tuple(f"w{i}" for i in range(B)),
+                           output_tokens=max(W, 2), scheduler_policy="throughput")
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = eng.generate_batch(inputs, request_ids=tuple(f"m{i}" for i in range(B)),
+                                 output_tokens=K + 1, scheduler_policy="throughput")
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - t0) * 1e3
+        m = res.metrics
+        decode_ms = float(m.decode_ms)
+        ttft = float(m.ttft_ms)
+        tpot = float(m.inter_token_latency_ms_p50)
+        vals = torch.tensor([decode_ms, ttft, tpot, float(B * K)], dtype=torch.float64, device=device)
+        if world > 1:
+            mx = vals.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            tot = vals.clone()
+            dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+            decode_ms, ttft, tpot = float(mx[0]), float(mx[1]), float(mx[2])
+        value = B_total * K / (decode_ms / 1e3)
+        return {
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": decode_ms / K, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random N(0,0.02) weights)",
+            "config": {"model": "qwen3-arch at llama-3-8b dims (reference has no llama path)",
+                       "global_batch": B_total, "seq_len": P, "decode_tokens": K,
+                       "parallelism": f"replica-dp{world}",
+                       "engine": "Qwen3FastEngine.generate_batch",
+                       "options": f"qwen3_fast, sdpa, {used}",
+                       "fallbacks": errors,
+                       "cuda_graph_status": getattr(m, "cuda_graph_admission_status", None)},
+            "ttft_ms_p50": ttft, "tpot_ms_p50": tpot, "wall_ms": wall_ms,
+            "impl": "reference",
+        }
+    except Exception as exc:  # noqa: BLE001
+        return {"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:400]}
+    finally:
+        if not os.environ.get("SIL_REF_KEEP_CKPT"):
+            shutil.rmtree(root, ignore_errors=True)

@@ -22,6 +22,16 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
                    const c10::optional<at::Tensor>& k_norm_w, double eps, at::Tensor& k_cache,
                    at::Tensor& v_cache, int64_t Hq, int64_t Hkv);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out);
+void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
+                    const std::vector<int64_t>& peers, int64_t rank, int64_t max_tiles,
+                    int64_t max_tokens, int64_t max_hidden, int64_t flags_off, int64_t slots_off,
+                    const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
+int64_t symm_alloc(int64_t bytes, int64_t device);
+void symm_free(int64_t ptr);
+std::string ipc_handle(int64_t ptr);
+int64_t ipc_open(const std::string& handle, int64_t device);
+void ipc_close(int64_t ptr);
+bool can_access_peer(int64_t dev, int64_t peer);
 void argmax(const at::Tensor& logits, at::Tensor& out);
 }  // namespace sil
 
@@ -34,4 +44,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_write", &sil::rope_kv_write, "q/k-norm + RoPE + paged KV write");
   m.def("embedding", &sil::embedding, "token embedding gather");
   m.def("argmax", &sil::argmax, "greedy argmax (lowest id on ties)");
+  m.def("gemm_allreduce", &sil::gemm_allreduce,
+        "tcgen05 GEMM fused with a one-shot all-reduce over NVLink peer memory (+ residual)");
+  m.def("symm_alloc", &sil::symm_alloc, "allocate a zeroed buffer for peer (IPC) sharing");
+  m.def("symm_free", &sil::symm_free, "free a symmetric buffer");
+  m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(sil::ipc_handle(p)); },
+        "CUDA IPC handle bytes of a symmetric buffer");
+  m.def("ipc_open", &sil::ipc_open, "open a peer's IPC handle; returns a device pointer");
+  m.def("ipc_close", &sil::ipc_close, "close a peer mapping");
+  m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

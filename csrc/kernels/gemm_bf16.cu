@@ -127,3 +127,68 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
 }
 
 }  // namespace sil
+
+namespace sil {
+using namespace gemm_detail;
+
+// h[T, H] += sum over the tensor-parallel group of (x_r[T, K_r] . W_r[H, K_r]^T).
+// One launch per rank: the tcgen05 GEMM computes this rank's partial, pushes it
+// tile by tile into every rank's symmetric buffer over NVLink, then reduces the
+// tiles it owns in rank order once all ranks have published them.
+void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
+                    const std::vector<int64_t>& peers, int64_t rank, int64_t max_tiles,
+                    int64_t max_tokens, int64_t max_hidden, int64_t flags_off, int64_t slots_off,
+                    const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  h.scalar_type() == at::kBFloat16,
+              "gemm_allreduce: bf16 tensors");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && h.stride(1) == 1, "gemm_allreduce: rows");
+  const int T = x.size(0), K = x.size(1), H = w.size(0);
+  TORCH_CHECK(w.size(1) == K && h.size(0) == T && h.size(1) == H, "gemm_allreduce: shapes");
+  const int size = static_cast<int>(peers.size());
+  TORCH_CHECK(size >= 1 && size <= kMaxTP && rank >= 0 && rank < size, "gemm_allreduce: group");
+  TORCH_CHECK(T <= max_tokens && T <= 128, "gemm_allreduce: too many tokens for the fused path");
+  TORCH_CHECK(H <= max_hidden && (H + BM - 1) / BM <= max_tiles, "gemm_allreduce: hidden too large");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  GemmArgs a{};
+  a.num_kb = (K + BK - 1) / BK;
+  a.inter = 0;
+  a.out = h.data_ptr();
+  a.ldo = h.stride(0);
+  a.res = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
+  a.ldr = h.stride(0);
+  a.ws = ws.data_ptr<float>();
+  a.counters = counters.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.tp_rank = static_cast<int>(rank);
+  a.tp_size = size;
+  for (int i = 0; i < size; ++i) a.peers[i] = reinterpret_cast<uint8_t*>(peers[i]);
+  a.flags_off = flags_off;
+  a.slots_off = slots_off;
+  a.max_tiles = static_cast<int>(max_tiles);
+  a.max_tokens = static_cast<int>(max_tokens);
+  a.max_hidden = static_cast<int>(max_hidden);
+  const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+  a.M = H;
+  a.N = T;
+  a.m_tiles = (H + BM - 1) / BM;
+  a.n_tiles = 1;
+  a.units = (long long)a.m_tiles * a.num_kb;
+  a.stream_k = 1;
+  a.group_m = 16;
+  const int sms = device_sm_count();
+  long long g = std::min<long long>(sms, a.units);
+  g = std::max<long long>(1, std::min<long long>(g, (a.units + 3) / 4));
+  TORCH_CHECK(g * 2 * bn * BM <= ws.numel(), "gemm_allreduce: workspace too small");
+  TORCH_CHECK(a.m_tiles <= counters.numel(), "gemm_allreduce: counters too small");
+  a.grid = static_cast<int>(g);
+  CUtensorMap ta = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, K,
+                                w.stride(0), BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K,
+                                x.stride(0), bn, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  dispatch_swap<kEpiAllReduce>(bn, ta, tb, a, stream);
+}
+
+}  // namespace sil

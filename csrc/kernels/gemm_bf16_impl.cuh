@@ -42,7 +42,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
-enum EpiKind : int { kEpiBf16 = 0, kEpiResAdd = 1, kEpiSwiGLU = 2, kEpiF32 = 3 };
+enum EpiKind : int { kEpiBf16 = 0, kEpiResAdd = 1, kEpiSwiGLU = 2, kEpiF32 = 3, kEpiAllReduce = 4 };
+
+constexpr int kMaxTP = 8;
 
 struct GemmArgs {
   int M;          // valid rows of A (features when swapped, tokens otherwise)
@@ -62,7 +64,60 @@ struct GemmArgs {
   float* ws;      // [G][2][ACC_COLS][128] partial tiles
   int* counters;  // per tile arrivals
   int* status;
+  // kEpiAllReduce: one-shot all-reduce over NVLink peer memory fused into the epilogue.
+  int tp_rank, tp_size;
+  uint8_t* peers[kMaxTP];   // symmetric buffer base of every rank (own rank included)
+  long long flags_off;      // byte offset of flags[2][kMaxTP][max_tiles] (uint32)
+  long long slots_off;      // byte offset of slots[2][kMaxTP][max_tokens][max_hidden] (bf16)
+  int max_tiles, max_tokens, max_hidden;
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t* ar_flag(const GemmArgs& a, int rank_buf, int par, int src,
+                                             int tile) {
+  return reinterpret_cast<uint32_t*>(a.peers[rank_buf] + a.flags_off) +
+         ((long long)(par * kMaxTP + src) * a.max_tiles + tile);
+}
+
+__device__ __forceinline__ __nv_bfloat16* ar_slot(const GemmArgs& a, int rank_buf, int par,
+                                                  int src) {
+  return reinterpret_cast<__nv_bfloat16*>(a.peers[rank_buf] + a.slots_off) +
+         (long long)(par * kMaxTP + src) * a.max_tokens * a.max_hidden;
+}
+
+// Push CW token columns of feature m (rank-local partial, rounded to bf16) into
+// slot [par][tp_rank] of every rank's buffer.
+template <int CW>
+__device__ __forceinline__ void ar_push(const GemmArgs& a, int par, int m, int n0,
+                                        const float (&v)[CW]) {
+  if (m >= a.M) return;
+  for (int p = 0; p < a.tp_size; ++p) {
+    __nv_bfloat16* dst = ar_slot(a, p, par, a.tp_rank);
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      const int n = n0 + j;
+      if (n < a.N) dst[(long long)n * a.max_hidden + m] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+// Publish a finished tile to every rank: each thread fences its stores, the
+// epilogue warps meet, one thread raises the tile's flag on every rank.
+__device__ __forceinline__ void ar_publish(const GemmArgs& a, int par, uint32_t epoch, int tile) {
+  __threadfence_system();
+  named_bar_sync(1, 128);
+  if (threadIdx.x == 64)
+    for (int p = 0; p < a.tp_size; ++p) st_release_sys(ar_flag(a, p, par, a.tp_rank, tile), epoch);
+}
 
 template <int BN, int STAGES, int EPI, bool SWAP>
 struct Cfg {
@@ -415,6 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q = warp & 3;
       const int row = q * 32 + lane;
       pdl_wait();  // residual, output and workspace belong to the previous kernel until now
+      uint32_t epoch = 0;
+      int par = 0;
+      if constexpr (EPI == kEpiAllReduce) {
+        epoch = *reinterpret_cast<volatile uint32_t*>(args.peers[args.tp_rank]) + 1u;
+        par = epoch & 1;
+      }
       int j = 0;
       Sched sch(args, cta);
       Segment sg;
@@ -444,8 +505,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_before();
               mbar_arrive(&acc_empty[b]);
             }
-            store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
+            if constexpr (EPI == kEpiAllReduce) ar_push<CW>(args, par, m_glob, nt * C::OUT_COLS + c0, v);
+            else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
           }
+          if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
         } else {
           // Partial tile: slot 0 = this CTA's first segment, slot 1 = its last.
           const int slot = sg.first ? 0 : 1;
@@ -479,22 +542,117 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[CW], uu[CW];
 #pragma unroll
               for (int t = 0; t < CW; ++t) { v[t] = 0.f; uu[t] = 0.f; }
-              for (int c = c_first; c <= c_last; ++c) {
-                const int sl = unit_begin(c, U, G) >= t0 ? 0 : 1;
-                const float* p = args.ws + ((long long)c * 2 + sl) * C::ACC_COLS * BM;
+              // Contributors in batches of 4: issue every load of a batch before
+              // summing, then add in contributor order (deterministic).
+              constexpr int NB = 4;
+              for (int cb = c_first; cb <= c_last; cb += NB) {
+                float pv[NB][CW];
 #pragma unroll
-                for (int t = 0; t < CW; ++t) v[t] += __ldcg(&p[(c0 + t) * BM + row]);
+                for (int q2 = 0; q2 < NB; ++q2) {
+                  const int c = cb + q2;
+                  if (c <= c_last) {
+                    const int sl = unit_begin(c, U, G) >= t0 ? 0 : 1;
+                    const float* p = args.ws + ((long long)c * 2 + sl) * C::ACC_COLS * BM;
+#pragma unroll
+                    for (int t = 0; t < CW; ++t) pv[q2][t] = __ldcg(&p[(c0 + t) * BM + row]);
+                  }
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < NB; ++q2)
+                  if (cb + q2 <= c_last) {
+#pragma unroll
+                    for (int t = 0; t < CW; ++t) v[t] += pv[q2][t];
+                  }
                 if constexpr (C::kSwiGLU) {
 #pragma unroll
-                  for (int t = 0; t < CW; ++t) uu[t] += __ldcg(&p[(c0 + UOFF + t) * BM + row]);
+                  for (int q2 = 0; q2 < NB; ++q2) {
+                    const int c = cb + q2;
+                    if (c <= c_last) {
+                      const int sl = unit_begin(c, U, G) >= t0 ? 0 : 1;
+                      const float* p = args.ws + ((long long)c * 2 + sl) * C::ACC_COLS * BM;
+#pragma unroll
+                      for (int t = 0; t < CW; ++t) pv[q2][t] = __ldcg(&p[(c0 + UOFF + t) * BM + row]);
+                    }
+                  }
+#pragma unroll
+                  for (int q2 = 0; q2 < NB; ++q2)
+                    if (cb + q2 <= c_last) {
+#pragma unroll
+                      for (int t = 0; t < CW; ++t) uu[t] += pv[q2][t];
+                    }
                 }
               }
-              store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
+              if constexpr (EPI == kEpiAllReduce) ar_push<CW>(args, par, m_glob, nt * C::OUT_COLS + c0, v);
+              else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
             }
             if (threadIdx.x == 64) args.counters[sg.tile] = 0;  // re-arm for the next launch
+            if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
           }
         }
         ++j;
+      }
+      if constexpr (EPI == kEpiAllReduce) {
+        // Phase 2: (tile, 8-token group) items spread over every CTA; each waits for the
+        // tile's flags from all ranks, then sums the bf16 partials in rank order (fp32)
+        // plus the residual, in place.  All loads of an item are issued before the sum.
+        const int NG = (args.N + 7) / 8;
+        const int items = args.m_tiles * NG;
+        for (int itm = cta; itm < items; itm += G) {
+          const int t = itm / NG, ng = itm % NG;
+          if (threadIdx.x == 64) {
+            for (int r = 0; r < args.tp_size; ++r) {
+              const uint32_t* f = ar_flag(args, args.tp_rank, par, r, t);
+              const uint64_t t_start = globaltimer_ns();
+              uint32_t it = 0;
+              while (ld_acquire_sys(f) != epoch) {
+                if ((++it & 255u) == 0 &&
+                    (load_status(args.status) != 0 || globaltimer_ns() - t_start > SIL_WAIT_TIMEOUT_NS)) {
+                  raise_status(args.status, kStatusTimeoutPeer);
+                  break;
+                }
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+          const int m = t * BM + row;
+          if (m < args.M) {
+            float acc[8];
+            __nv_bfloat16 pv[kMaxTP][8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int n = ng * 8 + jj;
+              acc[jj] = n < args.N ? __bfloat162float(args.res[(long long)n * args.ldr + m]) : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxTP; ++r) {
+              if (r < args.tp_size) {
+                const __nv_bfloat16* src = ar_slot(args, args.tp_rank, par, r);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                  const int n = ng * 8 + jj;
+                  pv[r][jj] = n < args.N ? __ldcg(src + (long long)n * args.max_hidden + m)
+                                         : __float2bfloat16_rn(0.f);
+                }
+              }
+            }
+            // Rank-ordered sum of the partials, then the residual (same order on every rank).
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              float sum = 0.f;
+#pragma unroll
+              for (int r = 0; r < kMaxTP; ++r)
+                if (r < args.tp_size) sum += __bfloat162float(pv[r][jj]);
+              acc[jj] += sum;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int n = ng * 8 + jj;
+              if (n < args.N)
+                reinterpret_cast<__nv_bfloat16*>(args.out)[(long long)n * args.ldo + m] =
+                    __float2bfloat16_rn(acc[jj]);
+            }
+          }
+        }
       }
     }
   }
@@ -503,6 +661,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (EPI == kEpiAllReduce) {
+    // Advance this rank's epoch once every CTA of the launch has read it.
+    if (threadIdx.x == 0) {
+      pdl_wait();
+      volatile uint32_t* st = reinterpret_cast<volatile uint32_t*>(args.peers[args.tp_rank]);
+      const uint32_t e = st[0] + 1u;
+      __threadfence();
+      const uint32_t old = atomicAdd(const_cast<uint32_t*>(&st[1]), 1u);
+      if (old == static_cast<uint32_t>(G - 1)) {
+        st[1] = 0u;
+        __threadfence();
+        st[0] = e;
+      }
+    }
   }
 }
 

@@ -214,8 +214,9 @@ class DenseModel:
         if self.tp.size == 1:
             gemm.linear(x, w, out=h, residual=h)
             return None
-        if getattr(self.comm, "fused_gemm_allreduce", None) is not None:
-            return self.comm.fused_gemm_allreduce(x, w)
+        fused = getattr(self.comm, "fused_gemm_allreduce_residual", None)
+        if fused is not None:
+            return fused(x, w, h)  # h += allreduce(x @ w.T) in one kernel
         out = gemm.linear(x, w)
         return self._reduce(out)
 

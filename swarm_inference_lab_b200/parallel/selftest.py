@@ -1,0 +1,97 @@
+"""Multi-GPU tensor-parallel self-test (one process per GPU).
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m swarm_inference_lab_b200.parallel.selftest
+
+Builds the same random model at TP=1 (every rank, full weights) and at
+TP=world (sharded) and compares greedy decode logits of the fused
+GEMM+all-reduce path and of the NCCL baseline path against TP=1, for a
+prefill (NCCL fallback) followed by decode steps (fused kernel).  Rank 0
+prints one JSON line.  Process-group timeout is short so a stuck peer ends
+the run with an error instead of waiting forever.
+"""
+from __future__ import annotations
+
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from ..engine.kv_cache import PagedKVCache
+    from ..models.config import preset
+    from ..models.dense import DenseModel, DenseWeights, ForwardBatch, TPInfo
+    from ..ops.workspace import get_workspace
+    from .comm import LocalComm, NcclComm
+    from .fused_tp import FusedTPComm
+
+    cfg = preset(os.environ.get("SIL_SELFTEST_MODEL", "tiny-llama-gpu")).replace(num_layers=2)
+    if cfg.num_kv_heads < world:
+        cfg = cfg.replace(num_kv_heads=world, num_heads=max(cfg.num_heads, world * 2))
+    B, P = 4, 100
+    nccl = NcclComm()
+    fused = FusedTPComm(nccl, dev, max_tokens=128, hidden=cfg.hidden_size)
+    results = {}
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(0))
+
+    def run(tp, comm):
+        w = DenseWeights.random(cfg, tp, dev, seed=7)
+        model = DenseModel(w, dev, comm=comm, max_positions=1024)
+        pages = (P + 8 + 63) // 64
+        kv = PagedKVCache(cfg.num_layers, model.num_kv_local, B * pages, dev)
+        bt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
+        flat = ids.reshape(-1).to(dev)
+        pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(B)
+        slots = (bt[:, :1] * 64).repeat(1, P).reshape(-1) + pos  # pages are contiguous per seq
+        fb = ForwardBatch(ids=flat, positions=pos, slots=slots.int(),
+                          seq_lens=torch.full((B,), P, dtype=torch.int32, device=dev),
+                          block_table=bt, last_idx=torch.arange(B, device=dev) * P + P - 1,
+                          is_decode=False,
+                          cu_q=torch.arange(0, B * P + 1, P, dtype=torch.int32, device=dev),
+                          max_q_len=P)
+        h = model.forward_hidden(fb, kv)
+        logits = [model.logits(h, fb)]
+        tok = model.greedy(logits[0])
+        for s in range(4):
+            p = P + s
+            fbd = ForwardBatch(ids=tok, positions=torch.full((B,), p, dtype=torch.int32, device=dev),
+                               slots=(bt[:, 0] * 64 + p).int(),
+                               seq_lens=torch.full((B,), p + 1, dtype=torch.int32, device=dev),
+                               block_table=bt, last_idx=torch.arange(B, device=dev), is_decode=True,
+                               decode_splits=2)
+            h = model.forward_hidden(fbd, kv)
+            lg = model.logits(h, fbd)
+            logits.append(lg)
+            tok = model.greedy(lg)
+        torch.cuda.synchronize()
+        return logits, tok
+
+    full, tok_full = run(TPInfo(), LocalComm())
+    for name, comm in (("nccl", nccl), ("fused", fused)):
+        shard, tok = run(TPInfo(rank, world), comm)
+        errs = []
+        for a, b in zip(full, shard):
+            v0, _ = TPInfo(rank, world).split(cfg.vocab_size)
+            ref = a[:, v0:v0 + b.shape[1]]
+            errs.append((ref - b).abs().max().item() / (ref.abs().max().item() + 1e-6))
+        results[name] = {"max_rel_err": max(errs), "tokens_equal": bool(torch.equal(tok, tok_full))}
+    get_workspace(dev).check()
+    ok = all(r["max_rel_err"] < 0.05 for r in results.values())
+    out = torch.tensor([1.0 if ok else 0.0], device=dev)
+    dist.all_reduce(out, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        print(json.dumps({"world": world, "ok": bool(out.item() == 1.0), **results}), flush=True)
+    fused.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
