@@ -27,6 +27,18 @@ void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
                     int64_t max_tokens, int64_t max_hidden, int64_t flags_off, int64_t slots_off,
                     const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
 int64_t symm_alloc(int64_t bytes, int64_t device);
+void gemm_grouped(const at::Tensor& xp, const at::Tensor& w, at::Tensor& out,
+                  const at::Tensor& offsets, int64_t num_groups, bool swiglu, int64_t rows_hint,
+                  const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
+void moe_topk(const at::Tensor& logits, int64_t k, int64_t mode, bool renorm,
+              const c10::optional<at::Tensor>& bias, int64_t n_group, int64_t topk_group,
+              double scale, at::Tensor& ids, at::Tensor& weights);
+void moe_permute(const at::Tensor& ids, int64_t E, at::Tensor& offsets, at::Tensor& rows,
+                 const c10::optional<at::Tensor>& counts);
+void moe_gather(const at::Tensor& x, const at::Tensor& rows, int64_t k, at::Tensor& xp);
+void moe_combine(const at::Tensor& y, const at::Tensor& rows, const at::Tensor& w, int64_t k,
+                 const c10::optional<at::Tensor>& res, const c10::optional<at::Tensor>& shared,
+                 at::Tensor& out, const c10::optional<at::Tensor>& row_limit);
 void symm_free(int64_t ptr);
 std::string ipc_handle(int64_t ptr);
 int64_t ipc_open(const std::string& handle, int64_t device);
@@ -46,6 +58,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &sil::argmax, "greedy argmax (lowest id on ties)");
   m.def("gemm_allreduce", &sil::gemm_allreduce,
         "tcgen05 GEMM fused with a one-shot all-reduce over NVLink peer memory (+ residual)");
+  m.def("gemm_grouped", &sil::gemm_grouped, "grouped (per-expert) tcgen05 GEMM");
+  m.def("moe_topk", &sil::moe_topk, "router top-k (softmax or sigmoid+bias+group)");
+  m.def("moe_permute", &sil::moe_permute, "expert counts, offsets and sorted rows");
+  m.def("moe_gather", &sil::moe_gather, "gather token rows into expert order");
+  m.def("moe_combine", &sil::moe_combine, "weighted combine of expert outputs");
   m.def("symm_alloc", &sil::symm_alloc, "allocate a zeroed buffer for peer (IPC) sharing");
   m.def("symm_free", &sil::symm_free, "free a symmetric buffer");
   m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(sil::ipc_handle(p)); },

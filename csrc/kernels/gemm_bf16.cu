@@ -192,3 +192,76 @@ void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
 }
 
 }  // namespace sil
+
+namespace sil {
+using namespace gemm_detail;
+
+// Grouped GEMM over experts.  xp: [R, K] expert-sorted activation rows; group g
+// owns rows [offsets[g], offsets[g+1]) (device int32, produced by moe_permute).
+// w: stacked weights [G * Wr, K] (Wr = 2*inter for SwiGLU).  out: [R, Nout].
+// `rows_hint` (expected rows per group) picks the operand order: swapped
+// (weights as the MMA M side) for decode-sized groups.
+void gemm_grouped(const at::Tensor& xp, const at::Tensor& w, at::Tensor& out,
+                  const at::Tensor& offsets, int64_t num_groups, bool swiglu, int64_t rows_hint,
+                  const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status) {
+  TORCH_CHECK(xp.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "gemm_grouped: bf16 tensors");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() >= num_groups + 1,
+              "gemm_grouped: int32 offsets [G+1]");
+  TORCH_CHECK(num_groups >= 1 && num_groups <= kMaxGroups, "gemm_grouped: 1..1024 groups");
+  const int R = xp.size(0), K = xp.size(1);
+  TORCH_CHECK(w.size(1) == K && w.size(0) % num_groups == 0, "gemm_grouped: weight shape");
+  const long long Wr = w.size(0) / num_groups;
+  const int inter = swiglu ? static_cast<int>(Wr / 2) : 0;
+  const int Nout = swiglu ? inter : static_cast<int>(Wr);
+  TORCH_CHECK(!swiglu || inter % 128 == 0, "gemm_grouped: SwiGLU inter % 128");
+  TORCH_CHECK(out.size(0) == R && out.size(1) == Nout, "gemm_grouped: output shape");
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(xp.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  GemmArgs a{};
+  a.num_kb = (K + BK - 1) / BK;
+  a.inter = inter;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.ws = ws.data_ptr<float>();
+  a.counters = counters.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.grp_offsets = offsets.data_ptr<int>();
+  a.num_groups = static_cast<int>(num_groups);
+  a.w_group_rows = Wr;
+  a.stream_k = 0;
+  a.group_m = 16;
+  const bool swap = rows_hint <= 64;
+  int bn;
+  CUtensorMap ta, tb;
+  if (swap) {
+    bn = rows_hint <= 16 ? 16 : rows_hint <= 32 ? 32 : 64;
+    a.M = Nout;
+    a.N = 0;  // per group
+    a.m_tiles = (Nout + BM - 1) / BM;
+    a.n_tiles = 1;
+    ta = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.size(0), K, w.stride(0),
+                      BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    tb = make_tmap_2d(xp.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, xp.stride(0), bn, BK,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    bn = 256;
+    const int out_cols = swiglu ? bn / 2 : bn;
+    a.M = 0;  // per group
+    a.N = Nout;
+    a.m_tiles = 1;
+    a.n_tiles = (Nout + out_cols - 1) / out_cols;
+    ta = make_tmap_2d(xp.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, xp.stride(0), BM, BK,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    tb = make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.size(0), K, w.stride(0),
+                      swiglu ? bn / 2 : bn, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  a.units = 0;
+  a.grid = device_sm_count();
+  if (swiglu) dispatch_grouped<kEpiSwiGLU>(swap, bn, ta, tb, a, stream);
+  else dispatch_grouped<kEpiBf16>(swap, bn, ta, tb, a, stream);
+}
+
+}  // namespace sil

@@ -70,7 +70,14 @@ struct GemmArgs {
   long long flags_off;      // byte offset of flags[2][kMaxTP][max_tiles] (uint32)
   long long slots_off;      // byte offset of slots[2][kMaxTP][max_tokens][max_hidden] (bf16)
   int max_tiles, max_tokens, max_hidden;
+  // Grouped (MoE expert) GEMM: group g owns activation/output rows
+  // [grp_offsets[g], grp_offsets[g+1]) and weight rows [g*w_group_rows, (g+1)*w_group_rows).
+  const int* grp_offsets;
+  int num_groups;
+  long long w_group_rows;
 };
+
+constexpr int kMaxGroups = 1024;
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -147,34 +154,35 @@ __device__ __forceinline__ long long unit_begin(int c, long long U, int G) {
 // Store CW consecutive accumulator columns [n0, n0+CW) of accumulator row `m_glob`.
 template <int EPI, bool SWAP, int CW>
 __device__ __forceinline__ void store_chunk(const GemmArgs& a, int m_glob, int n0,
-                                            const float (&v)[CW], const float (&u)[CW]) {
-  if (m_glob >= a.M) return;
+                                            const float (&v)[CW], const float (&u)[CW],
+                                            int Mv, int Nv, int roff) {
+  if (m_glob >= Mv) return;
   if constexpr (SWAP) {
 #pragma unroll
     for (int j = 0; j < CW; ++j) {
       const int n = n0 + j;
-      if (n < a.N) {
+      if (n < Nv) {
         float r = v[j];
         if constexpr (EPI == kEpiSwiGLU) r = silu_f(v[j]) * u[j];
         if constexpr (EPI == kEpiF32) {
-          reinterpret_cast<float*>(a.out)[(long long)n * a.ldo + m_glob] = r;
+          reinterpret_cast<float*>(a.out)[(long long)(roff + n) * a.ldo + m_glob] = r;
         } else {
-          if constexpr (EPI == kEpiResAdd) r += __bfloat162float(a.res[(long long)n * a.ldr + m_glob]);
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)n * a.ldo + m_glob] =
+          if constexpr (EPI == kEpiResAdd) r += __bfloat162float(a.res[(long long)(roff + n) * a.ldr + m_glob]);
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(long long)(roff + n) * a.ldo + m_glob] =
               __float2bfloat16_rn(r);
         }
       }
     }
   } else {
     if constexpr (EPI == kEpiF32) {
-      float* o = reinterpret_cast<float*>(a.out) + (long long)m_glob * a.ldo;
-      if (n0 + CW <= a.N && (a.ldo & 3) == 0) {
+      float* o = reinterpret_cast<float*>(a.out) + (long long)(roff + m_glob) * a.ldo;
+      if (n0 + CW <= Nv && (a.ldo & 3) == 0) {
 #pragma unroll
         for (int j = 0; j < CW; j += 4)
           *reinterpret_cast<float4*>(o + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       } else {
         for (int j = 0; j < CW; ++j)
-          if (n0 + j < a.N) o[n0 + j] = v[j];
+          if (n0 + j < Nv) o[n0 + j] = v[j];
       }
     } else {
       float r[CW];
@@ -183,12 +191,12 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int m_glob, int n
         r[j] = v[j];
         if constexpr (EPI == kEpiSwiGLU) r[j] = silu_f(v[j]) * u[j];
       }
-      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (long long)m_glob * a.ldo;
-      const bool vec = (n0 + CW <= a.N) && ((a.ldo & 7) == 0) &&
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (long long)(roff + m_glob) * a.ldo;
+      const bool vec = (n0 + CW <= Nv) && ((a.ldo & 7) == 0) &&
                        (EPI != kEpiResAdd || (a.ldr & 7) == 0);
       if (vec) {
         if constexpr (EPI == kEpiResAdd) {
-          const __nv_bfloat16* rr = a.res + (long long)m_glob * a.ldr + n0;
+          const __nv_bfloat16* rr = a.res + (long long)(roff + m_glob) * a.ldr + n0;
 #pragma unroll
           for (int j = 0; j < CW; j += 8) {
             uint4 q = *reinterpret_cast<const uint4*>(rr + j);
@@ -210,9 +218,9 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int m_glob, int n
       } else {
         for (int j = 0; j < CW; ++j) {
           const int n = n0 + j;
-          if (n < a.N) {
+          if (n < Nv) {
             float x = r[j];
-            if constexpr (EPI == kEpiResAdd) x += __bfloat162float(a.res[(long long)m_glob * a.ldr + n]);
+            if constexpr (EPI == kEpiResAdd) x += __bfloat162float(a.res[(long long)(roff + m_glob) * a.ldr + n]);
             o[n] = __float2bfloat16_rn(x);
           }
         }
@@ -247,12 +255,12 @@ struct Segment {
 struct Sched {
   long long u, u_end, u_begin;
   int t, tiles;
-  __device__ __forceinline__ Sched(const GemmArgs& a, int cta) {
+  __device__ __forceinline__ Sched(const GemmArgs& a, int cta, int total_tiles = -1) {
     u_begin = (a.units * cta) / a.grid;
     u_end = (a.units * (cta + 1)) / a.grid;
     u = u_begin;
     t = cta;
-    tiles = a.m_tiles * a.n_tiles;
+    tiles = total_tiles >= 0 ? total_tiles : a.m_tiles * a.n_tiles;
   }
   __device__ __forceinline__ bool next(const GemmArgs& a, Segment& s) {
     if (a.stream_k) {
@@ -291,12 +299,63 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mt
   nt = in / gm;
 }
 
+// Where a tile's operands and outputs live.  Non-grouped: the whole problem.
+// Grouped: the expert group that owns the tile (found in the per-CTA prefix of
+// tiles per group, s_pref[0..num_groups]).
+struct TileCtx {
+  int mt, nt;
+  int a_base, b_base;  // tensor-map row of the group's first A / B row
+  int Mv, Nv;          // valid accumulator rows / columns
+  int roff;            // output row offset of the group
+};
 
-template <int BN, int STAGES, int EPI, bool SWAP>
+template <bool GROUPED, bool SWAP>
+__device__ __forceinline__ TileCtx make_ctx(const GemmArgs& a, int tile, const int* s_pref) {
+  TileCtx c;
+  if constexpr (!GROUPED) {
+    tile_coords(a, tile, c.mt, c.nt);
+    c.a_base = c.b_base = c.roff = 0;
+    c.Mv = a.M;
+    c.Nv = a.N;
+  } else {
+    int lo = 0, hi = a.num_groups;  // largest g with s_pref[g] <= tile
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_pref[mid] <= tile) lo = mid; else hi = mid;
+    }
+    const int g = lo;
+    const int lt = tile - s_pref[g];
+    const int off0 = a.grp_offsets[g];
+    const int cnt = a.grp_offsets[g + 1] - off0;
+    const long long wrow = (long long)g * a.w_group_rows;
+    c.roff = off0;
+    if constexpr (SWAP) {
+      c.mt = lt % a.m_tiles;
+      c.nt = lt / a.m_tiles;
+      c.a_base = static_cast<int>(wrow);
+      c.b_base = off0;
+      c.Mv = a.M;
+      c.Nv = cnt;
+    } else {
+      const int mtg = (cnt + BM - 1) / BM;
+      c.mt = lt % mtg;
+      c.nt = lt / mtg;
+      c.a_base = off0;
+      c.b_base = static_cast<int>(wrow);
+      c.Mv = cnt;
+      c.Nv = a.N;
+    }
+  }
+  return c;
+}
+
+
+template <int BN, int STAGES, int EPI, bool SWAP, bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using C = Cfg<BN, STAGES, EPI, SWAP>;
+  static_assert(!GROUPED || EPI != kEpiAllReduce, "grouped all-reduce is not supported");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -306,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;    // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] skip, [1] last contributor
+  int* s_pref = flags + 4;                              // grouped: tiles before group g
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -339,6 +399,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const bool skip = flags[0] != 0;
+  int total_tiles = -1;
+  if constexpr (GROUPED) {
+    // Group sizes come from the previous kernel (routing): wait, then build the
+    // per-group tile prefix in shared memory.
+    pdl_wait();
+    for (int g = threadIdx.x; g < args.num_groups; g += kThreads) {
+      const int cnt = args.grp_offsets[g + 1] - args.grp_offsets[g];
+      s_pref[g + 1] = SWAP ? args.m_tiles * ((cnt + BN - 1) / BN)
+                           : ((cnt + BM - 1) / BM) * args.n_tiles;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_pref[0] = 0;
+      for (int g = 0; g < args.num_groups; ++g) s_pref[g + 1] += s_pref[g];
+    }
+    __syncthreads();
+    total_tiles = s_pref[args.num_groups];
+  }
 
   if (!skip) {
     if (warp == 0) {
@@ -346,43 +424,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t pol_w = l2_policy_evict_first();
         const uint64_t pol_x = l2_policy_evict_last();
         // Weight operand: A when swapped, B otherwise.  Issue the weight halves of the
-        // first stages before waiting on the previous kernel.
+        // first stages before waiting on the previous kernel (not for grouped GEMMs,
+        // whose tile -> expert map comes from the previous kernel).
+        constexpr int BROWS = (C::kSwiGLU && !SWAP) ? BN / 2 : BN;  // B rows per load
         int i = 0;
-        bool waited = false;
-        // Pre-issue weights for up to STAGES k-blocks.
-        {
+        bool waited = GROUPED;
+        int npre = 0;
+        if constexpr (!GROUPED) {
           Sched pre(args, cta);
           Segment sg;
-          int pi = 0;
-          while (pi < STAGES && pre.next(args, sg)) {
-            int mt, nt;
-            tile_coords(args, sg.tile, mt, nt);
-            for (int kb = sg.kb0; kb < sg.kb1 && pi < STAGES; ++kb, ++pi) {
-              uint8_t* sa = smem + pi * C::STAGE_BYTES;
+          while (npre < STAGES && pre.next(args, sg)) {
+            const TileCtx tc = make_ctx<GROUPED, SWAP>(args, sg.tile, s_pref);
+            for (int kb = sg.kb0; kb < sg.kb1 && npre < STAGES; ++kb, ++npre) {
+              uint8_t* sa = smem + npre * C::STAGE_BYTES;
               uint8_t* sb = sa + C::NUM_A * C::A_BYTES;
-              mbar_arrive_expect_tx(&full[pi], C::STAGE_BYTES);
+              mbar_arrive_expect_tx(&full[npre], C::STAGE_BYTES);
               const int kx = kb * BK;
               if constexpr (SWAP) {
-                tma_load_2d_hint(sa, &tmA, &full[pi], kx, mt * BM, pol_w);
+                tma_load_2d_hint(sa, &tmA, &full[npre], kx, tc.a_base + tc.mt * BM, pol_w);
                 if constexpr (C::NUM_A == 2)
-                  tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[pi], kx, mt * BM + args.inter, pol_w);
+                  tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[npre], kx,
+                                   tc.a_base + tc.mt * BM + args.inter, pol_w);
               } else {
-                if constexpr (C::kSwiGLU) {
-                  tma_load_2d_hint(sb, &tmB, &full[pi], kx, nt * (BN / 2), pol_w);
-                  tma_load_2d_hint(sb + (BN / 2) * 128, &tmB, &full[pi], kx,
-                                   nt * (BN / 2) + args.inter, pol_w);
-                } else {
-                  tma_load_2d_hint(sb, &tmB, &full[pi], kx, nt * BN, pol_w);
-                }
+                tma_load_2d_hint(sb, &tmB, &full[npre], kx, tc.b_base + tc.nt * BROWS, pol_w);
+                if constexpr (C::kSwiGLU)
+                  tma_load_2d_hint(sb + BROWS * 128, &tmB, &full[npre], kx,
+                                   tc.b_base + tc.nt * BROWS + args.inter, pol_w);
               }
             }
           }
         }
-        Sched sch(args, cta);
+        Sched sch(args, cta, total_tiles);
         Segment sg;
         while (sch.next(args, sg)) {
-          int mt, nt;
-          tile_coords(args, sg.tile, mt, nt);
+          const TileCtx tc = make_ctx<GROUPED, SWAP>(args, sg.tile, s_pref);
           bool ok = true;
           for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
             const int s = i % STAGES;
@@ -390,18 +465,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* sa = smem + s * C::STAGE_BYTES;
             uint8_t* sb = sa + C::NUM_A * C::A_BYTES;
             const int kx = kb * BK;
-            if (i < STAGES) {
+            if (i < npre) {
               // Weight half already in flight; activations need the previous kernel.
               if (!waited) {
                 pdl_wait();
                 waited = true;
               }
               if constexpr (SWAP) {
-                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_x);
+                tma_load_2d_hint(sb, &tmB, &full[s], kx, tc.b_base + tc.nt * BN, pol_x);
               } else {
-                tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_x);
+                tma_load_2d_hint(sa, &tmA, &full[s], kx, tc.a_base + tc.mt * BM, pol_x);
               }
               continue;
+            }
+            if (!waited) {
+              pdl_wait();
+              waited = true;
             }
             if (!mbar_wait(&empty[s], (r & 1) ^ 1, args.status, kStatusTimeoutEmpty)) {
               ok = false;
@@ -409,19 +488,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
             if constexpr (SWAP) {
-              tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_w);
+              tma_load_2d_hint(sa, &tmA, &full[s], kx, tc.a_base + tc.mt * BM, pol_w);
               if constexpr (C::NUM_A == 2)
-                tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[s], kx, mt * BM + args.inter, pol_w);
-              tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_x);
+                tma_load_2d_hint(sa + C::A_BYTES, &tmA, &full[s], kx,
+                                 tc.a_base + tc.mt * BM + args.inter, pol_w);
+              tma_load_2d_hint(sb, &tmB, &full[s], kx, tc.b_base + tc.nt * BN, pol_x);
             } else {
-              tma_load_2d_hint(sa, &tmA, &full[s], kx, mt * BM, pol_x);
-              if constexpr (C::kSwiGLU) {
-                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * (BN / 2), pol_w);
-                tma_load_2d_hint(sb + (BN / 2) * 128, &tmB, &full[s], kx,
-                                 nt * (BN / 2) + args.inter, pol_w);
-              } else {
-                tma_load_2d_hint(sb, &tmB, &full[s], kx, nt * BN, pol_w);
-              }
+              tma_load_2d_hint(sa, &tmA, &full[s], kx, tc.a_base + tc.mt * BM, pol_x);
+              tma_load_2d_hint(sb, &tmB, &full[s], kx, tc.b_base + tc.nt * BROWS, pol_w);
+              if constexpr (C::kSwiGLU)
+                tma_load_2d_hint(sb + BROWS * 128, &tmB, &full[s], kx,
+                                 tc.b_base + tc.nt * BROWS + args.inter, pol_w);
             }
           }
           if (!ok) break;
@@ -432,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
         int i = 0, j = 0;
         bool ok = true;
-        Sched sch(args, cta);
+        Sched sch(args, cta, total_tiles);
         Segment sg;
         while (ok && sch.next(args, sg)) {
           const int b = j & 1;
@@ -477,13 +554,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         par = epoch & 1;
       }
       int j = 0;
-      Sched sch(args, cta);
+      Sched sch(args, cta, total_tiles);
       Segment sg;
       while (sch.next(args, sg)) {
         const int b = j & 1;
-        int mt, nt;
-        tile_coords(args, sg.tile, mt, nt);
-        const int m_glob = mt * BM + row;
+        const TileCtx tc = make_ctx<GROUPED, SWAP>(args, sg.tile, s_pref);
+        const int nt = tc.nt;
+        const int m_glob = tc.mt * BM + row;
         if (!mbar_wait(&acc_full[b], (j >> 1) & 1, args.status, kStatusTimeoutAccum)) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + b * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
@@ -506,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive(&acc_empty[b]);
             }
             if constexpr (EPI == kEpiAllReduce) ar_push<CW>(args, par, m_glob, nt * C::OUT_COLS + c0, v);
-            else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
+            else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
           }
           if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
         } else {
@@ -583,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
               if constexpr (EPI == kEpiAllReduce) ar_push<CW>(args, par, m_glob, nt * C::OUT_COLS + c0, v);
-              else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu);
+              else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
             }
             if (threadIdx.x == 64) args.counters[sg.tile] = 0;  // re-arm for the next launch
             if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
@@ -679,22 +756,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES, int EPI, bool SWAP>
+template <int BN, int STAGES, int EPI, bool SWAP, bool GROUPED = false>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
             cudaStream_t stream) {
   using C = Cfg<BN, STAGES, EPI, SWAP>;
-  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, SWAP>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, SWAP, GROUPED>;
+  constexpr int kSmem = C::SMEM_BYTES + (GROUPED ? (kMaxGroups + 8) * 4 : 0);
   static bool configured = false;
   if (!configured) {
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::SMEM_BYTES),
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem),
                "cudaFuncSetAttribute(gemm smem)");
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(args.grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -710,6 +787,9 @@ void dispatch_swap(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const G
 template <int EPI>
 void dispatch_normal(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                      cudaStream_t st);
+template <int EPI>
+void dispatch_grouped(bool swap, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const GemmArgs& a, cudaStream_t st);
 
 }  // namespace gemm_detail
 }  // namespace sil

@@ -220,6 +220,12 @@ class DenseModel:
         out = gemm.linear(x, w)
         return self._reduce(out)
 
+    def mlp(self, li: int, L, x: torch.Tensor, h: torch.Tensor):
+        """SwiGLU MLP on the normalised input ``x``; adds into ``h`` (returns None) or
+        returns the partial sum still to be added by the next norm."""
+        act = gemm.linear(x, L.w_gate_up, swiglu=True)
+        return self._row_parallel(act, L.w_down, h)
+
     def forward_hidden(self, fb: ForwardBatch, kv, h: torch.Tensor | None = None) -> torch.Tensor:
         """Run the local layers; returns the residual stream ``h`` [T, H] (bf16)."""
         cfg = self.cfg
@@ -251,8 +257,7 @@ class DenseModel:
                 norm.rmsnorm(h, L.mlp_norm, eps, out=x)
             else:
                 norm.rmsnorm(pending, L.mlp_norm, eps, out=x, residual=h)
-            act = gemm.linear(x, L.w_gate_up, swiglu=True)
-            pending = self._row_parallel(act, L.w_down, h)
+            pending = self.mlp(li, L, x, h)
         if pending is not None:
             h.add_(pending)
         return h

@@ -80,10 +80,22 @@ class ReferenceDecoder:
                 "wv": t(p + "self_attn.v_proj.weight", (cfg.num_kv_heads * D, H)),
                 "wo": t(p + "self_attn.o_proj.weight", (H, cfg.num_heads * D)),
                 "ln2": t(p + "post_attention_layernorm.weight", (H,)),
-                "wg": t(p + "mlp.gate_proj.weight", (cfg.intermediate_size, H)),
-                "wu": t(p + "mlp.up_proj.weight", (cfg.intermediate_size, H)),
-                "wd": t(p + "mlp.down_proj.weight", (H, cfg.intermediate_size)),
             }
+            if cfg.is_moe and li >= cfg.first_k_dense:
+                E, I = cfg.num_experts, cfg.moe_intermediate_size
+                L["router"] = t(p + "mlp.gate.weight", (E, H))
+                L["experts"] = [(t(f"{p}mlp.experts.{e}.gate_proj.weight", (I, H)),
+                                 t(f"{p}mlp.experts.{e}.up_proj.weight", (I, H)),
+                                 t(f"{p}mlp.experts.{e}.down_proj.weight", (H, I))) for e in range(E)]
+                if cfg.n_shared_experts:
+                    Is = I * cfg.n_shared_experts
+                    L["shared"] = (t(p + "mlp.shared_experts.gate_proj.weight", (Is, H)),
+                                   t(p + "mlp.shared_experts.up_proj.weight", (Is, H)),
+                                   t(p + "mlp.shared_experts.down_proj.weight", (H, Is)))
+            else:
+                L["wg"] = t(p + "mlp.gate_proj.weight", (cfg.intermediate_size, H))
+                L["wu"] = t(p + "mlp.up_proj.weight", (cfg.intermediate_size, H))
+                L["wd"] = t(p + "mlp.down_proj.weight", (H, cfg.intermediate_size))
             if cfg.qk_norm:
                 L["qn"] = t(p + "self_attn.q_norm.weight", (D,))
                 L["kn"] = t(p + "self_attn.k_norm.weight", (D,))
@@ -95,6 +107,29 @@ class ReferenceDecoder:
             self.lm_head = t(name, (cfg.vocab_size, H))
         mp = max_positions or cfg.max_position_embeddings
         self.cos_sin = rope_cos_sin_table(mp, D, cfg.rope_theta, cfg.rope_scaling).to(self.device)
+
+    def _moe(self, L, m: torch.Tensor) -> torch.Tensor:
+        from ..ops.moe import MODE_SIGMOID_GROUP, MODE_SOFTMAX, route_reference
+        cfg = self.cfg
+        sig = cfg.router == "sigmoid_group"
+        ids, w = route_reference(m.float() @ L["router"].float().T, cfg.num_experts_per_tok,
+                                 mode=MODE_SIGMOID_GROUP if sig else MODE_SOFTMAX,
+                                 renorm=cfg.norm_topk_prob, n_group=cfg.n_group,
+                                 topk_group=cfg.topk_group,
+                                 scale=cfg.routed_scaling_factor if sig else 1.0)
+        out = torch.zeros_like(m, dtype=torch.float32)
+        for e in torch.unique(ids).tolist():
+            sel = (ids == e)
+            tok = sel.any(-1).nonzero().squeeze(-1)
+            we = (w * sel).sum(-1)[tok]
+            g, u, d = L["experts"][e]
+            xe = m[tok]
+            ye = (torch.nn.functional.silu(xe @ g.T) * (xe @ u.T)) @ d.T
+            out.index_add_(0, tok, we[:, None].float() * ye.float())
+        if "shared" in L:
+            g, u, d = L["shared"]
+            out += ((torch.nn.functional.silu(m @ g.T) * (m @ u.T)) @ d.T).float()
+        return out.to(m.dtype)
 
     def new_cache(self) -> RefCache:
         return RefCache()
@@ -145,8 +180,11 @@ class ReferenceDecoder:
             o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vf).to(self.dtype)
             h = h + o.reshape(T, nq * D) @ L["wo"].T
             m = _rms(h, L["ln2"], eps)
-            act = torch.nn.functional.silu(m @ L["wg"].T) * (m @ L["wu"].T)
-            h = h + act @ L["wd"].T
+            if "router" in L:
+                h = h + self._moe(L, m)
+            else:
+                act = torch.nn.functional.silu(m @ L["wg"].T) * (m @ L["wu"].T)
+                h = h + act @ L["wd"].T
         if not self.with_head:
             return h
         return (_rms(h, self.norm, eps).float() @ self.lm_head.float().T)

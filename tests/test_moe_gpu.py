@@ -1,0 +1,112 @@
+"""MoE kernels (router top-k, permute, grouped tcgen05 GEMM, combine) vs fp32 PyTorch."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (37, 8, 2), (64, 128, 8), (5, 384, 8)])
+def test_softmax_topk(T, E, k):
+    from swarm_inference_lab_b200.ops import moe
+    logits = torch.randn(T, E, device="cuda")
+    ids, w = moe.route(logits, k)
+    rid, rw = moe.route_reference(logits, k)
+    assert torch.equal(ids, rid)
+    assert torch.allclose(w, rw, atol=1e-5)
+
+
+@pytest.mark.parametrize("n_group,topk_group", [(1, 1), (8, 4)])
+def test_sigmoid_group_topk(n_group, topk_group):
+    from swarm_inference_lab_b200.ops import moe
+    T, E, k = 33, 256, 8
+    logits = torch.randn(T, E, device="cuda")
+    bias = 0.1 * torch.randn(E, device="cuda")
+    kw = dict(mode=moe.MODE_SIGMOID_GROUP, renorm=True, bias=bias, n_group=n_group,
+              topk_group=topk_group, scale=2.5)
+    ids, w = moe.route(logits, k, **kw)
+    rid, rw = moe.route_reference(logits, k, **kw)
+    assert torch.equal(ids, rid)
+    assert torch.allclose(w, rw, atol=1e-5)
+
+
+def test_permute_is_a_bucket_sort():
+    from swarm_inference_lab_b200.ops import moe
+    E, T, k = 16, 100, 4
+    ids = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
+    offsets, rows, counts = moe.permute(ids, E)
+    assert torch.equal(counts.long(), torch.bincount(ids.reshape(-1).long(), minlength=E))
+    assert offsets[0].item() == 0 and offsets[-1].item() == T * k
+    r = rows.long()
+    assert torch.equal(torch.sort(r).values, torch.arange(T * k, device="cuda"))
+    e = ids.reshape(-1).long()
+    assert bool(((r >= offsets[e].long()) & (r < offsets[e + 1].long())).all())
+
+
+@pytest.mark.parametrize("rows_hint", [4, 32, 200])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_grouped_gemm(rows_hint, swiglu):
+    from swarm_inference_lab_b200.ops import moe
+    E, K, N = 6, 512, 256
+    counts = torch.tensor([0, 3, 17, 1, 140, 9])
+    offsets = torch.zeros(E + 1, dtype=torch.int32)
+    offsets[1:] = counts.cumsum(0)
+    R = int(offsets[-1])
+    xp = torch.randn(R, K, device="cuda").bfloat16()
+    rows = 2 * N if swiglu else N
+    w = (0.05 * torch.randn(E * rows, K, device="cuda")).bfloat16()
+    out = moe.grouped_linear(xp, w, offsets.cuda(), E, swiglu=swiglu, rows_hint=rows_hint)
+    torch.cuda.synchronize()
+    for g in range(E):
+        a, b = int(offsets[g]), int(offsets[g + 1])
+        if a == b:
+            continue
+        ref = xp[a:b].float() @ w[g * rows:(g + 1) * rows].float().T
+        if swiglu:
+            ref = torch.nn.functional.silu(ref[:, :N]) * ref[:, N:]
+        err = (out[a:b].float() - ref).abs().max().item()
+        assert err < 3e-2 * ref.abs().max().item() + 1e-2, (g, err)
+
+
+@pytest.mark.parametrize("T,E,k,inter", [(4, 8, 2, 256), (64, 32, 4, 128), (300, 8, 2, 256)])
+def test_moe_mlp_end_to_end(T, E, k, inter):
+    from swarm_inference_lab_b200.ops import moe
+    H = 512
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    router = (0.05 * torch.randn(E, H, device="cuda")).bfloat16()
+    gu = (0.05 * torch.randn(E * 2 * inter, H, device="cuda")).bfloat16()
+    dn = (0.05 * torch.randn(E * H, inter, device="cuda")).bfloat16()
+    res = torch.randn(T, H, device="cuda").bfloat16()
+    out = moe.moe_mlp(x, router, gu, dn, E, k, residual=res)
+    ref, _, _ = moe.moe_mlp_reference(x, router, gu, dn, E, k, residual=res)
+    torch.cuda.synchronize()
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err < 5e-2, err
+
+
+def test_moe_model_matches_reference():
+    from swarm_inference_lab_b200.engine.kv_cache import PagedKVCache
+    from swarm_inference_lab_b200.models.config import ModelConfig
+    from swarm_inference_lab_b200.models.dense import ForwardBatch, TPInfo
+    from swarm_inference_lab_b200.models.moe import MoEModel, MoEWeights
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    cfg = ModelConfig(name="tiny-moe", family="qwen3_moe", vocab_size=2048, hidden_size=512,
+                      num_layers=2, num_heads=4, num_kv_heads=2, head_dim=128,
+                      intermediate_size=1024, qk_norm=True, num_experts=8,
+                      num_experts_per_tok=2, moe_intermediate_size=256, rms_norm_eps=1e-6)
+    w = MoEWeights.random(cfg, TPInfo(), "cuda", seed=11)
+    model = MoEModel(w, "cuda", max_positions=512)
+    kv = PagedKVCache(cfg.num_layers, cfg.num_kv_heads, 8, "cuda")
+    T = 70
+    ids = torch.randint(0, cfg.vocab_size, (T,), device="cuda")
+    fb = ForwardBatch(ids=ids, positions=torch.arange(T, dtype=torch.int32, device="cuda"),
+                      slots=torch.arange(T, dtype=torch.int32, device="cuda"),
+                      seq_lens=torch.tensor([T], dtype=torch.int32, device="cuda"),
+                      block_table=torch.arange(8, dtype=torch.int32, device="cuda")[None],
+                      last_idx=torch.arange(T, device="cuda"), is_decode=False,
+                      cu_q=torch.tensor([0, T], dtype=torch.int32, device="cuda"), max_q_len=T)
+    logits = model.logits(model.forward_hidden(fb, kv), fb)
+    ref = ReferenceDecoder(cfg, random_source(11, device="cuda"), device="cuda", dtype=torch.bfloat16)
+    rl = ref.forward(ids)
+    rel = (logits - rl).abs().max().item() / rl.abs().max().item()
+    agree = (logits.argmax(-1) == rl.argmax(-1)).float().mean().item()
+    assert rel < 0.08 and agree > 0.8, (rel, agree)
