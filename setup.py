@@ -50,6 +50,7 @@ if native_sources:
             include_dirs=[os.path.join(ROOT, "csrc", "include")],
             extra_compile_args={"cxx": ["-O3", "-std=c++17", "-fopenmp"]},
             extra_link_args=["-fopenmp"],
+            libraries=["crypto"],
         )
     )
 
@@ -59,4 +60,5 @@ setup(
     packages=["swarm_inference_lab_b200"],
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={"console_scripts": ["swarm=swarm_inference_lab_b200.cli:main"]},
 )

@@ -1,0 +1,190 @@
+"""Control plane on CPU: identities, leases, TLS, pairing, state, planner, engines, CLI."""
+import asyncio
+import json
+import time
+
+import pytest
+
+from swarm_inference_lab_b200.security.identity import (Identity, LeaseVerifier, RouteLease,
+                                                        SignatureError, StageAssignment, issue_lease,
+                                                        sign_record, verify_record)
+
+
+def _lease(gen=1, ttl=60.0, wfp="sha256:w"):
+    return RouteLease("topo", gen, "rev", "tok", "dense", "bfloat16",
+                      [StageAssignment(0, "w0", wfp, 0, 2, "127.0.0.1:1", "127.0.0.1:2")],
+                      expires_at=time.time() + ttl)
+
+
+def test_signatures_and_tamper():
+    a = Identity.generate("a")
+    rec = sign_record(a, {"x": 1})
+    assert verify_record(rec, {a.fingerprint})["x"] == 1
+    rec2 = dict(rec, x=2)
+    with pytest.raises(SignatureError):
+        verify_record(rec2)
+    with pytest.raises(SignatureError):
+        verify_record(rec, {"sha256:someone-else"})
+
+
+def test_identity_persistence(tmp_path):
+    p = tmp_path / "id.json"
+    a = Identity.load_or_create(p, "n")
+    b = Identity.load(p)
+    assert a.fingerprint == b.fingerprint
+    assert (p.stat().st_mode & 0o777) == 0o600
+
+
+def test_route_lease_rules():
+    coord = Identity.generate("coord")
+    v = LeaseVerifier(coord.fingerprint)
+    signed = issue_lease(coord, _lease(gen=1))
+    v.verify(signed, worker_fingerprint="sha256:w", model_revision="rev")
+    with pytest.raises(SignatureError, match="nonce|stale"):
+        v.verify(signed)  # replay
+    with pytest.raises(SignatureError, match="stale"):
+        v.verify(issue_lease(coord, _lease(gen=1)))
+    with pytest.raises(SignatureError, match="expired"):
+        v.verify(issue_lease(coord, _lease(gen=5, ttl=-1)))
+    other = Identity.generate("evil")
+    with pytest.raises(SignatureError, match="untrusted"):
+        v.verify(issue_lease(other, _lease(gen=9)))
+    with pytest.raises(SignatureError, match="does not assign"):
+        v.verify(issue_lease(coord, _lease(gen=10)), worker_fingerprint="sha256:other")
+
+
+def test_tls_cert_binds_fingerprint():
+    from swarm_inference_lab_b200.security.tls import cert_fingerprint_binding, create_ca, issue_node_cert
+    ca = create_ca("c")
+    node = issue_node_cert(ca, "n1", "sha256:abc", ["127.0.0.1", "node1"])
+    assert cert_fingerprint_binding(node.cert) == "sha256:abc"
+
+
+def test_pairing_end_to_end(tmp_path):
+    from swarm_inference_lab_b200.cluster.pairing import PairingError, PairingManager, join
+    from swarm_inference_lab_b200.cluster.state import ClusterStateStore
+    from swarm_inference_lab_b200.security.tls import cert_fingerprint_binding, create_ca
+    coord = ClusterStateStore(tmp_path / "coord")
+    ca = create_ca("lab")
+
+    async def go():
+        pm = PairingManager(coord, "127.0.0.1:0")
+        port = await pm.start("127.0.0.1", 0)
+        pm.endpoint = f"127.0.0.1:{port}"
+        coord.create_cluster("lab", pm.endpoint, ca.cert, ca.key)
+        inv = pm.invite()
+        node = ClusterStateStore(tmp_path / "node")
+        rep = await join(inv.uri(), node, "gpu-node-1", capabilities={"gpus": 8})
+        # single use
+        with pytest.raises(PairingError):
+            await join(inv.uri(), ClusterStateStore(tmp_path / "node2"), "n2")
+        await pm.close()
+        return node, rep
+    node, rep = asyncio.run(go())
+    assert rep["cluster"] == "lab"
+    members = coord.load_cluster()["members"]
+    assert "gpu-node-1" in members and members["gpu-node-1"]["capabilities"]["gpus"] == 8
+    cert = (node.root / "tls" / "node.crt").read_bytes()
+    assert cert_fingerprint_binding(cert) == node.identity().fingerprint
+    fp = coord.revoke("gpu-node-1")
+    assert fp in coord.load_cluster()["revoked"]
+
+
+def test_durable_state_and_restart(tmp_path):
+    from swarm_inference_lab_b200.coordinator.state import DurableState
+    s = DurableState(tmp_path / "s.json")
+    s.record_request("r1", [1, 2], {"max_new_tokens": 4})
+    s.accept_token("r1", 7)
+    s2 = DurableState(tmp_path / "s.json")
+    assert s2.replay_tokens("r1") == [1, 2, 7]
+    assert s2.mark_restart_boundaries() == ["r1"]
+    assert s2.data["requests"]["r1"]["state"] == "replay_required"
+
+
+def test_event_stream_order():
+    from swarm_inference_lab_b200.coordinator.state import EventStream
+
+    async def go():
+        es = EventStream("r")
+        for i in range(3):
+            await es.put("TOKEN_GENERATED", token=i)
+        await es.put("REQUEST_COMPLETED")
+        return [e async for e in es]
+    evs = asyncio.run(go())
+    assert [e["seq"] for e in evs] == [1, 2, 3, 4]
+
+
+def test_registry_heartbeats():
+    from swarm_inference_lab_b200.coordinator.state import WorkerRecord, WorkerRegistry
+    r = WorkerRegistry(heartbeat_timeout_s=10)
+    r.register(WorkerRecord("w1", "fp", "e"))
+    r.workers["w1"].last_heartbeat -= 20
+    assert r.sweep() == ["w1"] and not r.healthy()
+
+
+def test_trace_critical_path(tmp_path):
+    from swarm_inference_lab_b200.telemetry.trace import TraceWriter, critical_path, read_trace
+    tw = TraceWriter(tmp_path / "t.jsonl", "p")
+    with tw.span("prefill") as a:
+        time.sleep(0.01)
+    with tw.span("recv_token", after=[a]):
+        time.sleep(0.005)
+    tw.close()
+    cp = critical_path(read_trace(tmp_path / "t.jsonl"))
+    assert cp["path"] == ["prefill", "recv_token"] and cp["token_critical_receives"] == 1
+
+
+def test_box_planner_refit_changes_choice():
+    from swarm_inference_lab_b200.models.config import LLAMA3_8B
+    from swarm_inference_lab_b200.planner.box_planner import BoxMeasurements, plan_box
+    fast = BoxMeasurements(ar_alpha_us=2.0, ar_beta_us_per_mb=1.0)
+    slow = BoxMeasurements(ar_alpha_us=400.0, ar_beta_us_per_mb=50.0)
+    pf = plan_box(LLAMA3_8B, 8, fast, batch=32, ctx=2304, prompt=2048)[0]
+    ps = plan_box(LLAMA3_8B, 8, slow, batch=32, ctx=2304, prompt=2048)[0]
+    assert pf.tp == 8          # cheap all-reduce: tensor parallel everywhere
+    assert ps.tp < 8           # expensive all-reduce: the refit planner backs off TP
+    m = BoxMeasurements()
+    m.fit_allreduce([(8192, 10.0), (1 << 20, 12.6), (4 << 20, 20.4)])
+    assert abs(m.ar_beta_us_per_mb - 2.6) < 0.2 and "ar_alpha_us" in m.measured
+    m.fit_decode([(20e9, 260, 6.29), (10e9, 260, 4.0), (2e9, 260, 2.0)])
+    assert 0 < m.eta <= 1 and m.launch_us >= 0
+
+
+def test_stage_planner_prefers_fast_links():
+    from swarm_inference_lab_b200.planner.stage_planner import WorkerCaps, build_plan
+    from swarm_inference_lab_b200.planner.topology import LinkProfile
+    ws = [WorkerCaps("a", 1.0, 1e12), WorkerCaps("b", 1.0, 1e12), WorkerCaps("c", 1.0, 1e12)]
+    links = {}
+    for x in "abc":
+        for y in "abc":
+            if x != y:
+                slow = "c" in (x, y)
+                links[(x, y)] = LinkProfile(x, y, 80.0 if slow else 1.0, 5.0 if slow else 1000.0)
+    plan = build_plan(8, 1e9, 1e8, 1e8, ws, links, boundary_bytes=8192, batch=1,
+                      mode="speed", max_stages=2)
+    assert {w for w, _, _ in plan.stages} <= {"a", "b"}
+
+
+def test_engine_competition_rejects_unavailable():
+    from swarm_inference_lab_b200.engines import ClusterCapabilities, EngineRegistry, RequestShape
+    from swarm_inference_lab_b200.models.config import QWEN3_30B_A3B
+    c = EngineRegistry().compete(QWEN3_30B_A3B, ClusterCapabilities(
+        nodes={"box": {"gpus": 8, "gpu_name": "NVIDIA B200"}}), RequestShape(batch=128))
+    assert c.winner is not None and c.winner.engine == "native-stage"
+    assert any(name == "llama.cpp-rpc" for name, _ in c.rejected)
+
+
+def test_cli_dry_run_and_inspect(tmp_path):
+    from typer.testing import CliRunner
+    from swarm_inference_lab_b200.cli import app
+    r = CliRunner().invoke(app, ["run", "llama-3-8b-shape", "--prompt", "hi", "--dry-run", "--json",
+                                 "--gpus", "8"])
+    assert r.exit_code == 0, r.output
+    d = json.loads(r.output.strip().splitlines()[-1])
+    assert d["plan"].startswith("local:") and "terms" in d
+    st = tmp_path / "st"
+    r = CliRunner().invoke(app, ["cluster", "create", "lab", "--state-dir", str(st), "--json"])
+    assert r.exit_code == 0, r.output
+    assert json.loads(r.output)["pairing_uri"].startswith("swarm-pair://")
+    r = CliRunner().invoke(app, ["cluster", "create", "lab", "--state-dir", str(st)])
+    assert r.exit_code == 3
