@@ -27,6 +27,11 @@ void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
                     int64_t max_tokens, int64_t max_hidden, int64_t flags_off, int64_t slots_off,
                     const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
 int64_t symm_alloc(int64_t bytes, int64_t device);
+void sample_tokens(at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
+                   const at::Tensor& top_p, const at::Tensor& penalty,
+                   const c10::optional<at::Tensor>& history,
+                   const c10::optional<at::Tensor>& history_len, const at::Tensor& seeds,
+                   const at::Tensor& offsets, at::Tensor& out);
 void gemm_grouped(const at::Tensor& xp, const at::Tensor& w, at::Tensor& out,
                   const at::Tensor& offsets, int64_t num_groups, bool swiglu, int64_t rows_hint,
                   const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
@@ -63,6 +68,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &sil::moe_permute, "expert counts, offsets and sorted rows");
   m.def("moe_gather", &sil::moe_gather, "gather token rows into expert order");
   m.def("moe_combine", &sil::moe_combine, "weighted combine of expert outputs");
+  m.def("sample_tokens", &sil::sample_tokens,
+        "penalty + temperature + top-k + top-p + Gumbel-max sampling (Philox)");
   m.def("symm_alloc", &sil::symm_alloc, "allocate a zeroed buffer for peer (IPC) sharing");
   m.def("symm_free", &sil::symm_free, "free a symmetric buffer");
   m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(sil::ipc_handle(p)); },

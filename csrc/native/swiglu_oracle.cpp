@@ -8,10 +8,11 @@
 //   fp8   - e4m3 weights with one fp32 scale per 128x128 weight block and
 //           activations quantised to e4m3 per 1x128 block (absmax / 448),
 //           the DeepSeek-V3 / Kimi-K2 block-scaled format.
-// Accumulation is fp32 in a fixed order (inner index ascending), OpenMP over rows.
+// Accumulation is fp32 in a fixed order (inner index ascending), rows in parallel.
 // Reference semantics: the C ABI swarm_moe_swiglu_{f32,bf16,int4_g32} of
 // integrations/colibri/adapter/swarm_moe_runtime.c:39-164 and the block
 // dequantisation of si/backends/colibri/sparse_moe.py:146-244.
+#include <ATen/Parallel.h>
 #include <torch/extension.h>
 
 #include <cmath>
@@ -57,11 +58,11 @@ inline uint8_t f32_to_e4m3(float x) {
   return sign | best;
 }
 
-template <typename Wget>
-void swiglu_rows(const float* x, int64_t rows, int64_t H, int64_t I, Wget gate, Wget up, Wget down,
+template <typename G, typename U, typename D>
+void swiglu_rows(const float* x, int64_t rows, int64_t H, int64_t I, G gate, U up, D down,
                  float* y) {
-#pragma omp parallel for schedule(static)
-  for (int64_t r = 0; r < rows; ++r) {
+  at::parallel_for(0, rows, 1, [&](int64_t r0, int64_t r1) {
+  for (int64_t r = r0; r < r1; ++r) {
     const float* xr = x + r * H;
     std::vector<float> a(I);
     for (int64_t i = 0; i < I; ++i) {
@@ -78,6 +79,7 @@ void swiglu_rows(const float* x, int64_t rows, int64_t H, int64_t I, Wget gate, 
       y[r * H + h] = acc;
     }
   }
+  });
 }
 
 }  // namespace
@@ -156,8 +158,8 @@ at::Tensor fp8_block_gemm(const at::Tensor& xq, const at::Tensor& xs, const at::
   auto y = at::empty({R, N}, at::TensorOptions().dtype(at::kFloat));
   float* yp = y.data_ptr<float>();
   const int64_t KB = K / 128;
-#pragma omp parallel for schedule(static)
-  for (int64_t r = 0; r < R; ++r)
+  at::parallel_for(0, R, 1, [&](int64_t r0, int64_t r1) {
+  for (int64_t r = r0; r < r1; ++r)
     for (int64_t n = 0; n < N; ++n) {
       float acc = 0.f;
       for (int64_t kb = 0; kb < KB; ++kb) {
@@ -168,6 +170,7 @@ at::Tensor fp8_block_gemm(const at::Tensor& xq, const at::Tensor& xs, const at::
       }
       yp[r * N + n] = acc;
     }
+  });
   return y;
 }
 
@@ -181,7 +184,6 @@ std::vector<at::Tensor> quant_fp8_1x128(const at::Tensor& x) {
   const float* xp = X.data_ptr<float>();
   uint8_t* qp = q.data_ptr<uint8_t>();
   float* sp = s.data_ptr<float>();
-#pragma omp parallel for schedule(static)
   for (int64_t r = 0; r < R; ++r)
     for (int64_t b = 0; b < K / 128; ++b) {
       float amax = 0.f;

@@ -48,8 +48,7 @@ if native_sources:
             name="swarm_inference_lab_b200._native",
             sources=native_sources,
             include_dirs=[os.path.join(ROOT, "csrc", "include")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-fopenmp"]},
-            extra_link_args=["-fopenmp"],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"]},
             libraries=["crypto"],
         )
     )

@@ -127,7 +127,7 @@ class MoEModel(DenseModel):
         self.el = weights.experts_local
         cfg = self.cfg
         self.mode = moe_ops.MODE_SIGMOID_GROUP if cfg.router == "sigmoid_group" else moe_ops.MODE_SOFTMAX
-        self.scale = cfg.routed_scaling_factor if cfg.router == "sigmoid_group" else 1.0
+        self.route_scale = cfg.routed_scaling_factor if cfg.router == "sigmoid_group" else 1.0
 
     def mlp(self, li: int, L, x: torch.Tensor, h: torch.Tensor):
         if getattr(L, "dense", True) and L.router is None:
@@ -138,7 +138,7 @@ class MoEModel(DenseModel):
         logits = gemm.linear(x, L.router, fp32_out=True)
         ids, w = moe_ops.route(logits, k, mode=self.mode, renorm=cfg.norm_topk_prob,
                                bias=L.router_bias, n_group=cfg.n_group, topk_group=cfg.topk_group,
-                               scale=self.scale)
+                               scale=self.route_scale)
         if self.tp.size > 1:
             # Global expert id -> local group; remote experts go to the trailing group.
             local = ids - self.e0

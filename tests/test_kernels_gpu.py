@@ -199,3 +199,28 @@ def test_argmax_ties_lowest():
 def test_status_word_clean():
     from swarm_inference_lab_b200.ops.workspace import get_workspace
     get_workspace().check()
+
+
+def test_sampling_distribution_matches_reference():
+    from swarm_inference_lab_b200.ops import sampling
+    torch.manual_seed(0)
+    V, N = 64, 4000
+    base = torch.randn(1, V, device="cuda") * 2
+    for temp, k, p in [(1.0, 0, 1.0), (0.7, 10, 1.0), (1.3, 0, 0.8), (1.0, 20, 0.9)]:
+        logits = base.repeat(N, 1).contiguous()
+        toks = sampling.sample(logits, temperature=temp, top_k=k, top_p=p,
+                               seeds=torch.arange(N, device="cuda"), offsets=0)
+        emp = torch.bincount(toks, minlength=V).float() / N
+        ref = sampling.sample_reference_probs(base, temp, k, p)[0]
+        assert (emp[ref == 0] == 0).all(), (temp, k, p)        # truncation is exact
+        assert (emp - ref).abs().max().item() < 0.04, (temp, k, p)
+
+
+def test_sampling_greedy_and_penalty():
+    from swarm_inference_lab_b200.ops import sampling
+    logits = torch.tensor([[1.0, 5.0, 4.9, -1.0]], device="cuda")
+    assert sampling.sample(logits.clone(), temperature=0.0).item() == 1
+    hist = torch.tensor([[1]], dtype=torch.int64, device="cuda")
+    out = sampling.sample(logits.clone(), temperature=0.0, repetition_penalty=2.0, history=hist,
+                          history_len=torch.tensor([1], dtype=torch.int32, device="cuda"))
+    assert out.item() == 2
