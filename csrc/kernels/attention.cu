@@ -586,3 +586,130 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
 }
 
 }  // namespace sil
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (declared and documented in sil/noalloc.h; it has
+// no counterpart in the reference).  The split-K scratch lives in the
+// file-scope array below instead of caller- or torch-allocated memory.
+#include "sil/noalloc.h"
+
+namespace {
+
+constexpr long long kNoAllocFloats = 1LL << 20;  // 4 MiB of fp32 partials
+constexpr int kNoAllocCounters = 4096;           // (sequence, kv-head) pairs
+
+struct NoAllocScratch {
+  float partial[kNoAllocFloats];
+  int counters[kNoAllocCounters];
+  int status[64];
+};
+
+static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
+
+thread_local std::string g_noalloc_error;
+std::mutex g_noalloc_mutex;
+NoAllocScratch* g_noalloc_ptr[64] = {};  // device address per device ordinal
+bool g_noalloc_smem_set[64] = {};
+
+int noalloc_fail(int code, const std::string& msg) {
+  g_noalloc_error = msg;
+  return code;
+}
+
+}  // namespace
+
+extern "C" const char* sil_noalloc_last_error(void) { return g_noalloc_error.c_str(); }
+extern "C" long long sil_noalloc_scratch_floats(void) { return kNoAllocFloats; }
+extern "C" int sil_noalloc_max_counters(void) { return kNoAllocCounters; }
+
+extern "C" int sil_paged_decode_noalloc(const void* q, long long q_stride, const void* k_cache,
+                                        const void* v_cache, long long num_pages, int kv_heads,
+                                        const int* block_table, long long bt_stride,
+                                        const int* seq_lens, void* out, long long out_stride,
+                                        int batch, int q_heads, float scale, int num_splits,
+                                        cudaStream_t stream) {
+  using namespace sil;
+  g_noalloc_error.clear();
+  if (!q || !k_cache || !v_cache || !block_table || !seq_lens || !out)
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "null pointer argument");
+  if (batch <= 0 || kv_heads <= 0 || q_heads <= 0 || num_pages <= 0 || num_splits <= 0)
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "sizes must be positive");
+  if (q_heads % kv_heads != 0 || q_heads / kv_heads > 16)
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "q_heads must be a multiple of kv_heads, ratio <= 16");
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15u) || (reinterpret_cast<uintptr_t>(v_cache) & 15u) ||
+      (reinterpret_cast<uintptr_t>(q) & 3u))
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "cache pointers must be 16-byte aligned, q 4-byte aligned");
+  const int G = q_heads / kv_heads;
+  const long long need = (long long)batch * kv_heads * num_splits * G * (kD + 2);
+  if (num_splits > 1 && need > kNoAllocFloats)
+    return noalloc_fail(SIL_NOALLOC_ETOOBIG,
+                        "request needs " + std::to_string(need) + " fp32 scratch values; the " +
+                            "allocation-free entry point holds " + std::to_string(kNoAllocFloats));
+  if (num_splits > 1 && (long long)batch * kv_heads > kNoAllocCounters)
+    return noalloc_fail(SIL_NOALLOC_ETOOBIG,
+                        "batch * kv_heads exceeds the " + std::to_string(kNoAllocCounters) +
+                            " split counters of the allocation-free entry point");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return noalloc_fail(SIL_NOALLOC_EINVAL, "device ordinal out of range");
+  NoAllocScratch* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      // Once per device, with the device current: the host-side name of the array
+      // is not a device address.
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess)
+        return noalloc_fail(SIL_NOALLOC_ECUDA,
+                            std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = static_cast<NoAllocScratch*>(p);
+    }
+    if (!g_noalloc_smem_set[dev]) {
+      e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSmemBytes);
+      if (e != cudaSuccess)
+        return noalloc_fail(SIL_NOALLOC_ECUDA,
+                            std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      g_noalloc_smem_set[dev] = true;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // Counters and the status word must start at zero (an earlier call that gave up
+  // may have left them set); partials are fully written before they are read.
+  const size_t nctr = static_cast<size_t>(std::min<long long>((long long)batch * kv_heads,
+                                                              kNoAllocCounters));
+  e = cudaMemsetAsync(scratch->counters, 0, nctr * sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(scratch->status, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
+  AttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_stride;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_stride = out_stride;
+  a.block_table = block_table;
+  a.bt_stride = bt_stride;
+  a.seq_lens = seq_lens;
+  a.Hq = q_heads;
+  a.Hkv = kv_heads;
+  a.G = G;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.num_splits = num_splits;
+  a.ws_o = scratch->partial;
+  a.ws_ml = scratch->partial + (long long)batch * kv_heads * num_splits * G * kD;
+  a.counters = scratch->counters;
+  a.status = scratch->status;
+  try {
+    const uint64_t rows = (uint64_t)num_pages * kv_heads * kPage;
+    CUtensorMap tk = make_tmap_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kD, kD, kPage,
+                                  64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tv = make_tmap_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kD, kD, kPage,
+                                  64, CU_TENSOR_MAP_SWIZZLE_128B);
+    launch_pdl(paged_decode_kernel, dim3(num_splits, kv_heads, batch), dim3(128), kSmemBytes,
+               stream, "paged_decode (allocation-free) launch", tk, tv, a);
+  } catch (const std::exception& ex) {
+    return noalloc_fail(SIL_NOALLOC_ECUDA, ex.what());
+  }
+  return SIL_NOALLOC_OK;
+}
