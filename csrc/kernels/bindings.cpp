@@ -27,6 +27,14 @@ void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
                     int64_t max_tokens, int64_t max_hidden, int64_t flags_off, int64_t slots_off,
                     const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
 int64_t symm_alloc(int64_t bytes, int64_t device);
+void gemm_fp8(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq, const at::Tensor& wsc,
+              at::Tensor& out, const c10::optional<at::Tensor>& res, int64_t epi,
+              const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status);
+void gemm_fp8_grouped(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq,
+                      const at::Tensor& wsc, at::Tensor& out, const at::Tensor& offsets,
+                      int64_t num_groups, bool swiglu, int64_t rows_hint, const at::Tensor& ws,
+                      const at::Tensor& counters, const at::Tensor& status);
+void quant_fp8_1x128(const at::Tensor& x, at::Tensor& q, at::Tensor& s);
 void sample_tokens(at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
                    const at::Tensor& top_p, const at::Tensor& penalty,
                    const c10::optional<at::Tensor>& history,
@@ -70,6 +78,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &sil::moe_combine, "weighted combine of expert outputs");
   m.def("sample_tokens", &sil::sample_tokens,
         "penalty + temperature + top-k + top-p + Gumbel-max sampling (Philox)");
+  m.def("gemm_fp8", &sil::gemm_fp8, "block-scaled e4m3 tcgen05 GEMM (128x128 / 1x128 scales)");
+  m.def("gemm_fp8_grouped", &sil::gemm_fp8_grouped, "grouped block-scaled e4m3 GEMM (experts)");
+  m.def("quant_fp8_1x128", &sil::quant_fp8_1x128, "bf16 -> e4m3 with 1x128 block scales");
   m.def("symm_alloc", &sil::symm_alloc, "allocate a zeroed buffer for peer (IPC) sharing");
   m.def("symm_free", &sil::symm_free, "free a symmetric buffer");
   m.def("ipc_handle", [](int64_t p) { return pybind11::bytes(sil::ipc_handle(p)); },
