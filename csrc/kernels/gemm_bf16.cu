@@ -4,6 +4,31 @@
 namespace sil {
 using namespace gemm_detail;
 
+// Persistent grid for a stream-K launch.  Splitting a tile over several CTAs
+// costs a fix-up chain (partial store, fence, arrival atomic, ordered
+// reduction: a few microseconds of latency); it only pays when the tile's own
+// streaming time is longer.  Model: one CTA streams ~kPerSmGBs from HBM, the
+// box at most kHbmGBs; choose the number of CTAs per tile minimising
+// bytes / bandwidth + fix-up.
+inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms) {
+  constexpr double kPerSmGBs = 110.0, kHbmGBs = 6000.0, kFixupUs = 3.0, kLatencyUs = 2.0;
+  const double tile_bytes = (double)bytes_per_kb * num_kb;
+  long long best_g = std::min<long long>(tiles, sms);
+  double best_t = 1e30;
+  for (int s = 1; s <= std::max(1, num_kb); ++s) {
+    const long long g = std::min<long long>((long long)tiles * s, sms);
+    const double per_cta = tile_bytes * tiles / g;
+    const double bw_us = std::max(per_cta / (kPerSmGBs * 1e3), tile_bytes * tiles / (kHbmGBs * 1e3));
+    const double t = bw_us + kLatencyUs + (g > tiles ? kFixupUs : 0.0);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best_g = g;
+    }
+    if (g >= sms) break;
+  }
+  return std::max<long long>(1, best_g);
+}
+
 // y = epilogue(x . W^T).  x: [T, K] bf16 (row pitch 16-byte aligned), W: [Nw, K] bf16,
 // out: [T, Nout] (bf16, or fp32 for epi=3).  For SwiGLU W = [gate; up] with
 // Nw = 2*inter and out = [T, inter].  `ws`/`counters`/`status` are the caller's
@@ -96,9 +121,7 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   a.group_m = 16;
   long long g;
   if (a.stream_k) {
-    g = std::min<long long>(sms, a.units);
-    const long long min_units = 4;
-    g = std::max<long long>(1, std::min<long long>(g, (a.units + min_units - 1) / min_units));
+    g = stream_k_grid(tiles, a.num_kb, (long long)((swap && swiglu ? 2 : 1) * BM + bn) * BK * 2, sms);
     if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
   } else {
     g = std::min<long long>(sms, tiles);
@@ -179,8 +202,7 @@ void gemm_allreduce(const at::Tensor& x, const at::Tensor& w, at::Tensor& h,
   a.stream_k = 1;
   a.group_m = 16;
   const int sms = device_sm_count();
-  long long g = std::min<long long>(sms, a.units);
-  g = std::max<long long>(1, std::min<long long>(g, (a.units + 3) / 4));
+  long long g = stream_k_grid(a.m_tiles, a.num_kb, (long long)(BM + bn) * BK * 2, sms);
   TORCH_CHECK(g * 2 * bn * BM <= ws.numel(), "gemm_allreduce: workspace too small");
   TORCH_CHECK(a.m_tiles <= counters.numel(), "gemm_allreduce: counters too small");
   a.grid = static_cast<int>(g);
