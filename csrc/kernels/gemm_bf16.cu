@@ -11,6 +11,14 @@ using namespace gemm_detail;
 // box at most kHbmGBs; choose the number of CTAs per tile minimising
 // bytes / bandwidth + fix-up.
 inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms) {
+  // Default ("fill"): one CTA per SM whenever the problem has >= 4 K blocks per CTA;
+  // measured faster on the full decode step than the latency model below, which is
+  // kept behind SIL_STREAMK=latency.
+  static const char* mode = std::getenv("SIL_STREAMK");
+  if (mode == nullptr || mode[0] != 'l') {
+    const long long units = tiles * num_kb;
+    return std::max<long long>(1, std::min<long long>(std::min<long long>(sms, units), (units + 3) / 4));
+  }
   constexpr double kPerSmGBs = 110.0, kHbmGBs = 6000.0, kFixupUs = 3.0, kLatencyUs = 2.0;
   const double tile_bytes = (double)bytes_per_kb * num_kb;
   long long best_g = std::min<long long>(tiles, sms);

@@ -32,14 +32,32 @@ def _peaks():
         return PEAKS
 
 
-def time_fn(fn, iters: int = 20, warmup: int = 3) -> float:
+def time_fn(fn, iters: int = 20, warmup: int = 3, graph: bool = True) -> float:
+    """Mean milliseconds per call.  With ``graph`` the calls are captured once into a
+    CUDA graph and replayed, so host launch overhead is excluded (GPU time only)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        s0 = torch.cuda.Stream()
+        s0.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s0):
+            fn()
+        torch.cuda.current_stream().wait_stream(s0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s0):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(iters):
-        fn()
+    if g is not None:
+        g.replay()
+    else:
+        for _ in range(iters):
+            fn()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
@@ -51,7 +69,7 @@ def op_gemm(a):
     x = torch.randn(T, K, device="cuda").bfloat16()
     rows = 2 * N if a.swiglu else N
     w = (torch.randn(rows, K, device="cuda") * 0.02).bfloat16()
-    ms = time_fn(lambda: gemm.linear(x, w, swiglu=a.swiglu), a.iters)
+    ms = time_fn(lambda: gemm.linear(x, w, swiglu=a.swiglu), a.iters, graph=not a.eager)
     bytes_ = rows * K * 2 + T * K * 2 + T * N * 2
     flops = 2 * T * rows * K
     pk = _peaks()
@@ -72,7 +90,8 @@ def op_decode_attn(a):
     sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
     q = torch.randn(B, hq, 128, device="cuda").bfloat16()
     splits = A.decode_splits(B, hkv, pages_per)
-    ms = time_fn(lambda: A.paged_decode(q, kc, vc, bt, sl, num_splits=splits), a.iters)
+    ms = time_fn(lambda: A.paged_decode(q, kc, vc, bt, sl, num_splits=splits), a.iters,
+                 graph=not a.eager)
     bytes_ = 2 * B * ctx * hkv * 128 * 2
     pk = _peaks()
     return {"op": "paged_decode", "batch": B, "ctx": ctx, "splits": splits, "ms": ms,
@@ -101,11 +120,11 @@ def decode_steps(a):
                       slots=slots.int(), seq_lens=pos + 1, block_table=bt,
                       last_idx=torch.arange(B, device="cuda"), is_decode=True,
                       decode_splits=A.decode_splits(B, cfg.num_kv_heads, pages_per))
-    ms = time_fn(lambda: model.forward(fb, kv), a.steps, warmup=2)
+    ms = time_fn(lambda: model.forward(fb, kv), a.steps, warmup=2, graph=not a.eager)
     wbytes = w.nbytes()
     kvbytes = 2 * B * (a.ctx + 1) * cfg.num_layers * cfg.num_kv_heads * 128 * 2
     pk = _peaks()
-    return {"mode": "decode_step_eager", "model": cfg.name, "batch": B, "ctx": a.ctx, "ms": ms,
+    return {"mode": "decode_step_eager" if a.eager else "decode_step_graph", "model": cfg.name, "batch": B, "ctx": a.ctx, "ms": ms,
             "weight_bytes": wbytes, "kv_bytes": kvbytes,
             "roofline_ms": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6,
             "frac_of_roofline": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6 / ms}
@@ -124,6 +143,7 @@ def main():
     ap.add_argument("--n", type=int, default=32)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--swiglu", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
     a = ap.parse_args()
     out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn}[a.op](a)
     print(json.dumps(out))

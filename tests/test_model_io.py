@@ -153,3 +153,32 @@ def test_balanced_ranges_memory_cap():
 def test_heterogeneous_capacities():
     r = partition.ranges_for_capacities([1.0] * 12, [2.0, 1.0], [100, 100], [1.0] * 12)
     assert r[0][1] - r[0][0] == 8  # the 2x faster stage takes twice the layers
+
+
+def test_stage_artifact_build_transfer_resume_and_evict(tmp_path):
+    from swarm_inference_lab_b200.cluster.artifacts import (ArtifactError, ArtifactStore,
+                                                           build_stage_artifact, transfer)
+    ck = tmp_path / "ck"
+    ck.mkdir()
+    tensors = _tiny_ckpt(ck)
+    res = ModelSourceResolver().inspect(str(ck))
+    src = ArtifactStore(tmp_path / "a")
+    man = build_stage_artifact(res, src.root, 1, 2, embed=False, head=True)
+    assert "lm_head.weight" in man.tensors and "model.embed_tokens.weight" not in man.tensors
+    assert all(not n.startswith("model.layers.0.") for n in man.tensors)
+    assert build_stage_artifact(res, src.root, 1, 2, embed=False, head=True).artifact_id == man.artifact_id
+    assert src.verify(man.artifact_id)
+    dst = ArtifactStore(tmp_path / "b")
+    with pytest.raises(ArtifactError, match="interrupted"):
+        transfer(src, dst, man.artifact_id, chunk=4096, fail_after_chunks=2)
+    n = transfer(src, dst, man.artifact_id, chunk=4096)       # resumes after the 2 verified chunks
+    total = -(-man.bytes // 4096)
+    assert n == total - 2 and dst.verify(man.artifact_id)
+    r = CheckpointReader(dst.path(man.artifact_id))
+    assert torch.equal(r.tensor("lm_head.weight"), tensors["lm_head.weight"])
+    r.close()
+    other = build_stage_artifact(res, src.root, 0, 1, embed=True, head=False)
+    src.lease(other.artifact_id)
+    src.budget = 1
+    gone = src.evict()
+    assert man.artifact_id in gone and other.artifact_id not in gone
