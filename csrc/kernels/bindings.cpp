@@ -58,6 +58,17 @@ int64_t ipc_open(const std::string& handle, int64_t device);
 void ipc_close(int64_t ptr);
 bool can_access_peer(int64_t dev, int64_t peer);
 void argmax(const at::Tensor& logits, at::Tensor& out);
+void mla_attention(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& cache,
+                   const at::Tensor& block_table, const at::Tensor& seq_lens,
+                   const c10::optional<at::Tensor>& cu_q, at::Tensor& out, double scale,
+                   int64_t max_q_len, int64_t num_splits, const at::Tensor& ws,
+                   const at::Tensor& counters, const at::Tensor& status);
+void mla_kv_write(const at::Tensor& kv, const at::Tensor& norm_w, double eps,
+                  const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& cos_sin,
+                  at::Tensor& cache);
+void mla_q_prep(const at::Tensor& q, const at::Tensor& positions, const at::Tensor& cos_sin,
+                at::Tensor& q_nope, at::Tensor& q_pe, int64_t H);
+void mla_heads_to_tokens(const at::Tensor& src, at::Tensor& dst, int64_t T, int64_t H);
 }  // namespace sil
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -87,5 +98,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "CUDA IPC handle bytes of a symmetric buffer");
   m.def("ipc_open", &sil::ipc_open, "open a peer's IPC handle; returns a device pointer");
   m.def("ipc_close", &sil::ipc_close, "close a peer mapping");
+  m.def("mla_attention", &sil::mla_attention, "MLA paged attention over the latent cache (absorbed form)");
+  m.def("mla_kv_write", &sil::mla_kv_write, "MLA latent KV write: RMSNorm(c_kv) + interleaved RoPE(k_pe)");
+  m.def("mla_q_prep", &sil::mla_q_prep, "MLA query split: q_nope head-major + RoPE(q_pe)");
+  m.def("mla_heads_to_tokens", &sil::mla_heads_to_tokens, "[H, T, 128] -> [T, H*128]");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

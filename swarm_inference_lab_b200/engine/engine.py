@@ -20,7 +20,9 @@ from dataclasses import dataclass, field
 import torch
 
 from ..models.config import ModelConfig
+from ..models.deepseek import MLAModel, MLAWeights
 from ..models.dense import DenseModel, DenseWeights, TPInfo
+from ..models.moe import MoEModel, MoEWeights
 from .kv_cache import PAGE, PagedKVCache
 from .runner import ModelRunner, bucket_for
 from .scheduler import ContinuousScheduler, SchedulerPolicy, SeqRequest
@@ -61,19 +63,29 @@ class LLMEngine:
                  tp: TPInfo | None = None, max_batch: int = 64, max_seq_len: int = 4096,
                  kv_pages: int | None = None, prefill_token_budget: int = 16384,
                  policy: str = SchedulerPolicy.BALANCED, use_cuda_graphs: bool = True):
-        if cfg.is_moe or cfg.mla:
-            raise ValueError("LLMEngine serves dense decoders; MoE/MLA models use MoEEngine")
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.tp = tp or TPInfo()
-        self.weights = weights or DenseWeights.random(cfg, self.tp, self.device, seed=seed)
-        self.model = DenseModel(self.weights, self.device, comm=comm,
-                                max_positions=max(max_seq_len, 1) + PAGE)
+        max_pos = max(max_seq_len, 1) + PAGE
         if kv_pages is None:
             kv_pages = max_batch * ((max_seq_len + PAGE - 1) // PAGE) + 8
-        self.kv = PagedKVCache(self.model.num_layers, self.model.num_kv_local, kv_pages, self.device)
+        if cfg.mla:
+            # MLA: data-parallel attention with a latent cache; ``tp`` is the expert-parallel group.
+            self.weights = weights or MLAWeights.random(cfg, self.tp, self.device, seed=seed)
+            self.model = MLAModel(self.weights, self.device, comm=comm, max_positions=max_pos)
+            self.kv = PagedKVCache(self.model.num_layers, 1, kv_pages, self.device,
+                                   latent_dim=self.model.latent_dim)
+        else:
+            if cfg.is_moe:
+                self.weights = weights or MoEWeights.random(cfg, self.tp, self.device, seed=seed)
+                self.model = MoEModel(self.weights, self.device, comm=comm, max_positions=max_pos)
+            else:
+                self.weights = weights or DenseWeights.random(cfg, self.tp, self.device, seed=seed)
+                self.model = DenseModel(self.weights, self.device, comm=comm, max_positions=max_pos)
+            self.kv = PagedKVCache(self.model.num_layers, self.model.num_kv_local, kv_pages,
+                                   self.device)
         self.runner = ModelRunner(self.model, self.kv, max_seq_len=max_seq_len,
                                   use_cuda_graphs=use_cuda_graphs)
         self.max_batch = max_batch

@@ -67,15 +67,23 @@ class SeqPages:
 
 class PagedKVCache:
     def __init__(self, num_layers: int, num_kv_heads: int, num_pages: int, device,
-                 head_dim: int = 128, dtype=torch.bfloat16):
+                 head_dim: int = 128, dtype=torch.bfloat16, latent_dim: int | None = None):
+        """``latent_dim`` set: one MLA latent row per token, ``k[layer] : [num_pages, 64,
+        latent_dim]`` and no separate V (the latent cache holds both)."""
         self.num_layers = num_layers
         self.num_kv_heads = num_kv_heads
         self.num_pages = num_pages
         self.head_dim = head_dim
+        self.latent_dim = latent_dim
         self.device = torch.device(device)
-        shape = (num_layers, num_pages, num_kv_heads, PAGE, head_dim)
-        self.k = torch.zeros(shape, dtype=dtype, device=self.device)
-        self.v = torch.zeros(shape, dtype=dtype, device=self.device)
+        if latent_dim is not None:
+            self.k = torch.zeros((num_layers, num_pages, PAGE, latent_dim), dtype=dtype,
+                                 device=self.device)
+            self.v = None
+        else:
+            shape = (num_layers, num_pages, num_kv_heads, PAGE, head_dim)
+            self.k = torch.zeros(shape, dtype=dtype, device=self.device)
+            self.v = torch.zeros(shape, dtype=dtype, device=self.device)
         self.alloc = PageAllocator(num_pages)
         self.seqs: dict[str, SeqPages] = {}
 
@@ -89,7 +97,7 @@ class PagedKVCache:
         return 2 * num_layers * num_kv_heads * PAGE * head_dim * elem
 
     def layer(self, i: int):
-        return self.k[i], self.v[i]
+        return self.k[i], (self.v[i] if self.v is not None else None)
 
     # ------------------------------------------------------------ sequences
     def open(self, seq_id: str) -> SeqPages:
@@ -135,7 +143,8 @@ class PagedKVCache:
         """Host copy of the sequence's KV (checkpoint / migration payload)."""
         s = self.seqs[seq_id]
         idx = torch.tensor(s.pages, dtype=torch.long, device=self.device)
-        return {"length": s.length, "k": self.k[:, idx].cpu(), "v": self.v[:, idx].cpu()}
+        return {"length": s.length, "k": self.k[:, idx].cpu(),
+                "v": self.v[:, idx].cpu() if self.v is not None else None}
 
     def restore(self, seq_id: str, snap: dict) -> None:
         if seq_id not in self.seqs:
@@ -144,5 +153,6 @@ class PagedKVCache:
         n = snap["k"].shape[1]
         idx = torch.tensor(s.pages[:n], dtype=torch.long, device=self.device)
         self.k[:, idx] = snap["k"].to(self.device)
-        self.v[:, idx] = snap["v"].to(self.device)
+        if self.v is not None:
+            self.v[:, idx] = snap["v"].to(self.device)
         s.length = int(snap["length"])

@@ -104,7 +104,11 @@ class ModelRunner:
         valid = torch.zeros(bsz, dtype=torch.bool, device=dev)
         bt = torch.zeros((bsz, self.max_pages), dtype=torch.int32, device=dev)
         out = torch.zeros(bsz, dtype=torch.int64, device=dev)
-        splits = attn_ops.decode_splits(bsz, self.model.num_kv_local, self.max_pages, self.sm_count)
+        if hasattr(self.model, "decode_splits"):
+            splits = self.model.decode_splits(bsz, self.max_pages, self.sm_count)
+        else:
+            splits = attn_ops.decode_splits(bsz, self.model.num_kv_local, self.max_pages,
+                                            self.sm_count)
         fb = ForwardBatch(ids=ids, positions=meta[0], slots=meta[1], seq_lens=meta[2], block_table=bt,
                           last_idx=torch.arange(bsz, dtype=torch.int64, device=dev), is_decode=True,
                           decode_splits=splits)

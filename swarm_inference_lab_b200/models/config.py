@@ -194,9 +194,18 @@ KIMI_K2 = ModelConfig(
     kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
     weight_dtype="fp8_block128")
 
+TINY_MLA_GPU = ModelConfig(
+    name="tiny-mla-gpu", family="deepseek_v3", vocab_size=1024, hidden_size=256, num_layers=3,
+    num_heads=4, num_kv_heads=4, head_dim=192, intermediate_size=384, rms_norm_eps=1e-6,
+    rope_theta=10000.0, num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+    norm_topk_prob=True, router="sigmoid_group", n_group=2, topk_group=1,
+    routed_scaling_factor=2.5, n_shared_experts=1, first_k_dense=1, mla=True, q_lora_rank=256,
+    kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+    weight_dtype="fp8_block128", max_position_embeddings=4096)
+
 PRESETS: dict[str, ModelConfig] = {
     c.name: c for c in (LLAMA3_8B, TINY_LLAMA_CPU, TINY_LLAMA_GPU, QWEN3_0_6B, MIXTRAL_8X7B,
-                        QWEN3_30B_A3B, KIMI_K2)
+                        QWEN3_30B_A3B, KIMI_K2, TINY_MLA_GPU)
 }
 
 

@@ -25,6 +25,9 @@ class LocalComm:
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         return x[None]
 
+    def reduce_scatter(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
     def barrier(self) -> None:
         pass
 
@@ -46,6 +49,13 @@ class NcclComm:
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
         dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        return out
+
+    def reduce_scatter(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum over ranks of ``x`` [size * n, ...]; returns this rank's ``[n, ...]`` slice."""
+        out = torch.empty((x.shape[0] // self.size,) + tuple(x.shape[1:]), dtype=x.dtype,
+                          device=x.device)
+        dist.reduce_scatter_tensor(out, x.contiguous(), group=self.group)
         return out
 
     def barrier(self) -> None:

@@ -73,6 +73,9 @@ class FusedTPComm:
     def all_gather(self, x):
         return self.base.all_gather(x)
 
+    def reduce_scatter(self, x):
+        return self.base.reduce_scatter(x)
+
     def barrier(self):
         self.base.barrier()
 
