@@ -86,6 +86,10 @@ def run_reference_arm(args, rank, world, local, metric):
         return {"impl": "reference", "unavailable": f"reference import failed: {exc}"[:300]}
     from pathlib import Path
 
+    if getattr(args, "model", "llama-3-8b-shape") != "llama-3-8b-shape":
+        return {"impl": "reference", "unavailable": (
+            f"the reference has no runnable path for {args.model} (its native engine serves "
+            "qwen3_dense / qwen3_moe only; DeepSeek/Kimi/Mixtral/Llama are metadata profiles)")}
     B_total, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
     if B_total % world:
         return {"impl": "reference", "unavailable": "batch not divisible by the replica count"}

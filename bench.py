@@ -1,7 +1,10 @@
-"""Decode-throughput benchmark: Llama-3-8B-shaped dense decoder, bf16, TP=N on one box.
+"""Decode-throughput benchmark: Llama-3-8B-shaped dense decoder, bf16, TP=N on one box
+(default), or another preset with ``--model`` (``kimi-k2-shape``: MLA + fp8 experts,
+data-parallel attention and EP=N; MoE presets: TP attention + EP experts).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 32] [--prompt-len 2048]
     torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1, one rank per GPU)
+    torchrun --nproc-per-node 8 bench.py --gpus 8 --model kimi-k2-shape --batch 256 --prompt-len 4096
     python bench.py --impl reference ...                       (the reference's own engine)
 
 Workload: synthetic token-id prompts (uniform random ids, seed 0) and random
@@ -30,7 +33,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 PUBLISHED = None  # the reference publishes no B200 / Llama-3-8B number
-METRIC = "decode tokens/s/box (Llama-3-8B-shape TP)"
+METRIC = "decode tokens/s/box + p50 TTFT/TPOT, K2-shape fp8 EP & 8B TP at 1/2/4/8 GPU"
 
 
 def parse():
@@ -95,21 +98,35 @@ def run_ours(args, rank, world, local):
     B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
     new_tokens = 2 * (K + W) + 4
     max_seq = P + new_tokens + 64
+    # MLA models: data-parallel attention, each rank serves B / N of the sequences.
+    dp = cfg.mla
+    if dp and B % world:
+        raise SystemExit(f"--batch {B} must be a multiple of --gpus {world} for {cfg.name}")
+    B_loc = B // world if dp else B
     comm = LocalComm()
     comm_kind = "none"
     if world > 1:
         comm = NcclComm()
         comm_kind = "nccl"
-        if args.comm == "fused":
+        if args.comm == "fused" and cfg.mla:
+            from swarm_inference_lab_b200.engine.runner import bucket_for as _bucket
+            from swarm_inference_lab_b200.parallel.fused_ep import FusedEPComm
+            comm = FusedEPComm(comm, torch.device("cuda", local), max_tokens=_bucket(B // world),
+                               hidden=cfg.hidden_size, top_k=cfg.num_experts_per_tok)
+            comm_kind = "fused_ep_dispatch_combine (decode) + nccl (prefill)"
+        elif args.comm == "fused":
             from swarm_inference_lab_b200.parallel.fused_tp import FusedTPComm
             comm = FusedTPComm(comm, torch.device("cuda", local), max_tokens=max(B, 256),
                                hidden=cfg.hidden_size)
             comm_kind = "fused_gemm_allreduce"
+    budget = min(B_loc * P, 4096) if dp else B * P
     eng = LLMEngine(cfg, device=torch.device("cuda", local), seed=0, comm=comm,
-                    tp=TPInfo(rank, world), max_batch=max(B, 1), max_seq_len=max_seq,
-                    prefill_token_budget=B * P)
+                    tp=TPInfo(rank, world), max_batch=max(B_loc, 1), max_seq_len=max_seq,
+                    prefill_token_budget=budget)
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g).tolist()
+    if dp:
+        prompts = prompts[rank * B_loc:(rank + 1) * B_loc]
     params = SamplingParams(max_new_tokens=new_tokens)
     for p in prompts:
         eng.add_request(p, params)
@@ -127,7 +144,7 @@ def run_ours(args, rank, world, local):
     e2e = None
     runner = eng.runner
     from swarm_inference_lab_b200.engine.runner import bucket_for
-    dg = runner.graph_for(bucket_for(B))
+    dg = runner.graph_for(bucket_for(B_loc))
     if not args.no_e2e:
         for _ in range(W):
             eng.step()
@@ -178,14 +195,23 @@ def run_ours(args, rank, world, local):
     _ = launches_before
     value = B * K / (total_ms / 1e3)
     clk = clocks.summary()
+    fp8w = cfg.weight_dtype.startswith("fp8")
+    wgb = eng.weights.nbytes() / 1e9
+    if dp:
+        par = f"dp{world}-attention+ep{world}"
+    elif cfg.is_moe:
+        par = f"tp{world}-attention+ep{world}"
+    else:
+        par = f"tp{world}"
     return {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": (value / PUBLISHED) if PUBLISHED else None, "dtype": "bf16",
+        "vs_baseline": (value / PUBLISHED) if PUBLISHED else None,
+        "dtype": "fp8-e4m3 weights (128x128 scales) + bf16 activations" if fp8w else "bf16",
         "data": "synthetic (uniform random token ids, random N(0,0.02) weights)",
         "config": {"model": cfg.name, "global_batch": B, "seq_len": P, "decode_tokens": K,
-                   "parallelism": f"tp{world}", "comm": comm_kind,
-                   "l2": "weights (16 GB/step) exceed L2; no flush needed",
+                   "parallelism": par, "comm": comm_kind,
+                   "l2": f"weights ({wgb:.0f} GB/step/rank) exceed L2; no flush needed",
                    "kv_pages_page_size": 64},
         "ttft_ms_p50": ttft_ms, "tpot_ms_p50": tpot_p50,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],

@@ -69,6 +69,23 @@ void mla_kv_write(const at::Tensor& kv, const at::Tensor& norm_w, double eps,
 void mla_q_prep(const at::Tensor& q, const at::Tensor& positions, const at::Tensor& cos_sin,
                 at::Tensor& q_nope, at::Tensor& q_pe, int64_t H);
 void mla_heads_to_tokens(const at::Tensor& src, at::Tensor& dst, int64_t T, int64_t H);
+void ep_dispatch(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& wts,
+                 const std::vector<int64_t>& peers, int64_t rank, int64_t e0, int64_t el,
+                 const std::vector<int64_t>& offs, const at::Tensor& status);
+void ep_recv_map(at::Tensor& local_ids, const std::vector<int64_t>& peers, int64_t rank, int64_t T,
+                 int64_t k, int64_t H, int64_t e0, int64_t el, const std::vector<int64_t>& offs,
+                 const at::Tensor& status);
+void ep_gather(const at::Tensor& rows, const at::Tensor& offsets, at::Tensor& xq, at::Tensor& xs,
+               const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k, int64_t H,
+               int64_t e0, int64_t el, const std::vector<int64_t>& offs, const at::Tensor& status);
+void ep_combine(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank, int64_t k,
+                int64_t e0, int64_t el, const std::vector<int64_t>& offs, const at::Tensor& status);
+void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq,
+                              const at::Tensor& wsc, const at::Tensor& offsets, int64_t num_groups,
+                              int64_t rows_hint, const at::Tensor& sorted_rows,
+                              const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
+                              int64_t e0, const std::vector<int64_t>& offs, const at::Tensor& ws,
+                              const at::Tensor& counters, const at::Tensor& status);
 }  // namespace sil
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -102,5 +119,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_kv_write", &sil::mla_kv_write, "MLA latent KV write: RMSNorm(c_kv) + interleaved RoPE(k_pe)");
   m.def("mla_q_prep", &sil::mla_q_prep, "MLA query split: q_nope head-major + RoPE(q_pe)");
   m.def("mla_heads_to_tokens", &sil::mla_heads_to_tokens, "[H, T, 128] -> [T, H*128]");
+  m.def("ep_dispatch", &sil::ep_dispatch, "EP dispatch: e4m3 quantise + push rows/routing to every rank");
+  m.def("ep_recv_map", &sil::ep_recv_map, "EP: wait for every source, map expert ids to local groups");
+  m.def("ep_gather", &sil::ep_gather, "EP: received e4m3 rows into expert order");
+  m.def("ep_combine", &sil::ep_combine, "EP: wait for every owner, sum combine slots into h");
+  m.def("gemm_fp8_grouped_scatter", &sil::gemm_fp8_grouped_scatter,
+        "grouped fp8 GEMM with the weighted EP combine scattered to the token owners");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

@@ -22,6 +22,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <vector>
+
+#include "sil/ep.h"
 #include "sil/host.h"
 #include "sil/ptx.cuh"
 
@@ -33,7 +36,10 @@ constexpr int BK = 128;  // fp8 elements per K block (= one 128-byte swizzled ro
 constexpr int kThreads = 192;
 constexpr int kMaxGroups = 1024;
 
-enum Epi : int { kBf16 = 0, kResAdd = 1, kSwiGLU = 2, kF32 = 3 };
+// kScatter (grouped, swapped order only): expert-parallel combine -- each output row is
+// one (token, slot) assignment; the value times its routing weight goes straight into
+// the token owner's combine slot over peer memory (layout in sil/ep.h).
+enum Epi : int { kBf16 = 0, kResAdd = 1, kSwiGLU = 2, kF32 = 3, kScatter = 4 };
 
 struct Fp8Args {
   int M, N, KB;
@@ -50,6 +56,8 @@ struct Fp8Args {
   const int* grp_offsets;
   int num_groups;
   long long w_group_rows;
+  EpLayout ep;           // kScatter only
+  const int* sc_rows;    // kScatter: sorted position -> flat assignment (src * T + t) * k + j
 };
 
 template <int BN, int STAGES, bool SWAP, int EPI>
@@ -168,6 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const bool skip = flags[0] != 0;
   pdl_wait();  // scales, activations and group offsets come from earlier kernels
+  uint32_t ep_epoch = 0;
+  if constexpr (EPI == kScatter)
+    ep_epoch = *reinterpret_cast<volatile uint32_t*>(args.ep.peers[args.ep.rank]) + 1u;
   int tiles = args.m_tiles * args.n_tiles;
   if constexpr (GROUPED) {
     for (int g = threadIdx.x; g < args.num_groups; g += kThreads) {
@@ -370,7 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               orow = c.roff + m_loc;
               ocol = n;
             }
-            if constexpr (EPI == kF32) {
+            if constexpr (EPI == kScatter) {
+              const EpLayout& L = args.ep;
+              const int par = ep_epoch & 1;
+              const int asg = args.sc_rows[orow];
+              const int tok = asg / L.k, slot = asg % L.k;
+              const int src = tok / L.T, t = tok % L.T;
+              const float wgt = reinterpret_cast<const float*>(L.peers[L.rank] + L.wts_off)
+                  [(((long long)par * L.world + src) * L.T + t) * L.k + slot];
+              reinterpret_cast<__nv_bfloat16*>(L.peers[src] + L.slots_off)
+                  [(((long long)par * L.T + t) * L.k + slot) * L.H + ocol] = __float2bfloat16_rn(v * wgt);
+            } else if constexpr (EPI == kF32) {
               reinterpret_cast<float*>(args.out)[(long long)orow * args.ldo + ocol] = v;
             } else {
               if constexpr (EPI == kResAdd) v += __bfloat162float(args.res[(long long)orow * args.ldr + ocol]);
@@ -387,6 +408,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (EPI == kScatter) {
+    // The grid's last CTA tells every rank that this rank's expert outputs have landed.
+    const EpLayout& L = args.ep;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t* ctr = reinterpret_cast<uint32_t*>(L.peers[L.rank]) + kEpCtrGemm;
+      if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+        *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;
+        for (int p = 0; p < L.world; ++p) {
+          uint32_t* f = reinterpret_cast<uint32_t*>(L.peers[p] + L.cflag_off) + (ep_epoch & 1) * 8 + L.rank;
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(ep_epoch) : "memory");
+        }
+      }
+    }
   }
 }
 
@@ -425,7 +462,8 @@ template <bool GROUPED>
 void run_fp8(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq, const at::Tensor& wsc,
              at::Tensor& out, const c10::optional<at::Tensor>& res, int64_t epi,
              const c10::optional<at::Tensor>& offsets, int64_t num_groups, int64_t rows_hint,
-             const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status) {
+             const at::Tensor& ws, const at::Tensor& counters, const at::Tensor& status,
+             const EpLayout* ep = nullptr, const int* sc_rows = nullptr) {
   TORCH_CHECK(xq.scalar_type() == at::kByte || xq.scalar_type() == at::kFloat8_e4m3fn,
               "fp8 gemm: e4m3 activations (uint8 view)");
   TORCH_CHECK(wq.scalar_type() == at::kByte || wq.scalar_type() == at::kFloat8_e4m3fn,
@@ -442,7 +480,9 @@ void run_fp8(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq, c
   TORCH_CHECK(Wr % BM == 0 && (!swiglu || inter % BM == 0), "fp8 gemm: weight rows per group % 128");
   TORCH_CHECK(wsc.size(0) == wq.size(0) / BM && wsc.size(1) == K / BK && wsc.is_contiguous(),
               "fp8 gemm: weight scales [rows/128, K/128]");
-  TORCH_CHECK(out.size(0) == T && out.size(1) == Nout, "fp8 gemm: output shape");
+  TORCH_CHECK(epi == kScatter || (out.size(0) == T && out.size(1) == Nout), "fp8 gemm: output shape");
+  TORCH_CHECK(epi != kScatter || (GROUPED && ep != nullptr && ep->H == Nout),
+              "fp8 gemm: scatter epilogue needs the grouped EP form");
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(xq.device());
   Fp8Args a{};
@@ -457,6 +497,10 @@ void run_fp8(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq, c
   a.ws = ws.data_ptr<float>();
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
+  if (ep != nullptr) {
+    a.ep = *ep;
+    a.sc_rows = sc_rows;
+  }
   const int sms = device_sm_count();
   const bool swap = GROUPED ? rows_hint <= 64 : T <= 64;
   int bn;
@@ -511,6 +555,14 @@ void run_fp8(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq, c
     case kResAdd: dispatch8<kResAdd, GROUPED>(swap, bn, ta, tb, a, st); break;
     case kSwiGLU: dispatch8<kSwiGLU, GROUPED>(swap, bn, ta, tb, a, st); break;
     case kF32: dispatch8<kF32, GROUPED>(swap, bn, ta, tb, a, st); break;
+    case kScatter:
+      if constexpr (GROUPED) {
+        TORCH_CHECK(swap, "fp8 gemm: the scatter epilogue runs in the swapped (decode) order");
+        if (bn == 16) launch8<16, 10, true, kScatter, true>(ta, tb, a, st);
+        else if (bn == 32) launch8<32, 9, true, kScatter, true>(ta, tb, a, st);
+        else launch8<64, 8, true, kScatter, true>(ta, tb, a, st);
+      }
+      break;
     default: TORCH_CHECK(false, "fp8 gemm: unknown epilogue");
   }
 }
@@ -569,6 +621,27 @@ void quant_fp8_1x128(const at::Tensor& x, at::Tensor& q, at::Tensor& s) {
              at::cuda::getCurrentCUDAStream(), "quant_fp8 launch",
              reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0), K,
              reinterpret_cast<uint8_t*>(q.data_ptr()), s.data_ptr<float>(), rows);
+}
+
+EpLayout ep_make_layout(const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
+                        int64_t H, int64_t e0, int64_t el, const std::vector<int64_t>& offs,
+                        const at::Tensor& status);
+
+// Down projection of the local experts with the weighted combine fused into the epilogue:
+// results go to the token owners' combine slots over peer memory (see sil/ep.h).
+void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq,
+                              const at::Tensor& wsc, const at::Tensor& offsets, int64_t num_groups,
+                              int64_t rows_hint, const at::Tensor& sorted_rows,
+                              const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
+                              int64_t e0, const std::vector<int64_t>& offs, const at::Tensor& ws,
+                              const at::Tensor& counters, const at::Tensor& status) {
+  const int64_t H = wq.size(0) / num_groups;
+  EpLayout L = ep_make_layout(peers, rank, T, k, H, e0, num_groups, offs, status);
+  TORCH_CHECK(sorted_rows.scalar_type() == at::kInt && sorted_rows.numel() >= xq.size(0),
+              "fp8 scatter: sorted rows");
+  at::Tensor dummy = xq;
+  run_fp8<true>(xq, xs, wq, wsc, dummy, c10::nullopt, kScatter, offsets, num_groups,
+                std::min<int64_t>(rows_hint, 64), ws, counters, status, &L, sorted_rows.data_ptr<int>());
 }
 
 }  // namespace sil

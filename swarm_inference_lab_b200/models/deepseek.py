@@ -8,10 +8,13 @@ Parallel layout on one box (``ep`` = ranks of the group):
 * attention is data parallel: each rank owns its own sequences, their latent KV
   pages and a replica of the attention / dense weights (MLA's cache is shared by
   all heads, so head sharding would replicate the cache instead);
-* routed experts are sharded contiguously over the ranks (expert parallel);
-  each rank gathers every rank's normalised tokens, routes all of them with the
-  replicated router, runs its own experts, and the weighted combine is
-  reduce-scattered back to the tokens' owners;
+* routed experts are sharded contiguously over the ranks (expert parallel).
+  Decode with a fused communicator (``parallel/fused_ep.py``): each rank routes
+  its own tokens and pushes them in e4m3 to every expert owner over peer
+  memory; the owners' grouped down projection writes the weighted results
+  straight back into the tokens' owners (combine fused into the epilogue).
+  Otherwise (prefill, NCCL baseline): all-gather of the normalised tokens,
+  replicated routing, local experts, reduce-scatter of the weighted combine;
 * the shared expert and the dense layers run on the local tokens.
 
 Forward of one layer (T local tokens, Hh heads):
@@ -267,11 +270,44 @@ class MLAModel:
         aq, as_ = fp8.quantize(act)
         fp8.linear(aq, as_, *L.w_down, epi=fp8.EPI_RESADD, residual=h, out=h)
 
+    def _shared(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor) -> None:
+        if L.shared_gate_up is not None:
+            xq, xs = fp8.quantize(x)
+            sa = fp8.linear(xq, xs, *L.shared_gate_up, epi=fp8.EPI_SWIGLU)
+            sq, ss = fp8.quantize(sa)
+            fp8.linear(sq, ss, *L.shared_down, epi=fp8.EPI_RESADD, residual=h, out=h)
+
+    def _moe_fused(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor, epc) -> None:
+        """Decode MoE over peer memory: local routing, e4m3 dispatch to the expert owners,
+        grouped GEMMs, combine fused into the down projection (``parallel/fused_ep.py``)."""
+        cfg = self.cfg
+        k = cfg.num_experts_per_tok
+        e0, el = self.w.expert_start, self.w.experts_local
+        T = x.shape[0]
+        logits = gemm.linear(x, L.router, fp32_out=True)
+        ids, wts = moe_ops.route(logits, k, mode=self.mode, renorm=cfg.norm_topk_prob,
+                                 bias=L.router_bias, n_group=cfg.n_group, topk_group=cfg.topk_group,
+                                 scale=self.route_scale)
+        epc.dispatch(x, ids, wts, e0, el)
+        local_ids = epc.recv_map(T, e0, el)
+        offsets, rows, _ = moe_ops.permute(local_ids, el + 1)
+        xpq, xps = epc.gather(rows, offsets, T, e0, el)
+        hint = max(1, (local_ids.numel() + cfg.num_experts - 1) // cfg.num_experts)
+        act = fp8.grouped_linear(xpq, xps, *L.experts_gate_up, offsets, el, swiglu=True,
+                                 rows_hint=hint)
+        aq, as_ = fp8.quantize(act)
+        epc.down_scatter(aq, as_, *L.experts_down, offsets, el, hint, rows, T, e0)
+        self._shared(L, x, h)
+        epc.combine(h, e0, el)
+
     def moe(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor) -> None:
         cfg = self.cfg
         k = cfg.num_experts_per_tok
         e0, el = self.w.expert_start, self.w.experts_local
         ep = self.ep.size
+        epc = getattr(self.comm, "ep_fused", None) if ep > 1 else None
+        if epc is not None and epc.fits(x.shape[0]):
+            return self._moe_fused(L, x, h, epc)
         xa = self.comm.all_gather(x).view(-1, x.shape[1]) if ep > 1 else x
         Ta = xa.shape[0]
         logits = gemm.linear(xa, L.router, fp32_out=True)
@@ -289,11 +325,7 @@ class MLAModel:
         aq, as_ = fp8.quantize(act)
         y = fp8.grouped_linear(aq, as_, *L.experts_down, offsets, el, rows_hint=hint)
         limit = offsets[el:el + 1]
-        if L.shared_gate_up is not None:
-            xq, xs = fp8.quantize(x)
-            sa = fp8.linear(xq, xs, *L.shared_gate_up, epi=fp8.EPI_SWIGLU)
-            sq, ss = fp8.quantize(sa)
-            fp8.linear(sq, ss, *L.shared_down, epi=fp8.EPI_RESADD, residual=h, out=h)
+        self._shared(L, x, h)
         if ep == 1:
             moe_ops.combine(y, rows, wts, k, residual=h, out=h, row_limit=limit)
             return
