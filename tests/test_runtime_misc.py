@@ -95,3 +95,83 @@ def test_canonical_runtime_dry_run():
                                                            output_tokens=256, mode="throughput"))
     assert r["winner"]["engine"] == "native-stage"
     json.dumps(r)
+
+
+def test_network_probe_signed_ticket_and_repository():
+    import asyncio
+
+    from swarm_inference_lab_b200.cluster.network import (DirectedNetworkMeasurer, LinkRepository, ProbeServer,
+                                                          issue_ticket)
+    from swarm_inference_lab_b200.security.identity import Identity, SignatureError
+
+    async def main():
+        coord = Identity.generate("coord")
+        srv = ProbeServer("w1", coord.fingerprint)
+        port = await srv.start()
+        t = issue_ticket(coord, "w0", "w1", nbytes=1 << 20)
+        m = await DirectedNetworkMeasurer("w0", pings=5).measure("127.0.0.1", port, t)
+        assert m.dst == "w1" and m.rtt_ms > 0 and m.upload_Bps > 0 and m.download_Bps > 0
+        with pytest.raises(SignatureError):           # replayed ticket
+            await DirectedNetworkMeasurer("w0", pings=2).measure("127.0.0.1", port, t)
+        other = Identity.generate("rogue")
+        with pytest.raises(SignatureError):           # untrusted signer
+            await DirectedNetworkMeasurer("w0").measure("127.0.0.1", port, issue_ticket(other, "w0", "w1"))
+        await srv.close()
+        repo = LinkRepository(ttl_s=10)
+        repo.record(m)
+        assert repo.fresh("w0", "w1") is m
+        assert repo.stale_links([("w0", "w1"), ("w1", "w0")]) == [("w1", "w0")]
+        assert repo.fresh("w0", "w1", now=m.measured_at + 11) is None
+
+    asyncio.run(main())
+
+
+def test_tcp_meter_and_emulated_transport():
+    import asyncio
+
+    from swarm_inference_lab_b200.transport.emulated import EmulatedTransport, LinkDropped, LinkModel
+    from swarm_inference_lab_b200.transport.tcp_meter import TcpMeterProxy
+
+    async def main():
+        async def echo(r, w):
+            while True:
+                b = await r.read(4096)
+                if not b:
+                    break
+                w.write(b)
+                await w.drain()
+            w.close()
+        up = await asyncio.start_server(echo, "127.0.0.1", 0)
+        proxy = TcpMeterProxy("127.0.0.1", up.sockets[0].getsockname()[1])
+        port = await proxy.start()
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        w.write(b"x" * 10000)
+        await w.drain()
+        got = b""
+        while len(got) < 10000:
+            got += await r.read(4096)
+        w.close()
+        await asyncio.sleep(0.05)
+        assert proxy.stats.bytes_up == 10000 and proxy.stats.bytes_down == 10000
+        await proxy.close()
+        up.close()
+
+        async def handler(msg):
+            return [msg]
+        from swarm_inference_lab_b200.protocol import stage_ring as sr
+        msg = sr.StageMessage(operation=sr.Operation.HEALTH, model_revision="m", tokenizer_revision="t",
+                              topology_id="x", stage_id=0, layer_start=0, layer_end=1, session_id="s",
+                              request_id="r", sequence_number=0, token_position=0, source_stage=0,
+                              destination_stage=0)
+        em = EmulatedTransport(handler, LinkModel(latency_s=1e-3, bandwidth_Bps=1e6))
+        await em.request(msg)
+        t1 = em.clock.now
+        assert t1 > 2e-3
+        em2 = EmulatedTransport(handler, LinkModel(latency_s=1e-3, bandwidth_Bps=1e6))
+        await em2.request(msg)
+        assert em2.clock.now == t1                      # deterministic
+        drop = EmulatedTransport(handler, LinkModel(drop_prob=1.0))
+        with pytest.raises(LinkDropped):
+            await drop.request(msg)
+
+    asyncio.run(main())
