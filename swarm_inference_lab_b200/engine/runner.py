@@ -62,9 +62,11 @@ class ModelRunner:
         self.stream = torch.cuda.current_stream(self.device)
 
     # ------------------------------------------------------------ prefill
-    def prefill(self, ids: list[list[int]], starts: list[int], pages: list[list[int]]) -> torch.Tensor:
+    def prefill(self, ids: list[list[int]], starts: list[int], pages: list[list[int]], *,
+                all_rows: bool = False) -> torch.Tensor:
         """Varlen prefill: sequence i appends ``ids[i]`` at positions ``starts[i]..``.
-        Returns the greedy token of each sequence's last row (device int64)."""
+        Returns the greedy token of each sequence's last row (device int64), or of every
+        row with ``all_rows`` (multi-token verification for speculative decoding)."""
         dev = self.device
         B = len(ids)
         flat, pos, slots, cu = [], [], [], [0]
@@ -87,7 +89,8 @@ class ModelRunner:
             slots=torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True),
             seq_lens=torch.tensor(seq_lens, dtype=torch.int32).to(dev, non_blocking=True),
             block_table=bt.to(dev, non_blocking=True),
-            last_idx=torch.tensor(last, dtype=torch.int64).to(dev, non_blocking=True),
+            last_idx=(torch.arange(cu[-1], dtype=torch.int64) if all_rows
+                      else torch.tensor(last, dtype=torch.int64)).to(dev, non_blocking=True),
             is_decode=False,
             cu_q=torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True),
             max_q_len=max(len(x) for x in ids),

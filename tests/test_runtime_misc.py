@@ -175,3 +175,31 @@ def test_tcp_meter_and_emulated_transport():
             await drop.request(msg)
 
     asyncio.run(main())
+
+
+def test_simulation_ring_and_expert_layer():
+    from swarm_inference_lab_b200.testing.simulation import (Link, StageNode, expert_layer_time, simulate_ring,
+                                                             zipf_tokens)
+
+    def ring(churn=(), corruption=0.0):
+        stages = [StageNode("s0", 0.010, 1e-4), StageNode("s1", 0.020, 1e-4)]
+        return simulate_ring(stages, Link(latency_s=1e-3, bandwidth_Bps=1e9, corruption=corruption),
+                             requests=4, prompt_tokens=32, output_tokens=16, hidden_bytes=8192,
+                             churn=churn, seed=1)
+    a, b = ring(), ring()
+    assert a == b and a["completed"] == 4                      # deterministic
+    # four requests share the 20 ms bottleneck stage: ~50 tokens/s, TPOT ~ 4 x 20 ms
+    assert 0.07 < a["tpot_p50_s"] < 0.09
+    assert 40 < a["tokens_per_s"] < 55
+    c = ring(churn=[(0.2, 1, 0.5)])
+    assert c["completed"] == 4 and c["replays"] > 0 and c["sim_time_s"] > a["sim_time_s"]
+    d = ring(corruption=0.3)
+    assert d["resends"] > 0
+    even = expert_layer_time([10] * 8, [i // 2 for i in range(8)], 4, flops_per_token=1e9, rate_flops=1e15,
+                             weight_bytes_per_expert=4e7, hbm_Bps=6e12, token_bytes=14336, link_Bps=7e11,
+                             link_latency_s=1e-5)
+    skew = zipf_tokens(8, 64, 2, skew=1.5)
+    uneven = expert_layer_time(skew, [i // 2 for i in range(8)], 4, flops_per_token=1e9, rate_flops=1e15,
+                               weight_bytes_per_expert=4e7, hbm_Bps=6e12, token_bytes=14336,
+                               link_Bps=7e11, link_latency_s=1e-5)
+    assert even["imbalance"] == pytest.approx(1.0) and uneven["imbalance"] > 1.0
