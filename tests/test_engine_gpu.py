@@ -71,3 +71,19 @@ def test_speculative_decoding_is_exact_wrt_its_verifier():
     # row, so the verifier's greedy tokens do not depend on the draft width.
     assert spec == plain, (plain, spec)
     assert st.steps <= 40 and st.drafted > 0
+
+
+def test_fast_path_ladder_selects_an_exact_candidate(tmp_path):
+    from swarm_inference_lab_b200.engine.engine import LLMEngine
+    from swarm_inference_lab_b200.engine.fast_path import ProfileStore, select_fast_path
+    from swarm_inference_lab_b200.models.config import TINY_LLAMA_GPU
+
+    def make(graphs):
+        return LLMEngine(TINY_LLAMA_GPU, device="cuda", seed=0, max_batch=2, max_seq_len=256,
+                         use_cuda_graphs=graphs)
+    store = ProfileStore(tmp_path / "profiles.json")
+    rec = select_fast_path(make, [[1, 2, 3], [4, 5, 6, 7]], store=store, key="tiny|b200|b2")
+    assert rec["selected"] in ("eager", "eager+pdl", "graph+pdl"), rec
+    assert all(c["exact"] for c in rec["candidates"]), rec
+    assert select_fast_path(make, [[1]], store=ProfileStore(tmp_path / "profiles.json"),
+                            key="tiny|b200|b2") == rec
