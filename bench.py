@@ -5,6 +5,7 @@ data-parallel attention and EP=N; MoE presets: TP attention + EP experts).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 32] [--prompt-len 2048]
     torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1, one rank per GPU)
     torchrun --nproc-per-node 8 bench.py --gpus 8 --model kimi-k2-shape --batch 256 --prompt-len 4096
+    torchrun --nproc-per-node 8 bench.py --gpus 8 --model qwen3-30b-a3b-shape --pp 2 --batch 128 --prompt-len 512
     python bench.py --impl reference ...                       (the reference's own engine)
 
 Workload: synthetic token-id prompts (uniform random ids, seed 0) and random
@@ -47,6 +48,8 @@ def parse():
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
     ap.add_argument("--model", default="llama-3-8b-shape")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--pp", type=int, default=1, help="pipeline stages (MoE presets; ranks = pp x ep)")
+    ap.add_argument("--micro-batches", type=int, default=4)
     return ap.parse_args()
 
 
@@ -247,6 +250,11 @@ def main():
     try:
         if args.impl == "reference":
             out = run_reference(args, rank, world, local)
+        elif args.pp > 1:
+            from swarm_inference_lab_b200.models.config import preset
+            from swarm_inference_lab_b200.parallel.pp_moe import run_pp_bench
+            args.metric = METRIC
+            out = run_pp_bench(args, preset(args.model), rank, world, local)
         else:
             out = run_ours(args, rank, world, local)
         if rank == 0:

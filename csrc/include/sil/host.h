@@ -80,15 +80,23 @@ inline int device_sm_count() {
   return n;
 }
 
-// Programmatic dependent launch is on unless SIL_PDL=0.
-inline bool pdl_enabled() {
+// Programmatic dependent launch is on unless SIL_PDL=0 (or set_pdl_enabled(false)).
+inline int& pdl_state() {
   static int v = -1;
+  return v;
+}
+
+inline bool pdl_enabled() {
+  int& v = pdl_state();
   if (v < 0) {
     const char* e = std::getenv("SIL_PDL");
     v = (e == nullptr || e[0] != '0') ? 1 : 0;
   }
   return v == 1;
 }
+
+// Affects launches issued afterwards (CUDA graphs keep the attributes they were captured with).
+inline void set_pdl_enabled(bool on) { pdl_state() = on ? 1 : 0; }
 
 // Launch `kern` with the programmatic-stream-serialization attribute so its
 // pre-`griddepcontrol.wait` prologue may overlap the previous kernel's tail.

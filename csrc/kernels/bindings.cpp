@@ -75,9 +75,10 @@ void ep_dispatch(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& w
 void ep_recv_map(at::Tensor& local_ids, const std::vector<int64_t>& peers, int64_t rank, int64_t T,
                  int64_t k, int64_t H, int64_t e0, int64_t el, const std::vector<int64_t>& offs,
                  const at::Tensor& status);
-void ep_gather(const at::Tensor& rows, const at::Tensor& offsets, at::Tensor& xq, at::Tensor& xs,
-               const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k, int64_t H,
-               int64_t e0, int64_t el, const std::vector<int64_t>& offs, const at::Tensor& status);
+void ep_gather(const at::Tensor& pos, const at::Tensor& offsets, at::Tensor& xq, at::Tensor& xs,
+               at::Tensor& inv, const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
+               int64_t H, int64_t e0, int64_t el, const std::vector<int64_t>& offs,
+               const at::Tensor& status);
 void ep_combine(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank, int64_t k,
                 int64_t e0, int64_t el, const std::vector<int64_t>& offs, const at::Tensor& status);
 void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& wq,
@@ -86,6 +87,8 @@ void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const 
                               const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
                               int64_t e0, const std::vector<int64_t>& offs, const at::Tensor& ws,
                               const at::Tensor& counters, const at::Tensor& status);
+void set_pdl(bool on);
+bool get_pdl();
 }  // namespace sil
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -125,5 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine", &sil::ep_combine, "EP: wait for every owner, sum combine slots into h");
   m.def("gemm_fp8_grouped_scatter", &sil::gemm_fp8_grouped_scatter,
         "grouped fp8 GEMM with the weighted EP combine scattered to the token owners");
+  m.def("set_pdl", &sil::set_pdl, "enable / disable programmatic dependent launch for later launches");
+  m.def("get_pdl", &sil::get_pdl, "whether programmatic dependent launch is enabled");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

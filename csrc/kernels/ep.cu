@@ -19,8 +19,9 @@
 //                          grid's last CTA raises dflag[par][rank] on every rank.
 //   ep_recv_map  (owner)   wait for every source's dflag, map expert ids to local groups
 //                          (remote experts -> a trailing group).
-//   moe_permute            (existing kernel) group offsets and sorted assignment rows.
-//   ep_gather    (owner)   copy the e4m3 rows / scales of local assignments into expert order.
+//   moe_permute            (existing kernel) group offsets and each assignment's sorted position.
+//   ep_gather    (owner)   copy the e4m3 rows / scales of local assignments into expert order
+//                          and record sorted position -> assignment for the epilogue.
 //   grouped fp8 GEMMs      gate/up (SwiGLU) then down; the down GEMM's epilogue multiplies
 //                          by the routing weight and stores bf16 straight into the source
 //                          rank's slot (gemm_fp8.cu, kScatter), and its last CTA raises
@@ -160,25 +161,31 @@ __global__ void ep_recv_map_kernel(int* __restrict__ local_ids, const EpLayout L
   }
 }
 
-// One warp per sorted assignment i < offsets[el]: copy its e4m3 row and scales.
-__global__ void ep_gather_kernel(const int* __restrict__ rows, const int* __restrict__ offsets,
-                                 uint8_t* __restrict__ xq, float* __restrict__ xs, const EpLayout L) {
+// One warp per routed assignment a (= (src * T + t) * k + j) whose sorted position
+// p = pos[a] falls in a local expert group (p < offsets[el]): copy the token's e4m3 row and
+// scales to row p, and record inv[p] = a for the scatter epilogue.
+__global__ void ep_gather_kernel(const int* __restrict__ pos, const int* __restrict__ offsets,
+                                 uint8_t* __restrict__ xq, float* __restrict__ xs, int* __restrict__ inv,
+                                 const EpLayout L) {
   pdl_trigger();
   pdl_wait();
   const uint32_t epoch = read_epoch(L);
   const int par = epoch & 1;
   const int limit = offsets[L.el];
+  const int n = L.world * L.T * L.k;
   const int lane = threadIdx.x & 31;
   const uint8_t* rbase = reinterpret_cast<const uint8_t*>(L.peers[L.rank] + L.rows_off);
   const float* sbase = reinterpret_cast<const float*>(L.peers[L.rank] + L.scales_off);
-  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < limit;
-       i += (gridDim.x * blockDim.x) >> 5) {
-    const int tok = rows[i] / L.k;  // src * T + t
-    const long long srow = (long long)par * L.world * L.T + tok;
+  for (int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; a < n;
+       a += (gridDim.x * blockDim.x) >> 5) {
+    const int p = pos[a];
+    if (p >= limit) continue;
+    const long long srow = (long long)par * L.world * L.T + a / L.k;  // src * T + t
     const uint4* s = reinterpret_cast<const uint4*>(rbase + srow * L.H);
-    uint4* d = reinterpret_cast<uint4*>(xq + (long long)i * L.H);
+    uint4* d = reinterpret_cast<uint4*>(xq + (long long)p * L.H);
     for (int u = lane; u < L.H / 16; u += 32) d[u] = s[u];
-    for (int u = lane; u < L.KB; u += 32) xs[(long long)i * L.KB + u] = sbase[srow * L.KB + u];
+    for (int u = lane; u < L.KB; u += 32) xs[(long long)p * L.KB + u] = sbase[srow * L.KB + u];
+    if (lane == 0) inv[p] = a;
   }
 }
 
@@ -285,16 +292,23 @@ void ep_recv_map(at::Tensor& local_ids, const std::vector<int64_t>& peers, int64
              at::cuda::getCurrentCUDAStream(), "ep_recv_map launch", local_ids.data_ptr<int>(), L);
 }
 
-void ep_gather(const at::Tensor& rows, const at::Tensor& offsets, at::Tensor& xq, at::Tensor& xs,
-               const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k, int64_t H,
-               int64_t e0, int64_t el, const std::vector<int64_t>& offs, const at::Tensor& status) {
+// pos: moe_permute's assignment -> sorted position map; inv receives the inverse for the
+// local rows.
+void ep_gather(const at::Tensor& pos, const at::Tensor& offsets, at::Tensor& xq, at::Tensor& xs,
+               at::Tensor& inv, const std::vector<int64_t>& peers, int64_t rank, int64_t T, int64_t k,
+               int64_t H, int64_t e0, int64_t el, const std::vector<int64_t>& offs,
+               const at::Tensor& status) {
   EpLayout L = make_layout(peers, rank, T, k, H, e0, el, offs, status);
-  TORCH_CHECK(xq.size(1) == H && xs.size(1) == H / 128 && xq.size(0) >= rows.size(0),
-              "ep_gather: output shapes");
+  const long long n = (long long)L.world * T * k;
+  TORCH_CHECK(pos.numel() == n && inv.numel() >= n && pos.scalar_type() == at::kInt &&
+                  inv.scalar_type() == at::kInt,
+              "ep_gather: pos / inv [W*T*k] int32");
+  TORCH_CHECK(xq.size(1) == H && xs.size(1) == H / 128 && xq.size(0) >= n, "ep_gather: output shapes");
   c10::cuda::CUDAGuard guard(xq.device());
-  launch_pdl(ep_gather_kernel, dim3(blocks_for((long long)rows.size(0) * 32)), dim3(256), 0,
-             at::cuda::getCurrentCUDAStream(), "ep_gather launch", rows.data_ptr<int>(),
-             offsets.data_ptr<int>(), xq.data_ptr<uint8_t>(), xs.data_ptr<float>(), L);
+  launch_pdl(ep_gather_kernel, dim3(blocks_for(n * 32)), dim3(256), 0,
+             at::cuda::getCurrentCUDAStream(), "ep_gather launch", pos.data_ptr<int>(),
+             offsets.data_ptr<int>(), xq.data_ptr<uint8_t>(), xs.data_ptr<float>(), inv.data_ptr<int>(),
+             L);
 }
 
 void ep_combine(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank, int64_t k,

@@ -294,4 +294,8 @@ void gemm_grouped(const at::Tensor& xp, const at::Tensor& w, at::Tensor& out,
   else dispatch_grouped<kEpiBf16>(swap, bn, ta, tb, a, stream);
 }
 
+void set_pdl(bool on) { set_pdl_enabled(on); }
+
+bool get_pdl() { return pdl_enabled(); }
+
 }  // namespace sil

@@ -57,7 +57,7 @@ struct Fp8Args {
   int num_groups;
   long long w_group_rows;
   EpLayout ep;           // kScatter only
-  const int* sc_rows;    // kScatter: sorted position -> flat assignment (src * T + t) * k + j
+  const int* sc_rows;    // kScatter: sorted position -> assignment (src * T + t) * k + j
 };
 
 template <int BN, int STAGES, bool SWAP, int EPI>

@@ -290,13 +290,13 @@ class MLAModel:
                                  scale=self.route_scale)
         epc.dispatch(x, ids, wts, e0, el)
         local_ids = epc.recv_map(T, e0, el)
-        offsets, rows, _ = moe_ops.permute(local_ids, el + 1)
-        xpq, xps = epc.gather(rows, offsets, T, e0, el)
+        offsets, pos, _ = moe_ops.permute(local_ids, el + 1)
+        xpq, xps, inv = epc.gather(pos, offsets, T, e0, el)
         hint = max(1, (local_ids.numel() + cfg.num_experts - 1) // cfg.num_experts)
         act = fp8.grouped_linear(xpq, xps, *L.experts_gate_up, offsets, el, swiglu=True,
                                  rows_hint=hint)
         aq, as_ = fp8.quantize(act)
-        epc.down_scatter(aq, as_, *L.experts_down, offsets, el, hint, rows, T, e0)
+        epc.down_scatter(aq, as_, *L.experts_down, offsets, el, hint, inv, T, e0)
         self._shared(L, x, h)
         epc.combine(h, e0, el)
 

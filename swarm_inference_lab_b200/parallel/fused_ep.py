@@ -119,18 +119,21 @@ class FusedEPComm:
                           get_workspace(self.device).status)
         return out
 
-    def gather(self, rows: torch.Tensor, offsets: torch.Tensor, T: int, e0: int, el: int):
-        N = rows.shape[0]
+    def gather(self, pos: torch.Tensor, offsets: torch.Tensor, T: int, e0: int, el: int):
+        """``pos``: each assignment's sorted position (``moe_ops.permute``).  Returns the e4m3
+        rows / scales in expert order and the sorted position -> assignment map."""
+        N = pos.shape[0]
         xq = torch.empty((N, self.hidden), dtype=torch.uint8, device=self.device)
         xs = torch.empty((N, self.hidden // 128), dtype=torch.float32, device=self.device)
-        ext().ep_gather(rows, offsets, xq, xs, self.peers, self.rank, T, self.top_k, self.hidden, e0,
-                        el, self.offs, get_workspace(self.device).status)
-        return xq, xs
+        inv = torch.empty(N, dtype=torch.int32, device=self.device)
+        ext().ep_gather(pos, offsets, xq, xs, inv, self.peers, self.rank, T, self.top_k, self.hidden,
+                        e0, el, self.offs, get_workspace(self.device).status)
+        return xq, xs, inv
 
-    def down_scatter(self, aq, as_, wq, wscale, offsets, el: int, rows_hint: int, rows, T: int,
+    def down_scatter(self, aq, as_, wq, wscale, offsets, el: int, rows_hint: int, inv, T: int,
                      e0: int) -> None:
         ws = get_workspace(self.device)
-        ext().gemm_fp8_grouped_scatter(aq, as_, wq, wscale, offsets, el, int(rows_hint), rows,
+        ext().gemm_fp8_grouped_scatter(aq, as_, wq, wscale, offsets, el, int(rows_hint), inv,
                                        self.peers, self.rank, T, self.top_k, e0, self.offs, ws.ws,
                                        ws.counters, ws.status)
 
