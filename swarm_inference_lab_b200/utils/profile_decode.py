@@ -3,6 +3,8 @@
     python -m swarm_inference_lab_b200.utils.profile_decode --batch 32 --ctx 2048 [--steps 5]
     python -m swarm_inference_lab_b200.utils.profile_decode --op gemm --m 28672 --n 32 --k 4096 --swiglu
     python -m swarm_inference_lab_b200.utils.profile_decode --op decode_attn --batch 32 --ctx 2048
+    python -m swarm_inference_lab_b200.utils.profile_decode --op mla_decode --batch 32 --ctx 4096
+    python -m swarm_inference_lab_b200.utils.profile_decode --op fp8_grouped --groups 48 --n 6 --m 7168 --k 2048
 
 The decode mode builds the Llama-3-8B-shaped model with random weights and
 a KV cache whose pages hold random values (attention cost depends only on
@@ -98,6 +100,47 @@ def op_decode_attn(a):
             "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"]}
 
 
+def op_mla_decode(a):
+    """Absorbed MLA decode over a [pages, 64, 576] latent cache, 64 heads."""
+    from ..ops import mla
+    B, ctx, H = a.batch, a.ctx, 64
+    pages_per = (ctx + 63) // 64
+    cache = torch.randn(B * pages_per, 64, 576, device="cuda").bfloat16()
+    bt = torch.arange(B * pages_per, dtype=torch.int32, device="cuda").view(B, pages_per)
+    sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    q_lat = torch.randn(B, H, 512, device="cuda").bfloat16()
+    q_pe = torch.randn(B, H, 64, device="cuda").bfloat16()
+    splits = mla.decode_splits(B, ctx, H)
+    ms = time_fn(lambda: mla.attention(q_lat, q_pe, cache, bt, sl, scale=192 ** -0.5,
+                                       num_splits=splits), a.iters, graph=not a.eager)
+    bytes_ = B * ctx * 576 * 2
+    flops = 2 * B * H * ctx * (576 + 512)
+    pk = _peaks()
+    return {"op": "mla_decode", "batch": B, "ctx": ctx, "heads": H, "splits": splits, "ms": ms,
+            "GBps": bytes_ / ms / 1e6, "TFLOPs": flops / ms / 1e9,
+            "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"],
+            "frac_bf16_of_measured": flops / ms / 1e9 / pk["bf16_tflops"]}
+
+
+def op_fp8_grouped(a):
+    """Grouped block-scaled e4m3 GEMM (experts): ``groups`` x [m, k] weights, ``n`` rows each."""
+    from ..ops import fp8
+    G, rows, N, K = a.groups, a.n, a.m, a.k
+    wq = torch.randint(0, 100, (G * N, K), dtype=torch.uint8, device="cuda")
+    ws = torch.rand(G * N // 128, K // 128, device="cuda") * 1e-3
+    x = torch.randn(G * rows, K, device="cuda").bfloat16()
+    xq, xs = fp8.quantize(x)
+    off = torch.arange(G + 1, dtype=torch.int32, device="cuda") * rows
+    ms = time_fn(lambda: fp8.grouped_linear(xq, xs, wq, ws, off, G, rows_hint=rows), a.iters,
+                 graph=not a.eager)
+    bytes_ = G * N * K + G * rows * K + G * rows * N * 2
+    flops = 2 * G * rows * N * K
+    pk = _peaks()
+    return {"op": "fp8_grouped", "groups": G, "rows_per_group": rows, "out": N, "k": K, "ms": ms,
+            "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"],
+            "TFLOPs": flops / ms / 1e9}
+
+
 def decode_steps(a):
     from ..engine.kv_cache import PagedKVCache
     from ..models.config import preset
@@ -132,7 +175,9 @@ def decode_steps(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["step", "gemm", "decode_attn"], default="step")
+    ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "mla_decode", "fp8_grouped"],
+                    default="step")
+    ap.add_argument("--groups", type=int, default=48)
     ap.add_argument("--model", default="llama-3-8b-shape")
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--batch", type=int, default=32)
@@ -145,7 +190,8 @@ def main():
     ap.add_argument("--swiglu", action="store_true")
     ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
     a = ap.parse_args()
-    out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn}[a.op](a)
+    out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn,
+           "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped}[a.op](a)
     print(json.dumps(out))
 
 

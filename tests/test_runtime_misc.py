@@ -203,3 +203,75 @@ def test_simulation_ring_and_expert_layer():
                                weight_bytes_per_expert=4e7, hbm_Bps=6e12, token_bytes=14336,
                                link_Bps=7e11, link_latency_s=1e-5)
     assert even["imbalance"] == pytest.approx(1.0) and uneven["imbalance"] > 1.0
+
+
+def test_coordinator_runtime_partial_start_rollback():
+    import asyncio
+
+    from swarm_inference_lab_b200.coordinator.runtime import CoordinatorRuntime
+    log = []
+    rt = CoordinatorRuntime()
+    rt.add("state", lambda: log.append("start state"), lambda: log.append("stop state"))
+
+    async def boom():
+        raise RuntimeError("port in use")
+    rt.add("server", boom, lambda: log.append("stop server"))
+    with pytest.raises(RuntimeError):
+        asyncio.run(rt.start())
+    assert log == ["start state", "stop state"] and not rt.running
+    ok = CoordinatorRuntime()
+    ok.add("a", lambda: log.append("a"), lambda: log.append("-a"))
+    asyncio.run(ok.start())
+    asyncio.run(ok.start())                      # idempotent
+    asyncio.run(ok.stop())
+    assert log[-2:] == ["a", "-a"]
+
+
+def test_model_catalog_and_node_agent():
+    from swarm_inference_lab_b200.cluster.agent import NodeAgent, RuntimeManager
+    from swarm_inference_lab_b200.coordinator.catalog import ModelCatalog, ModelReport, probe_report
+    cat = ModelCatalog()
+    cat.report(probe_report("w0", "llama-3-8b-shape"))
+    cat.report(ModelReport("w1", "m", "rev-a", "qwen3", 10, 2, True, reported_at=1))
+    cat.report(ModelReport("w2", "m", "rev-a", "qwen3", 10, 2, True, reported_at=2))
+    cat.report(ModelReport("w3", "m", "rev-b", "qwen3", 10, 2, True, reported_at=3))
+    assert cat.resolve("m").revision == "rev-a" and cat.holders("rev-a") == ["w1", "w2"]
+    assert cat.resolve("llama-3-8b-shape").family == "llama"
+    cat.forget_worker("w1")
+    assert cat.holders("rev-a") == ["w2"]
+    cfg = RuntimeManager().configure({"devices": [{"memory_gb": 180}], "host_memory_gb": 64})
+    assert len({cfg.control_port, cfg.data_port, cfg.probe_port}) == 3
+    assert cfg.device_memory_bytes[0] < 180e9
+
+    class H:
+        def __init__(self):
+            self.up = True
+
+        def alive(self):
+            return self.up
+
+        def stop(self):
+            self.up = False
+    t = [0.0]
+    made = []
+
+    def factory():
+        h = H()
+        made.append(h)
+        return h
+    beats = []
+    ag = NodeAgent("n0", heartbeat=beats.append, max_restarts=2, backoff_s=1.0, clock=lambda: t[0])
+    ag.add("worker", factory)
+    ag.start()
+    assert ag.tick() == {"worker": "running"}
+    made[-1].up = False
+    assert ag.tick() == {"worker": "restarted"}
+    made[-1].up = False
+    assert ag.tick() == {"worker": "backoff"}
+    t[0] = 5.0
+    assert ag.tick() == {"worker": "restarted"}
+    made[-1].up = False
+    t[0] = 100.0
+    assert ag.tick() == {"worker": "failed"}
+    assert len(beats) == 5
+    ag.stop()
