@@ -275,3 +275,46 @@ def test_model_catalog_and_node_agent():
     assert ag.tick() == {"worker": "failed"}
     assert len(beats) == 5
     ag.stop()
+
+
+def test_compatibility_registry_and_engine_leases(tmp_path):
+    from swarm_inference_lab_b200.engines.compat import CompatibilityRegistry, engine_facts, probe_native_stage
+    from swarm_inference_lab_b200.engines.worker_control import EngineController, issue_engine_lease
+    from swarm_inference_lab_b200.security.identity import Identity, SignatureError
+    facts = engine_facts({"devices": [{"capability": "10.0", "memory_gb": 183}], "host_memory_gb": 2000})
+    assert facts["sm100a_kernels"] and "fp8_e4m3" in facts["dtypes"]
+    reg = CompatibilityRegistry(tmp_path / "compat.json")
+    assert probe_native_stage(reg, facts, "llama", "bf16", lambda: None).ok
+
+    def bad():
+        raise RuntimeError("kernel failed")
+    assert not probe_native_stage(reg, facts, "deepseek_v3", "fp8_block128", bad).ok
+    again = CompatibilityRegistry(tmp_path / "compat.json")
+    assert again.check("native-stage", "deepseek_v3", "fp8_block128", "b200")[0] is False
+    assert again.check("native-stage", "qwen3", "bf16", "b200") == (True, "unprobed", 0.9)
+    cpu = engine_facts({"devices": []})
+    assert not probe_native_stage(reg, cpu, "llama", "bf16", lambda: None).ok
+
+    coord, worker = Identity.generate("c"), Identity.generate("w")
+    t = [1000.0]
+    started = []
+
+    class Handle:
+        def __init__(self, n):
+            self.n = n
+            started.append(n)
+
+        def stop(self):
+            started.remove(self.n)
+    ctl = EngineController(worker.fingerprint, coord.fingerprint, lambda e, rev: Handle(e), clock=lambda: t[0])
+    lease = issue_engine_lease(coord, worker_fingerprint=worker.fingerprint, engine="native-stage",
+                               model_revision="r1", generation=1, ttl_s=60)
+    assert ctl.apply(lease) == "started" and started == ["native-stage"]
+    with pytest.raises(SignatureError):
+        ctl.apply(lease)                              # replay
+    other = issue_engine_lease(coord, worker_fingerprint="someone-else", engine="x", model_revision="r",
+                               generation=2)
+    with pytest.raises(SignatureError):
+        ctl.apply(other)
+    t[0] = 1e12
+    assert ctl.sweep() == ["native-stage"] and started == []
