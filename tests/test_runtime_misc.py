@@ -318,3 +318,33 @@ def test_compatibility_registry_and_engine_leases(tmp_path):
         ctl.apply(other)
     t[0] = 1e12
     assert ctl.sweep() == ["native-stage"] and started == []
+
+
+def test_tensor_paths_and_shard_manager(tmp_path):
+    from swarm_inference_lab_b200.model_io.resolver import ModelSourceResolver
+    from swarm_inference_lab_b200.runtime.shard_manager import ShardIntegrityError, ShardLimitError, ShardManager
+    from swarm_inference_lab_b200.transport.tensor_paths import choose_path
+    t = torch.randn(3, 5)
+    for same_proc, same_host in ((True, True), (False, True), (False, False)):
+        p = choose_path(same_proc, same_host, peer_access=False)
+        assert torch.equal(p.recv(p.send(t)), t), p.name
+    import importlib.util
+    import pathlib
+    spec = importlib.util.spec_from_file_location("tmio", pathlib.Path(__file__).with_name("test_model_io.py"))
+    tmio = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tmio)
+    _tiny_ckpt = tmio._tiny_ckpt
+    ck = tmp_path / "ck"
+    ck.mkdir()
+    _tiny_ckpt(ck)
+    res = ModelSourceResolver().inspect(str(ck))
+    sm = ShardManager(budget_bytes=res.stage_bytes(0, 1, embed=True, head=False))
+    st = sm.load_stage(res, 0, 1, embed=True, head=False)
+    assert "model.embed_tokens.weight" in st.tensors and all(".layers.1." not in n for n in st.tensors)
+    with pytest.raises(ShardLimitError):
+        sm.load_stage(res, 1, 2, embed=False, head=True)
+    sm.unload(st.key)
+    assert sm.used == 0
+    with pytest.raises(ShardIntegrityError):
+        ShardManager(budget_bytes=1 << 30).load_stage(res, 1, 2, embed=False, head=True,
+                                                      file_digests={"x": "0"})
