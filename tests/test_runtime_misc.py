@@ -348,3 +348,40 @@ def test_tensor_paths_and_shard_manager(tmp_path):
     with pytest.raises(ShardIntegrityError):
         ShardManager(budget_bytes=1 << 30).load_stage(res, 1, 2, embed=False, head=True,
                                                       file_digests={"x": "0"})
+
+
+def test_grpc_control_envelopes_and_chunk_stream():
+    import asyncio
+
+    from swarm_inference_lab_b200.transport.grpc_control import (EnvelopeError, GrpcControlClient,
+                                                                 GrpcControlServer, pack, unpack)
+    k, o = unpack(pack("WorkerHello", {"b": 1, "a": [1, 2]}))
+    assert k == "WorkerHello" and o == {"a": [1, 2], "b": 1}
+    assert pack("X", {"b": 1, "a": 2}).value == b'{"a":2,"b":1}'
+
+    async def main():
+        workers = {}
+
+        async def register(kind, obj):
+            workers[obj["worker_id"]] = obj
+            return "RegisterAck", {"accepted": True, "count": len(workers)}
+
+        async def echo_stream(tid, data):
+            return data[::-1]
+        srv = GrpcControlServer({("swarm.v1.Coordinator", "Register"): register},
+                                stream_handler=echo_stream)
+        port = await srv.start()
+        cli = GrpcControlClient(f"127.0.0.1:{port}")
+        kind, rep = await cli.call("swarm.v1.Coordinator", "Register", "WorkerRegistration",
+                                   {"worker_id": "w0", "gpus": 8}, expect="RegisterAck")
+        assert rep == {"accepted": True, "count": 1}
+        data = bytes(range(256)) * 12000           # ~3 MB, several chunks
+        out = await cli.execute_stream("t0", data, chunk_bytes=1 << 20)
+        assert out == data[::-1]
+        with pytest.raises(EnvelopeError):
+            await cli.call("swarm.v1.Coordinator", "Register", "WorkerRegistration", {"worker_id": "w1"},
+                           expect="Other")
+        await cli.close()
+        await srv.stop()
+
+    asyncio.run(main())
