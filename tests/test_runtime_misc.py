@@ -385,3 +385,26 @@ def test_grpc_control_envelopes_and_chunk_stream():
         await srv.stop()
 
     asyncio.run(main())
+
+
+def test_replica_placement_reservations_and_scheduler():
+    from swarm_inference_lab_b200.coordinator.replicas import (AtomicRouteAllocator, CapacityExhausted,
+                                                               ReplicaScheduler, place_replicas)
+    speeds = {f"w{i}": s for i, s in enumerate([100, 90, 80, 70, 60, 50])}
+    routes = place_replicas(speeds, replicas=2, stages=3, capacity=2)
+    bott = sorted(min(speeds[w] for w in r.workers) for r in routes)
+    assert len(routes) == 2 and all(len(r.workers) == 3 for r in routes)
+    assert bott[0] >= 50 and len({w for r in routes for w in r.workers}) == 6
+    t = [0.0]
+    alloc = AtomicRouteAllocator(routes, ttl_s=10, clock=lambda: t[0])
+    sch = ReplicaScheduler(alloc)
+    grants = [sch.submit(100, 50) for _ in range(4)]
+    assert {g.route_id for g in grants} == {"replica0", "replica1"}
+    with pytest.raises(CapacityExhausted):
+        sch.submit(100, 50)
+    alloc.release(grants[0].lease_id)
+    sch.submit(100, 50)
+    t[0] = 100.0                                     # every lease expired -> reclaimed
+    alloc.reserve("replica0")
+    assert alloc.routes["replica0"].active == 1 and alloc.routes["replica1"].active == 0
+    assert all(v in (0, 1) for v in alloc.worker_load.values())
