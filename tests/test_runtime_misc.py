@@ -408,3 +408,21 @@ def test_replica_placement_reservations_and_scheduler():
     alloc.reserve("replica0")
     assert alloc.routes["replica0"].active == 1 and alloc.routes["replica1"].active == 0
     assert all(v in (0, 1) for v in alloc.worker_load.values())
+
+
+def test_platform_adapters_and_acceptance(tmp_path):
+    from swarm_inference_lab_b200 import platforms
+    from swarm_inference_lab_b200.testing.acceptance import model_matrix, pre_physical_gate, write_evidence
+    lx = platforms.LinuxAdapter()
+    unit = lx.service_definition(["/usr/bin/python3", "-m", "swarm_inference_lab_b200.cli", "node", "run"])
+    assert "ExecStart=/usr/bin/python3 -m" in unit and "Restart=on-failure" in unit
+    assert "tcp dport { 7000, 7001 }" in lx.firewall_rules([7001, 7000])
+    assert "host_memory_gb" in lx.hardware()
+    assert "<key>Label</key>" in platforms.MacAdapter().service_definition(["a"])
+    assert platforms.WindowsAdapter().service_definition(["C:\\\\x.exe"]).startswith("sc.exe create")
+    gate = pre_physical_gate()
+    assert gate["ok"], gate
+    rows = {r["model"]: r for r in model_matrix()}
+    assert rows["llama-3-8b-shape"]["fits"] and rows["kimi-k2-shape"]["params"] > 9e11
+    p = write_evidence(gate, tmp_path)
+    assert p.exists()
