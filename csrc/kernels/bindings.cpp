@@ -16,7 +16,7 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
                    const at::Tensor& status);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
              const c10::optional<at::Tensor>& residual_out, const at::Tensor& w, at::Tensor& y,
-             double eps);
+             double eps, const c10::optional<at::Tensor>& yq, const c10::optional<at::Tensor>& ys);
 void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,
                    const at::Tensor& cos_sin, const c10::optional<at::Tensor>& q_norm_w,
                    const c10::optional<at::Tensor>& k_norm_w, double eps, at::Tensor& k_cache,

@@ -10,6 +10,7 @@
 // lowest token id (si/model/qwen3_sampling.py:79-96, si/microsharding/dense.py:825-838).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cuda_fp8.h>
 #include <torch/extension.h>
 
 #include "sil/host.h"
@@ -35,7 +36,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
                                const __nv_bfloat16* __restrict__ r, long long ldr,
                                __nv_bfloat16* __restrict__ res_out, long long ldro,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                               long long ldy, int H, float eps) {
+                               long long ldy, int H, float eps, uint8_t* __restrict__ yq,
+                               float* __restrict__ ys) {
   __shared__ float red[32];
   pdl_trigger();
   pdl_wait();
@@ -66,20 +68,49 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
   }
   const float tot = block_sum(ss, red);
   const float rstd = rsqrtf(tot / H + eps);
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    uint4 wq = *reinterpret_cast<const uint4*>(w + i);
-    float wv[8] = {bf16_lo(wq.x), bf16_hi(wq.x), bf16_lo(wq.y), bf16_hi(wq.y),
-                   bf16_lo(wq.z), bf16_hi(wq.z), bf16_lo(wq.w), bf16_hi(wq.w)};
-    float o[8];
+  // Every thread runs the same number of iterations so the 16-lane shuffles of the
+  // e4m3 path see full warps; out-of-range lanes carry zeros.
+  for (int base = 0; base < H; base += blockDim.x * 8) {
+    const int i = base + threadIdx.x * 8;
+    const bool in = i < H;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (in) {
+      uint4 wq = *reinterpret_cast<const uint4*>(w + i);
+      float wv[8] = {bf16_lo(wq.x), bf16_hi(wq.x), bf16_lo(wq.y), bf16_hi(wq.y),
+                     bf16_lo(wq.z), bf16_hi(wq.z), bf16_lo(wq.w), bf16_hi(wq.w)};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float nrm = __bfloat162float(__float2bfloat16_rn(vals[i + j] * rstd));
-      o[j] = wv[j] * nrm;
+      for (int j = 0; j < 8; ++j) {
+        const float nrm = __bfloat162float(__float2bfloat16_rn(vals[i + j] * rstd));
+        o[j] = __bfloat162float(__float2bfloat16_rn(wv[j] * nrm));
+      }
+      uint4 q;
+      q.x = pack_bf16x2(o[0], o[1]); q.y = pack_bf16x2(o[2], o[3]);
+      q.z = pack_bf16x2(o[4], o[5]); q.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(y + row * ldy + i) = q;
     }
-    uint4 q;
-    q.x = pack_bf16x2(o[0], o[1]); q.y = pack_bf16x2(o[2], o[3]);
-    q.z = pack_bf16x2(o[4], o[5]); q.w = pack_bf16x2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(y + row * ldy + i) = q;
+    if (yq != nullptr) {
+      // e4m3 with one scale per 128 columns (16 lanes x 8 values), like quant_fp8_1x128.
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(o[j]));
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      const float sc = amax > 0.f ? amax / 448.f : 1.f;
+      const float inv = 1.f / sc;
+      if (in) {
+        uint32_t pk[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const __nv_fp8x2_storage_t a = __nv_cvt_float2_to_fp8x2(
+              make_float2(o[4 * h] * inv, o[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+          const __nv_fp8x2_storage_t b = __nv_cvt_float2_to_fp8x2(
+              make_float2(o[4 * h + 2] * inv, o[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+          pk[h] = static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
+        }
+        *reinterpret_cast<uint2*>(yq + (long long)row * H + i) = make_uint2(pk[0], pk[1]);
+        if ((threadIdx.x & 15) == 0) ys[(long long)row * (H / 128) + i / 128] = sc;
+      }
+    }
   }
 }
 
@@ -215,7 +246,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, long long ld, in
 
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
              const c10::optional<at::Tensor>& residual_out, const at::Tensor& w, at::Tensor& y,
-             double eps) {
+             double eps, const c10::optional<at::Tensor>& yq, const c10::optional<at::Tensor>& ys) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
               "rmsnorm: x must be 2-D bf16 with contiguous rows");
   const int T = x.size(0), H = x.size(1);
@@ -232,13 +263,22 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
     rop = reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr());
     ldro = residual_out->stride(0);
   }
+  uint8_t* qp = nullptr;
+  float* sp = nullptr;
+  if (yq.has_value()) {
+    TORCH_CHECK(ys.has_value() && H % 128 == 0 && yq->is_contiguous() && ys->is_contiguous() &&
+                    yq->numel() == (long long)T * H && ys->numel() == (long long)T * (H / 128),
+                "rmsnorm: e4m3 output [T, H] with scales [T, H/128] (H % 128 == 0)");
+    qp = reinterpret_cast<uint8_t*>(yq->data_ptr());
+    sp = ys->data_ptr<float>();
+  }
   const int threads = std::min(1024, std::max(32, ((H / 8 + 31) / 32) * 32));
   launch_pdl(rmsnorm_kernel, dim3(T), dim3(threads), H * sizeof(float),
              at::cuda::getCurrentCUDAStream(), "rmsnorm launch",
              reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0), rp, ldr,
              rop, ldro, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
              reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), (long long)y.stride(0), H,
-             static_cast<float>(eps));
+             static_cast<float>(eps), qp, sp);
 }
 
 void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,

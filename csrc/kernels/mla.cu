@@ -13,11 +13,13 @@
 // MQA problem with 64 query heads per token.
 //
 // One CTA owns 64 query rows (row = token * H + head, heads fastest) of one
-// sequence and one split of its context.  Eight warps: warp w holds rows
-// (w % 4) * 16 .. +16 and value columns (w / 4) * 256 .. +256 of the output;
-// for the scores the same warp pair splits the 32 keys of a tile, exchanges
-// row maxima and sums through shared memory, and writes P (bf16) for both.
-// Split partials are merged in split order by the last CTA of the row block.
+// sequence and one split of its context.  Eight warps.  Scores: warp w computes
+// rows (w % 4) * 16 .. +16 x keys (w / 4) * 16 .. +16 of each 32-key tile; row
+// maxima and sums are exchanged through shared memory and P (bf16) is written
+// there.  Output: warp w owns all 64 rows x value columns w * 64 .. +64, so every
+// V fragment is read from shared memory once per tile.  The running max / sum
+// and the per-tile rescale factors live in shared memory.  With more than one
+// split, a second kernel merges the fp32 partials in split order (deterministic).
 //
 // The reference has no MLA kernel (DeepSeek/Kimi are metadata profiles only:
 // si/model/architecture_adapters.py:735-976); the math follows the DeepSeek-V3
@@ -48,7 +50,7 @@ constexpr int kQBytes = kChunks * kQChunkBytes;    // 72 KB
 constexpr int kPStride = 40;               // bf16 elements per P row (80 B: conflict-free)
 constexpr int kThreads = 256;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kQBytes + kRows * kPStride * 2 +
-                           4 * kRows * 4 + 64;
+                           8 * kRows * 4 + 64;
 
 struct MlaArgs {
   const __nv_bfloat16* q_lat;   // [.., 512] rows at token * qt_stride + head * qh_stride
@@ -66,7 +68,6 @@ struct MlaArgs {
   float scale_log2;
   float* ws_o;                  // [B, RB, S, 64, 512] partial outputs
   float* ws_ml;                 // [B, RB, S, 64, 2]
-  int* counters;                // [B * RB]
   int* status;
 };
 
@@ -96,7 +97,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(sQ + kQBytes);
   float* red_max = reinterpret_cast<float*>(sP + kRows * kPStride);  // [2][64]
   float* red_sum = red_max + 2 * kRows;                                // [2][64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red_sum + 2 * kRows);
+  float* s_m = red_sum + 2 * kRows;                                    // running max [64]
+  float* s_l = s_m + kRows;                                            // running sum [64]
+  float* s_alpha = s_l + kRows;                                        // this tile's rescale [64]
+  float* s_mnew = s_alpha + kRows;                                     // this tile's max [64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_mnew + kRows);
   int* sflag = reinterpret_cast<int*>(full + kStages);
 
   pdl_trigger();
@@ -156,19 +161,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
-  // Per-thread rows (g, g + 8 of this warp's 16) and their last visible key.
+  // Scores: warp (rg, vh) owns rows rg*16..+16 and keys vh*16..+16 of each tile.
   int lim[2];
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const int row = row0 + rg * 16 + g + 8 * rr;
     lim[rr] = row < rows_total ? min(kv_len - 1, pos0 + row / H) : -1;
   }
-
-  float o[32][4];
+  if (threadIdx.x < kRows) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
+  }
+  // Output: warp w owns all 64 rows x value columns w*64..+64 (4 m-tiles x 8 n-tiles).
+  float o[4][8][4];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
   bool alive = !skip;
+  __syncthreads();
 
   for (int i = 0; i < count; ++i) {
     const int s = i % kStages;
@@ -211,60 +222,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t == 0) red_max[vh * kRows + rg * 16 + g + 8 * rr] = mx[rr];
     }
     __syncthreads();
-    float alpha[2], m_use[2];
+    // Probabilities with the row's new running max; the vh == 0 warp publishes alpha.
+    float rs[2] = {0.f, 0.f};
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
       const int r = rg * 16 + g + 8 * rr;
-      const float m_new = fmaxf(m_r[rr], fmaxf(red_max[r], red_max[kRows + r]));
-      m_use[rr] = m_new == -INFINITY ? 0.f : m_new;
-      alpha[rr] = exp2f(m_r[rr] - m_use[rr]);
-      m_r[rr] = m_new;
-    }
-    float rs[2] = {0.f, 0.f};
+      const float m_old = s_m[r];
+      const float m_new = fmaxf(m_old, fmaxf(red_max[r], red_max[kRows + r]));
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const float p0 = exp2f(sc[nt][2 * jj] - m_use[jj]);
-        const float p1 = exp2f(sc[nt][2 * jj + 1] - m_use[jj]);
-        rs[jj] += p0 + p1;
-        const int r = rg * 16 + g + 8 * jj;
+      for (int nt = 0; nt < 2; ++nt) {
+        const float p0 = exp2f(sc[nt][2 * rr] - m_use);
+        const float p1 = exp2f(sc[nt][2 * rr + 1] - m_use);
+        rs[rr] += p0 + p1;
         *reinterpret_cast<uint32_t*>(sP + r * kPStride + vh * 16 + nt * 8 + 2 * t) =
             pack_bf16x2(p0, p1);
       }
-    }
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
       rs[rr] += __shfl_xor_sync(0xffffffffu, rs[rr], 1);
       rs[rr] += __shfl_xor_sync(0xffffffffu, rs[rr], 2);
-      if (t == 0) red_sum[vh * kRows + rg * 16 + g + 8 * rr] = rs[rr];
+      if (t == 0) {
+        red_sum[vh * kRows + r] = rs[rr];
+        if (vh == 0) {
+          s_alpha[r] = exp2f(m_old - m_use);
+          s_mnew[r] = m_new;
+        }
+      }
     }
     __syncthreads();
+    if (threadIdx.x < kRows) {
+      const int r = threadIdx.x;
+      s_l[r] = s_l[r] * s_alpha[r] + red_sum[r] + red_sum[kRows + r];
+      s_m[r] = s_mnew[r];
+    }
+    float al[4][2];
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int r = rg * 16 + g + 8 * rr;
-      l_r[rr] = l_r[rr] * alpha[rr] + red_sum[r] + red_sum[kRows + r];
+    for (int mt = 0; mt < 4; ++mt) {
+      al[mt][0] = s_alpha[mt * 16 + g];
+      al[mt][1] = s_alpha[mt * 16 + g + 8];
     }
 #pragma unroll
-    for (int nd = 0; nd < 32; ++nd) {
-      o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
-      o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
-    }
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        o[mt][nt][0] *= al[mt][0]; o[mt][nt][1] *= al[mt][0];
+        o[mt][nt][2] *= al[mt][1]; o[mt][nt][3] *= al[mt][1];
+      }
     if (alive) {
       const uint32_t pbase = smem_u32(sP);
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
-        uint32_t pa[4];
-        ldmatrix_x4(pbase + ((rg * 16 + (lane & 15)) * kPStride + kk * 16 + (lane >> 4) * 8) * 2,
-                    pa[0], pa[1], pa[2], pa[3]);
+        uint32_t pa[4][4];
 #pragma unroll
-        for (int nd2 = 0; nd2 < 16; ++nd2) {
+        for (int mt = 0; mt < 4; ++mt)
+          ldmatrix_x4(pbase + ((mt * 16 + (lane & 15)) * kPStride + kk * 16 + (lane >> 4) * 8) * 2,
+                      pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3]);
+#pragma unroll
+        for (int nd2 = 0; nd2 < 4; ++nd2) {
           uint32_t b0, b1, b2, b3;
           ldmatrix_x4_trans(kv_addr(kvb, kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8,
-                                    vh * 256 + nd2 * 16 + (lane >> 4) * 8),
+                                    warp * 64 + nd2 * 16 + (lane >> 4) * 8),
                             b0, b1, b2, b3);
-          mma_bf16_16816(o[2 * nd2], pa, b0, b1);
-          mma_bf16_16816(o[2 * nd2 + 1], pa, b2, b3);
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            mma_bf16_16816(o[mt][2 * nd2], pa[mt], b0, b1);
+            mma_bf16_16816(o[mt][2 * nd2 + 1], pa[mt], b2, b3);
+          }
         }
       }
     }
@@ -273,58 +295,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       issue_tile(smem + s * kStageBytes, &tmC, &full[s], tile_row(t_begin + i + kStages));
   }
 
+  // Epilogue: final rows (one split) or fp32 partials + (max, sum) for the merge kernel.
   const long long slot = ((long long)b * RB + rb) * S + split;
 #pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const int r = rg * 16 + g + 8 * rr;
-    const int row = row0 + r;
-    if (row >= rows_total) continue;
-    if (S == 1) {
-      if (skip) continue;
-      const float inv = l_r[rr] > 0.f ? 1.f / l_r[rr] : 0.f;
-      const int tok = q_begin + row / H, h = row % H;
-      __nv_bfloat16* dst = args.out + tok * args.ot_stride + h * args.oh_stride + vh * 256 + 2 * t;
+  for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-      for (int nd = 0; nd < 32; ++nd)
-        *reinterpret_cast<uint32_t*>(dst + nd * 8) =
-            pack_bf16x2(o[nd][2 * rr] * inv, o[nd][2 * rr + 1] * inv);
-    } else {
-      float* dst = args.ws_o + (slot * kRows + r) * kLat + vh * 256 + 2 * t;
+    for (int rr = 0; rr < 2; ++rr) {
+      const int r = mt * 16 + g + 8 * rr;
+      const int row = row0 + r;
+      if (row >= rows_total || skip) continue;
+      if (S == 1) {
+        const float L = s_l[r];
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        const int tok = q_begin + row / H, h = row % H;
+        __nv_bfloat16* dst = args.out + tok * args.ot_stride + h * args.oh_stride + warp * 64 + 2 * t;
 #pragma unroll
-      for (int nd = 0; nd < 32; ++nd)
-        *reinterpret_cast<float2*>(dst + nd * 8) = make_float2(o[nd][2 * rr], o[nd][2 * rr + 1]);
-      if (vh == 0 && t == 0) {
-        args.ws_ml[(slot * kRows + r) * 2] = m_r[rr];
-        args.ws_ml[(slot * kRows + r) * 2 + 1] = l_r[rr];
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<uint32_t*>(dst + nt * 8) =
+              pack_bf16x2(o[mt][nt][2 * rr] * inv, o[mt][nt][2 * rr + 1] * inv);
+      } else {
+        float* dst = args.ws_o + (slot * kRows + r) * kLat + warp * 64 + 2 * t;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(o[mt][nt][2 * rr], o[mt][nt][2 * rr + 1]);
+        if (warp == 0 && t == 0) {
+          args.ws_ml[(slot * kRows + r) * 2] = s_m[r];
+          args.ws_ml[(slot * kRows + r) * 2 + 1] = s_l[r];
+        }
       }
     }
-  }
-  if (S == 1 || skip) return;
-  __threadfence();
-  __syncthreads();
-  const long long cidx = (long long)b * RB + rb;
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(&args.counters[cidx], 1);
-    sflag[1] = old == S - 1;
-  }
-  __syncthreads();
-  if (!sflag[1]) return;
-  __threadfence();
+}
+
+// Merge the split partials of one (sequence, row block) in split order: 8 rows per CTA.
+__global__ void __launch_bounds__(256)
+    mla_merge_kernel(const MlaArgs args, int RB) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.z, rb = blockIdx.y, r0 = blockIdx.x * 8;
+  const int S = args.num_splits, H = args.H;
+  const int q_begin = args.cu_q ? args.cu_q[b] : b;
+  const int q_len = args.cu_q ? args.cu_q[b + 1] - q_begin : 1;
+  const int rows_total = q_len * H;
+  if (load_status(args.status) != 0) return;
   const long long base0 = ((long long)b * RB + rb) * S;
-  for (int e = threadIdx.x; e < kRows * (kLat / 4); e += kThreads) {
-    const int r = e / (kLat / 4), d = (e % (kLat / 4)) * 4;
-    const int row = row0 + r;
+  for (int e = threadIdx.x; e < 8 * (kLat / 4); e += blockDim.x) {
+    const int r = r0 + e / (kLat / 4), d = (e % (kLat / 4)) * 4;
+    const int row = rb * kRows + r;
     if (row >= rows_total) continue;
     float M = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, __ldcg(&args.ws_ml[((base0 + sp) * kRows + r) * 2]));
+    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, args.ws_ml[((base0 + sp) * kRows + r) * 2]);
     const float Mu = M == -INFINITY ? 0.f : M;
     float L = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sp = 0; sp < S; ++sp) {
       const long long sr = (base0 + sp) * kRows + r;
-      const float f = exp2f(__ldcg(&args.ws_ml[sr * 2]) - Mu);
-      L += __ldcg(&args.ws_ml[sr * 2 + 1]) * f;
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(args.ws_o + sr * kLat + d));
+      const float f = exp2f(args.ws_ml[sr * 2] - Mu);
+      L += args.ws_ml[sr * 2 + 1] * f;
+      const float4 v = *reinterpret_cast<const float4*>(args.ws_o + sr * kLat + d);
       acc.x += v.x * f; acc.y += v.y * f; acc.z += v.z * f; acc.w += v.w * f;
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -333,7 +360,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint2*>(dst) =
         make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
   }
-  if (threadIdx.x == 0) args.counters[cidx] = 0;
 }
 
 // kv_a row [c(512) | k_pe(64)] -> cache[slot] = [rmsnorm(c) * w | rope_interleaved(k_pe)].
@@ -444,7 +470,6 @@ void mla_attention(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   const int RB = static_cast<int>((max_q_len * H + kRows - 1) / kRows);
   TORCH_CHECK(S == 1 || (long long)B * RB * S * kRows * (kLat + 2) <= ws.numel(),
               "mla: split workspace too small");
-  TORCH_CHECK(S == 1 || (long long)B * RB <= counters.numel(), "mla: counters too small");
   c10::cuda::CUDAGuard guard(q_lat.device());
   MlaArgs a{};
   a.q_lat = reinterpret_cast<const __nv_bfloat16*>(q_lat.data_ptr());
@@ -465,7 +490,7 @@ void mla_attention(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   a.ws_o = ws.data_ptr<float>();
   a.ws_ml = a.ws_o + (long long)B * RB * S * kRows * kLat;
-  a.counters = counters.data_ptr<int>();
+  (void)counters;  // split partials are merged by mla_merge_kernel; no arrival counters
   a.status = status.data_ptr<int>();
   const uint64_t rows = (uint64_t)cache.size(0) * kPage;
   CUtensorMap tm = make_tmap_2d(cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kQK, kQK,
@@ -480,6 +505,9 @@ void mla_attention(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   dim3 grid(S, RB, B);
   launch_pdl(mla_attention_kernel, grid, dim3(kThreads), kSmemBytes,
              at::cuda::getCurrentCUDAStream(), "mla_attention launch", tm, a);
+  if (S > 1)
+    launch_pdl(mla_merge_kernel, dim3(kRows / 8, RB, B), dim3(256), 0,
+               at::cuda::getCurrentCUDAStream(), "mla_merge launch", a, RB);
 }
 
 void mla_kv_write(const at::Tensor& kv, const at::Tensor& norm_w, double eps,

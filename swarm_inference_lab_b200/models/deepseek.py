@@ -236,24 +236,23 @@ class MLAModel:
         return o
 
     # ------------------------------------------------------------ blocks
-    def attention(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor, fb: ForwardBatch,
-                  cache: torch.Tensor) -> None:
+    def attention(self, L: MLALayerWeights, xq: torch.Tensor, xs: torch.Tensor, h: torch.Tensor,
+                  fb: ForwardBatch, cache: torch.Tensor) -> None:
+        """``xq`` / ``xs``: the normalised input in e4m3 with 1x128 scales."""
         cfg = self.cfg
-        T, Hh = x.shape[0], self.heads
+        T, Hh = xq.shape[0], self.heads
         eps = cfg.rms_norm_eps
-        xq, xs = fp8.quantize(x)
         qkv_a = fp8.linear(xq, xs, *L.w_qkv_a)
         q_a = qkv_a[:, : self.qr]
         kv_a = qkv_a[:, self.qr:]
-        qn = norm.rmsnorm(q_a, L.q_a_norm, eps, out=torch.empty((T, self.qr), dtype=x.dtype,
-                                                                 device=x.device))
-        qnq, qns = fp8.quantize(qn)
+        _, qnq, qns = norm.rmsnorm_fp8(q_a, L.q_a_norm, eps,
+                                       out=torch.empty((T, self.qr), dtype=h.dtype, device=h.device))
         q = fp8.linear(qnq, qns, *L.w_q_b)
         mla.kv_write(kv_a, L.kv_a_norm, eps, fb.positions, fb.slots, self.cos_sin, cache)
         q_nope, q_pe = mla.q_prep(q, fb.positions, self.cos_sin, Hh)
         offs = self._offsets(T)
         q_lat = moe_ops.grouped_linear(q_nope.view(Hh * T, -1), L.w_uk, offs, Hh, rows_hint=T)
-        o_lat = torch.empty((Hh, T, mla.LAT), dtype=x.dtype, device=x.device)
+        o_lat = torch.empty((Hh, T, mla.LAT), dtype=h.dtype, device=h.device)
         mla.attention(q_lat.view(Hh, T, mla.LAT).transpose(0, 1), q_pe, cache, fb.block_table,
                       fb.seq_lens, cu_q=None if fb.is_decode else fb.cu_q,
                       max_q_len=1 if fb.is_decode else fb.max_q_len, scale=self.scale,
@@ -264,20 +263,18 @@ class MLAModel:
         aq, as_ = fp8.quantize(a)
         fp8.linear(aq, as_, *L.w_o, epi=fp8.EPI_RESADD, residual=h, out=h)
 
-    def dense_mlp(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor) -> None:
-        xq, xs = fp8.quantize(x)
+    def dense_mlp(self, L: MLALayerWeights, xq: torch.Tensor, xs: torch.Tensor, h: torch.Tensor) -> None:
         act = fp8.linear(xq, xs, *L.w_gate_up, epi=fp8.EPI_SWIGLU)
         aq, as_ = fp8.quantize(act)
         fp8.linear(aq, as_, *L.w_down, epi=fp8.EPI_RESADD, residual=h, out=h)
 
-    def _shared(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor) -> None:
+    def _shared(self, L: MLALayerWeights, xq: torch.Tensor, xs: torch.Tensor, h: torch.Tensor) -> None:
         if L.shared_gate_up is not None:
-            xq, xs = fp8.quantize(x)
             sa = fp8.linear(xq, xs, *L.shared_gate_up, epi=fp8.EPI_SWIGLU)
             sq, ss = fp8.quantize(sa)
             fp8.linear(sq, ss, *L.shared_down, epi=fp8.EPI_RESADD, residual=h, out=h)
 
-    def _moe_fused(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor, epc) -> None:
+    def _moe_fused(self, L: MLALayerWeights, x: torch.Tensor, xq, xs, h: torch.Tensor, epc) -> None:
         """Decode MoE over peer memory: local routing, e4m3 dispatch to the expert owners,
         grouped GEMMs, combine fused into the down projection (``parallel/fused_ep.py``)."""
         cfg = self.cfg
@@ -297,17 +294,18 @@ class MLAModel:
                                  rows_hint=hint)
         aq, as_ = fp8.quantize(act)
         epc.down_scatter(aq, as_, *L.experts_down, offsets, el, hint, inv, T, e0)
-        self._shared(L, x, h)
+        self._shared(L, xq, xs, h)
         epc.combine(h, e0, el)
 
-    def moe(self, L: MLALayerWeights, x: torch.Tensor, h: torch.Tensor) -> None:
+    def moe(self, L: MLALayerWeights, x: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor,
+            h: torch.Tensor) -> None:
         cfg = self.cfg
         k = cfg.num_experts_per_tok
         e0, el = self.w.expert_start, self.w.experts_local
         ep = self.ep.size
         epc = getattr(self.comm, "ep_fused", None) if ep > 1 else None
         if epc is not None and epc.fits(x.shape[0]):
-            return self._moe_fused(L, x, h, epc)
+            return self._moe_fused(L, x, xq, xs, h, epc)
         xa = self.comm.all_gather(x).view(-1, x.shape[1]) if ep > 1 else x
         Ta = xa.shape[0]
         logits = gemm.linear(xa, L.router, fp32_out=True)
@@ -325,7 +323,7 @@ class MLAModel:
         aq, as_ = fp8.quantize(act)
         y = fp8.grouped_linear(aq, as_, *L.experts_down, offsets, el, rows_hint=hint)
         limit = offsets[el:el + 1]
-        self._shared(L, x, h)
+        self._shared(L, xq, xs, h)
         if ep == 1:
             moe_ops.combine(y, rows, wts, k, residual=h, out=h, row_limit=limit)
             return
@@ -340,13 +338,14 @@ class MLAModel:
         x = torch.empty_like(h)
         for li, L in enumerate(self.w.layers):
             cache, _ = kv.layer(li)
-            norm.rmsnorm(h, L.attn_norm, cfg.rms_norm_eps, out=x)
-            self.attention(L, x, h, fb, cache)
-            norm.rmsnorm(h, L.mlp_norm, cfg.rms_norm_eps, out=x)
+            # RMSNorm emits the e4m3 / 1x128 activation the fp8 GEMMs read in the same pass.
+            _, xq, xs = norm.rmsnorm_fp8(h, L.attn_norm, cfg.rms_norm_eps, out=x)
+            self.attention(L, xq, xs, h, fb, cache)
+            _, xq, xs = norm.rmsnorm_fp8(h, L.mlp_norm, cfg.rms_norm_eps, out=x)
             if L.dense:
-                self.dense_mlp(L, x, h)
+                self.dense_mlp(L, xq, xs, h)
             else:
-                self.moe(L, x, h)
+                self.moe(L, x, xq, xs, h)
         return h
 
     def logits(self, h: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:

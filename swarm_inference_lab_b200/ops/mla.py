@@ -31,12 +31,13 @@ def softmax_scale(qk_head_dim: int, rope_scaling: dict | None = None) -> float:
 
 
 def decode_splits(batch: int, max_ctx: int, heads: int = 64, sm_count: int = 148) -> int:
-    """Split-KV factor: one wave of CTAs (one CTA per SM), >= 4 key tiles per split."""
+    """Split-KV factor: one wave of CTAs (one CTA per SM), >= 2 key tiles per split; the
+    partials are merged by a separate, fully parallel kernel."""
     rb = max(1, (heads + 63) // 64)
     base = batch * rb
     want = max(1, sm_count // base)
     tiles = max(1, (max_ctx + 31) // 32)
-    return int(max(1, min(want, tiles // 4 if tiles >= 8 else 1, 32)))
+    return int(max(1, min(want, tiles // 2, 64)))
 
 
 def kv_write(kv_a: torch.Tensor, norm_w: torch.Tensor, eps: float, positions: torch.Tensor,

@@ -15,8 +15,24 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, *, out: torch.Ten
         out = torch.empty_like(x)
     if residual is not None and residual_out is None:
         residual_out = residual
-    ext().rmsnorm(x, residual, residual_out, weight, out, float(eps))
+    ext().rmsnorm(x, residual, residual_out, weight, out, float(eps), None, None)
     return out
+
+
+def rmsnorm_fp8(x: torch.Tensor, weight: torch.Tensor, eps: float, *, out: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None):
+    """``rmsnorm`` that also emits the normalised rows quantised to e4m3 with one fp32
+    scale per 1x128 block (the input format of the block-scaled fp8 GEMMs) in the same
+    pass.  Returns (bf16 out, e4m3 codes uint8 [T, H], scales [T, H/128])."""
+    T, H = x.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=x.dtype, device=x.device)
+    if residual is not None and residual_out is None:
+        residual_out = residual
+    q = torch.empty((T, H), dtype=torch.uint8, device=x.device)
+    s = torch.empty((T, H // 128), dtype=torch.float32, device=x.device)
+    ext().rmsnorm(x, residual, residual_out, weight, out, float(eps), q, s)
+    return out, q, s
 
 
 def rmsnorm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:

@@ -74,3 +74,15 @@ def test_fp8_grouped(hint):
         gu = xd[a:b] @ wd[g * 2 * N:(g + 1) * 2 * N].T
         ref = torch.nn.functional.silu(gu[:, :N]) * gu[:, N:]
         assert (out[a:b].float() - ref).abs().max().item() < 2e-2 * ref.abs().max().item() + 1e-2, g
+
+
+@pytest.mark.parametrize("T,H", [(1, 7168), (37, 1536), (5, 2048), (3, 640)])
+def test_rmsnorm_fp8_matches_rmsnorm_then_quantize(T, H):
+    from swarm_inference_lab_b200.ops import fp8, norm
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = (torch.rand(H, device="cuda") + 0.5).bfloat16()
+    y, q, s = norm.rmsnorm_fp8(x, w, 1e-6)
+    y_ref = norm.rmsnorm(x, w, 1e-6)
+    q_ref, s_ref = fp8.quantize(y_ref)
+    assert torch.equal(y, y_ref)
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
