@@ -226,9 +226,52 @@ class DenseModel:
         act = gemm.linear(x, L.w_gate_up, swiglu=True)
         return self._row_parallel(act, L.w_down, h)
 
+    sequence_parallel = False  # prefill: shard the residual stream over tokens between TP blocks
+
+    def _forward_hidden_sp(self, fb: ForwardBatch, kv) -> torch.Tensor:
+        """Sequence-parallel prefill: between tensor-parallel blocks the residual stream is
+        sharded over tokens (rank r holds rows [r*T/tp, (r+1)*T/tp)), so RMSNorm runs on a
+        1/tp slice; each block all-gathers its normalised input and reduce-scatters its
+        row-parallel output (the same bytes as one all-reduce).  Reference semantics:
+        si/microsharding/sequence_parallel.py:20-81 (prefill only)."""
+        cfg = self.cfg
+        tp, r = self.tp.size, self.tp.rank
+        eps = cfg.rms_norm_eps
+        nq, nkv, D = self.num_q_local, self.num_kv_local, cfg.head_dim
+        full = sampling.embedding(fb.ids, self.w.embed)
+        T, H = full.shape
+        Ts = T // tp
+        h = full[r * Ts:(r + 1) * Ts].contiguous()
+        xl = torch.empty_like(h)
+        pending = None
+        for li, L in enumerate(self.w.layers):
+            if pending is None:
+                norm.rmsnorm(h, L.attn_norm, eps, out=xl)
+            else:
+                norm.rmsnorm(pending, L.attn_norm, eps, out=xl, residual=h)
+            x = self.comm.all_gather(xl).view(T, H)
+            qkv = gemm.linear(x, L.wqkv)
+            k_cache, v_cache = kv.layer(li)
+            rope.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, k_cache, v_cache, nq, nkv,
+                               L.q_norm, L.k_norm, eps)
+            q = qkv.as_strided((T, nq, D), (qkv.stride(0), D, 1))
+            a = attn_ops.paged_prefill(q, k_cache, v_cache, fb.block_table, fb.seq_lens, fb.cu_q,
+                                       fb.max_q_len, scale=self.scale)
+            pending = self.comm.reduce_scatter(gemm.linear(a, L.wo))
+            norm.rmsnorm(pending, L.mlp_norm, eps, out=xl, residual=h)
+            x = self.comm.all_gather(xl).view(T, H)
+            act = gemm.linear(x, L.w_gate_up, swiglu=True)
+            pending = self.comm.reduce_scatter(gemm.linear(act, L.w_down))
+        h.add_(pending)
+        return self.comm.all_gather(h).view(T, H)
+
     def forward_hidden(self, fb: ForwardBatch, kv, h: torch.Tensor | None = None) -> torch.Tensor:
         """Run the local layers; returns the residual stream ``h`` [T, H] (bf16)."""
         cfg = self.cfg
+        if (h is None and self.sequence_parallel and not fb.is_decode and self.tp.size > 1
+                and fb.ids.shape[0] % self.tp.size == 0 and type(self).mlp is DenseModel.mlp
+                and self.w.layers):
+            return self._forward_hidden_sp(fb, kv)
         if h is None:
             h = sampling.embedding(fb.ids, self.w.embed)
         T = h.shape[0]

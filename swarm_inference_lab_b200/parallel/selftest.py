@@ -5,7 +5,8 @@
 Builds the same random model at TP=1 (every rank, full weights) and at
 TP=world (sharded) and compares greedy decode logits of the fused
 GEMM+all-reduce path and of the NCCL baseline path against TP=1, for a
-prefill (NCCL fallback) followed by decode steps (fused kernel).  Rank 0
+prefill (NCCL fallback) followed by decode steps (fused kernel), and of the
+sequence-parallel prefill (reduce-scatter / all-gather around the norms).  Rank 0
 prints one JSON line.  Process-group timeout is short so a stuck peer ends
 the run with an error instead of waiting forever.
 """
@@ -42,9 +43,10 @@ def main():
     results = {}
     ids = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(0))
 
-    def run(tp, comm):
+    def run(tp, comm, sp=False):
         w = DenseWeights.random(cfg, tp, dev, seed=7)
         model = DenseModel(w, dev, comm=comm, max_positions=1024)
+        model.sequence_parallel = sp
         pages = (P + 8 + 63) // 64
         kv = PagedKVCache(cfg.num_layers, model.num_kv_local, B * pages, dev)
         bt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
@@ -75,8 +77,9 @@ def main():
         return logits, tok
 
     full, tok_full = run(TPInfo(), LocalComm())
-    for name, comm in (("nccl", nccl), ("fused", fused)):
-        shard, tok = run(TPInfo(rank, world), comm)
+    for name, comm, sp in (("nccl", nccl, False), ("fused", fused, False),
+                           ("nccl_sequence_parallel_prefill", nccl, True)):
+        shard, tok = run(TPInfo(rank, world), comm, sp)
         errs = []
         for a, b in zip(full, shard):
             v0, _ = TPInfo(rank, world).split(cfg.vocab_size)
