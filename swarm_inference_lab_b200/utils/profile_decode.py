@@ -100,6 +100,39 @@ def op_decode_attn(a):
             "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"]}
 
 
+def op_gemm_ar1(a):
+    """The fused row-parallel GEMM + all-reduce kernel with a one-rank group (its own buffer
+    as the only peer): the kernel's own cost without NVLink, next to the plain GEMM with the
+    residual epilogue.  One GPU, so it can be profiled."""
+    from ..ops import gemm
+    from ..ops._ext import ext
+    from ..ops.workspace import get_workspace
+    T, N, K = a.n, a.m, a.k
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    h = torch.randn(T, N, device="cuda").bfloat16()
+    max_tiles, max_tokens = (N + 127) // 128, 128
+    flags_off = 256
+    slots_off = ((flags_off + 2 * 8 * max_tiles * 4 + 255) // 256) * 256
+    nbytes = slots_off + 2 * 8 * max_tokens * N * 2
+    e = ext()
+    buf = e.symm_alloc(nbytes, torch.cuda.current_device())
+    ws = get_workspace()
+    try:
+        fused = time_fn(lambda: e.gemm_allreduce(x, w, h, [buf], 0, max_tiles, max_tokens, N, flags_off,
+                                                 slots_off, ws.ws, ws.counters, ws.status),
+                        a.iters, graph=not a.eager)
+        plain = time_fn(lambda: gemm.linear(x, w, out=h, residual=h), a.iters, graph=not a.eager)
+        ws.check()
+    finally:
+        torch.cuda.synchronize()
+        e.symm_free(buf)
+    bytes_ = N * K * 2
+    pk = _peaks()
+    return {"op": "gemm_allreduce_1rank", "tokens": T, "out": N, "k": K, "fused_ms": fused,
+            "plain_residual_ms": plain, "weight_frac_hbm_fused": bytes_ / fused / 1e6 / pk["hbm_gbs"]}
+
+
 def op_mla_decode(a):
     """Absorbed MLA decode over a [pages, 64, 576] latent cache, 64 heads."""
     from ..ops import mla
@@ -175,7 +208,8 @@ def decode_steps(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "mla_decode", "fp8_grouped"],
+    ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "mla_decode", "fp8_grouped",
+                                     "gemm_ar1"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
     ap.add_argument("--model", default="llama-3-8b-shape")
@@ -191,7 +225,8 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
     a = ap.parse_args()
     out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn,
-           "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped}[a.op](a)
+           "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped,
+           "gemm_ar1": op_gemm_ar1}[a.op](a)
     print(json.dumps(out))
 
 
