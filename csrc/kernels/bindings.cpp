@@ -89,6 +89,10 @@ void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const 
                               const at::Tensor& counters, const at::Tensor& status);
 void set_pdl(bool on);
 bool get_pdl();
+void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
+                       int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                       const at::Tensor& status);
+at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);
 }  // namespace sil
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -130,5 +134,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "grouped fp8 GEMM with the weighted EP combine scattered to the token owners");
   m.def("set_pdl", &sil::set_pdl, "enable / disable programmatic dependent launch for later launches");
   m.def("get_pdl", &sil::get_pdl, "whether programmatic dependent launch is enabled");
+  m.def("oneshot_allreduce", &sil::oneshot_allreduce,
+        "one-shot all-reduce of symmetric-buffer partials into h (NVLink pull, per-CTA barriers)");
+  m.def("symm_tensor", &sil::symm_tensor, "bf16 tensor view over a symmetric buffer (no ownership)");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

@@ -1,0 +1,111 @@
+"""Tensor-parallel row-parallel projections with a one-shot NVLink all-reduce.
+
+``OneShotTPComm`` gives every rank a symmetric buffer (CUDA IPC, mapped by every
+peer).  A row-parallel projection ``h += allreduce(x @ w.T)`` then runs as two
+kernels: the tcgen05 GEMM writes its partial straight into this rank's buffer, and
+``oneshot_allreduce`` (``csrc/kernels/allreduce.cu``) has every CTA pull its slice of
+the partial from every rank with 16-byte NVLink loads, sum in rank order (fp32; all
+ranks obtain identical sums) and add into the residual stream.  Two per-CTA
+cross-rank barriers bracket the pull, so no rank overwrites a partial a peer is
+still reading.  Prefill-sized calls (more tokens than the buffer holds) use GEMM +
+NCCL.  ``all_reduce`` / ``all_gather`` / ``reduce_scatter`` forward to NCCL.
+
+The model calls ``fused_gemm_allreduce_residual`` (the same hook as the fused
+GEMM+all-reduce communicator), so either communicator can be plugged in.
+
+Reference semantics: deterministic rank-ordered all-reduce of row-parallel
+projections, si/microsharding/dense.py:600-708.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import gemm
+from ..ops._ext import ext
+from ..ops.workspace import get_workspace
+
+MAX_RANKS = 8
+MAX_CTAS = 256
+
+
+class OneShotTPComm:
+    def __init__(self, base, device: torch.device, *, max_tokens: int = 128, hidden: int = 4096):
+        self.base = base
+        self.rank = base.rank
+        self.size = base.size
+        if self.size > MAX_RANKS:
+            raise ValueError(f"one-shot all-reduce supports up to {MAX_RANKS} ranks")
+        self.device = torch.device(device)
+        self.max_tokens = max_tokens
+        self.hidden = hidden
+        self.start_off = 256
+        self.end_off = self.start_off + MAX_RANKS * MAX_CTAS * 4
+        self.partial_off = ((self.end_off + MAX_RANKS * MAX_CTAS * 4 + 255) // 256) * 256
+        self.max_elems = max_tokens * hidden
+        nbytes = self.partial_off + self.max_elems * 2
+        e = ext()
+        dev = self.device.index
+        self.local = e.symm_alloc(nbytes, dev)
+        handles = [None] * self.size
+        dist.all_gather_object(handles, (self.rank, e.ipc_handle(self.local)), group=base.group)
+        self.peers = [0] * self.size
+        self._opened = []
+        for r, h in handles:
+            if r == self.rank:
+                self.peers[r] = self.local
+            else:
+                p = e.ipc_open(h, dev)
+                self.peers[r] = p
+                self._opened.append(p)
+        self._views: dict[tuple[int, int], torch.Tensor] = {}
+        torch.cuda.synchronize(self.device)
+        base.barrier()
+
+    # NCCL collectives (prefill path and plumbing)
+    def all_reduce(self, x):
+        return self.base.all_reduce(x)
+
+    def all_gather(self, x):
+        return self.base.all_gather(x)
+
+    def reduce_scatter(self, x):
+        return self.base.reduce_scatter(x)
+
+    def barrier(self):
+        self.base.barrier()
+
+    def _partial(self, T: int, H: int) -> torch.Tensor:
+        v = self._views.get((T, H))
+        if v is None:
+            v = ext().symm_tensor(self.local, self.partial_off, T, H, self.device.index)
+            self._views[(T, H)] = v
+        return v
+
+    def fused_gemm_allreduce_residual(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor):
+        """h += allreduce(x @ w.T) over the group; returns None (residual already added)."""
+        T, H = x.shape[0], w.shape[0]
+        if T * H > self.max_elems or T > self.max_tokens or not h.is_contiguous():
+            out = gemm.linear(x, w)
+            self.base.all_reduce(out)
+            h.add_(out)
+            return None
+        part = self._partial(T, H)
+        gemm.linear(x, w, out=part)
+        ext().oneshot_allreduce(h, self.peers, self.rank, self.start_off, self.end_off,
+                                self.partial_off, self.max_elems, get_workspace(x.device).status)
+        return None
+
+    fused_gemm_allreduce = None
+
+    def close(self):
+        e = ext()
+        torch.cuda.synchronize(self.device)
+        self._views.clear()
+        for p in self._opened:
+            e.ipc_close(p)
+        self._opened = []
+        if self.local:
+            self.base.barrier()
+            e.symm_free(self.local)
+            self.local = 0

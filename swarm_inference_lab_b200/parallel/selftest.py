@@ -4,7 +4,8 @@
 
 Builds the same random model at TP=1 (every rank, full weights) and at
 TP=world (sharded) and compares greedy decode logits of the fused
-GEMM+all-reduce path and of the NCCL baseline path against TP=1, for a
+GEMM+all-reduce path, of GEMM + one-shot NVLink all-reduce, and of the NCCL
+baseline path against TP=1, for a
 prefill (NCCL fallback) followed by decode steps (fused kernel), and of the
 sequence-parallel prefill (reduce-scatter / all-gather around the norms).  Rank 0
 prints one JSON line.  Process-group timeout is short so a stuck peer ends
@@ -33,6 +34,7 @@ def main():
     from ..ops.workspace import get_workspace
     from .comm import LocalComm, NcclComm
     from .fused_tp import FusedTPComm
+    from .oneshot_tp import OneShotTPComm
 
     cfg = preset(os.environ.get("SIL_SELFTEST_MODEL", "tiny-llama-gpu")).replace(num_layers=2)
     if cfg.num_kv_heads < world:
@@ -77,7 +79,8 @@ def main():
         return logits, tok
 
     full, tok_full = run(TPInfo(), LocalComm())
-    for name, comm, sp in (("nccl", nccl, False), ("fused", fused, False),
+    oneshot = OneShotTPComm(nccl, dev, max_tokens=128, hidden=cfg.hidden_size)
+    for name, comm, sp in (("nccl", nccl, False), ("fused", fused, False), ("oneshot", oneshot, False),
                            ("nccl_sequence_parallel_prefill", nccl, True)):
         shard, tok = run(TPInfo(rank, world), comm, sp)
         errs = []
@@ -93,6 +96,7 @@ def main():
     if rank == 0:
         print(json.dumps({"world": world, "ok": bool(out.item() == 1.0), **results}), flush=True)
     fused.close()
+    oneshot.close()
     dist.destroy_process_group()
 
 

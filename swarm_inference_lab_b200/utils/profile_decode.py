@@ -71,11 +71,13 @@ def op_gemm(a):
     x = torch.randn(T, K, device="cuda").bfloat16()
     rows = 2 * N if a.swiglu else N
     w = (torch.randn(rows, K, device="cuda") * 0.02).bfloat16()
-    ms = time_fn(lambda: gemm.linear(x, w, swiglu=a.swiglu), a.iters, graph=not a.eager)
+    ms = time_fn(lambda: gemm.linear(x, w, swiglu=a.swiglu, force_splits=a.splits), a.iters,
+                 graph=not a.eager)
     bytes_ = rows * K * 2 + T * K * 2 + T * N * 2
     flops = 2 * T * rows * K
     pk = _peaks()
-    return {"op": "gemm", "tokens": T, "out_features": N, "k": K, "swiglu": a.swiglu, "ms": ms,
+    return {"op": "gemm", "tokens": T, "out_features": N, "k": K, "swiglu": a.swiglu,
+            "splits": a.splits or "auto", "ms": ms,
             "GBps": bytes_ / ms / 1e6, "TFLOPs": flops / ms / 1e9,
             "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"],
             "frac_bf16_of_measured": flops / ms / 1e9 / pk["bf16_tflops"]}
@@ -98,6 +100,20 @@ def op_decode_attn(a):
     pk = _peaks()
     return {"op": "paged_decode", "batch": B, "ctx": ctx, "splits": splits, "ms": ms,
             "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"]}
+
+
+def op_launch_floor(a):
+    """Device time per launch of the smallest kernels in a captured graph (the per-kernel
+    floor a decode step pays): a 1x128 RMSNorm and a 128x128x64 GEMM."""
+    from ..ops import gemm, norm
+    x = torch.randn(1, 128, device="cuda").bfloat16()
+    wn = torch.ones(128, device="cuda").bfloat16()
+    y = torch.empty_like(x)
+    w = torch.randn(128, 64, device="cuda").bfloat16()
+    xg = torch.randn(1, 64, device="cuda").bfloat16()
+    return {"op": "launch_floor",
+            "rmsnorm_us": 1e3 * time_fn(lambda: norm.rmsnorm(x, wn, 1e-6, out=y), a.iters),
+            "gemm_tiny_us": 1e3 * time_fn(lambda: gemm.linear(xg, w), a.iters)}
 
 
 def op_gemm_ar1(a):
@@ -209,7 +225,7 @@ def decode_steps(a):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "mla_decode", "fp8_grouped",
-                                     "gemm_ar1"],
+                                     "gemm_ar1", "launch_floor"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
     ap.add_argument("--model", default="llama-3-8b-shape")
@@ -222,11 +238,12 @@ def main():
     ap.add_argument("--n", type=int, default=32)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--swiglu", action="store_true")
+    ap.add_argument("--splits", type=int, default=0, help="force K splits (0 = heuristic)")
     ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
     a = ap.parse_args()
     out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn,
            "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped,
-           "gemm_ar1": op_gemm_ar1}[a.op](a)
+           "gemm_ar1": op_gemm_ar1, "launch_floor": op_launch_floor}[a.op](a)
     print(json.dumps(out))
 
 
