@@ -11,12 +11,33 @@ using namespace gemm_detail;
 // box at most kHbmGBs; choose the number of CTAs per tile minimising
 // bytes / bandwidth + fix-up.
 inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms) {
-  // Default ("fill"): one CTA per SM whenever the problem has >= 4 K blocks per CTA;
-  // measured faster on the full decode step than the latency model below, which is
-  // kept behind SIL_STREAMK=latency.
+  // Default: tile-aligned splits from a calibrated cost model when there are few tiles,
+  // otherwise ("fill") one CTA per SM whenever the problem has >= 4 K blocks per CTA.  The
+  // older latency model below is kept behind SIL_STREAMK=latency.
   static const char* mode = std::getenv("SIL_STREAMK");
   if (mode == nullptr || mode[0] != 'l') {
     const long long units = tiles * num_kb;
+    if (tiles * 2 <= sms) {
+      // Few tiles (decode projections under TP, o_proj, QKV): split every tile into the same
+      // number s of K ranges so no CTA straddles two tiles.  Calibrated on B200 (32 tokens,
+      // 4096 x {512, 4096} weights, s = 1, 2, 4): ~2.2 us fixed cost, ~48 GB/s streamed per
+      // CTA, a split fix-up of ~2.5 us + 0.5 us per split; the box streams at most ~6000 GB/s.
+      constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kFixupUs = 2.5, kFixupPerSplitUs = 0.5,
+                       kBoxGBs = 6000.0;
+      const double tile_bytes = (double)bytes_per_kb * num_kb;
+      long long best_s = 1;
+      double best_t = 1e30;
+      for (long long s = 1; s <= num_kb && tiles * s <= sms; ++s) {
+        const double t = kFixedUs + std::max(tile_bytes / s / (kPerCtaGBs * 1e3),
+                                             tile_bytes * tiles / (kBoxGBs * 1e3)) +
+                         (s > 1 ? kFixupUs + kFixupPerSplitUs * s : 0.0);
+        if (t < best_t - 1e-9) {
+          best_t = t;
+          best_s = s;
+        }
+      }
+      return tiles * best_s;
+    }
     return std::max<long long>(1, std::min<long long>(std::min<long long>(sms, units), (units + 3) / 4));
   }
   constexpr double kPerSmGBs = 110.0, kHbmGBs = 6000.0, kFixupUs = 3.0, kLatencyUs = 2.0;
