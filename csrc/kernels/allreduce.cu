@@ -9,8 +9,8 @@
 //                        there directly, so no copy precedes the reduction)
 //
 // CTA c of every rank handles the same slice of the T*H elements:
-//   1. raise start[rank][c] on every rank (after a system fence, so the partial the
-//      previous kernel wrote is visible), wait until every rank raised start[*][c];
+//   1. raise start[rank][c] on every rank (the partial was written by the previous kernel,
+//      complete before this one starts), wait until every rank raised start[*][c];
 //   2. pull the slice from every rank's partial with 16-byte loads, sum in rank order in
 //      fp32 (the same order on every rank, so all ranks get bit-identical sums), add the
 //      residual and store into h;
@@ -88,7 +88,6 @@ __global__ void __launch_bounds__(kThreadsAR)
   pdl_trigger();
   pdl_wait();  // the partial comes from the previous kernel (the row-parallel GEMM)
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
-  __threadfence_system();
   bool ok = cross_rank_barrier(a, a.start_off, epoch);
   const long long units = a.n / 8;  // 16-byte units of bf16
   const long long per = (units + gridDim.x - 1) / gridDim.x;
@@ -131,7 +130,123 @@ __global__ void __launch_bounds__(kThreadsAR)
   }
 }
 
+// Row-sliced variant fused with the next RMSNorm: CTA t owns token row t, so after the
+// rank-ordered sum it holds the whole row and can also write x = rmsnorm(h) * w.
+__global__ void __launch_bounds__(kThreadsAR)
+    oneshot_allreduce_norm_kernel(const OneShotArgs a, int H, const __nv_bfloat16* __restrict__ nw,
+                                  float eps, __nv_bfloat16* __restrict__ x_out) {
+  extern __shared__ float row[];  // H fp32 values of h after the sum
+  __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
+  bool ok = cross_rank_barrier(a, a.start_off, epoch);
+  const int t = blockIdx.x;
+  const long long base = (long long)t * H / 8;  // first 16-byte unit of this row
+  float ss = 0.f;
+  if (ok) {
+    for (int u = threadIdx.x; u < H / 8; u += blockDim.x) {
+      const uint4 r = reinterpret_cast<const uint4*>(a.h)[base + u];
+      float v[8] = {bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y),
+                    bf16_lo(r.z), bf16_hi(r.z), bf16_lo(r.w), bf16_hi(r.w)};
+      uint4 pv[kMaxRanks];
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.world) pv[p] = __ldcv(reinterpret_cast<const uint4*>(a.peers[p] + a.partial_off) + base + u);
+      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.world) {
+          s[0] += bf16_lo(pv[p].x); s[1] += bf16_hi(pv[p].x); s[2] += bf16_lo(pv[p].y); s[3] += bf16_hi(pv[p].y);
+          s[4] += bf16_lo(pv[p].z); s[5] += bf16_hi(pv[p].z); s[6] += bf16_lo(pv[p].w); s[7] += bf16_hi(pv[p].w);
+        }
+      uint4 o;
+      o.x = pack_bf16x2(v[0] + s[0], v[1] + s[1]);
+      o.y = pack_bf16x2(v[2] + s[2], v[3] + s[3]);
+      o.z = pack_bf16x2(v[4] + s[4], v[5] + s[5]);
+      o.w = pack_bf16x2(v[6] + s[6], v[7] + s[7]);
+      reinterpret_cast<uint4*>(a.h)[base + u] = o;
+      // The norm sees the bf16-rounded residual stream, as the unfused RMSNorm would.
+      const float hv[8] = {bf16_lo(o.x), bf16_hi(o.x), bf16_lo(o.y), bf16_hi(o.y),
+                           bf16_lo(o.z), bf16_hi(o.z), bf16_lo(o.w), bf16_hi(o.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        row[u * 8 + j] = hv[j];
+        ss += hv[j] * hv[j];
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / H + eps);
+  if (ok) {
+    for (int u = threadIdx.x; u < H / 8; u += blockDim.x) {
+      const uint4 wq = reinterpret_cast<const uint4*>(nw)[u];
+      const float wv[8] = {bf16_lo(wq.x), bf16_hi(wq.x), bf16_lo(wq.y), bf16_hi(wq.y),
+                           bf16_lo(wq.z), bf16_hi(wq.z), bf16_lo(wq.w), bf16_hi(wq.w)};
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = wv[j] * __bfloat162float(__float2bfloat16_rn(row[u * 8 + j] * rstd));
+      uint4 q;
+      q.x = pack_bf16x2(o[0], o[1]); q.y = pack_bf16x2(o[2], o[3]);
+      q.z = pack_bf16x2(o[4], o[5]); q.w = pack_bf16x2(o[6], o[7]);
+      reinterpret_cast<uint4*>(x_out)[base + u] = q;
+    }
+  }
+  __syncthreads();
+  ok = cross_rank_barrier(a, a.end_off, epoch) && ok;
+  if (threadIdx.x == 0) {
+    uint32_t* st = reinterpret_cast<uint32_t*>(a.peers[a.rank]);
+    if (atomicAdd(st + 1, 1u) == gridDim.x - 1) {
+      st[1] = 0u;
+      __threadfence();
+      *reinterpret_cast<volatile uint32_t*>(st) = epoch;
+    }
+  }
+}
+
 }  // namespace
+
+// h [T, H] += sum of the ranks' partials, then x_out = rmsnorm(h) * w (one CTA per token).
+void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
+                            int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                            const at::Tensor& norm_w, double eps, at::Tensor& x_out,
+                            const at::Tensor& status) {
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2,
+              "oneshot_allreduce_norm: h [T, H] bf16 contiguous");
+  TORCH_CHECK(x_out.is_contiguous() && x_out.sizes() == h.sizes() && x_out.scalar_type() == at::kBFloat16,
+              "oneshot_allreduce_norm: x_out like h");
+  const int world = static_cast<int>(peers.size());
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world, "oneshot_allreduce_norm: group");
+  const int T = h.size(0), H = h.size(1);
+  TORCH_CHECK(H % 8 == 0 && (long long)T * H <= max_elems && T <= kMaxCtas && norm_w.numel() == H &&
+                  norm_w.scalar_type() == at::kBFloat16,
+              "oneshot_allreduce_norm: shapes");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(h.device());
+  OneShotArgs a{};
+  for (int i = 0; i < world; ++i) a.peers[i] = peers[i];
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  a.start_off = start_off;
+  a.end_off = end_off;
+  a.partial_off = partial_off;
+  a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  a.n = (long long)T * H;
+  a.status = status.data_ptr<int>();
+  launch_pdl(oneshot_allreduce_norm_kernel, dim3(T), dim3(kThreadsAR), H * sizeof(float),
+             at::cuda::getCurrentCUDAStream(), "oneshot_allreduce_norm launch", a, H,
+             reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr()), static_cast<float>(eps),
+             reinterpret_cast<__nv_bfloat16*>(x_out.data_ptr()));
+}
 
 // h [T, H] bf16 contiguous += sum over ranks of each rank's partial (same shape) stored at
 // byte offset `partial_off` of its symmetric buffer.

@@ -92,6 +92,10 @@ bool get_pdl();
 void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
                        int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
                        const at::Tensor& status);
+void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
+                            int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                            const at::Tensor& norm_w, double eps, at::Tensor& x_out,
+                            const at::Tensor& status);
 at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);
 }  // namespace sil
 
@@ -136,6 +140,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("get_pdl", &sil::get_pdl, "whether programmatic dependent launch is enabled");
   m.def("oneshot_allreduce", &sil::oneshot_allreduce,
         "one-shot all-reduce of symmetric-buffer partials into h (NVLink pull, per-CTA barriers)");
+  m.def("oneshot_allreduce_norm", &sil::oneshot_allreduce_norm,
+        "one-shot all-reduce into h fused with the next RMSNorm (x_out = rmsnorm(h) * w)");
   m.def("symm_tensor", &sil::symm_tensor, "bf16 tensor view over a symmetric buffer (no ownership)");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

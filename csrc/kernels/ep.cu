@@ -67,12 +67,14 @@ __device__ __forceinline__ uint32_t read_epoch(const EpLayout& L) {
   return *reinterpret_cast<volatile uint32_t*>(state_of(L, L.rank)) + 1u;
 }
 
-// Grid-wide "last CTA" election on a counter in this rank's state words.  Every thread
-// must have fenced its stores before the call.
-__device__ __forceinline__ bool last_cta(const EpLayout& L, int which) {
+// Grid-wide "last CTA" election on a counter in this rank's state words.  With `fence_sys`
+// thread 0 issues a system-scope fence after the CTA barrier, before it counts in, which
+// orders the CTA's peer stores before whatever the last CTA publishes.
+__device__ __forceinline__ bool last_cta(const EpLayout& L, int which, bool fence_sys = false) {
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (fence_sys) __threadfence_system();
     uint32_t* ctr = state_of(L, L.rank) + which;
     const uint32_t old = atomicAdd(ctr, 1u);
     s_last = old == gridDim.x - 1;
@@ -136,8 +138,7 @@ __global__ void ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, long lon
       }
     }
   }
-  __threadfence_system();
-  if (last_cta(L, kEpCtrDispatch) && threadIdx.x == 0) {
+  if (last_cta(L, kEpCtrDispatch, /*fence_sys=*/true) && threadIdx.x == 0) {
     for (int p = 0; p < L.world; ++p)
       st_rel_sys(reinterpret_cast<uint32_t*>(L.peers[p] + L.dflag_off) + par * 8 + L.rank, epoch);
   }

@@ -117,13 +117,15 @@ __device__ __forceinline__ void ar_push(const GemmArgs& a, int par, int m, int n
   }
 }
 
-// Publish a finished tile to every rank: each thread fences its stores, the
-// epilogue warps meet, one thread raises the tile's flag on every rank.
+// Publish a finished tile to every rank: the epilogue warps meet, then one thread issues a
+// system-scope fence (cumulative over the warps' stores ordered before it by the barrier) and
+// raises the tile's flag on every rank.
 __device__ __forceinline__ void ar_publish(const GemmArgs& a, int par, uint32_t epoch, int tile) {
-  __threadfence_system();
   named_bar_sync(1, 128);
-  if (threadIdx.x == 64)
+  if (threadIdx.x == 64) {
+    __threadfence_system();
     for (int p = 0; p < a.tp_size; ++p) st_release_sys(ar_flag(a, p, par, a.tp_rank, tile), epoch);
+  }
 }
 
 template <int BN, int STAGES, int EPI, bool SWAP>

@@ -412,9 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (EPI == kScatter) {
     // The grid's last CTA tells every rank that this rank's expert outputs have landed.
     const EpLayout& L = args.ep;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+      __threadfence_system();  // cumulative over this CTA's scatter stores (ordered by the barrier)
       uint32_t* ctr = reinterpret_cast<uint32_t*>(L.peers[L.rank]) + kEpCtrGemm;
       if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
         *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;

@@ -279,8 +279,16 @@ class DenseModel:
         nq, nkv, D = self.num_q_local, self.num_kv_local, cfg.head_dim
         pending = None
         x = torch.empty_like(h)
-        for li, L in enumerate(self.w.layers):
-            if pending is None:
+        # With a communicator that fuses the all-reduce with the following RMSNorm, every
+        # row-parallel projection also produces the next block's normalised input.
+        ar_norm = (getattr(self.comm, "fused_gemm_allreduce_residual_norm", None)
+                   if self.tp.size > 1 and type(self).mlp is DenseModel.mlp else None)
+        x_ready = False
+        layers = self.w.layers
+        for li, L in enumerate(layers):
+            if x_ready:
+                x_ready = False
+            elif pending is None:
                 norm.rmsnorm(h, L.attn_norm, eps, out=x)
             else:
                 norm.rmsnorm(pending, L.attn_norm, eps, out=x, residual=h)
@@ -295,6 +303,16 @@ class DenseModel:
             else:
                 a = attn_ops.paged_prefill(q, k_cache, v_cache, fb.block_table, fb.seq_lens,
                                            fb.cu_q, fb.max_q_len, scale=self.scale)
+            if ar_norm is not None:
+                ar_norm(a, L.wo, h, L.mlp_norm, eps, x)
+                act = gemm.linear(x, L.w_gate_up, swiglu=True)
+                if li + 1 < len(layers):
+                    ar_norm(act, L.w_down, h, layers[li + 1].attn_norm, eps, x)
+                    x_ready = True
+                else:
+                    self.comm.fused_gemm_allreduce_residual(act, L.w_down, h)
+                pending = None
+                continue
             pending = self._row_parallel(a, L.wo, h)
             if pending is None:
                 norm.rmsnorm(h, L.mlp_norm, eps, out=x)

@@ -96,6 +96,22 @@ class OneShotTPComm:
                                 self.partial_off, self.max_elems, get_workspace(x.device).status)
         return None
 
+    def fused_gemm_allreduce_residual_norm(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor,
+                                           norm_w: torch.Tensor, eps: float, x_out: torch.Tensor):
+        """h += allreduce(x @ w.T); x_out = rmsnorm(h) * norm_w -- the next block's input,
+        produced by the all-reduce kernel itself (one CTA per token row)."""
+        T, H = x.shape[0], w.shape[0]
+        if T * H > self.max_elems or T > self.max_tokens or not h.is_contiguous() or H % 8:
+            self.fused_gemm_allreduce_residual(x, w, h)
+            from ..ops import norm
+            norm.rmsnorm(h, norm_w, eps, out=x_out)
+            return
+        part = self._partial(T, H)
+        gemm.linear(x, w, out=part)
+        ext().oneshot_allreduce_norm(h, self.peers, self.rank, self.start_off, self.end_off,
+                                     self.partial_off, self.max_elems, norm_w, float(eps), x_out,
+                                     get_workspace(x.device).status)
+
     fused_gemm_allreduce = None
 
     def close(self):
