@@ -451,3 +451,53 @@ def test_synthetic_stages_are_deterministic_and_calibrated():
     a = ring(0)
     assert _t.perf_counter() - t0 >= 0.006          # three decode steps x 2 ms on stage 1
     assert a == ring(0) and a != ring(1)
+
+
+def test_universal_worker_abi_and_queue():
+    import asyncio
+
+    from swarm_inference_lab_b200.runtime.abi import ExecutionQueue, GreedyVerifier, UniversalWorker
+
+    class Backend:
+        def __init__(self):
+            self.batched = 0
+
+        @staticmethod
+        def next_token(ctx):
+            return (sum(ctx) * 7 + len(ctx)) % 50
+
+        def generate(self, prompt, max_new_tokens):
+            out, ctx = [], list(prompt)
+            for _ in range(max_new_tokens):
+                t = self.next_token(ctx)
+                out.append(t)
+                ctx.append(t)
+            return {"tokens": out}
+
+        def generate_batch(self, jobs):
+            self.batched += len(jobs)
+            return [self.generate(**j) for j in jobs]
+
+        def verify(self, context, candidates):
+            return GreedyVerifier(self.next_token).verify(context, candidates)
+
+    be = Backend()
+    w = UniversalWorker(be)
+    gen = w.run({"kind": "generate", "prompt": [1, 2], "max_new_tokens": 4, "job_id": "a"})
+    assert gen["status"] == "OK" and len(gen["result"]["tokens"]) == 4
+    toks = gen["result"]["tokens"]
+    ok = w.run({"kind": "verify", "context": [1, 2], "candidates": toks[:3] + [toks[3] + 1]})
+    assert ok["result"] == {"accepted": 3, "next": toks[3]}
+    assert w.run({"kind": "draft", "context": [1], "k": 2})["status"] == "REJECTED"
+    assert w.run({"kind": "nope"})["status"] == "REJECTED"
+
+    async def main():
+        q = ExecutionQueue(w, max_pending=16, max_batch=8)
+        await q.start()
+        res = await asyncio.gather(*[q.submit({"kind": "generate", "prompt": [i], "max_new_tokens": 2,
+                                               "job_id": i}) for i in range(6)])
+        await q.close()
+        return res
+    res = asyncio.run(main())
+    assert all(r["status"] == "OK" for r in res) and [r["job_id"] for r in res] == list(range(6))
+    assert be.batched >= 2
