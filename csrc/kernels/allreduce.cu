@@ -2,23 +2,25 @@
 //
 // Every rank of the group owns a symmetric buffer (CUDA IPC, mapped by every peer):
 //
-//   [0, 256)             state: epoch, arrival counter (local use)
-//   start[8][kMaxCtas]   u32, written by peers: "my partial for this epoch is complete"
-//   end[8][kMaxCtas]     u32, written by peers: "I have finished reading your slice"
-//   partial[T][H]        bf16, this rank's row-parallel GEMM output (the GEMM writes it
-//                        there directly, so no copy precedes the reduction)
+//   [0, 256)                state: epoch, arrival counter (local use)
+//   flags[8][kMaxCtas]      u32, written by peers: "slice c of my partial has landed here"
+//   partial[T][H]           bf16, this rank's row-parallel GEMM output (the GEMM writes it
+//                           there directly)
+//   recv[2][8][T][H]        bf16, the peers' partials pushed here (alternating by epoch parity)
 //
-// CTA c of every rank handles the same slice of the T*H elements:
-//   1. raise start[rank][c] on every rank (the partial was written by the previous kernel,
-//      complete before this one starts), wait until every rank raised start[*][c];
-//   2. pull the slice from every rank's partial with 16-byte loads, sum in rank order in
-//      fp32 (the same order on every rank, so all ranks get bit-identical sums), add the
-//      residual and store into h;
-//   3. raise end[rank][c] everywhere and wait for end[*][c], so no rank overwrites its
-//      partial (next GEMM) while a peer still reads it.
-// Each CTA synchronises only with its counterparts on the other GPUs (no block of one
-// launch waits for another block of the same launch).  Flags carry the epoch; every wait
-// is bounded and reports through the sticky status word.  The last CTA advances the epoch.
+// CTA c of every rank owns the same slice of the T*H elements:
+//   1. push its slice of the local partial into recv[parity][rank] of every peer with
+//      16-byte stores, then (after a barrier, one system fence) raise flags[rank][c] on
+//      every peer;
+//   2. wait until every peer's flags[*][c] reached this epoch, sum the slice in rank order (the
+//      local partial for this rank's term; the same order on every rank, so all ranks get
+//      bit-identical sums), add the residual and store into h.
+// Data crosses NVLink once, as fire-and-forget stores.  A peer can only push epoch e+2 into
+// the parity this CTA reads at epoch e after it has seen this rank's flag for epoch e+1,
+// which this rank raises after finishing epoch e, so no second barrier is needed.  Each CTA
+// synchronises only with its counterparts on the other GPUs (no block of one launch waits
+// for another block of the same launch).  Every wait is bounded and reports through the
+// sticky status word.  The last CTA advances the epoch.
 //
 // Reference semantics: the rank-ordered deterministic all-reduce of row-parallel
 // projections, si/microsharding/dense.py:600-708.
@@ -41,7 +43,8 @@ constexpr int kThreadsAR = 256;
 struct OneShotArgs {
   long long peers[kMaxRanks];
   int rank, world;
-  long long start_off, end_off, partial_off;
+  long long flags_off, partial_off, recv_off;
+  long long max_elems;
   __nv_bfloat16* h;      // [T, H] contiguous: h += sum of partials
   long long n;           // T * H
   int* status;
@@ -57,19 +60,42 @@ __device__ __forceinline__ void st_rel(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Threads 0..world-1: raise flag[rank][c] on peer `tid`, then wait for flag[tid][c] here.
-__device__ __forceinline__ bool cross_rank_barrier(const OneShotArgs& a, long long off, uint32_t epoch) {
+__device__ __forceinline__ __nv_bfloat16* recv_slot(const OneShotArgs& a, int owner, int par, int src) {
+  return reinterpret_cast<__nv_bfloat16*>(a.peers[owner] + a.recv_off) +
+         ((long long)par * kMaxRanks + src) * a.max_elems;
+}
+
+// Push units [u0, u1) of the local partial to every peer, then raise flags[rank][c] there.
+__device__ __forceinline__ void push_slice(const OneShotArgs& a, int par, uint32_t epoch,
+                                           long long u0, long long u1) {
+  const uint4* src = reinterpret_cast<const uint4*>(a.peers[a.rank] + a.partial_off);
+  for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+    const uint4 v = src[u];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < a.world && p != a.rank) reinterpret_cast<uint4*>(recv_slot(a, p, par, a.rank))[u] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();  // cumulative over the CTA's pushes
+  __syncthreads();
+  const int p = threadIdx.x;
+  if (p < a.world && p != a.rank)
+    st_rel(reinterpret_cast<uint32_t*>(a.peers[p] + a.flags_off) + a.rank * kMaxCtas + blockIdx.x, epoch);
+}
+
+// Threads 0..world-1 wait for flags[p][c] >= epoch (p != rank).
+__device__ __forceinline__ bool wait_slice(const OneShotArgs& a, uint32_t epoch) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
   const int p = threadIdx.x;
-  if (p < a.world) {
-    uint32_t* remote = reinterpret_cast<uint32_t*>(a.peers[p] + off) + a.rank * kMaxCtas + blockIdx.x;
-    st_rel(remote, epoch);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.peers[a.rank] + off) + p * kMaxCtas + blockIdx.x;
+  if (p < a.world && p != a.rank) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers[a.rank] + a.flags_off) + p * kMaxCtas + blockIdx.x;
     const uint64_t t0 = globaltimer_ns();
     uint32_t it = 0;
-    while (ld_acq(mine) != epoch) {
+    // >= rather than ==: a fast peer may already have raised the next epoch's flag (it only
+    // needs this rank's flag for the current epoch to go on), and epochs only grow.
+    while (static_cast<int>(ld_acq(f) - epoch) < 0) {
       if ((++it & 255u) == 0) {
         if (load_status(a.status) != 0 || globaltimer_ns() - t0 > SIL_WAIT_TIMEOUT_NS) {
           raise_status(a.status, kStatusTimeoutPeer);
@@ -83,43 +109,25 @@ __device__ __forceinline__ bool cross_rank_barrier(const OneShotArgs& a, long lo
   return ok != 0;
 }
 
-__global__ void __launch_bounds__(kThreadsAR)
-    oneshot_allreduce_kernel(const OneShotArgs a) {
-  pdl_trigger();
-  pdl_wait();  // the partial comes from the previous kernel (the row-parallel GEMM)
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
-  bool ok = cross_rank_barrier(a, a.start_off, epoch);
-  const long long units = a.n / 8;  // 16-byte units of bf16
-  const long long per = (units + gridDim.x - 1) / gridDim.x;
-  const long long u0 = blockIdx.x * per, u1 = min(units, u0 + per);
-  if (ok) {
-    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
-      float acc[8];
-      const uint4 r = reinterpret_cast<const uint4*>(a.h)[u];
-      acc[0] = bf16_lo(r.x); acc[1] = bf16_hi(r.x); acc[2] = bf16_lo(r.y); acc[3] = bf16_hi(r.y);
-      acc[4] = bf16_lo(r.z); acc[5] = bf16_hi(r.z); acc[6] = bf16_lo(r.w); acc[7] = bf16_hi(r.w);
-      uint4 v[kMaxRanks];
+// Rank-ordered fp32 sum of unit u over all ranks (local partial for this rank's term).
+__device__ __forceinline__ void sum_unit(const OneShotArgs& a, int par, long long u, float (&s)[8]) {
 #pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.world)
-          v[p] = __ldcv(reinterpret_cast<const uint4*>(a.peers[p] + a.partial_off) + u);
-      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < 8; ++j) s[j] = 0.f;
+  uint4 v[kMaxRanks];
 #pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.world) {
-          s[0] += bf16_lo(v[p].x); s[1] += bf16_hi(v[p].x); s[2] += bf16_lo(v[p].y); s[3] += bf16_hi(v[p].y);
-          s[4] += bf16_lo(v[p].z); s[5] += bf16_hi(v[p].z); s[6] += bf16_lo(v[p].w); s[7] += bf16_hi(v[p].w);
-        }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0] + s[0], acc[1] + s[1]);
-      o.y = pack_bf16x2(acc[2] + s[2], acc[3] + s[3]);
-      o.z = pack_bf16x2(acc[4] + s[4], acc[5] + s[5]);
-      o.w = pack_bf16x2(acc[6] + s[6], acc[7] + s[7]);
-      reinterpret_cast<uint4*>(a.h)[u] = o;
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (p < a.world)
+      v[p] = p == a.rank ? reinterpret_cast<const uint4*>(a.peers[a.rank] + a.partial_off)[u]
+                         : __ldcv(reinterpret_cast<const uint4*>(recv_slot(a, a.rank, par, p)) + u);
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (p < a.world) {
+      s[0] += bf16_lo(v[p].x); s[1] += bf16_hi(v[p].x); s[2] += bf16_lo(v[p].y); s[3] += bf16_hi(v[p].y);
+      s[4] += bf16_lo(v[p].z); s[5] += bf16_hi(v[p].z); s[6] += bf16_lo(v[p].w); s[7] += bf16_hi(v[p].w);
     }
-  }
-  __syncthreads();
-  ok = cross_rank_barrier(a, a.end_off, epoch) && ok;
+}
+
+__device__ __forceinline__ void bump_epoch(const OneShotArgs& a, uint32_t epoch) {
   if (threadIdx.x == 0) {
     uint32_t* st = reinterpret_cast<uint32_t*>(a.peers[a.rank]);
     if (atomicAdd(st + 1, 1u) == gridDim.x - 1) {
@@ -128,6 +136,32 @@ __global__ void __launch_bounds__(kThreadsAR)
       *reinterpret_cast<volatile uint32_t*>(st) = epoch;
     }
   }
+}
+
+__global__ void __launch_bounds__(kThreadsAR)
+    oneshot_allreduce_kernel(const OneShotArgs a) {
+  pdl_trigger();
+  pdl_wait();  // the partial comes from the previous kernel (the row-parallel GEMM)
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
+  const int par = epoch & 1;
+  const long long units = a.n / 8;  // 16-byte units of bf16
+  const long long per = (units + gridDim.x - 1) / gridDim.x;
+  const long long u0 = blockIdx.x * per, u1 = min(units, u0 + per);
+  push_slice(a, par, epoch, u0, u1);
+  if (wait_slice(a, epoch)) {
+    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+      float s[8];
+      sum_unit(a, par, u, s);
+      const uint4 r = reinterpret_cast<const uint4*>(a.h)[u];
+      uint4 o;
+      o.x = pack_bf16x2(bf16_lo(r.x) + s[0], bf16_hi(r.x) + s[1]);
+      o.y = pack_bf16x2(bf16_lo(r.y) + s[2], bf16_hi(r.y) + s[3]);
+      o.z = pack_bf16x2(bf16_lo(r.z) + s[4], bf16_hi(r.z) + s[5]);
+      o.w = pack_bf16x2(bf16_lo(r.w) + s[6], bf16_hi(r.w) + s[7]);
+      reinterpret_cast<uint4*>(a.h)[u] = o;
+    }
+  }
+  bump_epoch(a, epoch);
 }
 
 // Row-sliced variant fused with the next RMSNorm: CTA t owns token row t, so after the
@@ -140,31 +174,22 @@ __global__ void __launch_bounds__(kThreadsAR)
   pdl_trigger();
   pdl_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
-  bool ok = cross_rank_barrier(a, a.start_off, epoch);
+  const int par = epoch & 1;
   const int t = blockIdx.x;
   const long long base = (long long)t * H / 8;  // first 16-byte unit of this row
+  push_slice(a, par, epoch, base, base + H / 8);
+  const bool ok = wait_slice(a, epoch);
   float ss = 0.f;
   if (ok) {
     for (int u = threadIdx.x; u < H / 8; u += blockDim.x) {
+      float s[8];
+      sum_unit(a, par, base + u, s);
       const uint4 r = reinterpret_cast<const uint4*>(a.h)[base + u];
-      float v[8] = {bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y),
-                    bf16_lo(r.z), bf16_hi(r.z), bf16_lo(r.w), bf16_hi(r.w)};
-      uint4 pv[kMaxRanks];
-#pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.world) pv[p] = __ldcv(reinterpret_cast<const uint4*>(a.peers[p] + a.partial_off) + base + u);
-      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.world) {
-          s[0] += bf16_lo(pv[p].x); s[1] += bf16_hi(pv[p].x); s[2] += bf16_lo(pv[p].y); s[3] += bf16_hi(pv[p].y);
-          s[4] += bf16_lo(pv[p].z); s[5] += bf16_hi(pv[p].z); s[6] += bf16_lo(pv[p].w); s[7] += bf16_hi(pv[p].w);
-        }
       uint4 o;
-      o.x = pack_bf16x2(v[0] + s[0], v[1] + s[1]);
-      o.y = pack_bf16x2(v[2] + s[2], v[3] + s[3]);
-      o.z = pack_bf16x2(v[4] + s[4], v[5] + s[5]);
-      o.w = pack_bf16x2(v[6] + s[6], v[7] + s[7]);
+      o.x = pack_bf16x2(bf16_lo(r.x) + s[0], bf16_hi(r.x) + s[1]);
+      o.y = pack_bf16x2(bf16_lo(r.y) + s[2], bf16_hi(r.y) + s[3]);
+      o.z = pack_bf16x2(bf16_lo(r.z) + s[4], bf16_hi(r.z) + s[5]);
+      o.w = pack_bf16x2(bf16_lo(r.w) + s[6], bf16_hi(r.w) + s[7]);
       reinterpret_cast<uint4*>(a.h)[base + u] = o;
       // The norm sees the bf16-rounded residual stream, as the unfused RMSNorm would.
       const float hv[8] = {bf16_lo(o.x), bf16_hi(o.x), bf16_lo(o.y), bf16_hi(o.y),
@@ -201,23 +226,14 @@ __global__ void __launch_bounds__(kThreadsAR)
       reinterpret_cast<uint4*>(x_out)[base + u] = q;
     }
   }
-  __syncthreads();
-  ok = cross_rank_barrier(a, a.end_off, epoch) && ok;
-  if (threadIdx.x == 0) {
-    uint32_t* st = reinterpret_cast<uint32_t*>(a.peers[a.rank]);
-    if (atomicAdd(st + 1, 1u) == gridDim.x - 1) {
-      st[1] = 0u;
-      __threadfence();
-      *reinterpret_cast<volatile uint32_t*>(st) = epoch;
-    }
-  }
+  bump_epoch(a, epoch);
 }
 
 }  // namespace
 
 // h [T, H] += sum of the ranks' partials, then x_out = rmsnorm(h) * w (one CTA per token).
 void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
-                            int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                            int64_t flags_off, int64_t recv_off, int64_t partial_off, int64_t max_elems,
                             const at::Tensor& norm_w, double eps, at::Tensor& x_out,
                             const at::Tensor& status) {
   TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2,
@@ -236,8 +252,9 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
   for (int i = 0; i < world; ++i) a.peers[i] = peers[i];
   a.rank = static_cast<int>(rank);
   a.world = world;
-  a.start_off = start_off;
-  a.end_off = end_off;
+  a.flags_off = flags_off;
+  a.recv_off = recv_off;
+  a.max_elems = max_elems;
   a.partial_off = partial_off;
   a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.n = (long long)T * H;
@@ -251,7 +268,7 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
 // h [T, H] bf16 contiguous += sum over ranks of each rank's partial (same shape) stored at
 // byte offset `partial_off` of its symmetric buffer.
 void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
-                       int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                       int64_t flags_off, int64_t recv_off, int64_t partial_off, int64_t max_elems,
                        const at::Tensor& status) {
   TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous(), "oneshot_allreduce: h bf16 contiguous");
   const int world = static_cast<int>(peers.size());
@@ -266,8 +283,9 @@ void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t
   for (int i = 0; i < world; ++i) a.peers[i] = peers[i];
   a.rank = static_cast<int>(rank);
   a.world = world;
-  a.start_off = start_off;
-  a.end_off = end_off;
+  a.flags_off = flags_off;
+  a.recv_off = recv_off;
+  a.max_elems = max_elems;
   a.partial_off = partial_off;
   a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.n = n;

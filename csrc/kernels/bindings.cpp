@@ -90,10 +90,10 @@ void gemm_fp8_grouped_scatter(const at::Tensor& xq, const at::Tensor& xs, const 
 void set_pdl(bool on);
 bool get_pdl();
 void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
-                       int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                       int64_t flags_off, int64_t recv_off, int64_t partial_off, int64_t max_elems,
                        const at::Tensor& status);
 void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
-                            int64_t start_off, int64_t end_off, int64_t partial_off, int64_t max_elems,
+                            int64_t flags_off, int64_t recv_off, int64_t partial_off, int64_t max_elems,
                             const at::Tensor& norm_w, double eps, at::Tensor& x_out,
                             const at::Tensor& status);
 at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);

@@ -3,11 +3,11 @@
 ``OneShotTPComm`` gives every rank a symmetric buffer (CUDA IPC, mapped by every
 peer).  A row-parallel projection ``h += allreduce(x @ w.T)`` then runs as two
 kernels: the tcgen05 GEMM writes its partial straight into this rank's buffer, and
-``oneshot_allreduce`` (``csrc/kernels/allreduce.cu``) has every CTA pull its slice of
-the partial from every rank with 16-byte NVLink loads, sum in rank order (fp32; all
-ranks obtain identical sums) and add into the residual stream.  Two per-CTA
-cross-rank barriers bracket the pull, so no rank overwrites a partial a peer is
-still reading.  Prefill-sized calls (more tokens than the buffer holds) use GEMM +
+``oneshot_allreduce`` (``csrc/kernels/allreduce.cu``) has every CTA push its slice of
+the partial into every peer's receive slot with 16-byte NVLink stores, raise a per-slice
+flag, wait for the peers' flags, and sum the slice in rank order (fp32; all ranks obtain
+identical sums) into the residual stream.  Receive slots alternate by epoch parity, so one
+flag exchange per call suffices.  Prefill-sized calls (more tokens than the buffer holds) use GEMM +
 NCCL.  ``all_reduce`` / ``all_gather`` / ``reduce_scatter`` forward to NCCL.
 
 The model calls ``fused_gemm_allreduce_residual`` (the same hook as the fused
@@ -39,11 +39,11 @@ class OneShotTPComm:
         self.device = torch.device(device)
         self.max_tokens = max_tokens
         self.hidden = hidden
-        self.start_off = 256
-        self.end_off = self.start_off + MAX_RANKS * MAX_CTAS * 4
-        self.partial_off = ((self.end_off + MAX_RANKS * MAX_CTAS * 4 + 255) // 256) * 256
+        self.flags_off = 256
+        self.partial_off = ((self.flags_off + MAX_RANKS * MAX_CTAS * 4 + 255) // 256) * 256
         self.max_elems = max_tokens * hidden
-        nbytes = self.partial_off + self.max_elems * 2
+        self.recv_off = ((self.partial_off + self.max_elems * 2 + 255) // 256) * 256
+        nbytes = self.recv_off + 2 * MAX_RANKS * self.max_elems * 2
         e = ext()
         dev = self.device.index
         self.local = e.symm_alloc(nbytes, dev)
@@ -92,7 +92,7 @@ class OneShotTPComm:
             return None
         part = self._partial(T, H)
         gemm.linear(x, w, out=part)
-        ext().oneshot_allreduce(h, self.peers, self.rank, self.start_off, self.end_off,
+        ext().oneshot_allreduce(h, self.peers, self.rank, self.flags_off, self.recv_off,
                                 self.partial_off, self.max_elems, get_workspace(x.device).status)
         return None
 
@@ -108,7 +108,7 @@ class OneShotTPComm:
             return
         part = self._partial(T, H)
         gemm.linear(x, w, out=part)
-        ext().oneshot_allreduce_norm(h, self.peers, self.rank, self.start_off, self.end_off,
+        ext().oneshot_allreduce_norm(h, self.peers, self.rank, self.flags_off, self.recv_off,
                                      self.partial_off, self.max_elems, norm_w, float(eps), x_out,
                                      get_workspace(x.device).status)
 
