@@ -501,3 +501,12 @@ def test_universal_worker_abi_and_queue():
     res = asyncio.run(main())
     assert all(r["status"] == "OK" for r in res) and [r["job_id"] for r in res] == list(range(6))
     assert be.batched >= 2
+
+
+def test_decode_split_heuristics():
+    from swarm_inference_lab_b200.ops import attention, mla
+    assert attention.decode_splits(32, 8, 34) == 4          # 1024 CTAs: 6.92 of 7 waves busy
+    assert attention.decode_splits(64, 8, 34) == 2
+    assert attention.decode_splits(1, 8, 34) == 17          # <1 wave: fill the most SMs
+    assert attention.decode_splits(128, 8, 1) == 1          # never below 2 pages per split
+    assert mla.decode_splits(32, 4096) == 4 and mla.decode_splits(1, 4096) == 64
