@@ -139,10 +139,6 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
         typer.echo("multi-GPU plans run under torchrun (see bench.py); serving this request on one GPU",
                    err=True)
     from .engine.engine import LLMEngine, SamplingParams
-    if cfg.is_moe or cfg.mla:
-        _out({"error": "single-process CLI serving covers dense models; MoE/MLA run via the "
-                       "stage workers"}, as_json or ndjson)
-        raise typer.Exit(EXIT_RUNTIME)
     t0 = time.perf_counter()
     eng = LLMEngine(cfg, device="cuda", seed=seed, max_batch=1,
                     max_seq_len=len(ids) + max_tokens + 64,
