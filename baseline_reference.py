@@ -94,12 +94,24 @@ def run_reference_arm(args, rank, world, local, metric):
     if B_total % world:
         return {"impl": "reference", "unavailable": "batch not divisible by the replica count"}
     B = B_total // world
-    root = os.environ.get("SIL_REF_CKPT_DIR") or tempfile.mkdtemp(prefix=f"ref_ckpt_r{rank}_")
+    # One checkpoint for every replica: rank 0 writes it (16 GB), the others wait at a barrier.
+    root = os.environ.get("SIL_REF_CKPT_DIR") or os.path.join(tempfile.gettempdir(),
+                                                              f"sil_ref_ckpt_{os.getuid()}")
     ckpt = os.path.join(root, "qwen3-arch-llama3-8b-dims")
     device = f"cuda:{local}"
     try:
+        write_err = None
+        if rank == 0 and not os.path.exists(os.path.join(ckpt, "model.safetensors.index.json")):
+            try:
+                _write_checkpoint(ckpt, seed=0, device=device)
+            except Exception as exc:  # noqa: BLE001 - every rank still reaches the barrier
+                write_err = exc
+        if world > 1:
+            dist.barrier()
+        if write_err is not None:
+            raise write_err
         if not os.path.exists(os.path.join(ckpt, "model.safetensors.index.json")):
-            _write_checkpoint(ckpt, seed=0, device=device)
+            raise RuntimeError("reference checkpoint was not written")
         # The reference's fastest stock options first; its static cache needs a
         # transformers<5 cache API, so fall back to its dynamic-cache path.
         attempts = [("static", "manual_cuda_graph"), ("dynamic_reference", "eager")]
