@@ -302,6 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int r = c.a_base + min(m_loc, max(c.Mv - 1, 0));
             srow = args.sA[(long long)r * args.KB + kb];
           }
+          // Swapped order: the columns are tokens.  Lane l loads token l's activation scale
+          // (and token l + 32 when BN = 64) once per K block; the others get it by shuffle.
+          float stok0 = 0.f, stok1 = 0.f;
+          if constexpr (SWAP) {
+            const int hi = max(c.Nv - 1, 0);
+            stok0 = args.sB[(long long)(c.b_base + min(c.nt * BN + (lane & (BN - 1) & 31), hi)) * args.KB + kb];
+            if constexpr (BN > 32)
+              stok1 = args.sB[(long long)(c.b_base + min(c.nt * BN + 32 + lane, hi)) * args.KB + kb];
+          }
 #pragma unroll
           for (int c0 = 0; c0 < C::ACC_COLS; c0 += CW) {
             uint32_t rv[CW];
@@ -311,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int col = c0 + t;
               float scol;
               if constexpr (SWAP) {
-                const int n = (col % BN) + c.nt * BN;
-                const int nn = min(n, max(c.Nv - 1, 0));
-                scol = args.sB[(long long)(c.b_base + nn) * args.KB + kb] *
-                       ((C::NUM_A == 2 && col >= BN) ? srow_up : srow);
+                const int j = col % BN;
+                const float st = (BN > 32 && j >= 32) ? __shfl_sync(0xffffffffu, stok1, j - 32)
+                                                      : __shfl_sync(0xffffffffu, stok0, j & 31);
+                scol = st * ((C::NUM_A == 2 && col >= BN) ? srow_up : srow);
               } else {
                 int wrow;
                 if constexpr (C::kIsSwiGLU)

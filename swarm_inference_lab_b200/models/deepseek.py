@@ -34,8 +34,7 @@ si/backends/colibri/sparse_moe.py:60-218 for the router and fp8 block-scale sema
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 
@@ -116,7 +115,6 @@ class MLAWeights:
     lm_head: torch.Tensor
     expert_start: int = 0
     experts_local: int = 0
-    dequant_kv_b: dict = field(default_factory=dict)
 
     @classmethod
     def random(cls, cfg: ModelConfig, ep: TPInfo, device, seed: int = 0,
