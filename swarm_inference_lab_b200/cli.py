@@ -275,6 +275,33 @@ def model_inspect(path: str, as_json: bool = typer.Option(True, "--json/--text")
           "total_bytes": res.total_bytes, **res.profile.summary()}, as_json)
 
 
+@model_app.command("feasibility")
+def model_feasibility(path: str, batch: int = 32, ctx: int = 4096,
+                      as_json: bool = typer.Option(True, "--json/--text")):
+    """Headers-only sizing of a checkpoint against B200 GPUs (180 GB each, 8 per box)."""
+    from .model_io.facts import b200_feasibility
+    from .model_io.resolver import ModelSourceResolver
+    _out(b200_feasibility(ModelSourceResolver().inspect(path), batch=batch, context=ctx), as_json)
+
+
+@model_app.command("variants")
+def model_variants(directory: str, memory_gb: float = 180.0, objective: str = "balanced",
+                   request: str = typer.Option(None, "--variant"),
+                   as_json: bool = typer.Option(True, "--json/--text")):
+    """Complete GGUF variants in a directory and the one selected for the objective."""
+    from pathlib import Path
+    from .model_io.facts import discover_gguf_variants, select_variant
+    root = Path(directory)
+    listing = {p.relative_to(root).as_posix(): p.stat().st_size for p in root.rglob("*.gguf")}
+    vs = discover_gguf_variants(listing)
+    sel = select_variant(vs, memory_bytes=int(memory_gb * 1e9), objective=objective, request=request)
+    _out({"selected": sel.selected.variant_id, "feasible": sel.feasible,
+          "candidates": [{"variant": c.variant.variant_id, "quant": c.variant.quant,
+                          "bytes": c.variant.total_bytes, "bits_per_weight": c.variant.bits_per_weight,
+                          "feasible": c.feasible, "reason": c.reason} for c in sel.candidates]},
+         as_json)
+
+
 @app.command("plan")
 def plan_command(model: str, gpus: int = 8, batch: int = 32, ctx: int = 2304, prompt: int = 2048,
                  mode: str = "throughput", as_json: bool = typer.Option(False, "--json")):

@@ -125,6 +125,7 @@ class StageDefinition(StrictModel):
     embed: bool = False
     head: bool = False
     endpoint: str = ""
+    weight_bytes: int = Field(default=0, ge=0)
 
 
 class ModelManifest(StrictModel):
@@ -134,6 +135,8 @@ class ModelManifest(StrictModel):
     num_layers: PositiveInt
     dtype: str = "bfloat16"
     stages: list[StageDefinition] = []
+    shard_hashes: dict[str, str] = {}       # shard file (or directory) -> sha256
+    total_weight_bytes: int = Field(default=0, ge=0)
 
     def check_union(self) -> None:
         """Every layer in exactly one stage, in order."""
