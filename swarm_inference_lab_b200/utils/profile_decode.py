@@ -198,11 +198,16 @@ def decode_steps(a):
     cfg = preset(a.model)
     if a.layers:
         cfg = cfg.replace(num_layers=a.layers)
-    w = DenseWeights.random(cfg, TPInfo(), "cuda", seed=0)
-    model = DenseModel(w, "cuda", max_positions=a.ctx + 64)
+    # --tp N: one rank's shard of an N-way tensor-parallel model with the all-reduces
+    # left out (a local communicator), i.e. the compute part of a TP decode step.
+    tp = TPInfo(0, a.tp)
+    w = DenseWeights.random(cfg, tp, "cuda", seed=0)
+    from ..parallel.comm import LocalComm
+    model = DenseModel(w, "cuda", comm=LocalComm(), max_positions=a.ctx + 64)
     B = a.batch
     pages_per = (a.ctx + 1 + 63) // 64
-    kv = PagedKVCache(cfg.num_layers, cfg.num_kv_heads, B * pages_per, "cuda")
+    kvh = tp.heads(cfg.num_kv_heads)[1]
+    kv = PagedKVCache(cfg.num_layers, kvh, B * pages_per, "cuda")
     kv.k.normal_()
     kv.v.normal_()
     bt = torch.arange(B * pages_per, dtype=torch.int32, device="cuda").view(B, pages_per)
@@ -211,12 +216,12 @@ def decode_steps(a):
     fb = ForwardBatch(ids=torch.randint(0, cfg.vocab_size, (B,), device="cuda"), positions=pos,
                       slots=slots.int(), seq_lens=pos + 1, block_table=bt,
                       last_idx=torch.arange(B, device="cuda"), is_decode=True,
-                      decode_splits=A.decode_splits(B, cfg.num_kv_heads, pages_per))
+                      decode_splits=A.decode_splits(B, kvh, pages_per))
     ms = time_fn(lambda: model.forward(fb, kv), a.steps, warmup=2, graph=not a.eager)
     wbytes = w.nbytes()
-    kvbytes = 2 * B * (a.ctx + 1) * cfg.num_layers * cfg.num_kv_heads * 128 * 2
+    kvbytes = 2 * B * (a.ctx + 1) * cfg.num_layers * kvh * cfg.head_dim * 2
     pk = _peaks()
-    return {"mode": "decode_step_eager" if a.eager else "decode_step_graph", "model": cfg.name, "batch": B, "ctx": a.ctx, "ms": ms,
+    return {"mode": "decode_step_eager" if a.eager else "decode_step_graph", "model": cfg.name, "tp": a.tp, "batch": B, "ctx": a.ctx, "ms": ms,
             "weight_bytes": wbytes, "kv_bytes": kvbytes,
             "roofline_ms": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6,
             "frac_of_roofline": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6 / ms}
@@ -228,6 +233,7 @@ def main():
                                      "gemm_ar1", "launch_floor"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
+    ap.add_argument("--tp", type=int, default=1, help="step: time one rank of a TP group, no all-reduce")
     ap.add_argument("--model", default="llama-3-8b-shape")
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--batch", type=int, default=32)
