@@ -10,7 +10,15 @@ using namespace gemm_detail;
 // streaming time is longer.  Model: one CTA streams ~kPerSmGBs from HBM, the
 // box at most kHbmGBs; choose the number of CTAs per tile minimising
 // bytes / bandwidth + fix-up.
-inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms) {
+// SIL_SPLIT_REDUCE=spread: tile-aligned splits (swapped order) reduce their partials across
+// all contributors of a tile; otherwise the last contributor to arrive reduces them all.
+inline bool split_reduce_spread() {
+  static const char* mode = std::getenv("SIL_SPLIT_REDUCE");
+  return mode != nullptr && mode[0] == 's';
+}
+
+inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms,
+                               bool spread = false) {
   // Default: tile-aligned splits from a calibrated cost model when there are few tiles,
   // otherwise ("fill") one CTA per SM whenever the problem has >= 4 K blocks per CTA.  The
   // older latency model below is kept behind SIL_STREAMK=latency.
@@ -22,8 +30,10 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       // number s of K ranges so no CTA straddles two tiles.  Calibrated on B200 (32 tokens,
       // 4096 x {512, 4096} weights, s = 1, 2, 4): ~2.2 us fixed cost, ~48 GB/s streamed per
       // CTA, a split fix-up of ~2.5 us + 0.5 us per split; the box streams at most ~6000 GB/s.
-      constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kFixupUs = 2.5, kFixupPerSplitUs = 0.5,
-                       kBoxGBs = 6000.0;
+      // The spread reduction reads s partial slices per contributor instead of s whole
+      // partials in one CTA, so its per-split cost is far lower.
+      constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kBoxGBs = 6000.0;
+      const double kFixupUs = spread ? 1.5 : 2.5, kFixupPerSplitUs = spread ? 0.08 : 0.5;
       const double tile_bytes = (double)bytes_per_kb * num_kb;
       long long best_s = 1;
       double best_t = 1e30;
@@ -103,7 +113,7 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 
   const bool swap = force_mode == 1 ? true : force_mode == 2 ? false : (T <= 128);
-  GemmArgs a;
+  GemmArgs a{};
   a.num_kb = (K + BK - 1) / BK;
   a.inter = inter;
   a.out = out.data_ptr();
@@ -150,14 +160,20 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   a.group_m = 16;
   long long g;
   if (a.stream_k) {
-    g = stream_k_grid(tiles, a.num_kb, (long long)((swap && swiglu ? 2 : 1) * BM + bn) * BK * 2, sms);
+    const bool spread = swap && split_reduce_spread();
+    g = stream_k_grid(tiles, a.num_kb, (long long)((swap && swiglu ? 2 : 1) * BM + bn) * BK * 2, sms,
+                      spread);
     if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
+    // Whole tiles split into equal K ranges: every contributor of a tile takes part in its
+    // reduction (each CTA owns exactly one K range of one tile).
+    if (spread && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb)
+      a.split_s = static_cast<int>(g / tiles);
   } else {
     g = std::min<long long>(sms, tiles);
   }
   const long long acc_cols = (swap && swiglu ? 2 : 1) * bn;
   TORCH_CHECK(g * 2 * acc_cols * BM <= ws.numel(), "gemm_bf16: workspace too small");
-  TORCH_CHECK(tiles <= counters.numel(), "gemm_bf16: counter array too small");
+  TORCH_CHECK(3 * tiles <= counters.numel(), "gemm_bf16: counter array too small");
   a.grid = static_cast<int>(g);
   if (swap) {
     switch (epi) {

@@ -75,9 +75,22 @@ struct GemmArgs {
   const int* grp_offsets;
   int num_groups;
   long long w_group_rows;
+  // Tile-aligned split-K (swapped order only): grid = tiles * split_s, CTA t*split_s + i
+  // owns the i-th K range of tile t, and the tile's partials are reduced by all of its
+  // contributors (see the epilogue).  0: stream-K with last-arriver reduction.
+  int split_s;
 };
 
 constexpr int kMaxGroups = 1024;
+// A split contributor waits this long for the other partials of its tile before leaving
+// its share of the reduction to the tile's last contributor (which never waits).
+constexpr unsigned long long kSplitWaitNs = 20000ull;
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -588,6 +601,105 @@ __global__ void __launch_bounds__(kThreads, 1)
             else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
           }
           if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
+        } else if (SWAP && EPI != kEpiAllReduce && args.split_s > 1) {
+          // Tile-aligned split.  The s contributors of tile t are CTAs t*s .. t*s+s-1, one K
+          // range each.  Every contributor stores its fp32 partial and arrives; the tile's
+          // 32 items (column chunk cc x row quarter q, k = 4*cc + q) are then reduced in
+          // contributor order (deterministic) by whoever claims them in the tile's claim
+          // mask: a contributor that sees all s arrivals within kSplitWaitNs claims its own
+          // items (k % s == its index); the last contributor to arrive claims its own items,
+          // then every item still unclaimed.  So the reduction is spread over the tile's
+          // CTAs when they run together, and no CTA ever waits for one that is not running.
+          const int s = args.split_s;
+          const int ci = cta - sg.tile * s;
+          float* mine = args.ws + (long long)cta * 2 * C::ACC_COLS * BM;
+#pragma unroll 1
+          for (int c0 = 0; c0 < C::ACC_COLS; c0 += CW) {
+            uint32_t rv[CW];
+            tmem_load<CW>(taddr + c0, rv);
+#pragma unroll
+            for (int t = 0; t < CW; ++t) __stcg(&mine[(c0 + t) * BM + row], __uint_as_float(rv[t]));
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[b]);
+          int* ctr = args.counters + 3LL * sg.tile;  // [0] arrivals [1] claim mask [2] departures
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64) {
+            int role = atomicAdd(&ctr[0], 1) == s - 1 ? 2 : 0;  // 2: last to arrive
+            if (role == 0) {
+              const uint64_t t0 = globaltimer_ns();
+              while (true) {
+                if (ld_acquire_gpu_s32(&ctr[0]) >= s) {
+                  role = 1;
+                  break;
+                }
+                if (globaltimer_ns() - t0 > kSplitWaitNs) break;
+              }
+            }
+            flags[1] = role;
+          }
+          named_bar_sync(1, 128);
+          const int role = flags[1];
+          if (role != 0) {
+            __threadfence();
+            constexpr int RW = C::OUT_COLS / 8;
+            // Contributors whose loads are in flight together (<= 32 staging registers).
+            constexpr int NBW = 32 / (RW * (C::kSwiGLU ? 2 : 1));
+            constexpr int NB = NBW < 1 ? 1 : NBW > 4 ? 4 : NBW;
+            const float* base = args.ws + (long long)sg.tile * s * 2 * C::ACC_COLS * BM;
+            const long long cstride = 2LL * C::ACC_COLS * BM;
+#pragma unroll 1
+            for (int pass = 0; pass < (role == 2 ? 2 : 1); ++pass) {
+#pragma unroll 1
+              for (int cc = 0; cc < 8; ++cc) {
+                const int k = cc * 4 + q;
+                const bool own = (k % s) == ci;
+                if (pass == 0 ? !own : own) continue;
+                unsigned won = 0;
+                if (lane == 0) won = (atomicOr(reinterpret_cast<unsigned*>(&ctr[1]), 1u << k) >> k) & 1u ? 0u : 1u;
+                won = __shfl_sync(0xffffffffu, won, 0);
+                if (!won) continue;
+                const int c0 = cc * RW;
+                float v[RW], uu[RW];
+#pragma unroll
+                for (int t = 0; t < RW; ++t) { v[t] = 0.f; uu[t] = 0.f; }
+#pragma unroll 1
+                for (int cb = 0; cb < s; cb += NB) {
+                  float pv[NB][RW], pu[NB][RW];
+#pragma unroll
+                  for (int q2 = 0; q2 < NB; ++q2)
+                    if (cb + q2 < s) {
+                      const float* p = base + (cb + q2) * cstride + row;
+#pragma unroll
+                      for (int t = 0; t < RW; ++t) {
+                        pv[q2][t] = __ldcg(p + (c0 + t) * BM);
+                        if constexpr (C::kSwiGLU) pu[q2][t] = __ldcg(p + (c0 + UOFF + t) * BM);
+                      }
+                    }
+#pragma unroll
+                  for (int q2 = 0; q2 < NB; ++q2)
+                    if (cb + q2 < s) {
+#pragma unroll
+                      for (int t = 0; t < RW; ++t) {
+                        v[t] += pv[q2][t];
+                        if constexpr (C::kSwiGLU) uu[t] += pu[q2][t];
+                      }
+                    }
+                }
+                store_chunk<EPI, SWAP, RW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64) {
+            __threadfence();
+            if (atomicAdd(&ctr[2], 1) == s - 1) {  // every contributor is done with the tile
+              ctr[0] = 0;
+              ctr[1] = 0;
+              ctr[2] = 0;
+            }
+          }
         } else {
           // Partial tile: slot 0 = this CTA's first segment, slot 1 = its last.
           const int slot = sg.first ? 0 : 1;

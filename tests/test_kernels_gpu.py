@@ -39,6 +39,58 @@ def test_gemm_modes_and_splits(mode, splits):
     assert (y.float() - ref).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("T", [1, 16, 32, 64, 128])
+@pytest.mark.parametrize("splits", [2, 5, 13, 24])
+@pytest.mark.parametrize("epi", ["plain", "residual", "swiglu", "fp32"])
+def test_gemm_tile_aligned_splits(T, splits, epi):
+    """Decode GEMMs with every tile split into equal K ranges: the partials are reduced by
+    all contributors of a tile (claimed items, contributor order), so the result matches
+    the fp32 reference and is bitwise identical from launch to launch."""
+    from swarm_inference_lab_b200.ops import gemm
+    N, K = (768, 1536) if epi == "swiglu" else (640, 1536)   # 3 / 5 tiles of 128 rows, 24 K blocks
+    g = torch.Generator(device="cuda").manual_seed(T * 31 + splits)
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).bfloat16()
+    h = torch.randn(T, N, device="cuda", generator=g).bfloat16()
+
+    def run():
+        if epi == "plain":
+            return gemm.linear(x, w, force_mode=1, force_splits=splits)
+        if epi == "fp32":
+            return gemm.linear(x, w, fp32_out=True, force_mode=1, force_splits=splits)
+        if epi == "swiglu":
+            return gemm.linear(x, w, swiglu=True, force_mode=1, force_splits=splits)
+        out = torch.empty_like(h)
+        return gemm.linear(x, w, out=out, residual=h, force_mode=1, force_splits=splits)
+    ys = [run() for _ in range(3)]
+    torch.cuda.synchronize()
+    ref = _ref_linear(x, w)
+    if epi == "swiglu":
+        ref = torch.nn.functional.silu(ref[:, :N // 2]) * ref[:, N // 2:]
+    elif epi == "residual":
+        ref = ref + h.float()
+    err = (ys[0].float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+
+
+def test_gemm_splits_beyond_resident_ctas():
+    """More split CTAs than SMs: contributors that cannot all be resident at once.  Early
+    contributors stop waiting and the last contributor of each tile reduces what is left."""
+    from swarm_inference_lab_b200.ops import gemm
+    from swarm_inference_lab_b200.ops.workspace import get_workspace
+    T, N, K = 32, 4096, 2048                       # 32 tiles x 8 splits = 256 CTAs
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    y = gemm.linear(x, w, force_mode=1, force_splits=8)
+    y2 = gemm.linear(x, w, force_mode=1, force_splits=8)
+    ref = _ref_linear(x, w)
+    torch.cuda.synchronize()
+    assert (y.float() - ref).abs().max().item() < 2e-2
+    assert torch.equal(y, y2)
+    get_workspace().check()
+
+
 @pytest.mark.parametrize("T", [3, 32, 200])
 def test_gemm_residual_inplace(T):
     from swarm_inference_lab_b200.ops import gemm
