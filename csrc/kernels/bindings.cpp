@@ -97,6 +97,10 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
                             const at::Tensor& norm_w, double eps, at::Tensor& x_out,
                             const at::Tensor& status);
 at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);
+void nvls_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t mc, int64_t rank,
+                    int64_t flags1_off, int64_t flags2_off, int64_t partial_off, int64_t sum_off,
+                    int64_t max_elems, const c10::optional<at::Tensor>& norm_w, double eps,
+                    const c10::optional<at::Tensor>& x_out, const at::Tensor& status);
 }  // namespace sil
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -142,6 +146,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "one-shot all-reduce of symmetric-buffer partials into h (NVLink pull, per-CTA barriers)");
   m.def("oneshot_allreduce_norm", &sil::oneshot_allreduce_norm,
         "one-shot all-reduce into h fused with the next RMSNorm (x_out = rmsnorm(h) * w)");
+  m.def("nvls_allreduce", &sil::nvls_allreduce,
+        "two-shot all-reduce through NVSwitch multicast into h, optionally fused with the next RMSNorm");
   m.def("symm_tensor", &sil::symm_tensor, "bf16 tensor view over a symmetric buffer (no ownership)");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

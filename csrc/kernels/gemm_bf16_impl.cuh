@@ -604,12 +604,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (SWAP && EPI != kEpiAllReduce && args.split_s > 1) {
           // Tile-aligned split.  The s contributors of tile t are CTAs t*s .. t*s+s-1, one K
           // range each.  Every contributor stores its fp32 partial and arrives; the tile's
-          // 32 items (column chunk cc x row quarter q, k = 4*cc + q) are then reduced in
-          // contributor order (deterministic) by whoever claims them in the tile's claim
-          // mask: a contributor that sees all s arrivals within kSplitWaitNs claims its own
-          // items (k % s == its index); the last contributor to arrive claims its own items,
-          // then every item still unclaimed.  So the reduction is spread over the tile's
-          // CTAs when they run together, and no CTA ever waits for one that is not running.
+          // items (row quarter x column chunk) are then reduced in contributor order
+          // (deterministic) by whoever claims them in the tile's claim mask: a contributor
+          // that sees all s arrivals within kSplitWaitNs claims its own items; the last
+          // contributor to arrive claims its own items, then every item still unclaimed.  So
+          // the reduction is spread over the tile's CTAs when they run together, and no CTA
+          // ever waits for one that is not running.
           const int s = args.split_s;
           const int ci = cta - sg.tile * s;
           float* mine = args.ws + (long long)cta * 2 * C::ACC_COLS * BM;
@@ -643,36 +643,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int role = flags[1];
           if (role != 0) {
             __threadfence();
-            constexpr int RW = C::OUT_COLS / 8;
-            // Contributors whose loads are in flight together (<= 32 staging registers).
-            constexpr int NBW = 32 / (RW * (C::kSwiGLU ? 2 : 1));
-            constexpr int NB = NBW < 1 ? 1 : NBW > 4 ? 4 : NBW;
+            // Items: row quarter (k & 3) x column chunk (k >> 2) of CWR columns, at most 32.
+            // Warp q of contributor ci owns the items k == 4*ci + q (mod 4s); it claims all of
+            // them with one atomicOr and reduces the ones it won.  The last contributor then
+            // claims what is left, each warp the items of its own row quarter.
+            constexpr int CWR = C::OUT_COLS / 8 > 8 ? C::OUT_COLS / 8 : 8;
+            constexpr int NI = 4 * (C::OUT_COLS / CWR);
+            static_assert(NI <= 32, "claim mask holds 32 items");
+            constexpr int NBW = 32 / (CWR * (C::kSwiGLU ? 2 : 1));  // partials per load batch
+            constexpr int NB = NBW < 1 ? 1 : NBW;
             const float* base = args.ws + (long long)sg.tile * s * 2 * C::ACC_COLS * BM;
             const long long cstride = 2LL * C::ACC_COLS * BM;
+            const int nslots = 4 * s;
+            const int slot = ci * 4 + q;
 #pragma unroll 1
             for (int pass = 0; pass < (role == 2 ? 2 : 1); ++pass) {
-#pragma unroll 1
-              for (int cc = 0; cc < 8; ++cc) {
-                const int k = cc * 4 + q;
-                const bool own = (k % s) == ci;
-                if (pass == 0 ? !own : own) continue;
-                unsigned won = 0;
-                if (lane == 0) won = (atomicOr(reinterpret_cast<unsigned*>(&ctr[1]), 1u << k) >> k) & 1u ? 0u : 1u;
-                won = __shfl_sync(0xffffffffu, won, 0);
-                if (!won) continue;
-                const int c0 = cc * RW;
-                float v[RW], uu[RW];
+              unsigned cand = 0;
+              for (int k = q; k < NI; k += 4) {
+                const bool own = (k % nslots) == slot;
+                if (pass == 0 ? own : !own) cand |= 1u << k;
+              }
+              unsigned won = 0;
+              if (lane == 0 && cand != 0u) won = cand & ~atomicOr(reinterpret_cast<unsigned*>(&ctr[1]), cand);
+              won = __shfl_sync(0xffffffffu, won, 0);
+              while (won != 0u) {
+                const int k = __ffs(won) - 1;
+                won &= won - 1u;
+                const int c0 = (k >> 2) * CWR;
+                float v[CWR], uu[CWR];
 #pragma unroll
-                for (int t = 0; t < RW; ++t) { v[t] = 0.f; uu[t] = 0.f; }
+                for (int t = 0; t < CWR; ++t) { v[t] = 0.f; uu[t] = 0.f; }
 #pragma unroll 1
                 for (int cb = 0; cb < s; cb += NB) {
-                  float pv[NB][RW], pu[NB][RW];
+                  float pv[NB][CWR], pu[NB][CWR];
 #pragma unroll
                   for (int q2 = 0; q2 < NB; ++q2)
                     if (cb + q2 < s) {
                       const float* p = base + (cb + q2) * cstride + row;
 #pragma unroll
-                      for (int t = 0; t < RW; ++t) {
+                      for (int t = 0; t < CWR; ++t) {
                         pv[q2][t] = __ldcg(p + (c0 + t) * BM);
                         if constexpr (C::kSwiGLU) pu[q2][t] = __ldcg(p + (c0 + UOFF + t) * BM);
                       }
@@ -681,13 +690,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                   for (int q2 = 0; q2 < NB; ++q2)
                     if (cb + q2 < s) {
 #pragma unroll
-                      for (int t = 0; t < RW; ++t) {
+                      for (int t = 0; t < CWR; ++t) {
                         v[t] += pv[q2][t];
                         if constexpr (C::kSwiGLU) uu[t] += pu[q2][t];
                       }
                     }
                 }
-                store_chunk<EPI, SWAP, RW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
+                store_chunk<EPI, SWAP, CWR>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
               }
             }
           }

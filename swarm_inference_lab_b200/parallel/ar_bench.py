@@ -76,6 +76,11 @@ def main():
     nccl = NcclComm()
     one = OneShotTPComm(nccl, dev, max_tokens=max(toks), hidden=H)
     st = get_workspace(dev).status
+    nv = None
+    if world > 1:
+        from .nvls_tp import NvlsTPComm
+        if NvlsTPComm.available(nccl, dev):
+            nv = NvlsTPComm(nccl, dev, max_tokens=max(toks), hidden=H)
     nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     out = []
     for T in toks:
@@ -96,16 +101,35 @@ def main():
         def f_norm():
             ext().oneshot_allreduce_norm(h, one.peers, one.rank, one.flags_off, one.recv_off,
                                          one.partial_off, one.max_elems, nw, 1e-5, x, st)
+        paths = [("nccl", f_nccl), ("oneshot", f_one), ("oneshot_norm", f_norm)]
+        if nv is not None:
+            nv._partial(T, H).copy_(part)
+            paths += [("nvls", lambda: nv._reduce(h)), ("nvls_norm", lambda: nv._reduce(h, nw, 1e-5, x))]
         bytes_ = T * H * 2
         roof_us = (world - 1) * bytes_ / (NVLINK_GBS * 1e3)
-        for name, fn in (("nccl", f_nccl), ("oneshot", f_one), ("oneshot_norm", f_norm)):
+        for name, fn in paths:
             us = _graph_us(fn, a.iters, dev)
             out.append({"path": name, "world": world, "tokens": T, "hidden": H, "bytes": bytes_,
                         "us_per_allreduce": round(us, 2), "nvlink_roofline_us": round(roof_us, 2)})
     get_workspace(dev).check()
     if rank == 0:
+        print(json.dumps({"nvls_multicast": nv is not None}), flush=True)
         for r in out:
             print(json.dumps(r), flush=True)
+    # Correctness of the NVLS sum against NCCL on the last token count.
+    if nv is not None:
+        T = toks[-1]
+        g = torch.Generator(device=dev).manual_seed(rank + 7)
+        p = torch.randn(T, H, device=dev, generator=g).bfloat16()
+        nv._partial(T, H).copy_(p)
+        hh = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
+        nv._reduce(hh)
+        ref = p.float()
+        dist.all_reduce(ref)
+        err = (hh.float() - ref).abs().max().item()
+        if rank == 0:
+            print(json.dumps({"nvls_check_max_abs_err": err, "ref_max": ref.abs().max().item()}), flush=True)
+        nv.close()
     one.close()
     dist.destroy_process_group()
 
