@@ -173,7 +173,7 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   }
   const long long acc_cols = (swap && swiglu ? 2 : 1) * bn;
   TORCH_CHECK(g * 2 * acc_cols * BM <= ws.numel(), "gemm_bf16: workspace too small");
-  TORCH_CHECK(3 * tiles <= counters.numel(), "gemm_bf16: counter array too small");
+  TORCH_CHECK((a.split_s > 1 ? 3 : 1) * tiles <= counters.numel(), "gemm_bf16: counter array too small");
   a.grid = static_cast<int>(g);
   if (swap) {
     switch (epi) {

@@ -85,7 +85,7 @@ def op_gemm(a):
 
 def op_decode_attn(a):
     from ..ops import attention as A
-    B, ctx, hq, hkv = a.batch, a.ctx, 32, 8
+    B, ctx, hq, hkv = a.batch, a.ctx, a.hq, a.hkv
     pages_per = (ctx + 63) // 64
     P = B * pages_per
     kc = torch.randn(P, hkv, 64, 128, device="cuda").bfloat16()
@@ -93,7 +93,7 @@ def op_decode_attn(a):
     bt = torch.arange(P, dtype=torch.int32, device="cuda").view(B, pages_per)
     sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
     q = torch.randn(B, hq, 128, device="cuda").bfloat16()
-    splits = A.decode_splits(B, hkv, pages_per)
+    splits = a.splits or A.decode_splits(B, hkv, pages_per)
     ms = time_fn(lambda: A.paged_decode(q, kc, vc, bt, sl, num_splits=splits), a.iters,
                  graph=not a.eager)
     bytes_ = 2 * B * ctx * hkv * 128 * 2
@@ -233,6 +233,8 @@ def main():
                                      "gemm_ar1", "launch_floor"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
+    ap.add_argument("--hq", type=int, default=32, help="decode_attn: query heads")
+    ap.add_argument("--hkv", type=int, default=8, help="decode_attn: KV heads")
     ap.add_argument("--tp", type=int, default=1, help="step: time one rank of a TP group, no all-reduce")
     ap.add_argument("--model", default="llama-3-8b-shape")
     ap.add_argument("--layers", type=int, default=0)
