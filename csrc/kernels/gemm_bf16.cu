@@ -10,15 +10,16 @@ using namespace gemm_detail;
 // streaming time is longer.  Model: one CTA streams ~kPerSmGBs from HBM, the
 // box at most kHbmGBs; choose the number of CTAs per tile minimising
 // bytes / bandwidth + fix-up.
-// SIL_SPLIT_REDUCE=spread: tile-aligned splits (swapped order) reduce their partials across
-// all contributors of a tile; otherwise the last contributor to arrive reduces them all.
-inline bool split_reduce_spread() {
+// SIL_SPLIT_REDUCE=cluster: tile-aligned splits (swapped order) run as one thread-block
+// cluster per tile and reduce through distributed shared memory; otherwise the last
+// contributor to arrive reduces the partials through global memory.
+inline bool split_reduce_cluster() {
   static const char* mode = std::getenv("SIL_SPLIT_REDUCE");
-  return mode != nullptr && mode[0] == 's';
+  return mode != nullptr && mode[0] == 'c';
 }
 
 inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms,
-                               bool spread = false) {
+                               bool cluster = false) {
   // Default: tile-aligned splits from a calibrated cost model when there are few tiles,
   // otherwise ("fill") one CTA per SM whenever the problem has >= 4 K blocks per CTA.  The
   // older latency model below is kept behind SIL_STREAMK=latency.
@@ -30,14 +31,15 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       // number s of K ranges so no CTA straddles two tiles.  Calibrated on B200 (32 tokens,
       // 4096 x {512, 4096} weights, s = 1, 2, 4): ~2.2 us fixed cost, ~48 GB/s streamed per
       // CTA, a split fix-up of ~2.5 us + 0.5 us per split; the box streams at most ~6000 GB/s.
-      // The spread reduction reads s partial slices per contributor instead of s whole
-      // partials in one CTA, so its per-split cost is far lower.
+      // A cluster reduces through shared memory with two cluster barriers, far cheaper than
+      // the global-memory fix-up; clusters hold at most kMaxClusterSplit CTAs.
       constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kBoxGBs = 6000.0;
-      const double kFixupUs = spread ? 1.5 : 2.5, kFixupPerSplitUs = spread ? 0.08 : 0.5;
+      const double kFixupUs = cluster ? 1.0 : 2.5, kFixupPerSplitUs = cluster ? 0.05 : 0.5;
+      const long long max_s = cluster ? kMaxClusterSplit : num_kb;
       const double tile_bytes = (double)bytes_per_kb * num_kb;
       long long best_s = 1;
       double best_t = 1e30;
-      for (long long s = 1; s <= num_kb && tiles * s <= sms; ++s) {
+      for (long long s = 1; s <= num_kb && s <= max_s && tiles * s <= sms; ++s) {
         const double t = kFixedUs + std::max(tile_bytes / s / (kPerCtaGBs * 1e3),
                                              tile_bytes * tiles / (kBoxGBs * 1e3)) +
                          (s > 1 ? kFixupUs + kFixupPerSplitUs * s : 0.0);
@@ -160,20 +162,20 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   a.group_m = 16;
   long long g;
   if (a.stream_k) {
-    const bool spread = swap && split_reduce_spread();
+    const bool cluster = swap && split_reduce_cluster();
     g = stream_k_grid(tiles, a.num_kb, (long long)((swap && swiglu ? 2 : 1) * BM + bn) * BK * 2, sms,
-                      spread);
+                      cluster);
     if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
-    // Whole tiles split into equal K ranges: every contributor of a tile takes part in its
-    // reduction (each CTA owns exactly one K range of one tile).
-    if (spread && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb)
+    // Whole tiles split into equal K ranges, one cluster per tile (each CTA owns exactly one
+    // K range of one tile).
+    if (cluster && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb && g / tiles <= kMaxClusterSplit)
       a.split_s = static_cast<int>(g / tiles);
   } else {
     g = std::min<long long>(sms, tiles);
   }
   const long long acc_cols = (swap && swiglu ? 2 : 1) * bn;
   TORCH_CHECK(g * 2 * acc_cols * BM <= ws.numel(), "gemm_bf16: workspace too small");
-  TORCH_CHECK((a.split_s > 1 ? 3 : 1) * tiles <= counters.numel(), "gemm_bf16: counter array too small");
+  TORCH_CHECK(tiles <= counters.numel(), "gemm_bf16: counter array too small");
   a.grid = static_cast<int>(g);
   if (swap) {
     switch (epi) {

@@ -75,20 +75,38 @@ struct GemmArgs {
   const int* grp_offsets;
   int num_groups;
   long long w_group_rows;
-  // Tile-aligned split-K (swapped order only): grid = tiles * split_s, CTA t*split_s + i
-  // owns the i-th K range of tile t, and the tile's partials are reduced by all of its
-  // contributors (see the epilogue).  0: stream-K with last-arriver reduction.
+  // Tile-aligned split-K in clusters (swapped order, non-grouped): grid = tiles * split_s,
+  // launched as clusters of split_s CTAs; CTA i of cluster t owns the i-th K range of tile
+  // t and the cluster reduces the tile through distributed shared memory.  0: stream-K
+  // with last-arriver reduction through global memory.
   int split_s;
 };
 
 constexpr int kMaxGroups = 1024;
-// A split contributor waits this long for the other partials of its tile before leaving
-// its share of the reduction to the tile's last contributor (which never waits).
-constexpr unsigned long long kSplitWaitNs = 20000ull;
+constexpr int kMaxClusterSplit = 8;  // portable cluster size
 
-__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Cluster-wide barrier (every thread of every CTA of the cluster): release this CTA's
+// shared-memory writes, acquire the peers'.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_cluster(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
 
@@ -601,114 +619,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             else store_chunk<EPI, SWAP, CW>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
           }
           if constexpr (EPI == kEpiAllReduce) ar_publish(args, par, epoch, sg.tile);
-        } else if (SWAP && EPI != kEpiAllReduce && args.split_s > 1) {
-          // Tile-aligned split.  The s contributors of tile t are CTAs t*s .. t*s+s-1, one K
-          // range each.  Every contributor stores its fp32 partial and arrives; the tile's
-          // items (row quarter x column chunk) are then reduced in contributor order
-          // (deterministic) by whoever claims them in the tile's claim mask: a contributor
-          // that sees all s arrivals within kSplitWaitNs claims its own items; the last
-          // contributor to arrive claims its own items, then every item still unclaimed.  So
-          // the reduction is spread over the tile's CTAs when they run together, and no CTA
-          // ever waits for one that is not running.
-          const int s = args.split_s;
-          const int ci = cta - sg.tile * s;
-          float* mine = args.ws + (long long)cta * 2 * C::ACC_COLS * BM;
+        } else if (SWAP && !GROUPED && EPI != kEpiAllReduce && args.split_s > 1) {
+          // Cluster split: keep this K range's fp32 partial in this CTA's shared memory
+          // ([ACC_COLS][BM], in the stage buffers, idle now that the only segment's MMAs are
+          // done); the cluster reduces the tile after the role loops.
+          static_assert(C::ACC_COLS * BM * 4 <= STAGES * C::STAGE_BYTES, "partial must fit the stages");
+          float* part = reinterpret_cast<float*>(smem);
 #pragma unroll 1
           for (int c0 = 0; c0 < C::ACC_COLS; c0 += CW) {
             uint32_t rv[CW];
             tmem_load<CW>(taddr + c0, rv);
 #pragma unroll
-            for (int t = 0; t < CW; ++t) __stcg(&mine[(c0 + t) * BM + row], __uint_as_float(rv[t]));
+            for (int t = 0; t < CW; ++t) part[(c0 + t) * BM + row] = __uint_as_float(rv[t]);
           }
           tc_fence_before();
           mbar_arrive(&acc_empty[b]);
-          int* ctr = args.counters + 3LL * sg.tile;  // [0] arrivals [1] claim mask [2] departures
-          __threadfence();
-          named_bar_sync(1, 128);
-          if (threadIdx.x == 64) {
-            int role = atomicAdd(&ctr[0], 1) == s - 1 ? 2 : 0;  // 2: last to arrive
-            if (role == 0) {
-              const uint64_t t0 = globaltimer_ns();
-              while (true) {
-                if (ld_acquire_gpu_s32(&ctr[0]) >= s) {
-                  role = 1;
-                  break;
-                }
-                if (globaltimer_ns() - t0 > kSplitWaitNs) break;
-              }
-            }
-            flags[1] = role;
-          }
-          named_bar_sync(1, 128);
-          const int role = flags[1];
-          if (role != 0) {
-            __threadfence();
-            // Items: row quarter (k & 3) x column chunk (k >> 2) of CWR columns, at most 32.
-            // Warp q of contributor ci owns the items k == 4*ci + q (mod 4s); it claims all of
-            // them with one atomicOr and reduces the ones it won.  The last contributor then
-            // claims what is left, each warp the items of its own row quarter.
-            constexpr int CWR = C::OUT_COLS / 8 > 8 ? C::OUT_COLS / 8 : 8;
-            constexpr int NI = 4 * (C::OUT_COLS / CWR);
-            static_assert(NI <= 32, "claim mask holds 32 items");
-            constexpr int NBW = 32 / (CWR * (C::kSwiGLU ? 2 : 1));  // partials per load batch
-            constexpr int NB = NBW < 1 ? 1 : NBW;
-            const float* base = args.ws + (long long)sg.tile * s * 2 * C::ACC_COLS * BM;
-            const long long cstride = 2LL * C::ACC_COLS * BM;
-            const int nslots = 4 * s;
-            const int slot = ci * 4 + q;
-#pragma unroll 1
-            for (int pass = 0; pass < (role == 2 ? 2 : 1); ++pass) {
-              unsigned cand = 0;
-              for (int k = q; k < NI; k += 4) {
-                const bool own = (k % nslots) == slot;
-                if (pass == 0 ? own : !own) cand |= 1u << k;
-              }
-              unsigned won = 0;
-              if (lane == 0 && cand != 0u) won = cand & ~atomicOr(reinterpret_cast<unsigned*>(&ctr[1]), cand);
-              won = __shfl_sync(0xffffffffu, won, 0);
-              while (won != 0u) {
-                const int k = __ffs(won) - 1;
-                won &= won - 1u;
-                const int c0 = (k >> 2) * CWR;
-                float v[CWR], uu[CWR];
-#pragma unroll
-                for (int t = 0; t < CWR; ++t) { v[t] = 0.f; uu[t] = 0.f; }
-#pragma unroll 1
-                for (int cb = 0; cb < s; cb += NB) {
-                  float pv[NB][CWR], pu[NB][CWR];
-#pragma unroll
-                  for (int q2 = 0; q2 < NB; ++q2)
-                    if (cb + q2 < s) {
-                      const float* p = base + (cb + q2) * cstride + row;
-#pragma unroll
-                      for (int t = 0; t < CWR; ++t) {
-                        pv[q2][t] = __ldcg(p + (c0 + t) * BM);
-                        if constexpr (C::kSwiGLU) pu[q2][t] = __ldcg(p + (c0 + UOFF + t) * BM);
-                      }
-                    }
-#pragma unroll
-                  for (int q2 = 0; q2 < NB; ++q2)
-                    if (cb + q2 < s) {
-#pragma unroll
-                      for (int t = 0; t < CWR; ++t) {
-                        v[t] += pv[q2][t];
-                        if constexpr (C::kSwiGLU) uu[t] += pu[q2][t];
-                      }
-                    }
-                }
-                store_chunk<EPI, SWAP, CWR>(args, m_glob, nt * C::OUT_COLS + c0, v, uu, tc.Mv, tc.Nv, tc.roff);
-              }
-            }
-          }
-          named_bar_sync(1, 128);
-          if (threadIdx.x == 64) {
-            __threadfence();
-            if (atomicAdd(&ctr[2], 1) == s - 1) {  // every contributor is done with the tile
-              ctr[0] = 0;
-              ctr[1] = 0;
-              ctr[2] = 0;
-            }
-          }
         } else {
           // Partial tile: slot 0 = this CTA's first segment, slot 1 = its last.
           const int slot = sg.first ? 0 : 1;
@@ -856,6 +781,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if constexpr (SWAP && !GROUPED && EPI != kEpiAllReduce) {
+    if (args.split_s > 1) {
+      // Every thread of every CTA of the cluster passes both barriers exactly once (all
+      // waits above are bounded and no thread leaves the kernel early), so the cluster
+      // cannot stall here.  Between them each CTA reduces its share of the tile's items
+      // (row quarter x column chunk) over the s partials in cluster-rank order, reading
+      // the peers' shared memory directly.
+      cluster_sync_all();
+      if (warp >= 2 && !skip) {
+        constexpr int CW = C::CW;
+        constexpr int UOFF = SWAP ? BN : BN / 2;
+        constexpr int CWR = C::OUT_COLS / 8 > 8 ? C::OUT_COLS / 8 : 8;
+        constexpr int NI = 4 * (C::OUT_COLS / CWR);
+        constexpr int NBW = 32 / (CWR * (C::kSwiGLU ? 2 : 1));
+        constexpr int NB = NBW < 1 ? 1 : NBW;
+        (void)CW;
+        const int s = args.split_s;
+        const uint32_t ci = cluster_ctarank();
+        const int tile = cta / s;
+        const TileCtx tc = make_ctx<false, SWAP>(args, tile, s_pref);
+        const uint32_t part = smem_u32(smem);
+        for (int k = static_cast<int>(ci) * 4 + (warp - 2); k < NI; k += 4 * s) {
+          const int r = (k & 3) * 32 + lane;
+          const int c0 = (k >> 2) * CWR;
+          float v[CWR], uu[CWR];
+#pragma unroll
+          for (int t = 0; t < CWR; ++t) { v[t] = 0.f; uu[t] = 0.f; }
+#pragma unroll 1
+          for (int cb = 0; cb < s; cb += NB) {
+            float pv[NB][CWR], pu[NB][CWR];
+#pragma unroll
+            for (int q2 = 0; q2 < NB; ++q2)
+              if (cb + q2 < s) {
+                const uint32_t base = mapa_cluster(part, static_cast<uint32_t>(cb + q2));
+#pragma unroll
+                for (int t = 0; t < CWR; ++t) {
+                  pv[q2][t] = ld_dsmem_f32(base + ((c0 + t) * BM + r) * 4);
+                  if constexpr (C::kSwiGLU) pu[q2][t] = ld_dsmem_f32(base + ((c0 + UOFF + t) * BM + r) * 4);
+                }
+              }
+#pragma unroll
+            for (int q2 = 0; q2 < NB; ++q2)
+              if (cb + q2 < s) {
+#pragma unroll
+                for (int t = 0; t < CWR; ++t) {
+                  v[t] += pv[q2][t];
+                  if constexpr (C::kSwiGLU) uu[t] += pu[q2][t];
+                }
+              }
+          }
+          store_chunk<EPI, SWAP, CWR>(args, tc.mt * BM + r, tc.nt * C::OUT_COLS + c0, v, uu, tc.Mv,
+                                      tc.Nv, tc.roff);
+        }
+      }
+      cluster_sync_all();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -896,11 +878,22 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (args.split_s > 1) {  // one cluster per tile: its K ranges reduce through shared memory
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = args.split_s;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = na;
   check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "gemm_bf16_kernel launch");
 }
 

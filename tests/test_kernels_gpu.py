@@ -40,12 +40,13 @@ def test_gemm_modes_and_splits(mode, splits):
 
 
 @pytest.mark.parametrize("T", [1, 16, 32, 64, 128])
-@pytest.mark.parametrize("splits", [2, 5, 13, 24])
+@pytest.mark.parametrize("splits", [2, 5, 8, 13, 24])
 @pytest.mark.parametrize("epi", ["plain", "residual", "swiglu", "fp32"])
 def test_gemm_tile_aligned_splits(T, splits, epi):
-    """Decode GEMMs with every tile split into equal K ranges: the partials are reduced by
-    all contributors of a tile (claimed items, contributor order), so the result matches
-    the fp32 reference and is bitwise identical from launch to launch."""
+    """Decode GEMMs with every tile split into equal K ranges (up to 8 per tile as one
+    thread-block cluster reducing through shared memory, more through the global-memory
+    fix-up): the partials are summed in K-range order, so the result matches the fp32
+    reference and is bitwise identical from launch to launch."""
     from swarm_inference_lab_b200.ops import gemm
     N, K = (768, 1536) if epi == "swiglu" else (640, 1536)   # 3 / 5 tiles of 128 rows, 24 K blocks
     g = torch.Generator(device="cuda").manual_seed(T * 31 + splits)
@@ -75,8 +76,7 @@ def test_gemm_tile_aligned_splits(T, splits, epi):
 
 
 def test_gemm_splits_beyond_resident_ctas():
-    """More split CTAs than SMs: contributors that cannot all be resident at once.  Early
-    contributors stop waiting and the last contributor of each tile reduces what is left."""
+    """More split CTAs than SMs (32 tiles x 8 K ranges): the tiles' clusters run in waves."""
     from swarm_inference_lab_b200.ops import gemm
     from swarm_inference_lab_b200.ops.workspace import get_workspace
     T, N, K = 32, 4096, 2048                       # 32 tiles x 8 splits = 256 CTAs
