@@ -10,12 +10,12 @@ using namespace gemm_detail;
 // streaming time is longer.  Model: one CTA streams ~kPerSmGBs from HBM, the
 // box at most kHbmGBs; choose the number of CTAs per tile minimising
 // bytes / bandwidth + fix-up.
-// SIL_SPLIT_REDUCE=cluster: tile-aligned splits (swapped order) run as one thread-block
-// cluster per tile and reduce through distributed shared memory; otherwise the last
-// contributor to arrive reduces the partials through global memory.
+// Tile-aligned splits (swapped order) run as one thread-block cluster per tile and reduce
+// through distributed shared memory; SIL_SPLIT_REDUCE=last selects the global-memory
+// fix-up by the last contributor instead.
 inline bool split_reduce_cluster() {
   static const char* mode = std::getenv("SIL_SPLIT_REDUCE");
-  return mode != nullptr && mode[0] == 'c';
+  return mode == nullptr || mode[0] != 'l';
 }
 
 inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms,
@@ -33,13 +33,17 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       // CTA, a split fix-up of ~2.5 us + 0.5 us per split; the box streams at most ~6000 GB/s.
       // A cluster reduces through shared memory with two cluster barriers, far cheaper than
       // the global-memory fix-up; clusters hold at most kMaxClusterSplit CTAs.
+      // Measured on B200 (32 tokens; 768 / 1792-SwiGLU / 4096 x {512, 4096}): ~2 us for the
+      // cluster fix-up.  A cluster split is only taken when every tile's cluster can be
+      // resident at once (clusters live inside one GPC, so fewer fit than SMs / s).
       constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kBoxGBs = 6000.0;
-      const double kFixupUs = cluster ? 1.0 : 2.5, kFixupPerSplitUs = cluster ? 0.05 : 0.5;
+      const double kFixupUs = cluster ? 2.0 : 2.5, kFixupPerSplitUs = cluster ? 0.05 : 0.5;
       const long long max_s = cluster ? kMaxClusterSplit : num_kb;
       const double tile_bytes = (double)bytes_per_kb * num_kb;
       long long best_s = 1;
       double best_t = 1e30;
       for (long long s = 1; s <= num_kb && s <= max_s && tiles * s <= sms; ++s) {
+        if (cluster && s > 1 && tiles > max_active_clusters(static_cast<int>(s))) continue;
         const double t = kFixedUs + std::max(tile_bytes / s / (kPerCtaGBs * 1e3),
                                              tile_bytes * tiles / (kBoxGBs * 1e3)) +
                          (s > 1 ? kFixupUs + kFixupPerSplitUs * s : 0.0);
@@ -168,7 +172,8 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
     if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
     // Whole tiles split into equal K ranges, one cluster per tile (each CTA owns exactly one
     // K range of one tile).
-    if (cluster && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb && g / tiles <= kMaxClusterSplit)
+    if (cluster && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb && g / tiles <= kMaxClusterSplit &&
+        max_active_clusters(static_cast<int>(g / tiles)) > 0)
       a.split_s = static_cast<int>(g / tiles);
   } else {
     g = std::min<long long>(sms, tiles);

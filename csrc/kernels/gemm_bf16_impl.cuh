@@ -897,6 +897,11 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
   check_cuda(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "gemm_bf16_kernel launch");
 }
 
+// Clusters of s split CTAs (one CTA per SM: every swapped-order configuration needs more
+// than half of an SM's shared memory) that the current device holds at once; 0 when such a
+// cluster cannot be launched.  Cached per device.
+int max_active_clusters(int s);
+
 template <int EPI>
 void dispatch_swap(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                    cudaStream_t st);

@@ -505,8 +505,11 @@ def test_universal_worker_abi_and_queue():
 
 def test_decode_split_heuristics():
     from swarm_inference_lab_b200.ops import attention, mla
-    assert attention.decode_splits(32, 8, 34) == 4          # 1024 CTAs: 6.92 of 7 waves busy
-    assert attention.decode_splits(64, 8, 34) == 2
-    assert attention.decode_splits(1, 8, 34) == 17          # <1 wave: fill the most SMs
-    assert attention.decode_splits(128, 8, 1) == 1          # never below 2 pages per split
+    assert attention.decode_splits(32, 8, 34) == 1          # 256 CTAs: one wave, nothing to merge
+    assert attention.decode_splits(64, 8, 34) == 1
+    assert attention.decode_splits(32, 1, 34) == 8          # one rank of TP8
+    assert attention.decode_splits(32, 4, 34) == 2
+    assert attention.decode_splits(1, 8, 34) == 8           # at most 8 splits
+    assert attention.decode_splits(1, 8, 6) == 3            # never below 2 pages per split
+    assert attention.decode_splits(128, 8, 1) == 1
     assert mla.decode_splits(32, 4096) == 4 and mla.decode_splits(1, 4096) == 64
