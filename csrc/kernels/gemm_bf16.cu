@@ -54,6 +54,19 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       }
       return tiles * best_s;
     }
+    if (cluster && tiles <= sms) {
+      // Between half a wave and one wave of tiles (the TP1 SwiGLU gate/up: 112 tiles):
+      // whole tiles, one CTA each, need no fix-up, while a stream-K fill of every SM
+      // straddles tiles and pays last-arriver fix-ups.  Measured on B200 (32 tokens,
+      // 28672 x 4096 SwiGLU): 40.5 us whole against 49.6 us filled.  Streamed per CTA
+      // ~60 GB/s, the box ~6400 GB/s, the fill's fix-up ~3 us.
+      constexpr double kFixedUs = 2.2, kPerCtaGBs = 60.0, kBoxGBs = 6400.0, kFillFixupUs = 3.0;
+      const double tile_bytes = (double)bytes_per_kb * num_kb;
+      const double box = tile_bytes * tiles / (kBoxGBs * 1e3);
+      const double t_whole = kFixedUs + std::max(tile_bytes / (kPerCtaGBs * 1e3), box);
+      const double t_fill = kFixedUs + std::max(tile_bytes * tiles / (sms * kPerCtaGBs * 1e3), box) + kFillFixupUs;
+      if (t_whole + 2.0 < t_fill) return tiles;
+    }
     return std::max<long long>(1, std::min<long long>(std::min<long long>(sms, units), (units + 3) / 4));
   }
   constexpr double kPerSmGBs = 110.0, kHbmGBs = 6000.0, kFixupUs = 3.0, kLatencyUs = 2.0;
