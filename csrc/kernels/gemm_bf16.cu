@@ -19,7 +19,8 @@ inline bool split_reduce_cluster() {
 }
 
 inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_kb, int sms,
-                               bool cluster = false) {
+                               bool cluster = false, bool* use_cluster = nullptr) {
+  if (use_cluster != nullptr) *use_cluster = false;
   // Default: tile-aligned splits from a calibrated cost model when there are few tiles,
   // otherwise ("fill") one CTA per SM whenever the problem has >= 4 K blocks per CTA.  The
   // older latency model below is kept behind SIL_STREAMK=latency.
@@ -36,22 +37,31 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       // Measured on B200 (32 tokens; 768 / 1792-SwiGLU / 4096 x {512, 4096}): ~2 us for the
       // cluster fix-up.  A cluster split is only taken when every tile's cluster can be
       // resident at once (clusters live inside one GPC, so fewer fit than SMs / s).
+      // Where a split's clusters do not all fit at once, that split is still priced with the
+      // global-memory fix-up (e.g. 48 tiles x 3 K ranges: 14.2 us, against 15.1 us for the
+      // 2-CTA clusters that fit).
       constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kBoxGBs = 6000.0;
-      const double kFixupUs = cluster ? 2.0 : 2.5, kFixupPerSplitUs = cluster ? 0.05 : 0.5;
-      const long long max_s = cluster ? kMaxClusterSplit : num_kb;
+      constexpr double kLastFixupUs = 2.5, kLastPerSplitUs = 0.5, kClusterFixupUs = 2.0,
+                       kClusterPerSplitUs = 0.05;
       const double tile_bytes = (double)bytes_per_kb * num_kb;
       long long best_s = 1;
+      bool best_cluster = false;
       double best_t = 1e30;
-      for (long long s = 1; s <= num_kb && s <= max_s && tiles * s <= sms; ++s) {
-        if (cluster && s > 1 && tiles > max_active_clusters(static_cast<int>(s))) continue;
-        const double t = kFixedUs + std::max(tile_bytes / s / (kPerCtaGBs * 1e3),
-                                             tile_bytes * tiles / (kBoxGBs * 1e3)) +
-                         (s > 1 ? kFixupUs + kFixupPerSplitUs * s : 0.0);
+      for (long long s = 1; s <= num_kb && tiles * s <= sms; ++s) {
+        const double stream = kFixedUs + std::max(tile_bytes / s / (kPerCtaGBs * 1e3),
+                                                  tile_bytes * tiles / (kBoxGBs * 1e3));
+        const bool fits = cluster && s > 1 && s <= kMaxClusterSplit &&
+                          tiles <= max_active_clusters(static_cast<int>(s));
+        const double t = s == 1 ? stream
+                         : fits ? stream + kClusterFixupUs + kClusterPerSplitUs * s
+                                : stream + kLastFixupUs + kLastPerSplitUs * s;
         if (t < best_t - 1e-9) {
           best_t = t;
           best_s = s;
+          best_cluster = fits;
         }
       }
+      if (use_cluster != nullptr) *use_cluster = best_cluster;
       return tiles * best_s;
     }
     if (cluster && tiles <= sms) {
@@ -180,13 +190,18 @@ void gemm_bf16(const at::Tensor& x, const at::Tensor& w, at::Tensor& out,
   long long g;
   if (a.stream_k) {
     const bool cluster = swap && split_reduce_cluster();
+    bool use_cluster = false;
     g = stream_k_grid(tiles, a.num_kb, (long long)((swap && swiglu ? 2 : 1) * BM + bn) * BK * 2, sms,
-                      cluster);
-    if (force_splits > 0) g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
+                      cluster, &use_cluster);
+    if (force_splits > 0) {
+      g = std::max<long long>(1, std::min<long long>(a.units, tiles * force_splits));
+      // Forced splits use clusters whenever a cluster of that size can be launched at all.
+      use_cluster = cluster && g > tiles && g % tiles == 0 && g / tiles <= kMaxClusterSplit &&
+                    max_active_clusters(static_cast<int>(g / tiles)) > 0;
+    }
     // Whole tiles split into equal K ranges, one cluster per tile (each CTA owns exactly one
     // K range of one tile).
-    if (cluster && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb && g / tiles <= kMaxClusterSplit &&
-        max_active_clusters(static_cast<int>(g / tiles)) > 0)
+    if (use_cluster && g > tiles && g % tiles == 0 && g / tiles <= a.num_kb && g / tiles <= kMaxClusterSplit)
       a.split_s = static_cast<int>(g / tiles);
   } else {
     g = std::min<long long>(sms, tiles);
