@@ -37,9 +37,10 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
       // Measured on B200 (32 tokens; 768 / 1792-SwiGLU / 4096 x {512, 4096}): ~2 us for the
       // cluster fix-up.  A cluster split is only taken when every tile's cluster can be
       // resident at once (clusters live inside one GPC, so fewer fit than SMs / s).
-      // Where a split's clusters do not all fit at once, that split is still priced with the
-      // global-memory fix-up (e.g. 48 tiles x 3 K ranges: 14.2 us, against 15.1 us for the
-      // 2-CTA clusters that fit).
+      // Splits whose clusters do not all fit at once are skipped in cluster mode: priced with
+      // the global-memory fix-up they can win in isolation (48 tiles x 3 K ranges: 14.3 us
+      // against 15.4 us for the 2-CTA clusters that fit) but the decode step got slower with
+      // them (4.96 against 4.89 ms at TP1).
       constexpr double kFixedUs = 2.2, kPerCtaGBs = 48.0, kBoxGBs = 6000.0;
       constexpr double kLastFixupUs = 2.5, kLastPerSplitUs = 0.5, kClusterFixupUs = 2.0,
                        kClusterPerSplitUs = 0.05;
@@ -52,6 +53,7 @@ inline long long stream_k_grid(long long tiles, int num_kb, long long bytes_per_
                                                   tile_bytes * tiles / (kBoxGBs * 1e3));
         const bool fits = cluster && s > 1 && s <= kMaxClusterSplit &&
                           tiles <= max_active_clusters(static_cast<int>(s));
+        if (cluster && s > 1 && !fits) continue;
         const double t = s == 1 ? stream
                          : fits ? stream + kClusterFixupUs + kClusterPerSplitUs * s
                                 : stream + kLastFixupUs + kLastPerSplitUs * s;
