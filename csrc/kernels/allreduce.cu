@@ -28,6 +28,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <vector>
 
 #include "sil/host.h"
@@ -48,7 +49,16 @@ struct OneShotArgs {
   __nv_bfloat16* h;      // [T, H] contiguous: h += sum of partials
   long long n;           // T * H
   int* status;
+  int late_trigger;      // 1: let the next kernel launch only after this one's exchange
 };
+
+// SIL_AR_LATE_TRIGGER=1 moves the programmatic-launch trigger of the one-shot kernels from
+// their first instruction to after the exchange, so the next GEMM's CTAs (and their weight
+// prefetch) do not start while this kernel is still waiting on its peers.
+inline int ar_late_trigger() {
+  static const char* v = std::getenv("SIL_AR_LATE_TRIGGER");
+  return v != nullptr && v[0] == '1' ? 1 : 0;
+}
 
 __device__ __forceinline__ uint32_t ld_acq(const uint32_t* p) {
   uint32_t v;
@@ -140,7 +150,7 @@ __device__ __forceinline__ void bump_epoch(const OneShotArgs& a, uint32_t epoch)
 
 __global__ void __launch_bounds__(kThreadsAR)
     oneshot_allreduce_kernel(const OneShotArgs a) {
-  pdl_trigger();
+  if (!a.late_trigger) pdl_trigger();
   pdl_wait();  // the partial comes from the previous kernel (the row-parallel GEMM)
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
   const int par = epoch & 1;
@@ -161,6 +171,7 @@ __global__ void __launch_bounds__(kThreadsAR)
       reinterpret_cast<uint4*>(a.h)[u] = o;
     }
   }
+  if (a.late_trigger) pdl_trigger();
   bump_epoch(a, epoch);
 }
 
@@ -171,7 +182,7 @@ __global__ void __launch_bounds__(kThreadsAR)
                                   float eps, __nv_bfloat16* __restrict__ x_out) {
   extern __shared__ float row[];  // H fp32 values of h after the sum
   __shared__ float red[32];
-  pdl_trigger();
+  if (!a.late_trigger) pdl_trigger();
   pdl_wait();
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(a.peers[a.rank]) + 1u;
   const int par = epoch & 1;
@@ -226,6 +237,7 @@ __global__ void __launch_bounds__(kThreadsAR)
       reinterpret_cast<uint4*>(x_out)[base + u] = q;
     }
   }
+  if (a.late_trigger) pdl_trigger();
   bump_epoch(a, epoch);
 }
 
@@ -259,6 +271,7 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
   a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.n = (long long)T * H;
   a.status = status.data_ptr<int>();
+  a.late_trigger = ar_late_trigger();
   launch_pdl(oneshot_allreduce_norm_kernel, dim3(T), dim3(kThreadsAR), H * sizeof(float),
              at::cuda::getCurrentCUDAStream(), "oneshot_allreduce_norm launch", a, H,
              reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr()), static_cast<float>(eps),
@@ -290,6 +303,7 @@ void oneshot_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t
   a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.n = n;
   a.status = status.data_ptr<int>();
+  a.late_trigger = ar_late_trigger();
   const long long units = n / 8;
   // Two 16-byte units per thread: 32 CTAs pull 2 MB (32 tokens x 4096 x 8 ranks) in parallel.
   const int grid = static_cast<int>(std::max<long long>(
