@@ -143,6 +143,18 @@ def run_ours(args, rank, world, local):
     if dp:
         prompts = prompts[rank * B_loc:(rank + 1) * B_loc]
     params = SamplingParams(max_new_tokens=new_tokens)
+    # ---------------- untimed warm-up prefill of the same shape (other random prompts, one
+    # token each, then freed): loads the kernels and grows the allocator's pools, as a
+    # serving engine would have done before the measured requests arrive.  The reference
+    # arm warms up the same way (a full-size generate before its timed run).
+    wg = torch.Generator().manual_seed(1)
+    warm = torch.randint(0, cfg.vocab_size, (len(prompts), P), generator=wg).tolist()
+    for p in warm:
+        eng.add_request(p, SamplingParams(max_new_tokens=1))
+    while eng.scheduler.has_work():
+        eng.step()
+    eng.scheduler.pop_finished()
+    torch.cuda.synchronize()
     for p in prompts:
         eng.add_request(p, params)
     # ---------------- prefill (TTFT): the whole batch in one varlen pass
