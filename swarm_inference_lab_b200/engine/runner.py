@@ -26,6 +26,29 @@ from .kv_cache import PAGE, PagedKVCache
 BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128)
 
 
+def prefill_host_batch(ids: list[list[int]], starts: list[int], pages: list[list[int]],
+                       max_pages: int) -> dict:
+    """Host-side arrays of a varlen prefill batch, built with array operations (a 32 x 2048
+    token batch is 65536 rows; per-token Python loops cost tens of milliseconds of TTFT):
+    flat token ids, absolute positions, KV-cache slots (page * PAGE + offset), per-sequence
+    context lengths, the block table and the cumulative query offsets."""
+    B = len(ids)
+    lens = np.fromiter((len(x) for x in ids), dtype=np.int64, count=B)
+    cu = np.zeros(B + 1, dtype=np.int64)
+    np.cumsum(lens, out=cu[1:])
+    flat = (np.concatenate([np.asarray(x, dtype=np.int64) for x in ids]) if B
+            else np.zeros(0, dtype=np.int64))
+    st = np.asarray(starts, dtype=np.int64)
+    seq_of_row = np.repeat(np.arange(B), lens)
+    pos = np.arange(int(cu[-1]), dtype=np.int64) - cu[:-1][seq_of_row] + st[seq_of_row]
+    bt = np.zeros((B, max_pages), dtype=np.int64)
+    for i, pg in enumerate(pages):
+        bt[i, :len(pg)] = pg
+    slots = bt[seq_of_row, pos // PAGE] * PAGE + pos % PAGE
+    return {"ids": flat, "positions": pos, "slots": slots, "seq_lens": st + lens,
+            "block_table": bt, "cu": cu, "max_q_len": int(lens.max()) if B else 0}
+
+
 def bucket_for(n: int) -> int:
     for b in BUCKETS:
         if n <= b:
@@ -68,32 +91,19 @@ class ModelRunner:
         Returns the greedy token of each sequence's last row (device int64), or of every
         row with ``all_rows`` (multi-token verification for speculative decoding)."""
         dev = self.device
-        B = len(ids)
-        flat, pos, slots, cu = [], [], [], [0]
-        seq_lens, last = [], []
-        for i in range(B):
-            n = len(ids[i])
-            flat.extend(ids[i])
-            p = list(range(starts[i], starts[i] + n))
-            pos.extend(p)
-            slots.extend(pages[i][q // PAGE] * PAGE + q % PAGE for q in p)
-            cu.append(cu[-1] + n)
-            seq_lens.append(starts[i] + n)
-            last.append(cu[-1] - 1)
-        bt = torch.zeros((B, self.max_pages), dtype=torch.int32)
-        for i in range(B):
-            bt[i, : len(pages[i])] = torch.tensor(pages[i], dtype=torch.int32)
+        h = prefill_host_batch(ids, starts, pages, self.max_pages)
+        to = lambda a, dt: torch.from_numpy(a).to(dt).to(dev, non_blocking=True)  # noqa: E731
         fb = ForwardBatch(
-            ids=torch.tensor(flat, dtype=torch.int64).to(dev, non_blocking=True),
-            positions=torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True),
-            slots=torch.tensor(slots, dtype=torch.int32).to(dev, non_blocking=True),
-            seq_lens=torch.tensor(seq_lens, dtype=torch.int32).to(dev, non_blocking=True),
-            block_table=bt.to(dev, non_blocking=True),
-            last_idx=(torch.arange(cu[-1], dtype=torch.int64) if all_rows
-                      else torch.tensor(last, dtype=torch.int64)).to(dev, non_blocking=True),
+            ids=to(h["ids"], torch.int64),
+            positions=to(h["positions"], torch.int32),
+            slots=to(h["slots"], torch.int32),
+            seq_lens=to(h["seq_lens"], torch.int32),
+            block_table=to(h["block_table"], torch.int32),
+            last_idx=(torch.arange(int(h["cu"][-1]), dtype=torch.int64).to(dev, non_blocking=True)
+                      if all_rows else to(h["cu"][1:] - 1, torch.int64)),
             is_decode=False,
-            cu_q=torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True),
-            max_q_len=max(len(x) for x in ids),
+            cu_q=to(h["cu"], torch.int32),
+            max_q_len=int(h["max_q_len"]),
         )
         return self.model.forward(fb, self.kv)
 
