@@ -242,6 +242,85 @@ __global__ void argmax_kernel(const float* __restrict__ logits, long long ld, in
   }
 }
 
+// Greedy argmax of one logits row split over a cluster of kArgmaxParts CTAs: CTA p scans
+// its quarter of the vocabulary (a CTA streams ~50 GB/s, so one CTA per 128k-entry row was
+// latency-bound), keeps its (value, index) in shared memory, and after a cluster barrier CTA
+// 0 combines the parts through distributed shared memory (largest value, lowest index on
+// ties, as the single-CTA kernel).  Every thread passes both cluster barriers exactly once.
+constexpr int kArgmaxParts = 4;
+
+__global__ void __launch_bounds__(1024)
+    argmax_cluster_kernel(const float* __restrict__ logits, long long ld, int V,
+                          long long* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ float part_v;
+  __shared__ int part_i;
+  pdl_trigger();
+  pdl_wait();
+  uint32_t part;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(part));
+  const int row_id = blockIdx.x / kArgmaxParts;
+  const float* row = logits + row_id * ld;
+  const int chunk = ((V + kArgmaxParts - 1) / kArgmaxParts + 3) & ~3;
+  const int lo = static_cast<int>(part) * chunk;
+  const int hi = min(V, lo + chunk);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  if ((ld % 4 == 0) && (V % 4 == 0)) {
+    for (int i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+      const float4 q = *reinterpret_cast<const float4*>(row + i);
+      if (q.x > best) { best = q.x; bi = i; }
+      if (q.y > best) { best = q.y; bi = i + 1; }
+      if (q.z > best) { best = q.z; bi = i + 2; }
+      if (q.w > best) { best = q.w; bi = i + 3; }
+    }
+  } else {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float v = row[i];
+      if (v > best) { best = v; bi = i; }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) { part_v = best; part_i = bi; }
+  }
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+  if (part == 0 && threadIdx.x == 0) {
+    float b = part_v;
+    int i0 = part_i;
+    for (uint32_t p = 1; p < kArgmaxParts; ++p) {
+      uint32_t av, ai;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(av) : "r"(smem_u32(&part_v)), "r"(p));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ai) : "r"(smem_u32(&part_i)), "r"(p));
+      float ov;
+      int oi;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ov) : "r"(av) : "memory");
+      asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(oi) : "r"(ai) : "memory");
+      if (ov > b || (ov == b && oi < i0)) { b = ov; i0 = oi; }
+    }
+    out[row_id] = i0 == 0x7fffffff ? 0 : i0;
+  }
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 }  // namespace
 
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
@@ -329,9 +408,34 @@ void argmax(const at::Tensor& logits, at::Tensor& out) {
   const int T = logits.size(0);
   if (T == 0) return;
   c10::cuda::CUDAGuard guard(logits.device());
-  launch_pdl(argmax_kernel, dim3(T), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
-             "argmax launch", (const float*)logits.data_ptr<float>(), (long long)logits.stride(0),
-             (int)logits.size(1), reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
+  const float* lp = logits.data_ptr<float>();
+  const long long ld = logits.stride(0);
+  const int V = static_cast<int>(logits.size(1));
+  long long* op = reinterpret_cast<long long*>(out.data_ptr<int64_t>());
+  if (V < 4096) {  // short rows: one CTA per row
+    launch_pdl(argmax_kernel, dim3(T), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
+               "argmax launch", lp, ld, V, op);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T * kArgmaxParts, 1, 1);
+  cfg.blockDim = dim3(1024, 1, 1);
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = kArgmaxParts;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  check_cuda(cudaLaunchKernelEx(&cfg, argmax_cluster_kernel, lp, ld, V, op), "argmax launch");
 }
 
 }  // namespace sil

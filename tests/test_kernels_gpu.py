@@ -248,6 +248,23 @@ def test_argmax_ties_lowest():
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("V", [128256, 4096, 1000, 163840])
+def test_argmax_split_rows(V):
+    """Rows split over a cluster of CTAs (V >= 4096) or one CTA (short rows): the maximum
+    in any quarter of the row, ties across quarters resolved to the lowest index."""
+    from swarm_inference_lab_b200.ops import sampling
+    g = torch.Generator(device="cuda").manual_seed(V)
+    x = torch.randn(33, V, device="cuda", generator=g)
+    x[0, V - 1] = 50.0                       # in the last quarter
+    x[1, 3] = 50.0
+    x[1, V - 2] = 50.0                       # tie across the first and last quarter
+    x[2, V // 2] = 50.0
+    x[2, V // 2 + 1] = 50.0                  # tie inside one quarter
+    out = sampling.argmax(x)
+    assert out[0].item() == V - 1 and out[1].item() == 3 and out[2].item() == V // 2
+    assert torch.equal(out, torch.argmax(x, dim=1))
+
+
 def test_status_word_clean():
     from swarm_inference_lab_b200.ops.workspace import get_workspace
     get_workspace().check()
