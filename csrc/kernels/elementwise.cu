@@ -114,64 +114,6 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
   }
 }
 
-// RMSNorm(+residual) for many rows (prefill): one warp per row, the row held in registers
-// (NV 16-byte chunks per lane, H = 256 * NV), one pass over memory and no block barriers.
-// Same arithmetic as rmsnorm_kernel: x + r rounded to bf16, fp32 sum of squares, both
-// products rounded to bf16.
-template <int NV>
-__global__ void __launch_bounds__(256)
-    rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
-                        const __nv_bfloat16* __restrict__ r, long long ldr,
-                        __nv_bfloat16* __restrict__ res_out, long long ldro,
-                        const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                        long long ldy, int T, float eps) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int H = 256 * NV;
-  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= T) return;
-  float v[NV][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int c = 0; c < NV; ++c) {
-    const int i = (c * 32 + lane) * 8;
-    const uint4 q = *reinterpret_cast<const uint4*>(x + row * ldx + i);
-    v[c][0] = bf16_lo(q.x); v[c][1] = bf16_hi(q.x); v[c][2] = bf16_lo(q.y); v[c][3] = bf16_hi(q.y);
-    v[c][4] = bf16_lo(q.z); v[c][5] = bf16_hi(q.z); v[c][6] = bf16_lo(q.w); v[c][7] = bf16_hi(q.w);
-    if (r != nullptr) {
-      const uint4 p = *reinterpret_cast<const uint4*>(r + row * ldr + i);
-      const float u[8] = {bf16_lo(p.x), bf16_hi(p.x), bf16_lo(p.y), bf16_hi(p.y),
-                          bf16_lo(p.z), bf16_hi(p.z), bf16_lo(p.w), bf16_hi(p.w)};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[c][j] = __bfloat162float(__float2bfloat16_rn(v[c][j] + u[j]));
-      uint4 o;
-      o.x = pack_bf16x2(v[c][0], v[c][1]); o.y = pack_bf16x2(v[c][2], v[c][3]);
-      o.z = pack_bf16x2(v[c][4], v[c][5]); o.w = pack_bf16x2(v[c][6], v[c][7]);
-      *reinterpret_cast<uint4*>(res_out + row * ldro + i) = o;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
-  }
-  ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / H + eps);
-#pragma unroll
-  for (int c = 0; c < NV; ++c) {
-    const int i = (c * 32 + lane) * 8;
-    const uint4 wq = *reinterpret_cast<const uint4*>(w + i);
-    const float wv[8] = {bf16_lo(wq.x), bf16_hi(wq.x), bf16_lo(wq.y), bf16_hi(wq.y),
-                         bf16_lo(wq.z), bf16_hi(wq.z), bf16_lo(wq.w), bf16_hi(wq.w)};
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      o[j] = __bfloat162float(__float2bfloat16_rn(wv[j] * __bfloat162float(__float2bfloat16_rn(v[c][j] * rstd))));
-    uint4 q;
-    q.x = pack_bf16x2(o[0], o[1]); q.y = pack_bf16x2(o[2], o[3]);
-    q.z = pack_bf16x2(o[4], o[5]); q.w = pack_bf16x2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(y + row * ldy + i) = q;
-  }
-}
-
 // One warp per (token, head).  qkv: [T, (Hq + 2*Hkv) * 128]; q heads are
 // rotated in place; k heads are normalised/rotated and written with v into
 // the paged cache at `slots[t]` (= page * 64 + offset; negative = skip).
@@ -408,21 +350,6 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
                 "rmsnorm: e4m3 output [T, H] with scales [T, H/128] (H % 128 == 0)");
     qp = reinterpret_cast<uint8_t*>(yq->data_ptr());
     sp = ys->data_ptr<float>();
-  }
-  const bool aligned = x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0 && ldr % 8 == 0 && ldro % 8 == 0;
-  if (qp == nullptr && T >= 1024 && aligned && (H == 2048 || H == 4096)) {
-    // Many rows: one warp per row, 8 rows per 256-thread block.
-    const dim3 grid((T + 7) / 8);
-    auto go = [&](auto kern) {
-      launch_pdl(kern, grid, dim3(256), 0, at::cuda::getCurrentCUDAStream(), "rmsnorm rows launch",
-                 reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0), rp, ldr,
-                 rop, ldro, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-                 reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), (long long)y.stride(0), T,
-                 static_cast<float>(eps));
-    };
-    if (H == 4096) go(rmsnorm_rows_kernel<16>);
-    else go(rmsnorm_rows_kernel<8>);
-    return;
   }
   const int threads = std::min(1024, std::max(32, ((H / 8 + 31) / 32) * 32));
   launch_pdl(rmsnorm_kernel, dim3(T), dim3(threads), H * sizeof(float),
