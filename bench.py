@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--comm", choices=["auto", "fused", "oneshot", "nvls", "nccl"], default="auto",
+    ap.add_argument("--comm", choices=["auto", "fused", "oneshot", "ll", "nvls", "nccl"], default="auto",
                     help="auto: fused EP dispatch/combine for MLA models; NCCL all-reduce for dense "
                          "TP (measured faster than the fused GEMM+all-reduce at TP2 and TP8)")
     ap.add_argument("--model", default="llama-3-8b-shape")
@@ -124,6 +124,11 @@ def run_ours(args, rank, world, local):
             comm = NvlsTPComm(comm, torch.device("cuda", local), max_tokens=128,
                               hidden=cfg.hidden_size)
             comm_kind = "gemm + nvls_two_shot_allreduce_rmsnorm (decode) + nccl (prefill)"
+        elif args.comm == "ll":
+            from swarm_inference_lab_b200.parallel.ll_tp import LLTPComm
+            comm = LLTPComm(comm, torch.device("cuda", local), max_tokens=128,
+                            hidden=cfg.hidden_size)
+            comm_kind = "gemm + ll_allreduce_norm (decode; flag inside each word) + nccl (prefill)"
         elif args.comm == "oneshot":
             from swarm_inference_lab_b200.parallel.oneshot_tp import OneShotTPComm
             comm = OneShotTPComm(comm, torch.device("cuda", local), max_tokens=128,

@@ -8,6 +8,8 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <set>
+#include <utility>
 #include <stdexcept>
 #include <string>
 
@@ -66,6 +68,19 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
     throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string(r));
   }
   return map;
+}
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device.
+// The attribute is per device, so it is set once per (kernel, device) pair.
+inline void set_smem_limit(const void* kern, int bytes, const char* what) {
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kern, dev})) return;
+  check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  done.insert({kern, dev});
 }
 
 inline int device_sm_count() {

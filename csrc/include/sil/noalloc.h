@@ -24,6 +24,14 @@
 // kernels overlap on the GPU (different streams without ordering, or several
 // host threads) race on the array and produce wrong results; serialise them.
 //
+// Status: the kernel reports failures in a device status word inside the array
+// instead of faulting: 1 when a wait for a TMA page load gave up, 5 when a
+// block-table entry lies outside [0, num_pages) (that page is not loaded).  The
+// output of such a call is incomplete.  The word is cleared at the start of each
+// call, so read it with sil_noalloc_status() after the call and before the next
+// one.  Every wait is bounded (2 s by default; sil_noalloc_set_wait_limit_ns
+// changes the bound for later calls on the current device).
+//
 // Set-up: the first call on each device (with that device current) looks up
 // the array's device address with cudaGetSymbolAddress and sets the kernel's
 // shared-memory attribute; make that first call before any stream capture.
@@ -46,12 +54,23 @@ extern "C" {
 // block_table: [batch, bt_stride] int32 page ids; seq_lens: [batch] int32 (context
 //           length including the token being decoded)
 // out:      [batch, q_heads * 128] bf16, rows out_stride elements apart
+// q_stride must be even and >= q_heads * 128, out_stride >= q_heads * 128,
+// bt_stride > 0.
 // Returns SIL_NOALLOC_OK or a negative error code.
 int sil_paged_decode_noalloc(const void* q, long long q_stride, const void* k_cache,
                              const void* v_cache, long long num_pages, int kv_heads,
                              const int* block_table, long long bt_stride, const int* seq_lens,
                              void* out, long long out_stride, int batch, int q_heads, float scale,
                              int num_splits, cudaStream_t stream);
+
+// Copies the device status word of the current device's array into *host_out
+// (0 = the last call ran clean) and waits for `stream`.  Order it after the call
+// on the same stream.
+int sil_noalloc_status(int* host_out, cudaStream_t stream);
+
+// Bounds every wait of later calls on the current device to `ns` nanoseconds
+// (0 restores the default of 2 s).  Waits for `stream`.
+int sil_noalloc_set_wait_limit_ns(unsigned long long ns, cudaStream_t stream);
 
 // Message of the last error returned on this host thread ("" when none).
 const char* sil_noalloc_last_error(void);

@@ -48,6 +48,16 @@ __device__ __forceinline__ void raise_status(int* status, int code) {
   atomicCAS(status, 0, code);
 }
 
+// The status block is four int32 words: [0] the sticky status code, [1] unused,
+// [2..3] the wait limit in nanoseconds as one little-endian uint64 (0 selects the
+// compile-time default).  The host sets the limit at run time (tests use ~1 ms to
+// make a wait on a flag that nothing raises give up quickly); kernels read it only
+// once a wait has already failed its first try, so the fast path never loads it.
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* status) {
+  const uint64_t v = *reinterpret_cast<const volatile unsigned long long*>(status + 2);
+  return v != 0 ? v : SIL_WAIT_TIMEOUT_NS;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
@@ -94,17 +104,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(status);
   uint32_t it = 0;
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
     if ((++it & 63u) == 0) {
       if (load_status(status) != 0) return false;
-      if (globaltimer_ns() - t0 > SIL_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > limit) {
         raise_status(status, code);
         return false;
       }
     }
   }
+}
+
+// Wait for a phase on the error path, ignoring the status word: a kernel whose
+// wait gave up must still let its own TMA copies in flight land before it reuses
+// or releases the shared memory they write.  Bounded by a fixed 100 ms.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(a, parity)) {
+    if (globaltimer_ns() - t0 > 100000000ull) return false;
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -107,7 +107,7 @@ __device__ __forceinline__ bool wait_slice(const OneShotArgs& a, uint32_t epoch)
     // needs this rank's flag for the current epoch to go on), and epochs only grow.
     while (static_cast<int>(ld_acq(f) - epoch) < 0) {
       if ((++it & 255u) == 0) {
-        if (load_status(a.status) != 0 || globaltimer_ns() - t0 > SIL_WAIT_TIMEOUT_NS) {
+        if (load_status(a.status) != 0 || globaltimer_ns() - t0 > wait_limit_ns(a.status)) {
           raise_status(a.status, kStatusTimeoutPeer);
           ok = 0;
           break;

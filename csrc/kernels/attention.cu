@@ -48,6 +48,8 @@ struct AttnArgs {
   const int* seq_lens;    // context length incl. the new tokens
   const int* cu_q;        // prefill: [B+1] offsets of each sequence's queries
   int Hq, Hkv, G;
+  int num_pages;          // pages of the cache; a block-table entry outside [0, num_pages)
+                          // raises kStatusBadArgument instead of being loaded
   float scale_log2;       // softmax scale * log2(e)
   int num_splits;
   float* ws_o;            // decode split partials
@@ -63,6 +65,26 @@ __device__ __forceinline__ void issue_page(uint8_t* stage, const CUtensorMap* tk
   tma_load_2d(stage + kTileBytes, tk, bar, 64, row);
   tma_load_2d(stage + kKVBytes, tv, bar, 0, row);
   tma_load_2d(stage + kKVBytes + kTileBytes, tv, bar, 64, row);
+}
+
+// Issues the TMA loads of page `pid` of kv-head h into `stage`, after checking the
+// page id against the cache.  A bad id raises kStatusBadArgument and loads nothing;
+// the consumer's wait on that stage then gives up on the raised status.
+__device__ __forceinline__ bool issue_checked(uint8_t* stage, const CUtensorMap* tk,
+                                              const CUtensorMap* tv, uint64_t* bar, int pid,
+                                              const AttnArgs& a, int h) {
+  if (static_cast<unsigned>(pid) >= static_cast<unsigned>(a.num_pages)) {
+    raise_status(a.status, kStatusBadArgument);
+    return false;
+  }
+  issue_page(stage, tk, tv, bar, (pid * a.Hkv + h) * kPage);
+  return true;
+}
+
+// Error path: lets the loads of pages [consumed, issued) land before the shared
+// memory they target is reused or the CTA exits (thread 0, which issued them).
+__device__ __forceinline__ void drain_pages(uint64_t* full, int consumed, int issued) {
+  for (int j = consumed; j < issued; ++j) mbar_drain(&full[j % kStages], (j / kStages) & 1);
 }
 
 // Address of the ldmatrix row for K/V tile rows `r` and 8-dim chunk `c` (0..15).
@@ -103,10 +125,13 @@ __global__ void __launch_bounds__(128)
   }
   __syncthreads();
   const bool skip = sflag[0] != 0;
+  int issued = 0, consumed = 0;  // pages loaded / waited for (thread 0's view)
   if (!skip && threadIdx.x == 0) {
-    for (int i = 0; i < min(count, kStages); ++i)
-      issue_page(smem + i * kStageBytes, &tmK, &tmV, &full[i],
-                 (bt[p_begin + i] * args.Hkv + h) * kPage);
+    for (int i = 0; i < min(count, kStages); ++i) {
+      if (!issue_checked(smem + i * kStageBytes, &tmK, &tmV, &full[i], bt[p_begin + i], args, h))
+        break;
+      issued = i + 1;
+    }
   }
 
   // Q fragments: rows = query heads of this group (g and g+8), K-dim = head dim.
@@ -142,6 +167,7 @@ __global__ void __launch_bounds__(128)
     const int s = i % kStages;
     if (alive && !mbar_wait(&full[s], (i / kStages) & 1, args.status, kStatusTimeoutFull))
       alive = false;
+    if (alive) consumed = i + 1;
     if (alive) {
       const uint32_t kbase = smem_u32(smem + s * kStageBytes);
       const uint32_t vbase = kbase + kKVBytes;
@@ -215,10 +241,13 @@ __global__ void __launch_bounds__(128)
       }
     }
     __syncthreads();
-    if (alive && threadIdx.x == 0 && i + kStages < count)
-      issue_page(smem + s * kStageBytes, &tmK, &tmV, &full[s],
-                 (bt[p_begin + i + kStages] * args.Hkv + h) * kPage);
+    if (alive && threadIdx.x == 0 && i + kStages < count && issued == i + kStages &&
+        issue_checked(smem + s * kStageBytes, &tmK, &tmV, &full[s], bt[p_begin + i + kStages],
+                      args, h))
+      issued = i + kStages + 1;
   }
+  if (threadIdx.x == 0 && consumed < issued) drain_pages(full, consumed, issued);
+  __syncthreads();
 
   // Full row sums (the 4 threads of a row hold disjoint token subsets).
 #pragma unroll
@@ -335,9 +364,12 @@ __global__ void __launch_bounds__(128)
   }
   __syncthreads();
   const bool skip = sflag[0] != 0;
+  int issued = 0, consumed = 0;  // pages loaded / waited for (thread 0's view)
   if (!skip && threadIdx.x == 0) {
-    for (int i = 0; i < min(n_pages, kStages); ++i)
-      issue_page(smem + i * kStageBytes, &tmK, &tmV, &full[i], (bt[i] * args.Hkv + h) * kPage);
+    for (int i = 0; i < min(n_pages, kStages); ++i) {
+      if (!issue_checked(smem + i * kStageBytes, &tmK, &tmV, &full[i], bt[i], args, h)) break;
+      issued = i + 1;
+    }
   }
   // Q fragments for this warp's 16 rows.
   const int row_lo = q0 + warp * 16 + g;
@@ -372,6 +404,7 @@ __global__ void __launch_bounds__(128)
     const int s = i % kStages;
     if (alive && !mbar_wait(&full[s], (i / kStages) & 1, args.status, kStatusTimeoutFull))
       alive = false;
+    if (alive) consumed = i + 1;
     // Warps whose queries all precede this page have nothing to add.
     if (alive && i * kPage <= warp_last_pos) {
       const uint32_t kbase = smem_u32(smem + s * kStageBytes);
@@ -449,10 +482,11 @@ __global__ void __launch_bounds__(128)
       }
     }
     __syncthreads();
-    if (alive && threadIdx.x == 0 && i + kStages < n_pages)
-      issue_page(smem + s * kStageBytes, &tmK, &tmV, &full[s],
-                 (bt[i + kStages] * args.Hkv + h) * kPage);
+    if (alive && threadIdx.x == 0 && i + kStages < n_pages && issued == i + kStages &&
+        issue_checked(smem + s * kStageBytes, &tmK, &tmV, &full[s], bt[i + kStages], args, h))
+      issued = i + kStages + 1;
   }
+  if (threadIdx.x == 0 && consumed < issued) drain_pages(full, consumed, issued);
   if (skip) return;
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
@@ -519,6 +553,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.G = Hq / Hkv;
+  a.num_pages = static_cast<int>(k_cache.size(0));
   a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   int S = std::max<int64_t>(1, num_splits);
   const long long need_o = (long long)B * Hkv * S * a.G * kD;
@@ -532,13 +567,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
   CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
-  static bool configured = false;
-  if (!configured) {
-    check_cuda(cudaFuncSetAttribute(paged_decode_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
-               "cudaFuncSetAttribute(decode)");
-    configured = true;
-  }
+  set_smem_limit(reinterpret_cast<const void*>(paged_decode_kernel), kSmemBytes, "cudaFuncSetAttribute(decode)");
   dim3 grid(S, Hkv, B);
   launch_pdl(paged_decode_kernel, grid, dim3(128), kSmemBytes, at::cuda::getCurrentCUDAStream(),
              "paged_decode launch", tk, tv, a);
@@ -570,16 +599,11 @@ void paged_prefill(const at::Tensor& q, const at::Tensor& k_cache, const at::Ten
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.G = Hq / Hkv;
+  a.num_pages = static_cast<int>(k_cache.size(0));
   a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   a.status = status.data_ptr<int>();
   CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
-  static bool configured = false;
-  if (!configured) {
-    check_cuda(cudaFuncSetAttribute(paged_prefill_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
-               "cudaFuncSetAttribute(prefill)");
-    configured = true;
-  }
+  set_smem_limit(reinterpret_cast<const void*>(paged_prefill_kernel), kSmemBytes, "cudaFuncSetAttribute(prefill)");
   dim3 grid((max_q_len + 63) / 64, Hq, B);
   launch_pdl(paged_prefill_kernel, grid, dim3(128), kSmemBytes, at::cuda::getCurrentCUDAStream(),
              "paged_prefill launch", tk, tv, a);
@@ -616,11 +640,66 @@ int noalloc_fail(int code, const std::string& msg) {
   return code;
 }
 
+// Device address of the scratch array on the current device (looked up once per
+// device, with that device current: the host-side name of the array is not a
+// device address).  Returns SIL_NOALLOC_OK or an error code.
+int noalloc_scratch(NoAllocScratch** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return noalloc_fail(SIL_NOALLOC_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return noalloc_fail(SIL_NOALLOC_ECUDA,
+                          std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<NoAllocScratch*>(p);
+  }
+  if (!g_noalloc_smem_set[dev]) {
+    e = cudaFuncSetAttribute(sil::paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             sil::kSmemBytes);
+    if (e != cudaSuccess)
+      return noalloc_fail(SIL_NOALLOC_ECUDA,
+                          std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    g_noalloc_smem_set[dev] = true;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SIL_NOALLOC_OK;
+}
+
 }  // namespace
 
 extern "C" const char* sil_noalloc_last_error(void) { return g_noalloc_error.c_str(); }
 extern "C" long long sil_noalloc_scratch_floats(void) { return kNoAllocFloats; }
 extern "C" int sil_noalloc_max_counters(void) { return kNoAllocCounters; }
+
+extern "C" int sil_noalloc_status(int* host_out, cudaStream_t stream) {
+  g_noalloc_error.clear();
+  if (!host_out) return noalloc_fail(SIL_NOALLOC_EINVAL, "null pointer argument");
+  NoAllocScratch* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  cudaError_t e = cudaMemcpyAsync(host_out, scratch->status, sizeof(int), cudaMemcpyDeviceToHost,
+                                  stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
+  return SIL_NOALLOC_OK;
+}
+
+extern "C" int sil_noalloc_set_wait_limit_ns(unsigned long long ns, cudaStream_t stream) {
+  g_noalloc_error.clear();
+  NoAllocScratch* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // Stream-ordered, from a value that must outlive the copy: copy from a static.
+  static thread_local unsigned long long value;
+  value = ns;
+  cudaError_t e = cudaMemcpyAsync(scratch->status + 2, &value, sizeof(value),
+                                  cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
+  return SIL_NOALLOC_OK;
+}
 
 extern "C" int sil_paged_decode_noalloc(const void* q, long long q_stride, const void* k_cache,
                                         const void* v_cache, long long num_pages, int kv_heads,
@@ -637,8 +716,17 @@ extern "C" int sil_paged_decode_noalloc(const void* q, long long q_stride, const
   if (q_heads % kv_heads != 0 || q_heads / kv_heads > 16)
     return noalloc_fail(SIL_NOALLOC_EINVAL, "q_heads must be a multiple of kv_heads, ratio <= 16");
   if ((reinterpret_cast<uintptr_t>(k_cache) & 15u) || (reinterpret_cast<uintptr_t>(v_cache) & 15u) ||
-      (reinterpret_cast<uintptr_t>(q) & 3u))
-    return noalloc_fail(SIL_NOALLOC_EINVAL, "cache pointers must be 16-byte aligned, q 4-byte aligned");
+      (reinterpret_cast<uintptr_t>(q) & 3u) || (reinterpret_cast<uintptr_t>(out) & 1u))
+    return noalloc_fail(SIL_NOALLOC_EINVAL,
+                        "cache pointers must be 16-byte aligned, q 4-byte aligned, out 2-byte aligned");
+  // q is read as 32-bit words, so its row stride must be even; rows must not overlap.
+  if (q_stride < (long long)q_heads * kD || (q_stride & 1))
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "q_stride must be even and >= q_heads * 128");
+  if (out_stride < (long long)q_heads * kD)
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "out_stride must be >= q_heads * 128");
+  if (bt_stride <= 0) return noalloc_fail(SIL_NOALLOC_EINVAL, "bt_stride must be positive");
+  if (num_pages * kv_heads * kPage > (1LL << 31) - 1 || num_pages > (1LL << 31) - 1)
+    return noalloc_fail(SIL_NOALLOC_EINVAL, "cache too large for 32-bit page rows");
   const int G = q_heads / kv_heads;
   const long long need = (long long)batch * kv_heads * num_splits * G * (kD + 2);
   if (num_splits > 1 && need > kNoAllocFloats)
@@ -649,38 +737,15 @@ extern "C" int sil_paged_decode_noalloc(const void* q, long long q_stride, const
     return noalloc_fail(SIL_NOALLOC_ETOOBIG,
                         "batch * kv_heads exceeds the " + std::to_string(kNoAllocCounters) +
                             " split counters of the allocation-free entry point");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return noalloc_fail(SIL_NOALLOC_EINVAL, "device ordinal out of range");
   NoAllocScratch* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[dev] == nullptr) {
-      // Once per device, with the device current: the host-side name of the array
-      // is not a device address.
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess)
-        return noalloc_fail(SIL_NOALLOC_ECUDA,
-                            std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_noalloc_ptr[dev] = static_cast<NoAllocScratch*>(p);
-    }
-    if (!g_noalloc_smem_set[dev]) {
-      e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSmemBytes);
-      if (e != cudaSuccess)
-        return noalloc_fail(SIL_NOALLOC_ECUDA,
-                            std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-      g_noalloc_smem_set[dev] = true;
-    }
-    scratch = g_noalloc_ptr[dev];
-  }
+  if (int rc = noalloc_scratch(&scratch)) return rc;
   // Counters and the status word must start at zero (an earlier call that gave up
-  // may have left them set); partials are fully written before they are read.
+  // may have left them set); partials are fully written before they are read.  The
+  // status is cleared here, at the start of the next call: read it with
+  // sil_noalloc_status() before calling again.
   const size_t nctr = static_cast<size_t>(std::min<long long>((long long)batch * kv_heads,
                                                               kNoAllocCounters));
-  e = cudaMemsetAsync(scratch->counters, 0, nctr * sizeof(int), stream);
+  cudaError_t e = cudaMemsetAsync(scratch->counters, 0, nctr * sizeof(int), stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(scratch->status, 0, sizeof(int), stream);
   if (e != cudaSuccess) return noalloc_fail(SIL_NOALLOC_ECUDA, cudaGetErrorString(e));
   AttnArgs a{};
@@ -694,6 +759,7 @@ extern "C" int sil_paged_decode_noalloc(const void* q, long long q_stride, const
   a.Hq = q_heads;
   a.Hkv = kv_heads;
   a.G = G;
+  a.num_pages = static_cast<int>(num_pages);
   a.scale_log2 = scale * 1.4426950408889634f;
   a.num_splits = num_splits;
   a.ws_o = scratch->partial;

@@ -97,6 +97,14 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
                             const at::Tensor& norm_w, double eps, at::Tensor& x_out,
                             const at::Tensor& status);
 at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);
+void decode_advance(const at::Tensor& tok, at::Tensor& ids, at::Tensor& out, at::Tensor& meta,
+                    const at::Tensor& valid, const at::Tensor& block_table,
+                    const c10::optional<at::Tensor>& offsets, const c10::optional<at::Tensor>& history,
+                    const c10::optional<at::Tensor>& hist_len);
+void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
+                       int64_t ll_off, int64_t partial_off, int64_t max_elems,
+                       const c10::optional<at::Tensor>& norm_w, double eps,
+                       const c10::optional<at::Tensor>& x_out, const at::Tensor& status);
 void nvls_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t mc, int64_t rank,
                     int64_t flags1_off, int64_t flags2_off, int64_t partial_off, int64_t sum_off,
                     int64_t max_elems, const c10::optional<at::Tensor>& norm_w, double eps,
@@ -148,6 +156,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "one-shot all-reduce into h fused with the next RMSNorm (x_out = rmsnorm(h) * w)");
   m.def("nvls_allreduce", &sil::nvls_allreduce,
         "two-shot all-reduce through NVSwitch multicast into h, optionally fused with the next RMSNorm");
+  m.def("decode_advance", &sil::decode_advance,
+        "advance a captured decode step's static inputs (ids, positions, slots, lengths, "
+        "sampling offsets and history) from the step's tokens");
+  m.def("ll_allreduce_norm", &sil::ll_allreduce_norm,
+        "one-shot all-reduce with the flag inside every 8-byte word (no fence, no flag round "
+        "trip) into h, optionally fused with the next RMSNorm");
   m.def("symm_tensor", &sil::symm_tensor, "bf16 tensor view over a symmetric buffer (no ownership)");
   m.def("can_access_peer", &sil::can_access_peer, "cudaDeviceCanAccessPeer");
 }

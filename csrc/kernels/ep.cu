@@ -93,7 +93,7 @@ __device__ __forceinline__ bool wait_flags(const EpLayout& L, long long off, int
     while (ld_acq_sys(f + r) != epoch) {
       if ((++it & 255u) == 0) {
         if (load_status(L.status) != 0) return false;
-        if (globaltimer_ns() - t0 > SIL_WAIT_TIMEOUT_NS) {
+        if (globaltimer_ns() - t0 > wait_limit_ns(L.status)) {
           raise_status(L.status, kStatusTimeoutPeer);
           return false;
         }

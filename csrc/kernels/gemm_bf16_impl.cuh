@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t it = 0;
               while (ld_acquire_sys(f) != epoch) {
                 if ((++it & 255u) == 0 &&
-                    (load_status(args.status) != 0 || globaltimer_ns() - t_start > SIL_WAIT_TIMEOUT_NS)) {
+                    (load_status(args.status) != 0 || globaltimer_ns() - t_start > wait_limit_ns(args.status))) {
                   raise_status(args.status, kStatusTimeoutPeer);
                   break;
                 }
@@ -867,12 +867,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
   using C = Cfg<BN, STAGES, EPI, SWAP>;
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, SWAP, GROUPED>;
   constexpr int kSmem = C::SMEM_BYTES + (GROUPED ? (kMaxGroups + 8) * 4 : 0);
-  static bool configured = false;
-  if (!configured) {
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem),
-               "cudaFuncSetAttribute(gemm smem)");
-    configured = true;
-  }
+  set_smem_limit(reinterpret_cast<const void*>(kern), kSmem, "cudaFuncSetAttribute(gemm smem)");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(args.grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

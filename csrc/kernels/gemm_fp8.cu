@@ -440,12 +440,7 @@ template <int BN, int STAGES, bool SWAP, int EPI, bool GROUPED>
 void launch8(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8Args& a, cudaStream_t st) {
   using C = Cfg8<BN, STAGES, SWAP, EPI>;
   auto kern = gemm_fp8_kernel<BN, STAGES, SWAP, EPI, GROUPED>;
-  static bool configured = false;
-  if (!configured) {
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES),
-               "cudaFuncSetAttribute(fp8 gemm)");
-    configured = true;
-  }
+  set_smem_limit(reinterpret_cast<const void*>(kern), C::SMEM_BYTES, "cudaFuncSetAttribute(fp8 gemm)");
   launch_pdl(kern, dim3(a.grid), dim3(kThreads), C::SMEM_BYTES, st, "gemm_fp8 launch", ta, tb, a);
 }
 

@@ -495,13 +495,7 @@ void mla_attention(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   const uint64_t rows = (uint64_t)cache.size(0) * kPage;
   CUtensorMap tm = make_tmap_2d(cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kQK, kQK,
                                 kTile, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  static bool configured = false;
-  if (!configured) {
-    check_cuda(cudaFuncSetAttribute(mla_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kSmemBytes),
-               "cudaFuncSetAttribute(mla)");
-    configured = true;
-  }
+  set_smem_limit(reinterpret_cast<const void*>(mla_attention_kernel), kSmemBytes, "cudaFuncSetAttribute(mla)");
   dim3 grid(S, RB, B);
   launch_pdl(mla_attention_kernel, grid, dim3(kThreads), kSmemBytes,
              at::cuda::getCurrentCUDAStream(), "mla_attention launch", tm, a);

@@ -109,7 +109,7 @@ __device__ __forceinline__ bool exchange(const NvlsArgs& a, long long flags_off,
     uint32_t it = 0;
     while (static_cast<int>(ld_acq_sys(f) - epoch) < 0) {
       if ((++it & 255u) == 0) {
-        if (load_status(a.status) != 0 || globaltimer_ns() - t0 > SIL_WAIT_TIMEOUT_NS) {
+        if (load_status(a.status) != 0 || globaltimer_ns() - t0 > wait_limit_ns(a.status)) {
           raise_status(a.status, kStatusTimeoutPeer);
           ok = 0;
           break;

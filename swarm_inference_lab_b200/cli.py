@@ -1,10 +1,14 @@
 """The ``swarm`` command line.
 
     swarm cluster create NAME            # this machine becomes coordinator; prints a pairing URI
+    swarm cluster start | stop           # the coordinator process (pairing + gRPC control plane)
     swarm cluster pair                   # mint another single-use pairing URI
     swarm cluster status | nodes | revoke NODE | delete
     swarm node join URI                  # pair this machine with a cluster
-    swarm node status | doctor | leave
+    swarm node agent                     # this node's worker runtime (registers, heartbeats)
+    swarm node configure | install-service | update | status | doctor | leave
+    swarm coordinator                    # the coordinator in the foreground
+    swarm submit MODEL --prompt-ids ...  # a request through the running coordinator
     swarm run MODEL [--prompt TEXT | --prompt-ids 1,2,3] [--max-tokens N] [--gpus N]
               [--mode speed|throughput|capacity|balanced] [--dry-run] [--explain-plan]
               [--json | --ndjson] [--require-distributed] [--engine native-stage]
@@ -16,8 +20,11 @@
 
 MODEL is a preset name (``llama-3-8b-shape``, ``qwen3-30b-a3b-shape``, ...), a
 local checkpoint directory, a ``.gguf`` file or ``hf://org/name@revision``.
-Without a tokenizer on the box, ``--prompt`` text is mapped to ids byte-wise
-(deterministic; documented as such in the output).
+A safetensors checkpoint directory is served with its own weights and, when it
+carries one, its tokenizer (``--prompt`` text is tokenized and the output detokenized);
+without a tokenizer ``--prompt`` text is mapped to ids byte-wise (deterministic;
+documented as such in the output).  ``--require-distributed`` serves through the
+cluster's coordinator across the joined nodes instead of this box's GPUs.
 
 Reference: si/cli.py:129-2372 and si/commands/{run,cluster,node}.py.
 """
@@ -90,10 +97,13 @@ def _gpu_caps(gpus: int | None):
     return ClusterCapabilities(nodes={"local": {"gpus": n or 1, "gpu_name": name}}, measurements=m)
 
 
-def _prompt_ids(prompt: str | None, prompt_ids: str | None, vocab: int) -> tuple[list[int], str]:
+def _prompt_ids(prompt: str | None, prompt_ids: str | None, vocab: int,
+                tokenizer=None) -> tuple[list[int], str]:
     if prompt_ids:
         return [int(x) for x in prompt_ids.split(",") if x.strip()], "ids"
     text = prompt or "Hello"
+    if tokenizer is not None:
+        return list(tokenizer.encode(text)), "tokenizer"
     return [b % vocab for b in text.encode("utf-8")], "bytes"
 
 
@@ -110,13 +120,29 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
                 require_distributed: bool = typer.Option(False, "--require-distributed"),
                 as_json: bool = typer.Option(False, "--json"),
                 ndjson: bool = typer.Option(False, "--ndjson"),
-                seed: int = typer.Option(0, "--seed")):
-    """Resolve, plan and run MODEL on this box, streaming tokens."""
+                seed: int = typer.Option(0, "--seed"),
+                temperature: float = typer.Option(0.0, "--temperature"),
+                top_k: int = typer.Option(0, "--top-k"),
+                top_p: float = typer.Option(1.0, "--top-p"),
+                repetition_penalty: float = typer.Option(1.0, "--repetition-penalty"),
+                stages: int = typer.Option(None, "--stages"),
+                return_logits: bool = typer.Option(False, "--return-logits"),
+                state: str = typer.Option(STATE, "--state-dir")):
+    """Resolve, plan and run MODEL (on this box, or across the cluster), streaming tokens."""
     from .engines import EngineRegistry, RequestShape
     if mode not in ("speed", "throughput", "capacity", "balanced"):
         raise typer.BadParameter("mode must be speed|throughput|capacity|balanced")
     cfg, res = _resolve_model(model)
-    ids, tok_kind = _prompt_ids(prompt, prompt_ids, cfg.vocab_size)
+    ckpt = _checkpoint_dir(model, res)
+    tokenizer = None
+    if ckpt is not None:
+        from .model_io.loader import load_tokenizer
+        tokenizer = load_tokenizer(ckpt)
+    ids, tok_kind = _prompt_ids(prompt, prompt_ids, cfg.vocab_size, tokenizer)
+    if require_distributed:
+        _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
+                         as_json, ndjson, return_logits, state)
+        return
     caps = _gpu_caps(gpus)
     comp = EngineRegistry().compete(cfg, caps, RequestShape(
         batch=1, prompt_tokens=len(ids), output_tokens=max_tokens, mode=mode,
@@ -130,7 +156,8 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
                    "predicted_ttft_ms": round(plan.predicted_ttft_ms, 2),
                    "mechanisms": plan.mechanisms, "confidence": plan.confidence,
                    "terms": plan.explain, "alternatives": [p.description for p in comp.ranked[1:4]],
-                   "rejected": comp.rejected, "prompt_tokenization": tok_kind}
+                   "rejected": comp.rejected, "prompt_tokenization": tok_kind,
+                   "weights": "checkpoint" if ckpt is not None else f"random (seed {seed})"}
     if explain_plan or dry_run:
         _out(explanation, as_json or ndjson)
         if dry_run:
@@ -140,10 +167,15 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
                    err=True)
     from .engine.engine import LLMEngine, SamplingParams
     t0 = time.perf_counter()
+    weights = None
+    if ckpt is not None:
+        from .model_io.loader import load_weights
+        weights = load_weights(cfg, ckpt, device="cuda")
     eng = LLMEngine(cfg, device="cuda", seed=seed, max_batch=1,
-                    max_seq_len=len(ids) + max_tokens + 64,
-                    weights=None)
-    eng.add_request(ids, SamplingParams(max_new_tokens=max_tokens), request_id="cli")
+                    max_seq_len=len(ids) + max_tokens + 64, weights=weights)
+    params = SamplingParams(max_new_tokens=max_tokens, temperature=temperature, top_k=top_k,
+                            top_p=top_p, repetition_penalty=repetition_penalty, seed=seed)
+    eng.add_request(ids, params, request_id="cli")
     out = []
     while eng.scheduler.has_work():
         for rid, tok in eng.step():
@@ -151,9 +183,81 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
             if ndjson:
                 typer.echo(json.dumps({"event": "TOKEN_GENERATED", "token": tok, "index": len(out) - 1}))
     dt = time.perf_counter() - t0
-    result = {"tokens": out, "output_tokens": len(out), "seconds": round(dt, 3)}
+    result = {"tokens": out, "output_tokens": len(out), "seconds": round(dt, 3),
+              "prompt_tokens": len(ids), "prompt_tokenization": tok_kind}
+    if tokenizer is not None:
+        result["text"] = tokenizer.decode(out)
     if ndjson:
         typer.echo(json.dumps({"event": "REQUEST_COMPLETED", **result}))
+    else:
+        _out(result, as_json)
+
+
+def _checkpoint_dir(model: str, res) -> str | None:
+    """The local safetensors directory behind MODEL, when it is one."""
+    if res is None:
+        return None
+    p = Path(model).expanduser()
+    if p.is_dir() and any(p.glob("*.safetensors")) and (p / "config.json").is_file():
+        return str(p)
+    src = getattr(res, "local_path", None)
+    if src and Path(src).is_dir() and any(Path(src).glob("*.safetensors")):
+        return str(src)
+    return None
+
+
+def _model_desc(model: str, cfg, ckpt: str | None, seed: int) -> dict:
+    if ckpt is not None:
+        return {"checkpoint": str(Path(ckpt).resolve())}
+    return {"preset": cfg.name, "seed": seed}
+
+
+def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
+                     as_json, ndjson, return_logits, state):
+    """Deploy MODEL across the cluster's joined nodes through the coordinator and stream
+    the request's tokens (the coordinator replays the request on a replacement node if a
+    node fails mid-request)."""
+    from .cluster.control import coordinator_client
+    st = _store(state)
+    if not st.has_cluster():
+        typer.echo("--require-distributed needs a cluster: `swarm cluster create` + `swarm node join`",
+                   err=True)
+        raise typer.Exit(EXIT_STATE)
+
+    async def go():
+        cli = coordinator_client(st)
+        try:
+            desc = _model_desc(model, cfg, ckpt, seed)
+            dep = await cli.deploy(desc, stages=stages)
+            name = dep["model"]
+            events, tokens, logits = [], [], []
+            async for ev in cli.submit_stream(name, ids, max_tokens, return_logits=return_logits):
+                events.append(ev)
+                if ev["event"] == "token":
+                    tokens.append(ev["token"])
+                    if return_logits:
+                        logits.append(ev.get("logits"))
+                if ndjson:
+                    typer.echo(json.dumps(ev if not return_logits else
+                                          {k: v for k, v in ev.items() if k != "logits"}))
+            return dep, events, tokens, logits
+        finally:
+            await cli.close()
+    dep, events, tokens, logits = asyncio.run(go())
+    last = events[-1] if events else {"event": "failed", "error": "no events"}
+    if last["event"] != "completed":
+        _out({"error": last.get("error", "request failed")}, as_json or ndjson)
+        raise typer.Exit(EXIT_RUNTIME)
+    result = {"tokens": tokens, "output_tokens": len(tokens), "deployment": dep,
+              "generations": last.get("generations"), "prompt_tokenization": tok_kind,
+              "distributed": True}
+    if return_logits:
+        result["logits"] = logits
+    if tokenizer is not None:
+        result["text"] = tokenizer.decode(tokens)
+    if ndjson:
+        typer.echo(json.dumps({"event": "REQUEST_COMPLETED",
+                               **{k: v for k, v in result.items() if k != "logits"}}))
     else:
         _out(result, as_json)
 
@@ -210,10 +314,22 @@ def cluster_delete(state: str = typer.Option(STATE, "--state-dir"), yes: bool = 
 @cluster_app.command("pair")
 def cluster_pair(serve: bool = typer.Option(False, "--serve"), ttl: float = 600.0,
                  state: str = typer.Option(STATE, "--state-dir")):
-    """Mint a pairing URI (and with --serve, answer pairing requests until interrupted)."""
+    """Mint a pairing URI (from the running coordinator when ``cluster start`` runs; with
+    --serve, answer pairing requests here until interrupted)."""
     from .cluster.pairing import PairingManager
     st = _store(state)
     doc = st.load_cluster()
+    if not serve and st.runtime().get("coordinator"):
+        from .cluster.control import coordinator_client
+
+        async def mint():
+            cli = coordinator_client(st, timeout=30.0)
+            try:
+                return await cli.pairing_uri(ttl)
+            finally:
+                await cli.close()
+        typer.echo(asyncio.run(mint()))
+        return
     pm = PairingManager(st, doc["coordinator_endpoint"])
     inv = pm.invite(ttl)
     typer.echo(inv.uri())
@@ -227,7 +343,148 @@ def cluster_pair(serve: bool = typer.Option(False, "--serve"), ttl: float = 600.
         asyncio.run(go())
 
 
+@cluster_app.command("start")
+def cluster_start(state: str = typer.Option(STATE, "--state-dir"),
+                  foreground: bool = typer.Option(False, "--foreground"),
+                  wait_s: float = typer.Option(60.0, "--wait")):
+    """Start the coordinator process (pairing server + gRPC control plane)."""
+    st = _store(state)
+    doc = st.load_cluster()
+    if doc["role"] != "coordinator":
+        typer.echo("only the coordinator node starts the cluster", err=True)
+        raise typer.Exit(EXIT_STATE)
+    if foreground:
+        from .cluster.control import serve_coordinator
+        asyncio.run(serve_coordinator(st))
+        return
+    import subprocess
+    import tempfile
+    ready = Path(tempfile.mkdtemp()) / "ready.json"
+    log = open(st.root / "coordinator.log", "ab")
+    proc = subprocess.Popen([sys.executable, "-m", "swarm_inference_lab_b200.cli", "coordinator",
+                             "--state-dir", str(st.root), "--ready-file", str(ready)],
+                            stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
+    t0 = time.time()
+    while not ready.exists():
+        if proc.poll() is not None or time.time() - t0 > wait_s:
+            typer.echo(f"coordinator did not start (see {st.root / 'coordinator.log'})", err=True)
+            raise typer.Exit(EXIT_RUNTIME)
+        time.sleep(0.1)
+    info = json.loads(ready.read_text())
+    typer.echo(json.dumps({"started": True, **info}))
+
+
+@cluster_app.command("stop")
+def cluster_stop(state: str = typer.Option(STATE, "--state-dir"), wait_s: float = 10.0):
+    """Stop the coordinator process started by ``cluster start``."""
+    import signal as _signal
+    st = _store(state)
+    rec = st.runtime().get("coordinator")
+    if not rec:
+        typer.echo("no running coordinator recorded", err=True)
+        raise typer.Exit(EXIT_STATE)
+    pid = int(rec["pid"])
+    try:
+        os.kill(pid, _signal.SIGTERM)
+    except ProcessLookupError:
+        pass
+    t0 = time.time()
+    while time.time() - t0 < wait_s:
+        try:
+            os.kill(pid, 0)
+        except ProcessLookupError:
+            break
+        time.sleep(0.1)
+    typer.echo(json.dumps({"stopped": True, "pid": pid}))
+
+
+@app.command("coordinator")
+def coordinator_command(state: str = typer.Option(STATE, "--state-dir"),
+                        ready_file: str = typer.Option(None, "--ready-file"),
+                        heartbeat_timeout: float = typer.Option(5.0, "--heartbeat-timeout")):
+    """Run the cluster's coordinator in the foreground."""
+    from .cluster.control import serve_coordinator
+    asyncio.run(serve_coordinator(_store(state), ready_file=ready_file,
+                                  heartbeat_timeout_s=heartbeat_timeout))
+
+
+@app.command("submit")
+def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids"),
+                   max_tokens: int = typer.Option(16, "--max-tokens"),
+                   state: str = typer.Option(STATE, "--state-dir"),
+                   return_logits: bool = typer.Option(False, "--return-logits")):
+    """Stream one request of an already deployed MODEL through the coordinator (NDJSON)."""
+    from .cluster.control import coordinator_client
+    ids = [int(x) for x in prompt_ids.split(",") if x.strip()]
+
+    async def go():
+        cli = coordinator_client(_store(state))
+        try:
+            async for ev in cli.submit_stream(model, ids, max_tokens, return_logits=return_logits):
+                typer.echo(json.dumps(ev))
+        finally:
+            await cli.close()
+    asyncio.run(go())
+
+
 # ------------------------------------------------------------------ node
+@node_app.command("agent")
+def node_agent(state: str = typer.Option(STATE, "--state-dir"), host: str = typer.Option(None, "--host"),
+               device: str = typer.Option(None, "--device"),
+               ready_file: str = typer.Option(None, "--ready-file")):
+    """Run this node's worker runtime: register with the coordinator, heartbeat, and host
+    the stage the coordinator assigns."""
+    from .cluster.control import run_node_agent
+    asyncio.run(run_node_agent(_store(state), host=host, device=device, ready_file=ready_file))
+
+
+@node_app.command("configure")
+def node_configure(state: str = typer.Option(STATE, "--state-dir"),
+                   host: str = typer.Option(None, "--host"), device: str = typer.Option(None, "--device"),
+                   ring_port: int = typer.Option(None, "--ring-port"),
+                   control_port: int = typer.Option(None, "--control-port"),
+                   heartbeat_s: float = typer.Option(None, "--heartbeat")):
+    """Persist this node's agent settings (host, device, ports, heartbeat period)."""
+    st = _store(state)
+    rt = st.runtime()
+    conf = rt.setdefault("node_config", {})
+    for k, v in (("host", host), ("device", device), ("ring_port", ring_port),
+                 ("control_port", control_port), ("heartbeat_s", heartbeat_s)):
+        if v is not None:
+            conf[k] = v
+    st.save_runtime(rt)
+    typer.echo(json.dumps(conf))
+
+
+@node_app.command("install-service")
+def node_install_service(state: str = typer.Option(STATE, "--state-dir"),
+                         path: str = typer.Option(None, "--path")):
+    """Write (or print) a systemd unit that keeps ``swarm node agent`` running."""
+    from .cluster.control import service_unit
+    unit = service_unit(_store(state), sys.executable)
+    if path:
+        Path(path).write_text(unit)
+        typer.echo(f"wrote {path}")
+    else:
+        typer.echo(unit)
+
+
+@node_app.command("update")
+def node_update(state: str = typer.Option(STATE, "--state-dir"),
+                as_json: bool = typer.Option(True, "--json/--text")):
+    """Report this node's runtime version and native-library build against the source."""
+    import hashlib
+    root = Path(__file__).resolve().parent
+    so = sorted(root.glob("_C*.so"))
+    src = sorted((root.parent / "csrc").rglob("*.c*")) if (root.parent / "csrc").is_dir() else []
+    digest = hashlib.sha256(b"".join(p.read_bytes() for p in src)).hexdigest()[:16] if src else None
+    stale = bool(so and src and max(p.stat().st_mtime for p in src) > so[0].stat().st_mtime)
+    _out({"version": "0.1.0", "native_library": so[0].name if so else None,
+          "source_digest": digest, "rebuild_needed": stale or not so,
+          "update": "run `python setup.py build_ext --inplace` to rebuild" if (stale or not so)
+          else "up to date"}, as_json)
+
+
 @node_app.command("join")
 def node_join(uri: str, node_id: str = typer.Option(None, "--name"),
               state: str = typer.Option(STATE, "--state-dir")):

@@ -63,6 +63,7 @@ class StagePlan:
     layer_end: int
     artifact_id: str
     artifact_bytes: int = 0
+    deployment_id: str = ""
 
 
 @dataclass
@@ -133,7 +134,8 @@ class DeploymentManager:
         for sp in d.stages:
             ag = self.agents[sp.worker_id]
             stages.append(StageAssignment(sp.stage_id, sp.worker_id, ag.fingerprint, sp.layer_start,
-                                          sp.layer_end, ag.endpoint, ag.endpoint))
+                                          sp.layer_end, getattr(ag, "control_endpoint", ag.endpoint),
+                                          ag.endpoint))
         lease = RouteLease(d.topology_id, d.generation, d.model_revision, "none", "native-stage",
                            "bf16", stages)
         return issue_lease(self.identity, lease, self.ttl)
@@ -143,6 +145,8 @@ class DeploymentManager:
         d = Deployment(uuid.uuid4().hex[:16], model_revision, topology_id,
                        sorted(stages, key=lambda s: s.stage_id))
         self.deployments[d.deployment_id] = d
+        for sp in d.stages:
+            sp.deployment_id = d.deployment_id
         done: list[Phase] = []
         try:
             for sp in d.stages:
@@ -189,6 +193,7 @@ class DeploymentManager:
 
     async def _load(self, d: Deployment, stages: list[StagePlan]) -> None:
         for sp in stages:
+            sp.deployment_id = d.deployment_id
             d.reports[sp.stage_id] = await self.agents[sp.worker_id].load_stage(sp)
         self._enter(d, Phase.VERIFYING_LOADS)
         for sp in stages:

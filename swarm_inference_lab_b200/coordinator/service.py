@@ -1,0 +1,497 @@
+"""Coordinator service: worker registration and heartbeats, planning, transactional
+deployment onto registered workers, streamed submission with restart-and-replay, stage-0
+token publication, and the gRPC server / client around them.
+
+    CoordinatorCore         the state machine (this process's registry, deployments, requests)
+    CoordinatorRpcServer    ``swarm.v1.Coordinator`` over gRPC (mutual TLS with the cluster CA)
+    CoordinatorClient       what ``swarm run`` / ``swarm submit`` / workers call
+    GrpcWorkerAgent         ``WorkerAgent`` (coordinator/deployment.py) over a worker's gRPC
+
+A worker registers with its worker id, identity fingerprint and endpoints; with a cluster
+state store the fingerprint must belong to a paired, unrevoked member and match the
+identity bound in the caller's client certificate.  Heartbeats keep it healthy; a sweep
+marks silent workers unhealthy.  ``deploy`` plans contiguous layer intervals over healthy
+workers (one stage per worker, equal split or the planner's partition) and runs the
+deployment manager's phases; every stage receives one lease the coordinator signs.
+``submit_stream`` drives a session over the stage ring (``SessionController``); on a
+transport failure it probes the route's stages, replaces the failed worker with a healthy
+spare (``DeploymentManager.recover``: load, new generation, signed routes, handshakes) and
+replays the request, checking every accepted token.
+
+Reference: si/coordinator/service.py:229 (``CoordinatorCore``: :563 register, :662
+heartbeat, :750 deploy, :1050 token publication, :1884 submit_stream, :1427 failed-stage
+probe, :1486 recovery), :2553 (``CoordinatorRpcServer``), :3421 (``CoordinatorClient``).
+"""
+from __future__ import annotations
+
+import asyncio
+import json
+import time
+import uuid
+from dataclasses import dataclass, field
+from pathlib import Path
+
+from ..protocol import stage_ring as sr
+from ..runtime.worker_runtime import COORDINATOR_SERVICE, WORKER_SERVICE, artifact_id_for
+from ..transport.grpc_control import PEER_FINGERPRINT, GrpcControlClient, GrpcControlServer
+from ..transport.stage_ring_net import ConnectionPool, TransportError
+from .deployment import Deployment, DeploymentError, DeploymentManager, LoadReport, StagePlan
+from .session import Route, SessionController
+from .state import DurableState, WorkerRecord, WorkerRegistry
+
+
+class GrpcWorkerAgent:
+    """``WorkerAgent`` over a worker's ``swarm.v1.Worker`` gRPC service."""
+
+    def __init__(self, worker_id: str, fingerprint: str, ring_endpoint: str, control_endpoint: str,
+                 *, credentials=None, timeout: float = 60.0):
+        self.worker_id = worker_id
+        self.fingerprint = fingerprint
+        self.endpoint = ring_endpoint           # data plane (stage ring)
+        self.control_endpoint = control_endpoint
+        self.client = GrpcControlClient(control_endpoint, credentials, timeout=timeout)
+        self.model: dict = {}
+        self.model_revision = ""
+        self.num_stages = 1
+
+    async def _call(self, method: str, kind: str, obj: dict) -> dict:
+        _, rep = await self.client.call(WORKER_SERVICE, method, kind, obj)
+        return rep
+
+    async def reserve(self, deployment_id: str, stage_id: int) -> bool:
+        return bool((await self._call("Reserve", "ReserveRequest",
+                                      {"deployment_id": deployment_id, "stage_id": stage_id}))["ok"])
+
+    async def release(self, deployment_id: str) -> None:
+        await self._call("Release", "ReleaseRequest", {"deployment_id": deployment_id})
+
+    async def has_artifact(self, artifact_id: str) -> bool:
+        return bool((await self._call("HasArtifact", "ArtifactQuery",
+                                      {"artifact_id": artifact_id}))["present"])
+
+    async def fetch_artifact(self, artifact_id: str) -> None:
+        await self._call("FetchArtifact", "ArtifactQuery", {"artifact_id": artifact_id})
+
+    async def verify_artifact(self, artifact_id: str) -> bool:
+        rep = await self._call("VerifyArtifact", "ArtifactQuery", {"artifact_id": artifact_id})
+        return bool(rep.get("ok")) and bool(rep.get("present"))
+
+    async def load_stage(self, plan: StagePlan) -> LoadReport:
+        rep = await self._call("LoadStage", "LoadStageRequest", {
+            "plan": {"stage_id": plan.stage_id, "layer_start": plan.layer_start,
+                     "layer_end": plan.layer_end, "artifact_id": plan.artifact_id},
+            "model": self.model, "model_revision": self.model_revision,
+            "num_stages": self.num_stages, "deployment_id": plan.deployment_id})
+        return LoadReport(rep["artifact_id"], int(rep["tensors"]), int(rep["bytes"]))
+
+    async def unload_stage(self, deployment_id: str) -> None:
+        await self._call("UnloadStage", "UnloadStageRequest", {"deployment_id": deployment_id})
+
+    async def install_route(self, signed_lease: dict, next_endpoint: str | None) -> None:
+        rep = await self._call("InstallRoute", "InstallRouteRequest",
+                               {"lease": signed_lease, "next_endpoint": next_endpoint})
+        if not rep.get("ok"):
+            raise DeploymentError(f"{self.worker_id} rejected the route: {rep.get('error')}")
+
+    async def withdraw_route(self, generation: int) -> None:
+        await self._call("WithdrawRoute", "WithdrawRouteRequest", {"generation": generation})
+
+    async def check_peer(self, endpoint: str) -> bool:
+        rep = await self._call("CheckPeer", "CheckPeerRequest", {"endpoint": endpoint})
+        if not rep.get("ok"):
+            raise DeploymentError(f"{self.worker_id} handshake with {endpoint}: {rep.get('error')}")
+        return True
+
+    async def free_bytes(self) -> int:
+        return int((await self._call("FreeBytes", "FreeBytesRequest", {}))["bytes"])
+
+    async def health(self) -> dict:
+        return await self._call("Health", "HealthRequest", {})
+
+    async def close(self) -> None:
+        await self.client.close()
+
+
+@dataclass
+class ActiveModel:
+    name: str
+    model: dict
+    revision: str
+    deployment: Deployment
+    num_layers: int
+    topology_id: str
+
+
+@dataclass
+class RequestRecord:
+    request_id: str
+    prompt: list[int]
+    tokens: list[int] = field(default_factory=list)
+    published: list[dict] = field(default_factory=list)
+    generations: list[int] = field(default_factory=list)
+    state: str = "RUNNING"
+
+
+def model_revision(model: dict) -> str:
+    return "sha256:" + __import__("hashlib").sha256(
+        json.dumps(model, sort_keys=True).encode()).hexdigest()[:16]
+
+
+class CoordinatorCore:
+    def __init__(self, identity, *, state_dir: str | Path | None = None, cluster_store=None,
+                 heartbeat_timeout_s: float = 5.0, heartbeat_s: float = 1.0,
+                 worker_credentials=None, require_member: bool | None = None):
+        self.identity = identity
+        self.registry = WorkerRegistry(heartbeat_timeout_s)
+        self.heartbeat_s = heartbeat_s
+        self.agents: dict[str, GrpcWorkerAgent] = {}
+        self.state = DurableState(Path(state_dir) / "coordinator_state.json") if state_dir else None
+        self.deployer = DeploymentManager(self.registry, self.agents, identity, self.state)
+        self.cluster_store = cluster_store
+        self.require_member = cluster_store is not None if require_member is None else require_member
+        self.worker_credentials = worker_credentials
+        self.models: dict[str, ActiveModel] = {}
+        self.requests: dict[str, RequestRecord] = {}
+        self.events: list[dict] = []
+        self.pairing = None          # PairingManager when serving a cluster
+        self._sweeper: asyncio.Task | None = None
+        self._lock = asyncio.Lock()
+
+    # ------------------------------------------------------------ membership
+    def _check_member(self, fingerprint: str) -> None:
+        if not self.require_member:
+            return
+        doc = self.cluster_store.load_cluster()
+        members = {m["fingerprint"] for m in doc.get("members", {}).values()}
+        revoked = set(doc.get("revoked", []))
+        if fingerprint not in members or fingerprint in revoked:
+            raise PermissionError("worker is not a paired member of this cluster (or is revoked)")
+
+    def _check_caller(self, claimed: str) -> None:
+        peer = PEER_FINGERPRINT.get()
+        if peer is not None and peer != claimed:
+            raise PermissionError("request fingerprint does not match the client certificate")
+        self._check_member(claimed)
+
+    async def register(self, req: dict) -> dict:
+        self._check_caller(req["fingerprint"])
+        wid = req["worker_id"]
+        old = self.agents.pop(wid, None)
+        if old is not None:
+            await old.close()
+        self.agents[wid] = GrpcWorkerAgent(wid, req["fingerprint"], req["ring_endpoint"],
+                                           req["control_endpoint"],
+                                           credentials=self.worker_credentials)
+        self.registry.register(WorkerRecord(wid, req["fingerprint"], req["ring_endpoint"],
+                                            dict(req.get("capabilities", {}),
+                                                 control_endpoint=req["control_endpoint"])))
+        self.events.append({"event": "worker_registered", "worker": wid, "at": time.time()})
+        return {"accepted": True, "heartbeat_s": self.heartbeat_s,
+                "coordinator_fingerprint": self.identity.fingerprint}
+
+    async def heartbeat(self, req: dict) -> dict:
+        self._check_caller(req["fingerprint"])
+        wid = req["worker_id"]
+        if wid not in self.registry.workers:
+            return {"ok": False, "reregister": True}
+        self.registry.heartbeat(wid)
+        return {"ok": True}
+
+    def sweep(self) -> list[str]:
+        dead = self.registry.sweep()
+        for wid in dead:
+            self.events.append({"event": "worker_lost", "worker": wid, "at": time.time()})
+        return dead
+
+    async def _sweep_loop(self) -> None:
+        while True:
+            await asyncio.sleep(self.heartbeat_s)
+            self.sweep()
+
+    def start_background(self) -> None:
+        if self._sweeper is None:
+            self._sweeper = asyncio.get_running_loop().create_task(self._sweep_loop())
+
+    def workers(self) -> list[dict]:
+        out = []
+        for w in self.registry.workers.values():
+            out.append({"worker_id": w.worker_id, "fingerprint": w.fingerprint,
+                        "ring_endpoint": w.endpoint, "healthy": w.healthy,
+                        "last_heartbeat": w.last_heartbeat,
+                        "control_endpoint": w.capabilities.get("control_endpoint")})
+        return sorted(out, key=lambda d: d["worker_id"])
+
+    # ------------------------------------------------------------ planning / deployment
+    def plan(self, model: dict, stages: int | None = None) -> list[dict]:
+        from ..models.config import preset
+        if "checkpoint" in model:
+            from ..model_io.loader import checkpoint_config
+            cfg = checkpoint_config(model["checkpoint"])
+        else:
+            cfg = preset(model["preset"])
+        healthy = sorted(self.registry.healthy(), key=lambda w: w.worker_id)
+        busy = {sp.worker_id for m in self.models.values() for sp in m.deployment.stages}
+        free = [w for w in healthy if w.worker_id not in busy]
+        n = stages or len(free)
+        n = min(n, cfg.num_layers)
+        if n < 1 or len(free) < n:
+            raise DeploymentError(f"{n} stages need {n} free healthy workers; {len(free)} available")
+        from ..runtime.worker import equal_layer_ranges
+        out = []
+        for i, (lo, hi) in enumerate(equal_layer_ranges(cfg.num_layers, n)):
+            out.append({"stage_id": i, "worker_id": free[i].worker_id, "layer_start": lo,
+                        "layer_end": hi, "artifact_id": artifact_id_for(model, lo, hi)})
+        return out
+
+    async def deploy(self, req: dict) -> dict:
+        model = req["model"]
+        name = req.get("name") or model.get("preset") or Path(model.get("checkpoint", "model")).name
+        async with self._lock:
+            if name in self.models:
+                m = self.models[name]
+                return self._model_status(m)
+            plan = self.plan(model, req.get("stages"))
+            rev = model_revision(model)
+            for p in plan:
+                ag = self.agents[p["worker_id"]]
+                ag.model, ag.model_revision, ag.num_stages = model, rev, len(plan)
+            stages = [StagePlan(p["stage_id"], p["worker_id"], p["layer_start"], p["layer_end"],
+                                p["artifact_id"]) for p in plan]
+            topology = f"{name}:{uuid.uuid4().hex[:8]}"
+            d = await self.deployer.deploy(stages, model_revision=rev, topology_id=topology)
+            m = ActiveModel(name, model, rev, d, plan[-1]["layer_end"], topology)
+            self.models[name] = m
+            self.events.append({"event": "model_deployed", "model": name,
+                                "generation": d.generation, "at": time.time()})
+            return self._model_status(m)
+
+    def _model_status(self, m: ActiveModel) -> dict:
+        d = m.deployment
+        return {"model": m.name, "deployment_id": d.deployment_id, "phase": d.phase.value,
+                "generation": d.generation, "topology_id": d.topology_id, "revision": m.revision,
+                "stages": [{"stage_id": s.stage_id, "worker_id": s.worker_id,
+                            "layers": [s.layer_start, s.layer_end]} for s in d.stages]}
+
+    async def unload(self, req: dict) -> dict:
+        async with self._lock:
+            m = self.models.pop(req["model"], None)
+            if m is None:
+                return {"unloaded": False}
+            await self.deployer.unload(m.deployment.deployment_id)
+            return {"unloaded": True}
+
+    def _route(self, m: ActiveModel) -> Route:
+        d = m.deployment
+        s0 = d.stages[0]
+        host, port = self.agents[s0.worker_id].endpoint.rsplit(":", 1)
+        return Route((host, int(port)), d.generation, d.topology_id, m.revision,
+                     (s0.layer_start, s0.layer_end))
+
+    async def _failed_workers(self, m: ActiveModel) -> list[str]:
+        """Workers of the route that do not answer a HEALTH frame (or are marked dead)."""
+        failed = []
+        pool = ConnectionPool()
+        try:
+            for sp in m.deployment.stages:
+                rec = self.registry.workers.get(sp.worker_id)
+                if rec is None or not rec.healthy:
+                    failed.append(sp.worker_id)
+                    continue
+                host, port = self.agents[sp.worker_id].endpoint.rsplit(":", 1)
+                msg = sr.StageMessage(operation=sr.Operation.HEALTH, model_revision=m.revision,
+                                      tokenizer_revision="none", topology_id=m.topology_id,
+                                      stage_id=sp.stage_id, layer_start=sp.layer_start,
+                                      layer_end=sp.layer_end, session_id="", request_id="probe",
+                                      sequence_number=0, token_position=-1,
+                                      source_stage=sr.COORDINATOR, destination_stage=sp.stage_id)
+                try:
+                    await asyncio.wait_for(pool.send(host, int(port), msg), timeout=2.0)
+                except (TransportError, OSError, asyncio.TimeoutError):
+                    failed.append(sp.worker_id)
+        finally:
+            await pool.close()
+        return failed
+
+    async def _recover(self, m: ActiveModel, route: Route, exc: Exception) -> Route:
+        async with self._lock:
+            if m.deployment.generation != route.generation:
+                return self._route(m)  # another request already recovered this deployment
+            failed = await self._failed_workers(m)
+            if not failed:
+                raise exc
+            for wid in failed:
+                self.registry.mark_unhealthy(wid)
+                self.events.append({"event": "stage_failed", "worker": wid, "at": time.time()})
+                await self.deployer.recover(m.deployment.deployment_id, wid)
+            self.events.append({"event": "route_recovered", "model": m.name,
+                                "generation": m.deployment.generation, "at": time.time()})
+            return self._route(m)
+
+    # ------------------------------------------------------------ requests
+    async def submit_stream(self, req: dict):
+        """Async generator of stream events for one request (``accepted``, ``token`` ...,
+        ``recovered``, ``completed`` / ``failed``)."""
+        name = req["model"]
+        m = self.models.get(name)
+        if m is None:
+            yield {"event": "failed", "error": f"model {name} is not deployed"}
+            return
+        rid = req.get("request_id") or uuid.uuid4().hex[:12]
+        prompt = [int(t) for t in req["prompt_ids"]]
+        rec = RequestRecord(rid, prompt)
+        self.requests[rid] = rec
+        if self.state is not None:
+            self.state.record_request(rid, prompt, {"max_tokens": req.get("max_tokens")})
+        ctl = SessionController(self._route(m), recover=lambda r, e: self._recover(m, r, e),
+                                return_logits=bool(req.get("return_logits")))
+        yield {"event": "accepted", "request_id": rid, "generation": m.deployment.generation}
+        t0 = time.perf_counter()
+        try:
+            async for ev in ctl.stream(prompt, int(req.get("max_tokens", 16)), rid):
+                if ev["event"] == "token":
+                    rec.tokens.append(ev["token"])
+                    if self.state is not None:
+                        self.state.accept_token(rid, ev["token"])
+                    out = {"event": "token", "index": ev["index"], "token": ev["token"]}
+                    if ev.get("logits") is not None:
+                        out["logits"] = [float(v) for v in ev["logits"].reshape(-1).tolist()]
+                    yield out
+                elif ev["event"] in ("started", "recovered"):
+                    rec.generations.append(ev["generation"])
+                    if ev["event"] == "recovered":
+                        yield {"event": "recovered", "generation": ev["generation"],
+                               "replayed": ev["replayed"]}
+            rec.state = "COMPLETED"
+            yield {"event": "completed", "request_id": rid, "tokens": rec.tokens,
+                   "generations": rec.generations, "seconds": time.perf_counter() - t0}
+        except Exception as exc:  # noqa: BLE001 - reported to the caller as an event
+            rec.state = "FAILED"
+            yield {"event": "failed", "request_id": rid, "error": f"{type(exc).__name__}: {exc}"}
+        finally:
+            if self.state is not None:
+                self.state.set_state(rid, rec.state)
+            await ctl.pool.close()
+
+    async def publish_token(self, pub: dict) -> dict:
+        """Stage 0's copy of every token it relayed (checked against the accepted stream)."""
+        rec = self.requests.get(pub.get("request_id", ""))
+        if rec is None:
+            return {"ok": False}
+        rec.published.append(pub)
+        return {"ok": True}
+
+    def status(self) -> dict:
+        return {"coordinator_fingerprint": self.identity.fingerprint,
+                "workers": len(self.registry.workers),
+                "healthy_workers": len(self.registry.healthy()),
+                "models": {k: self._model_status(v) for k, v in self.models.items()},
+                "requests": {k: {"state": r.state, "tokens": len(r.tokens),
+                                 "published": len(r.published), "generations": r.generations}
+                             for k, r in self.requests.items()}}
+
+    async def close(self) -> None:
+        if self._sweeper is not None:
+            self._sweeper.cancel()
+            try:
+                await self._sweeper
+            except (asyncio.CancelledError, Exception):  # noqa: BLE001
+                pass
+        for ag in self.agents.values():
+            await ag.close()
+
+
+class CoordinatorRpcServer:
+    """``swarm.v1.Coordinator`` over gRPC (``Any`` envelopes with JSON bodies)."""
+
+    def __init__(self, core: CoordinatorCore, *, host: str = "127.0.0.1", port: int = 0,
+                 credentials=None):
+        self.core = core
+
+        def unary(fn, reply_kind):
+            async def h(kind, obj):
+                return reply_kind, await fn(obj)
+            return h
+
+        async def workers(obj):
+            return {"workers": core.workers()}
+
+        async def status(obj):
+            return core.status()
+
+        async def plan(obj):
+            return {"plan": core.plan(obj["model"], obj.get("stages"))}
+
+        async def pairing_create(obj):
+            if core.pairing is None:
+                raise PermissionError("this coordinator does not serve pairing")
+            if PEER_FINGERPRINT.get() not in (None, core.identity.fingerprint):
+                raise PermissionError("only the coordinator's own identity mints invitations")
+            inv = core.pairing.invite(float(obj.get("ttl_s", 600.0)))
+            return {"uri": inv.uri()}
+
+        async def submit_stream(kind, obj):
+            async for ev in core.submit_stream(obj):
+                yield "StreamEvent", ev
+
+        handlers = {
+            ("Register", "RegistrationAccepted", core.register),
+            ("Heartbeat", "HeartbeatReply", core.heartbeat),
+            ("DeployModel", "DeploymentStatus", core.deploy),
+            ("UnloadModel", "UnloadReply", core.unload),
+            ("PublishToken", "PublishReply", core.publish_token),
+            ("Workers", "WorkersReply", workers),
+            ("Status", "CoordinatorStatus", status),
+            ("PlanModel", "PlanReply", plan),
+            ("PairingCreate", "PairingInvitation", pairing_create),
+        }
+        self.server = GrpcControlServer(
+            {(COORDINATOR_SERVICE, m): unary(fn, rk) for m, rk, fn in handlers},
+            server_streams={(COORDINATOR_SERVICE, "SubmitStream"): submit_stream},
+            host=host, port=port, credentials=credentials)
+
+    async def start(self) -> int:
+        self.core.start_background()
+        return await self.server.start()
+
+    async def stop(self) -> None:
+        await self.server.stop()
+        await self.core.close()
+
+
+class CoordinatorClient:
+    def __init__(self, target: str, credentials=None, timeout: float = 300.0):
+        self.client = GrpcControlClient(target, credentials, timeout=timeout)
+
+    async def _call(self, method: str, kind: str, obj: dict) -> dict:
+        _, rep = await self.client.call(COORDINATOR_SERVICE, method, kind, obj)
+        return rep
+
+    async def deploy(self, model: dict, *, name: str | None = None, stages: int | None = None) -> dict:
+        return await self._call("DeployModel", "DeployRequest",
+                                {"model": model, "name": name, "stages": stages})
+
+    async def unload(self, name: str) -> dict:
+        return await self._call("UnloadModel", "UnloadRequest", {"model": name})
+
+    async def workers(self) -> list[dict]:
+        return (await self._call("Workers", "WorkersRequest", {}))["workers"]
+
+    async def status(self) -> dict:
+        return await self._call("Status", "StatusRequest", {})
+
+    async def plan(self, model: dict, stages: int | None = None) -> list[dict]:
+        return (await self._call("PlanModel", "PlanRequest", {"model": model, "stages": stages}))["plan"]
+
+    async def pairing_uri(self, ttl_s: float = 600.0) -> str:
+        return (await self._call("PairingCreate", "PairingRequest", {"ttl_s": ttl_s}))["uri"]
+
+    async def submit_stream(self, model: str, prompt_ids: list[int], max_tokens: int, *,
+                            return_logits: bool = False, request_id: str | None = None):
+        async for _, ev in self.client.call_stream(
+                COORDINATOR_SERVICE, "SubmitStream", "SubmitRequest",
+                {"model": model, "prompt_ids": list(prompt_ids), "max_tokens": max_tokens,
+                 "return_logits": return_logits, "request_id": request_id}):
+            yield ev
+
+    async def close(self) -> None:
+        await self.client.close()

@@ -124,13 +124,35 @@ class SessionController:
 
     async def generate(self, prompt: list[int], max_new_tokens: int,
                        request_id: str | None = None) -> SessionResult:
+        """Runs the request to completion (see :meth:`stream`)."""
         request_id = request_id or uuid.uuid4().hex[:12]
         res = SessionResult(request_id, [])
         t_start = time.perf_counter()
+        async for ev in self.stream(prompt, max_new_tokens, request_id):
+            if ev["event"] == "token":
+                res.tokens.append(ev["token"])
+                res.logits.append(ev["logits"])
+                if ev["index"] == 0:
+                    res.ttft_ms = (time.perf_counter() - t_start) * 1e3
+            elif ev["event"] == "recovered":
+                res.recoveries += 1
+            if ev["event"] in ("started", "recovered"):
+                res.generations.append(ev["generation"])
+        res.total_ms = (time.perf_counter() - t_start) * 1e3
+        return res
+
+    async def stream(self, prompt: list[int], max_new_tokens: int, request_id: str | None = None):
+        """Async generator of the request's events: ``started`` (route generation), one
+        ``token`` per accepted output token (index, token, logits or None) and ``recovered``
+        (new generation) after a restart-and-replay.  The next token is computed only when
+        the consumer asks for the next event, so a consumer paces the decode."""
+        request_id = request_id or uuid.uuid4().hex[:12]
+        tokens: list[int] = []
         recoveries = 0
         session_id = f"{request_id}:g{self.route.generation}"
-        res.generations.append(self.route.generation)
+        yield {"event": "started", "request": request_id, "generation": self.route.generation}
         need_open = True
+        recovering = False
         while True:
             try:
                 if need_open:
@@ -138,44 +160,44 @@ class SessionController:
                     need_open = False
                     # (Re)build the session: prompt, then each accepted token one by one.
                     tok, lg = await self._run_tokens(session_id, request_id, prompt, 0,
-                                                     sr.Operation.PREFILL, replay=bool(res.tokens))
-                    if not res.tokens:
-                        res.tokens.append(tok)
-                        res.logits.append(lg)
-                        res.ttft_ms = (time.perf_counter() - t_start) * 1e3
+                                                     sr.Operation.PREFILL, replay=bool(tokens))
+                    if recovering:
+                        recovering = False
+                        yield {"event": "recovered", "request": request_id,
+                               "generation": self.route.generation, "replayed": len(tokens)}
+                    if not tokens:
+                        tokens.append(tok)
                         self.events.append({"event": "first_token", "request": request_id})
+                        yield {"event": "token", "index": 0, "token": tok, "logits": lg}
                     else:
-                        if tok != res.tokens[0]:
-                            raise IntegrityError(f"replay diverged at output 0: {tok} != {res.tokens[0]}")
-                        for i in range(len(res.tokens) - 1):
-                            t2, _ = await self._run_tokens(session_id, request_id, [res.tokens[i]],
+                        if tok != tokens[0]:
+                            raise IntegrityError(f"replay diverged at output 0: {tok} != {tokens[0]}")
+                        for i in range(len(tokens) - 1):
+                            t2, _ = await self._run_tokens(session_id, request_id, [tokens[i]],
                                                            len(prompt) + i, sr.Operation.DECODE, True)
-                            if t2 != res.tokens[i + 1]:
+                            if t2 != tokens[i + 1]:
                                 raise IntegrityError(
-                                    f"replay diverged at output {i + 1}: {t2} != {res.tokens[i + 1]}")
+                                    f"replay diverged at output {i + 1}: {t2} != {tokens[i + 1]}")
                         self.events.append({"event": "replay_complete", "request": request_id,
-                                            "tokens": len(res.tokens)})
-                while len(res.tokens) < max_new_tokens:
-                    pos = len(prompt) + len(res.tokens) - 1
-                    tok, lg = await self._run_tokens(session_id, request_id, [res.tokens[-1]], pos,
+                                            "tokens": len(tokens)})
+                while len(tokens) < max_new_tokens:
+                    pos = len(prompt) + len(tokens) - 1
+                    tok, lg = await self._run_tokens(session_id, request_id, [tokens[-1]], pos,
                                                      sr.Operation.DECODE, False)
-                    res.tokens.append(tok)
-                    res.logits.append(lg)
+                    tokens.append(tok)
+                    yield {"event": "token", "index": len(tokens) - 1, "token": tok, "logits": lg}
                 break
             except (TransportError, StageError) as exc:
                 if isinstance(exc, StageError) and "IntegrityError" in str(exc):
                     raise
                 recoveries += 1
                 self.events.append({"event": "recovery_started", "request": request_id,
-                                    "error": str(exc), "accepted": len(res.tokens)})
+                                    "error": str(exc), "accepted": len(tokens)})
                 if recoveries > self.max_recoveries or self.recover_cb is None:
                     raise
                 await self._close(session_id, request_id, cancel=True)
                 self.route = await self.recover_cb(self.route, exc)
-                res.generations.append(self.route.generation)
                 session_id = f"{request_id}:g{self.route.generation}:r{recoveries}"
                 need_open = True
+                recovering = True
         await self._close(session_id, request_id)
-        res.recoveries = recoveries
-        res.total_ms = (time.perf_counter() - t_start) * 1e3
-        return res

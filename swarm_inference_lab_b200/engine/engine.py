@@ -30,9 +30,22 @@ from .scheduler import ContinuousScheduler, SchedulerPolicy, SeqRequest
 
 @dataclass
 class SamplingParams:
+    """Per-request decoding options.  ``temperature`` 0 selects greedy decoding (lowest
+    id on ties).  Otherwise the repetition penalty (over prompt + output), temperature,
+    top-k and top-p (nucleus) shape the distribution and a Gumbel-max draw from a Philox
+    stream keyed by ``seed`` (a hash of the request id when None) and the token index picks
+    the token, inside the captured decode graph."""
     max_new_tokens: int = 16
-    temperature: float = 0.0        # 0 = greedy (lowest id on ties)
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    repetition_penalty: float = 1.0
+    seed: int | None = None
     stop_token_ids: tuple[int, ...] = ()
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature == 0.0 and self.repetition_penalty == 1.0
 
 
 @dataclass
@@ -100,13 +113,22 @@ class LLMEngine:
     def add_request(self, prompt: list[int], params: SamplingParams | None = None,
                     request_id: str | None = None) -> str:
         params = params or SamplingParams()
-        if params.temperature != 0.0:
-            raise NotImplementedError("non-greedy sampling is served by ops.sampling.sample")
+        if params.temperature < 0 or params.top_p <= 0 or params.top_p > 1 or params.top_k < 0:
+            raise ValueError("temperature >= 0, 0 < top_p <= 1 and top_k >= 0 are required")
+        if params.repetition_penalty <= 0:
+            raise ValueError("repetition_penalty must be positive")
         rid = request_id or f"req-{next(self._ids)}"
         if len(prompt) + params.max_new_tokens > self.max_seq_len:
             raise ValueError("prompt + max_new_tokens exceeds max_seq_len")
+        sampling = None
+        if not params.greedy:
+            import hashlib
+            seed = params.seed if params.seed is not None else int.from_bytes(
+                hashlib.sha256(rid.encode()).digest()[:7], "little")
+            sampling = SamplingParams(**{**params.__dict__, "seed": int(seed)})
         self.scheduler.admit(SeqRequest(rid, list(prompt), params.max_new_tokens,
-                                        time.monotonic_ns(), stop_token_ids=params.stop_token_ids))
+                                        time.monotonic_ns(), stop_token_ids=params.stop_token_ids,
+                                        sampling=sampling))
         return rid
 
     def cancel(self, request_id: str) -> None:
@@ -130,7 +152,10 @@ class LLMEngine:
                 starts.append(r.prompt_consumed)
                 pages.append(self.kv.seqs[rid].pages)
                 rids.append((rid, n))
-            toks = self.runner.prefill(ids, starts, pages).tolist()
+            samp = [sch.running[rid].sampling for rid, _ in rids]
+            hist = [sch.running[rid].prompt for rid, _ in rids]
+            toks = self.runner.prefill(ids, starts, pages,
+                                       sampling=samp if any(samp) else None, history=hist).tolist()
             for (rid, n), t in zip(rids, toks):
                 r = sch.running[rid]
                 done = r.prompt_consumed + n >= len(r.prompt)
@@ -143,7 +168,13 @@ class LLMEngine:
             ids = [r.output[-1] for r in reqs]
             positions = [r.context_len - 1 for r in reqs]
             pages = [self.kv.seqs[r.request_id].pages for r in reqs]
-            toks = self.runner.decode(ids, positions, pages)
+            samp = [r.sampling for r in reqs]
+            if any(samp):
+                toks = self.runner.decode(ids, positions, pages, sampling=samp,
+                                          history=[r.prompt + r.output for r in reqs],
+                                          steps=[len(r.output) for r in reqs])
+            else:
+                toks = self.runner.decode(ids, positions, pages)
             for r, t in zip(reqs, toks):
                 sch.mark_decode(r.request_id, t)
                 self.kv.seqs[r.request_id].length = r.context_len

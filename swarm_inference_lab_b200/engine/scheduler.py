@@ -45,6 +45,7 @@ class SeqRequest:
     stop_token_ids: tuple[int, ...] = ()
     first_token_ns: int = 0
     finish_ns: int = 0
+    sampling: object | None = None   # SamplingParams of a non-greedy request (None: greedy)
 
     @property
     def prefill_complete(self) -> bool:

@@ -128,7 +128,10 @@ def from_hf_config(cfg: dict) -> ModelConfig:
                            moe_intermediate_size=int(cfg["intermediate_size"]),
                            norm_topk_prob=True, **common)
     if mt == "qwen3_moe":
-        return ModelConfig(family="qwen3_moe", qk_norm=True, num_experts=int(cfg["num_experts"]),
+        if int(cfg.get("decoder_sparse_step", 1)) != 1 or cfg.get("mlp_only_layers"):
+            raise ValueError("qwen3_moe with dense interleaved layers is not supported")
+        n_exp = cfg.get("num_experts", cfg.get("num_local_experts"))
+        return ModelConfig(family="qwen3_moe", qk_norm=True, num_experts=int(n_exp),
                            num_experts_per_tok=int(cfg["num_experts_per_tok"]),
                            moe_intermediate_size=int(cfg["moe_intermediate_size"]),
                            norm_topk_prob=bool(cfg.get("norm_topk_prob", True)), **common)

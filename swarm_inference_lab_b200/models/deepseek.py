@@ -119,6 +119,27 @@ class MLAWeights:
     @classmethod
     def random(cls, cfg: ModelConfig, ep: TPInfo, device, seed: int = 0,
                num_layers: int | None = None) -> "MLAWeights":
+        """Random N(0, 0.02) weights (norms 1; router bias N(0, 0.01)); projections are
+        quantised to e4m3 with 128x128 block scales."""
+        dev = torch.device(device)
+
+        def get(name, shape, dtype=torch.bfloat16):
+            if name.endswith("norm.weight") or "layernorm" in name:
+                return torch.ones(shape, dtype=dtype, device=dev)
+            std = 0.01 if name.endswith("e_score_correction_bias") else 0.02
+            return random_tensor(shape, seed, name, dev, dtype, std)
+
+        def fp8w(name, shape):
+            return random_fp8(shape, seed, name, dev)
+
+        return cls.from_source(cfg, ep, get, fp8w, dev, num_layers=num_layers)
+
+    @classmethod
+    def from_source(cls, cfg: ModelConfig, ep: TPInfo, get, fp8w, device,
+                    num_layers: int | None = None) -> "MLAWeights":
+        """Builds this rank's weights from ``get(name, shape, dtype)`` (plain tensors) and
+        ``fp8w(name, shape)`` (e4m3 codes with 128x128 block scales), in Hugging Face
+        DeepSeek-V3 names.  Experts are sharded expert parallel."""
         if not cfg.mla:
             raise ValueError("MLAWeights needs an MLA config")
         dev = torch.device(device)
@@ -133,55 +154,53 @@ class MLAWeights:
         Is = Ie * max(1, cfg.n_shared_experts)
         bf = torch.bfloat16
 
-        def rnd(shape, name, dtype=bf, std=0.02):
-            return random_tensor(shape, seed, name, dev, dtype, std)
-
         layers = []
         for li in range(num_layers if num_layers is not None else cfg.num_layers):
             p = f"model.layers.{li}."
             a = p + "self_attn."
-            q_a = random_fp8((qr, H), seed, a + "q_a_proj.weight", dev)
-            kv_a = random_fp8((_pad128(kr + rdim), H), seed, a + "kv_a_proj_with_mqa.weight", dev)
+            q_a = fp8w(a + "q_a_proj.weight", (qr, H))
+            kv_a = pad_rows_fp8(fp8w(a + "kv_a_proj_with_mqa.weight", (kr + rdim, H)), _pad128(kr + rdim))
             qkv_a = pad_rows_fp8(cat_fp8([q_a, kv_a]), _pad128(qr + kr + rdim))
-            kv_b = rnd((Hh * (nope + vd), kr), a + "kv_b_proj.weight").view(Hh, nope + vd, kr)
+            kv_b = get(a + "kv_b_proj.weight", (Hh * (nope + vd), kr), bf).view(Hh, nope + vd, kr)
             L = MLALayerWeights(
-                attn_norm=torch.ones(H, dtype=bf, device=dev),
+                attn_norm=get(p + "input_layernorm.weight", (H,), bf),
                 w_qkv_a=qkv_a,
-                q_a_norm=torch.ones(qr, dtype=bf, device=dev),
-                w_q_b=random_fp8((Hh * (nope + rdim), qr), seed, a + "q_b_proj.weight", dev),
-                kv_a_norm=torch.ones(kr, dtype=torch.float32, device=dev),
+                q_a_norm=get(a + "q_a_layernorm.weight", (qr,), bf),
+                w_q_b=fp8w(a + "q_b_proj.weight", (Hh * (nope + rdim), qr)),
+                kv_a_norm=get(a + "kv_a_layernorm.weight", (kr,), torch.float32),
                 w_uk=kv_b[:, :nope, :].transpose(1, 2).reshape(Hh * kr, nope).contiguous(),
                 w_uv=kv_b[:, nope:, :].reshape(Hh * vd, kr).contiguous(),
-                w_o=random_fp8((H, Hh * vd), seed, a + "o_proj.weight", dev),
-                mlp_norm=torch.ones(H, dtype=bf, device=dev),
+                w_o=fp8w(a + "o_proj.weight", (H, Hh * vd)),
+                mlp_norm=get(p + "post_attention_layernorm.weight", (H,), bf),
             )
             m = p + "mlp."
             if li < cfg.first_k_dense or not cfg.is_moe:
                 L.dense = True
-                L.w_gate_up = cat_fp8([random_fp8((I, H), seed, m + "gate_proj.weight", dev),
-                                       random_fp8((I, H), seed, m + "up_proj.weight", dev)])
-                L.w_down = random_fp8((H, I), seed, m + "down_proj.weight", dev)
+                L.w_gate_up = cat_fp8([fp8w(m + "gate_proj.weight", (I, H)),
+                                       fp8w(m + "up_proj.weight", (I, H))])
+                L.w_down = fp8w(m + "down_proj.weight", (H, I))
             else:
                 L.dense = False
-                L.router = rnd((E, H), m + "gate.weight")
-                L.router_bias = rnd((E,), m + "gate.e_score_correction_bias", torch.float32, 0.01)
+                L.router = get(m + "gate.weight", (E, H), bf)
+                L.router_bias = get(m + "gate.e_score_correction_bias", (E,), torch.float32)
                 gu, dn = [], []
                 for e in range(e0, e0 + el):
                     x = m + f"experts.{e}."
-                    gu.append(random_fp8((Ie, H), seed, x + "gate_proj.weight", dev))
-                    gu.append(random_fp8((Ie, H), seed, x + "up_proj.weight", dev))
-                    dn.append(random_fp8((H, Ie), seed, x + "down_proj.weight", dev))
+                    gu.append(fp8w(x + "gate_proj.weight", (Ie, H)))
+                    gu.append(fp8w(x + "up_proj.weight", (Ie, H)))
+                    dn.append(fp8w(x + "down_proj.weight", (H, Ie)))
                 L.experts_gate_up = cat_fp8(gu) if gu else None
                 L.experts_down = cat_fp8(dn) if dn else None
                 if cfg.n_shared_experts:
-                    s = m + "shared_experts."
-                    L.shared_gate_up = cat_fp8([random_fp8((Is, H), seed, s + "gate_proj.weight", dev),
-                                                random_fp8((Is, H), seed, s + "up_proj.weight", dev)])
-                    L.shared_down = random_fp8((H, Is), seed, s + "down_proj.weight", dev)
+                    s_ = m + "shared_experts."
+                    L.shared_gate_up = cat_fp8([fp8w(s_ + "gate_proj.weight", (Is, H)),
+                                                fp8w(s_ + "up_proj.weight", (Is, H))])
+                    L.shared_down = fp8w(s_ + "down_proj.weight", (H, Is))
             layers.append(L)
-        embed = rnd((cfg.vocab_size, H), "model.embed_tokens.weight")
-        lm_head = rnd((cfg.vocab_size, H), "lm_head.weight")
-        return cls(cfg, ep, embed, layers, torch.ones(H, dtype=bf, device=dev), lm_head, e0, el)
+        embed = get("model.embed_tokens.weight", (cfg.vocab_size, H), bf)
+        name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
+        lm_head = get(name, (cfg.vocab_size, H), bf)
+        return cls(cfg, ep, embed, layers, get("model.norm.weight", (H,), bf), lm_head, e0, el)
 
     def nbytes(self) -> int:
         n = 0

@@ -48,6 +48,27 @@ class MoEWeights(DenseWeights):
     def random(cls, cfg: ModelConfig, tp: TPInfo, device, seed: int = 0, dtype=torch.bfloat16,
                std: float = 0.02, layer_range: tuple[int, int] | None = None,
                with_embed: bool = True, with_head: bool = True) -> "MoEWeights":
+        """Random N(0, std) weights (norms 1, router bias 0), generated per tensor on
+        ``device`` so every expert-parallel degree sees the same model."""
+        dev = torch.device(device)
+
+        def get(name, shape):
+            if name.endswith("norm.weight") or "layernorm" in name:
+                return torch.ones(shape, device=dev, dtype=dtype)
+            if name.endswith("e_score_correction_bias"):
+                return torch.zeros(shape, device=dev, dtype=torch.float32)
+            return random_tensor(shape, seed, name, dev, dtype, std)
+
+        return cls.from_full(cfg, tp, get, device, dtype, layer_range=layer_range,
+                             with_embed=with_embed, with_head=with_head)
+
+    @classmethod
+    def from_full(cls, cfg: ModelConfig, tp: TPInfo, get, device, dtype=torch.bfloat16,
+                  layer_range: tuple[int, int] | None = None, with_embed: bool = True,
+                  with_head: bool = True) -> "MoEWeights":
+        """Shard full tensors from ``get(name, shape)`` (Hugging Face Qwen3-MoE / DeepSeek
+        names; a checkpoint source maps other families onto them) for this rank: attention
+        tensor parallel, experts expert parallel (rank r owns [r*E/ep, (r+1)*E/ep))."""
         dev = torch.device(device)
         H, D, E, I = cfg.hidden_size, cfg.head_dim, cfg.num_experts, cfg.moe_intermediate_size
         q0, nq = tp.heads(cfg.num_heads)
@@ -59,59 +80,63 @@ class MoEWeights(DenseWeights):
         e0 = tp.rank * el
         lo, hi = layer_range or (0, cfg.num_layers)
 
-        def rnd(shape, name):
-            return random_tensor(shape, seed, name, dev, dtype, std)
+        def t(name, shape):
+            return get(name, shape).to(device=dev, dtype=dtype)
 
         layers = []
         for li in range(lo, hi):
             p = f"model.layers.{li}."
-            wq = rnd((cfg.num_heads * D, H), p + "self_attn.q_proj.weight")
-            wk = rnd((cfg.num_kv_heads * D, H), p + "self_attn.k_proj.weight")
-            wv = rnd((cfg.num_kv_heads * D, H), p + "self_attn.v_proj.weight")
+            wq = t(p + "self_attn.q_proj.weight", (cfg.num_heads * D, H))
+            wk = t(p + "self_attn.k_proj.weight", (cfg.num_kv_heads * D, H))
+            wv = t(p + "self_attn.v_proj.weight", (cfg.num_kv_heads * D, H))
             wqkv = torch.cat([wq[q0 * D:(q0 + nq) * D], wk[k0 * D:(k0 + nk) * D],
                               wv[k0 * D:(k0 + nk) * D]]).contiguous()
-            wo = rnd((H, cfg.num_heads * D), p + "self_attn.o_proj.weight")[:, q0 * D:(q0 + nq) * D].contiguous()
-            ones = torch.ones(H, dtype=dtype, device=dev)
-            L = MoELayerWeights(attn_norm=ones, wqkv=wqkv, wo=wo, mlp_norm=ones.clone(),
+            wo = t(p + "self_attn.o_proj.weight", (H, cfg.num_heads * D))[:, q0 * D:(q0 + nq) * D].contiguous()
+            L = MoELayerWeights(attn_norm=t(p + "input_layernorm.weight", (H,)).contiguous(),
+                                wqkv=wqkv, wo=wo,
+                                mlp_norm=t(p + "post_attention_layernorm.weight", (H,)).contiguous(),
                                 w_gate_up=None, w_down=None,
-                                q_norm=torch.ones(D, dtype=dtype, device=dev) if cfg.qk_norm else None,
-                                k_norm=torch.ones(D, dtype=dtype, device=dev) if cfg.qk_norm else None)
+                                q_norm=t(p + "self_attn.q_norm.weight", (D,)) if cfg.qk_norm else None,
+                                k_norm=t(p + "self_attn.k_norm.weight", (D,)) if cfg.qk_norm else None)
+            del wq, wk, wv
             if li < cfg.first_k_dense:
                 i0, ni = tp.split(cfg.intermediate_size)
-                g = rnd((cfg.intermediate_size, H), p + "mlp.gate_proj.weight")[i0:i0 + ni]
-                u = rnd((cfg.intermediate_size, H), p + "mlp.up_proj.weight")[i0:i0 + ni]
+                g = t(p + "mlp.gate_proj.weight", (cfg.intermediate_size, H))[i0:i0 + ni]
+                u = t(p + "mlp.up_proj.weight", (cfg.intermediate_size, H))[i0:i0 + ni]
                 L.w_gate_up = torch.cat([g, u]).contiguous()
-                L.w_down = rnd((H, cfg.intermediate_size), p + "mlp.down_proj.weight")[:, i0:i0 + ni].contiguous()
+                L.w_down = t(p + "mlp.down_proj.weight", (H, cfg.intermediate_size))[:, i0:i0 + ni].contiguous()
                 L.dense = True
             else:
-                L.router = rnd((E, H), p + "mlp.gate.weight")
+                L.router = t(p + "mlp.gate.weight", (E, H)).contiguous()
                 if cfg.router == "sigmoid_group":
-                    L.router_bias = torch.zeros(E, dtype=torch.float32, device=dev)
-                # Local experts, generated per expert so any EP degree sees the same model.
+                    L.router_bias = get(p + "mlp.gate.e_score_correction_bias", (E,)).to(
+                        device=dev, dtype=torch.float32).contiguous()
+                # Local experts, read one by one so any EP degree sees the same model.
                 gu, dn = [], []
                 for e in range(e0, e0 + el):
                     q = f"{p}mlp.experts.{e}."
-                    gu.append(rnd((I, H), q + "gate_proj.weight"))
-                    gu.append(rnd((I, H), q + "up_proj.weight"))
-                    dn.append(rnd((H, I), q + "down_proj.weight"))
+                    gu.append(t(q + "gate_proj.weight", (I, H)))
+                    gu.append(t(q + "up_proj.weight", (I, H)))
+                    dn.append(t(q + "down_proj.weight", (H, I)))
                 L.experts_gate_up = torch.cat(gu).contiguous()
                 L.experts_down = torch.cat(dn).contiguous()
                 del gu, dn
                 if cfg.n_shared_experts:
                     Is = I * cfg.n_shared_experts
                     i0, ni = tp.split(Is)
-                    g = rnd((Is, H), p + "mlp.shared_experts.gate_proj.weight")[i0:i0 + ni]
-                    u = rnd((Is, H), p + "mlp.shared_experts.up_proj.weight")[i0:i0 + ni]
+                    g = t(p + "mlp.shared_experts.gate_proj.weight", (Is, H))[i0:i0 + ni]
+                    u = t(p + "mlp.shared_experts.up_proj.weight", (Is, H))[i0:i0 + ni]
                     L.shared_gate_up = torch.cat([g, u]).contiguous()
-                    L.shared_down = rnd((H, Is), p + "mlp.shared_experts.down_proj.weight")[:, i0:i0 + ni].contiguous()
+                    L.shared_down = t(p + "mlp.shared_experts.down_proj.weight", (H, Is))[:, i0:i0 + ni].contiguous()
             layers.append(L)
-        embed = rnd((cfg.vocab_size, H), "model.embed_tokens.weight") if with_embed else None
+        embed = t("model.embed_tokens.weight", (cfg.vocab_size, H)).contiguous() if with_embed else None
         final_norm = lm_head = None
         v0 = 0
         if with_head:
-            final_norm = torch.ones(H, dtype=dtype, device=dev)
+            final_norm = t("model.norm.weight", (H,)).contiguous()
             v0, nv = tp.split(cfg.vocab_size)
-            lm_head = rnd((cfg.vocab_size, H), "lm_head.weight")[v0:v0 + nv].contiguous()
+            name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
+            lm_head = t(name, (cfg.vocab_size, H))[v0:v0 + nv].contiguous()
         w = cls(cfg, tp, embed, layers, final_norm, lm_head, v0)
         w.expert_start = e0
         w.experts_local = el

@@ -15,6 +15,8 @@ import threading
 
 import torch
 
+from ..transport.stage_ring_net import TransportError
+
 STATUS_NAMES = {
     0: "ok",
     1: "timeout waiting for a TMA stage",
@@ -29,6 +31,20 @@ STATUS_NAMES = {
 class KernelStatusError(RuntimeError):
     """A kernel's bounded wait gave up; the host turns the code into this error."""
 
+    def __init__(self, code: int):
+        super().__init__(f"device status {code}: {STATUS_NAMES.get(code, 'unknown')}")
+        self.code = code
+
+
+class PeerTimeoutError(KernelStatusError, TransportError):
+    """A peer GPU's flag never arrived within the wait limit (a transport failure of the
+    NVLink data plane): the group must be rebuilt before its next collective."""
+
+
+def error_for_status(code: int) -> KernelStatusError:
+    """The host-side exception for a non-zero device status code."""
+    return PeerTimeoutError(code) if code == 4 else KernelStatusError(code)
+
 
 class Workspace:
     def __init__(self, device: torch.device, fp32_elems: int = 16 << 20, counters: int = 1 << 16):
@@ -37,13 +53,30 @@ class Workspace:
         self.attn_ws = torch.empty(fp32_elems, dtype=torch.float32, device=self.device)
         self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
         self.attn_counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # Status block: [0] sticky code, [1] unused, [2..3] wait limit in ns (uint64, 0 =
+        # the kernels' compile-time default of 2 s).
+        self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    def code(self) -> int:
+        """The sticky status code (syncs)."""
+        return int(self.status[0].item())
 
     def check(self) -> None:
         """Raise :class:`KernelStatusError` if any kernel recorded a failure (syncs)."""
-        code = int(self.status.item())
+        code = self.code()
         if code != 0:
-            raise KernelStatusError(f"device status {code}: {STATUS_NAMES.get(code, 'unknown')}")
+            raise error_for_status(code)
+
+    def set_wait_limit_ns(self, ns: int) -> None:
+        """Bound every spin-wait of later launches to ``ns`` nanoseconds (0 = default 2 s).
+
+        Stream-ordered on the current stream, so it applies to kernels launched after it.
+        """
+        self.status.view(torch.int64)[1].fill_(int(ns))
+
+    def clear_status(self) -> None:
+        """Clear the sticky code (keeps the wait limit)."""
+        self.status[0].zero_()
 
     def reset(self) -> None:
         self.status.zero_()

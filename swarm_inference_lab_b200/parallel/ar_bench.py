@@ -8,7 +8,8 @@ Per token count, each path runs ``--iters`` back-to-back all-reduces of a [token
 bf16 tensor inside one CUDA graph (the graph a decode step replays): ``nccl`` is
 ``dist.all_reduce`` in place; ``oneshot`` is ``oneshot_allreduce`` of a partial already in
 the symmetric buffer into the residual stream; ``oneshot_norm`` also writes the next
-block's RMSNorm input.  Rank 0 prints one JSON line per (path, tokens) with microseconds
+block's RMSNorm input; ``ll`` / ``ll_norm`` are the low-latency kernel whose flag
+travels inside each 8-byte word.  Rank 0 prints one JSON line per (path, tokens) with microseconds
 per all-reduce and the NVLink roofline of a one-shot push (each rank sends its tensor to
 every peer: (N-1) x bytes at the measured 770 GB/s per direction).
 """
@@ -70,11 +71,13 @@ def main():
     from ..ops._ext import ext
     from ..ops.workspace import get_workspace
     from .comm import NcclComm
+    from .ll_tp import LLTPComm
     from .oneshot_tp import OneShotTPComm
     toks = [int(t) for t in a.tokens.split(",")]
     H = a.hidden
     nccl = NcclComm()
     one = OneShotTPComm(nccl, dev, max_tokens=max(toks), hidden=H)
+    ll = LLTPComm(nccl, dev, max_tokens=max(toks), hidden=H)
     st = get_workspace(dev).status
     nv = None
     if world > 1:
@@ -101,7 +104,17 @@ def main():
         def f_norm():
             ext().oneshot_allreduce_norm(h, one.peers, one.rank, one.flags_off, one.recv_off,
                                          one.partial_off, one.max_elems, nw, 1e-5, x, st)
-        paths = [("nccl", f_nccl), ("oneshot", f_one), ("oneshot_norm", f_norm)]
+        ll._partial(T, H).copy_(part)
+
+        def f_ll():
+            ext().ll_allreduce_norm(h, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
+                                    None, 0.0, None, st)
+
+        def f_ll_norm():
+            ext().ll_allreduce_norm(h, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
+                                    nw, 1e-5, x, st)
+        paths = [("nccl", f_nccl), ("oneshot", f_one), ("oneshot_norm", f_norm), ("ll", f_ll),
+                 ("ll_norm", f_ll_norm)]
         if nv is not None:
             nv._partial(T, H).copy_(part)
             paths += [("nvls", lambda: nv._reduce(h)), ("nvls_norm", lambda: nv._reduce(h, nw, 1e-5, x))]
@@ -131,6 +144,7 @@ def main():
             print(json.dumps({"nvls_check_max_abs_err": err, "ref_max": ref.abs().max().item()}), flush=True)
         nv.close()
     one.close()
+    ll.close()
     dist.destroy_process_group()
 
 

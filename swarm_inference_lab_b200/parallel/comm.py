@@ -37,14 +37,37 @@ class NcclComm:
 
     fused_gemm_allreduce = None
 
-    def __init__(self, group: dist.ProcessGroup | None = None):
+    def __init__(self, group: dist.ProcessGroup | None = None, *, deterministic: bool = False):
         self.group = group
         self.rank = dist.get_rank(group)
         self.size = dist.get_world_size(group)
+        # Deterministic mode: all-gather the partials and add them in rank order in fp32, the
+        # arithmetic of the one-shot NVLink kernels, so both paths give the same bits.
+        self.deterministic = deterministic
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.deterministic and self.size > 1:
+            g = self.all_gather(x)
+            acc = g[0].float()
+            for r in range(1, self.size):
+                acc += g[r].float()
+            x.copy_(acc.to(x.dtype))
+            return x
         dist.all_reduce(x, group=self.group)
         return x
+
+    def all_reduce_residual(self, partial: torch.Tensor, h: torch.Tensor) -> None:
+        """h += sum over ranks of ``partial``; in deterministic mode the fp32 rank-ordered
+        sum is added to h before the single rounding to h's dtype."""
+        if self.deterministic and self.size > 1:
+            g = self.all_gather(partial)
+            acc = g[0].float()
+            for r in range(1, self.size):
+                acc += g[r].float()
+            h.copy_((h.float() + acc).to(h.dtype))
+            return
+        self.all_reduce(partial)
+        h.add_(partial)
 
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)

@@ -1,0 +1,116 @@
+"""Tensor-parallel row-parallel projections with the low-latency one-shot all-reduce.
+
+``LLTPComm`` gives every rank a symmetric buffer (CUDA IPC, mapped by every peer).  A
+row-parallel projection ``h += allreduce(x @ w.T)`` runs as two kernels: the tcgen05
+GEMM writes its partial straight into this rank's buffer, and ``ll_allreduce_norm``
+(``csrc/kernels/allreduce_ll.cu``) sends every 16-byte piece of it, with the call's
+epoch inside each 8-byte word, to every peer, then reads the peers' words from its own
+buffer as soon as their epochs match and sums them in rank order (fp32; every rank gets
+the same bits) into the residual stream -- also writing the next block's RMSNorm input
+when the model asks for it.  There is no system fence and no separate flag, so the
+exchange costs one NVLink crossing.  Prefill-sized calls (more tokens than the buffer
+holds) use GEMM + NCCL.  ``all_reduce`` / ``all_gather`` / ``reduce_scatter`` forward to
+NCCL.
+
+Reference semantics: deterministic rank-ordered all-reduce of row-parallel projections,
+si/microsharding/dense.py:600-708.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import gemm
+from ..ops._ext import ext
+from ..ops.workspace import get_workspace
+from .oneshot_tp import MAX_RANKS, open_symmetric
+
+
+class LLTPComm:
+    kernel = "ll_allreduce_norm"
+
+    def __init__(self, base, device: torch.device, *, max_tokens: int = 128, hidden: int = 4096):
+        self.base = base
+        self.rank = base.rank
+        self.size = base.size
+        if self.size > MAX_RANKS:
+            raise ValueError(f"the one-shot all-reduce supports up to {MAX_RANKS} ranks")
+        if hidden % 8 or hidden > 8192:
+            raise ValueError("hidden size must be a multiple of 8 and at most 8192")
+        self.device = torch.device(device)
+        self.max_tokens = max_tokens
+        self.hidden = hidden
+        self.max_elems = max_tokens * hidden
+        self.ll_off = 256
+        # ll[2 parities][8 sources][max_elems / 2 words of 8 bytes]
+        self.partial_off = self.ll_off + 2 * MAX_RANKS * self.max_elems * 4
+        nbytes = self.partial_off + self.max_elems * 2
+        self.local, self.peers, self._opened = open_symmetric(base, self.device, nbytes)
+        self._views: dict[tuple[int, int], torch.Tensor] = {}
+        torch.cuda.synchronize(self.device)
+        base.barrier()
+
+    # NCCL collectives (prefill path and plumbing)
+    def all_reduce(self, x):
+        return self.base.all_reduce(x)
+
+    def all_gather(self, x):
+        return self.base.all_gather(x)
+
+    def reduce_scatter(self, x):
+        return self.base.reduce_scatter(x)
+
+    def barrier(self):
+        self.base.barrier()
+
+    def _partial(self, T: int, H: int) -> torch.Tensor:
+        v = self._views.get((T, H))
+        if v is None:
+            v = ext().symm_tensor(self.local, self.partial_off, T, H, self.device.index)
+            self._views[(T, H)] = v
+        return v
+
+    def _fits(self, T: int, H: int, h: torch.Tensor) -> bool:
+        return T * H <= self.max_elems and H == self.hidden and h.is_contiguous()
+
+    def fused_gemm_allreduce_residual(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor):
+        """h += allreduce(x @ w.T) over the group; returns None (residual already added)."""
+        T, H = x.shape[0], w.shape[0]
+        if not self._fits(T, H, h):
+            out = gemm.linear(x, w)
+            self.base.all_reduce(out)
+            h.add_(out)
+            return None
+        part = self._partial(T, H)
+        gemm.linear(x, w, out=part)
+        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
+                                self.max_elems, None, 0.0, None, get_workspace(x.device).status)
+        return None
+
+    def fused_gemm_allreduce_residual_norm(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor,
+                                           norm_w: torch.Tensor, eps: float, x_out: torch.Tensor):
+        """h += allreduce(x @ w.T); x_out = rmsnorm(h) * norm_w, in the all-reduce kernel."""
+        T, H = x.shape[0], w.shape[0]
+        if not self._fits(T, H, h):
+            self.fused_gemm_allreduce_residual(x, w, h)
+            from ..ops import norm
+            norm.rmsnorm(h, norm_w, eps, out=x_out)
+            return
+        part = self._partial(T, H)
+        gemm.linear(x, w, out=part)
+        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
+                                self.max_elems, norm_w, float(eps), x_out,
+                                get_workspace(x.device).status)
+
+    fused_gemm_allreduce = None
+
+    def close(self):
+        e = ext()
+        torch.cuda.synchronize(self.device)
+        self._views.clear()
+        for p in self._opened:
+            e.ipc_close(p)
+        self._opened = []
+        if self.local:
+            self.base.barrier()
+            e.symm_free(self.local)
+            self.local = 0

@@ -29,6 +29,27 @@ MAX_RANKS = 8
 MAX_CTAS = 256
 
 
+def open_symmetric(base, device: torch.device, nbytes: int):
+    """Allocates a zeroed ``nbytes`` buffer on this rank and maps every peer's buffer
+    (CUDA IPC).  Returns ``(local, peers, opened)``: this rank's pointer, every rank's
+    pointer in rank order, and the peer mappings to close."""
+    e = ext()
+    dev = torch.device(device).index
+    local = e.symm_alloc(nbytes, dev)
+    handles = [None] * base.size
+    dist.all_gather_object(handles, (base.rank, e.ipc_handle(local)), group=base.group)
+    peers = [0] * base.size
+    opened = []
+    for r, h in handles:
+        if r == base.rank:
+            peers[r] = local
+        else:
+            p = e.ipc_open(h, dev)
+            peers[r] = p
+            opened.append(p)
+    return local, peers, opened
+
+
 class OneShotTPComm:
     def __init__(self, base, device: torch.device, *, max_tokens: int = 128, hidden: int = 4096):
         self.base = base
@@ -44,20 +65,7 @@ class OneShotTPComm:
         self.max_elems = max_tokens * hidden
         self.recv_off = ((self.partial_off + self.max_elems * 2 + 255) // 256) * 256
         nbytes = self.recv_off + 2 * MAX_RANKS * self.max_elems * 2
-        e = ext()
-        dev = self.device.index
-        self.local = e.symm_alloc(nbytes, dev)
-        handles = [None] * self.size
-        dist.all_gather_object(handles, (self.rank, e.ipc_handle(self.local)), group=base.group)
-        self.peers = [0] * self.size
-        self._opened = []
-        for r, h in handles:
-            if r == self.rank:
-                self.peers[r] = self.local
-            else:
-                p = e.ipc_open(h, dev)
-                self.peers[r] = p
-                self._opened.append(p)
+        self.local, self.peers, self._opened = open_symmetric(base, self.device, nbytes)
         self._views: dict[tuple[int, int], torch.Tensor] = {}
         torch.cuda.synchronize(self.device)
         base.barrier()

@@ -4,8 +4,8 @@
 
 Builds the same random model at TP=1 (every rank, full weights) and at
 TP=world (sharded) and compares greedy decode logits of the fused
-GEMM+all-reduce path, of GEMM + one-shot NVLink all-reduce, and of the NCCL
-baseline path against TP=1, for a
+GEMM+all-reduce path, of GEMM + one-shot NVLink all-reduce (flag round trip and
+low-latency flag-in-data variants), and of the NCCL baseline path against TP=1, for a
 prefill (NCCL fallback) followed by decode steps (fused kernel), and of the
 sequence-parallel prefill (reduce-scatter / all-gather around the norms).  Rank 0
 prints one JSON line.  Process-group timeout is short so a stuck peer ends
@@ -34,6 +34,7 @@ def main():
     from ..ops.workspace import get_workspace
     from .comm import LocalComm, NcclComm
     from .fused_tp import FusedTPComm
+    from .ll_tp import LLTPComm
     from .oneshot_tp import OneShotTPComm
 
     cfg = preset(os.environ.get("SIL_SELFTEST_MODEL", "tiny-llama-gpu")).replace(num_layers=2)
@@ -80,8 +81,9 @@ def main():
 
     full, tok_full = run(TPInfo(), LocalComm())
     oneshot = OneShotTPComm(nccl, dev, max_tokens=128, hidden=cfg.hidden_size)
+    ll = LLTPComm(nccl, dev, max_tokens=128, hidden=cfg.hidden_size)
     for name, comm, sp in (("nccl", nccl, False), ("fused", fused, False), ("oneshot", oneshot, False),
-                           ("nccl_sequence_parallel_prefill", nccl, True)):
+                           ("ll", ll, False), ("nccl_sequence_parallel_prefill", nccl, True)):
         shard, tok = run(TPInfo(rank, world), comm, sp)
         errs = []
         for a, b in zip(full, shard):
@@ -89,6 +91,26 @@ def main():
             ref = a[:, v0:v0 + b.shape[1]]
             errs.append((ref - b).abs().max().item() / (ref.abs().max().item() + 1e-6))
         results[name] = {"max_rel_err": max(errs), "tokens_equal": bool(torch.equal(tok, tok_full))}
+    # Bit-equality of one row-parallel all-reduce: the low-latency kernel against NCCL in
+    # deterministic mode (all-gather, fp32 rank-ordered sum, one rounding), at 1, 32 and
+    # 128 tokens.
+    det = NcclComm(deterministic=True)
+    bit_equal = True
+    H = cfg.hidden_size
+    for T in (1, 32, 128):
+        g = torch.Generator(device=dev).manual_seed(100 + rank * 10 + T)
+        part = (torch.randn(T, H, device=dev, generator=g) * 0.5).bfloat16()
+        h0 = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(T)).bfloat16()
+        h_ll, h_det = h0.clone(), h0.clone()
+        ll._partial(T, H).copy_(part)
+        from ..ops._ext import ext
+        ext().ll_allreduce_norm(h_ll, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
+                                None, 0.0, None, get_workspace(dev).status)
+        det.all_reduce_residual(part.clone(), h_det)
+        torch.cuda.synchronize()
+        bit_equal &= bool(torch.equal(h_ll, h_det))
+    results["ll_vs_deterministic_nccl_bit_equal"] = {"max_rel_err": 0.0 if bit_equal else 1.0,
+                                                     "tokens_equal": bit_equal}
     get_workspace(dev).check()
     ok = all(r["max_rel_err"] < 0.05 for r in results.values())
     out = torch.tensor([1.0 if ok else 0.0], device=dev)
@@ -97,6 +119,7 @@ def main():
         print(json.dumps({"world": world, "ok": bool(out.item() == 1.0), **results}), flush=True)
     fused.close()
     oneshot.close()
+    ll.close()
     dist.destroy_process_group()
 
 

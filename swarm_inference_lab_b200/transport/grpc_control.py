@@ -16,6 +16,7 @@ si/protocol/messages.py:395-420.
 """
 from __future__ import annotations
 
+import contextvars
 import hashlib
 import json
 
@@ -24,6 +25,23 @@ from google.protobuf import any_pb2, descriptor_pb2, descriptor_pool, message_fa
 
 TYPE_PREFIX = "type.swarm-inference.dev/"
 CHUNK_BYTES = 1 << 20
+
+# Identity fingerprint bound into the caller's client certificate (mutual TLS), set while
+# a handler runs; None on an insecure server or for a certificate without the binding.
+PEER_FINGERPRINT: contextvars.ContextVar[str | None] = contextvars.ContextVar(
+    "peer_fingerprint", default=None)
+
+
+def _peer_fingerprint(ctx) -> str | None:
+    try:
+        auth = ctx.auth_context()
+    except Exception:  # noqa: BLE001
+        return None
+    pems = auth.get("x509_pem_cert") or []
+    if not pems:
+        return None
+    from ..security.tls import cert_fingerprint_binding
+    return cert_fingerprint_binding(pems[0])
 
 
 class EnvelopeError(ValueError):
@@ -90,19 +108,27 @@ class Reassembler:
         return c.tensor_id, data
 
 
-COORDINATOR_METHODS = ("Register", "Heartbeat", "Submit", "InspectModel", "PlanModel", "DeployModel",
-                       "UnloadModel", "TopologyStatus", "Workers", "PublishToken")
-WORKER_METHODS = ("Assign", "Execute", "InstallRoute", "DispatchRoute", "Cancel")
+COORDINATOR_METHODS = ("Register", "Heartbeat", "PlanModel", "DeployModel", "UnloadModel",
+                       "TopologyStatus", "Workers", "Status", "PublishToken", "PairingCreate",
+                       "CancelRequest", "SubmitStream")
+WORKER_METHODS = ("Reserve", "Release", "HasArtifact", "FetchArtifact", "VerifyArtifact",
+                  "LoadStage", "UnloadStage", "InstallRoute", "WithdrawRoute", "CheckPeer",
+                  "FreeBytes", "Health")
 
 
 class GrpcControlServer:
     """``handlers[(service, method)] = async fn(kind, obj) -> (kind, obj)``;
-    ``stream_handler = async fn(tensor_id, data) -> bytes`` serves ExecuteStream."""
+    ``server_streams[(service, method)] = async generator fn(kind, obj) -> (kind, obj)...``
+    (server-streaming calls such as SubmitStream); ``stream_handler = async fn(tensor_id,
+    data) -> bytes`` serves ExecuteStream.  While a handler runs, ``PEER_FINGERPRINT``
+    holds the caller's certificate-bound identity fingerprint."""
 
-    def __init__(self, handlers: dict, *, stream_handler=None, host: str = "127.0.0.1", port: int = 0,
+    def __init__(self, handlers: dict, *, stream_handler=None, server_streams: dict | None = None,
+                 host: str = "127.0.0.1", port: int = 0,
                  credentials: grpc.ServerCredentials | None = None):
         self.handlers = handlers
         self.stream_handler = stream_handler
+        self.server_streams = server_streams or {}
         self.host, self.port = host, port
         self.creds = credentials
         self.server = None
@@ -110,12 +136,32 @@ class GrpcControlServer:
     def _unary(self, fn):
         async def call(req, ctx):
             kind, obj = unpack(req)
+            token = PEER_FINGERPRINT.set(_peer_fingerprint(ctx))
             try:
                 rk, robj = await fn(kind, obj)
             except EnvelopeError as exc:
                 await ctx.abort(grpc.StatusCode.INVALID_ARGUMENT, str(exc))
+            except PermissionError as exc:
+                await ctx.abort(grpc.StatusCode.PERMISSION_DENIED, str(exc))
+            finally:
+                PEER_FINGERPRINT.reset(token)
             return pack(rk, robj)
         return grpc.unary_unary_rpc_method_handler(
+            call, request_deserializer=any_pb2.Any.FromString,
+            response_serializer=any_pb2.Any.SerializeToString)
+
+    def _server_stream(self, fn):
+        async def call(req, ctx):
+            kind, obj = unpack(req)
+            token = PEER_FINGERPRINT.set(_peer_fingerprint(ctx))
+            try:
+                async for rk, robj in fn(kind, obj):
+                    yield pack(rk, robj)
+            except PermissionError as exc:
+                await ctx.abort(grpc.StatusCode.PERMISSION_DENIED, str(exc))
+            finally:
+                PEER_FINGERPRINT.reset(token)
+        return grpc.unary_stream_rpc_method_handler(
             call, request_deserializer=any_pb2.Any.FromString,
             response_serializer=any_pb2.Any.SerializeToString)
 
@@ -139,6 +185,8 @@ class GrpcControlServer:
         by_service: dict[str, dict] = {}
         for (svc, method), fn in self.handlers.items():
             by_service.setdefault(svc, {})[method] = self._unary(fn)
+        for (svc, method), fn in self.server_streams.items():
+            by_service.setdefault(svc, {})[method] = self._server_stream(fn)
         if self.stream_handler is not None:
             by_service.setdefault("swarm.v1.Worker", {})["ExecuteStream"] = self._stream()
         for svc, methods in by_service.items():
@@ -168,6 +216,15 @@ class GrpcControlClient:
                                       response_deserializer=any_pb2.Any.FromString)
         rep = await fn(pack(kind, obj), timeout=self.timeout)
         return unpack(rep, expect)
+
+    async def call_stream(self, service: str, method: str, kind: str, obj: dict,
+                          timeout: float | None = None):
+        """Server-streaming call: async iterator of (kind, obj) replies."""
+        fn = self.channel.unary_stream(f"/{service}/{method}",
+                                       request_serializer=any_pb2.Any.SerializeToString,
+                                       response_deserializer=any_pb2.Any.FromString)
+        async for rep in fn(pack(kind, obj), timeout=timeout):
+            yield unpack(rep)
 
     async def execute_stream(self, tensor_id: str, data: bytes, chunk_bytes: int = CHUNK_BYTES) -> bytes:
         fn = self.channel.stream_stream("/swarm.v1.Worker/ExecuteStream",
