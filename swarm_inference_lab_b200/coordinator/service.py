@@ -319,6 +319,9 @@ class CoordinatorCore:
             failed = await self._failed_workers(m)
             if not failed:
                 raise exc
+            for ag in self.agents.values():   # any healthy worker may become the replacement
+                ag.model, ag.model_revision = m.model, m.revision
+                ag.num_stages = len(m.deployment.stages)
             for wid in failed:
                 self.registry.mark_unhealthy(wid)
                 self.events.append({"event": "stage_failed", "worker": wid, "at": time.time()})
