@@ -32,6 +32,7 @@ from dataclasses import dataclass, field
 from pathlib import Path
 
 from ..protocol import stage_ring as sr
+from ..telemetry.metrics import METRICS
 from ..runtime.worker_runtime import COORDINATOR_SERVICE, WORKER_SERVICE, artifact_id_for
 from ..transport.grpc_control import PEER_FINGERPRINT, GrpcControlClient, GrpcControlServer
 from ..transport.stage_ring_net import ConnectionPool, TransportError
@@ -186,6 +187,8 @@ class CoordinatorCore:
                                             dict(req.get("capabilities", {}),
                                                  control_endpoint=req["control_endpoint"])))
         self.events.append({"event": "worker_registered", "worker": wid, "at": time.time()})
+        METRICS.inc("coordinator_registrations")
+        METRICS.set("coordinator_workers_healthy", len(self.registry.healthy()))
         return {"accepted": True, "heartbeat_s": self.heartbeat_s,
                 "coordinator_fingerprint": self.identity.fingerprint}
 
@@ -195,12 +198,15 @@ class CoordinatorCore:
         if wid not in self.registry.workers:
             return {"ok": False, "reregister": True}
         self.registry.heartbeat(wid)
+        METRICS.inc("coordinator_heartbeats")
         return {"ok": True}
 
     def sweep(self) -> list[str]:
         dead = self.registry.sweep()
         for wid in dead:
             self.events.append({"event": "worker_lost", "worker": wid, "at": time.time()})
+            METRICS.inc("coordinator_workers_lost")
+        METRICS.set("coordinator_workers_healthy", len(self.registry.healthy()))
         return dead
 
     async def _sweep_loop(self) -> None:
@@ -328,6 +334,7 @@ class CoordinatorCore:
                 await self.deployer.recover(m.deployment.deployment_id, wid)
             self.events.append({"event": "route_recovered", "model": m.name,
                                 "generation": m.deployment.generation, "at": time.time()})
+            METRICS.inc("coordinator_recoveries")
             return self._route(m)
 
     # ------------------------------------------------------------ requests
@@ -348,10 +355,17 @@ class CoordinatorCore:
         ctl = SessionController(self._route(m), recover=lambda r, e: self._recover(m, r, e),
                                 return_logits=bool(req.get("return_logits")))
         yield {"event": "accepted", "request_id": rid, "generation": m.deployment.generation}
+        METRICS.inc("coordinator_requests")
         t0 = time.perf_counter()
+        t_last = t0
         try:
             async for ev in ctl.stream(prompt, int(req.get("max_tokens", 16)), rid):
                 if ev["event"] == "token":
+                    now = time.perf_counter()
+                    METRICS.observe("coordinator_ttft_ms" if ev["index"] == 0
+                                    else "coordinator_tpot_ms", (now - t_last) * 1e3)
+                    METRICS.inc("coordinator_tokens")
+                    t_last = now
                     rec.tokens.append(ev["token"])
                     if self.state is not None:
                         self.state.accept_token(rid, ev["token"])
@@ -369,6 +383,9 @@ class CoordinatorCore:
                    "generations": rec.generations, "seconds": time.perf_counter() - t0}
         except Exception as exc:  # noqa: BLE001 - reported to the caller as an event
             rec.state = "FAILED"
+            METRICS.inc("coordinator_requests_failed")
+            if isinstance(exc, TransportError):
+                METRICS.inc("coordinator_transport_errors")
             yield {"event": "failed", "request_id": rid, "error": f"{type(exc).__name__}: {exc}"}
         finally:
             if self.state is not None:
@@ -421,6 +438,9 @@ class CoordinatorRpcServer:
         async def status(obj):
             return core.status()
 
+        async def metrics(obj):
+            return {"snapshot": METRICS.snapshot(), "prometheus": METRICS.prometheus()}
+
         async def plan(obj):
             return {"plan": core.plan(obj["model"], obj.get("stages"))}
 
@@ -446,6 +466,7 @@ class CoordinatorRpcServer:
             ("Status", "CoordinatorStatus", status),
             ("PlanModel", "PlanReply", plan),
             ("PairingCreate", "PairingInvitation", pairing_create),
+            ("Metrics", "MetricsReply", metrics),
         }
         self.server = GrpcControlServer(
             {(COORDINATOR_SERVICE, m): unary(fn, rk) for m, rk, fn in handlers},
@@ -484,6 +505,9 @@ class CoordinatorClient:
 
     async def plan(self, model: dict, stages: int | None = None) -> list[dict]:
         return (await self._call("PlanModel", "PlanRequest", {"model": model, "stages": stages}))["plan"]
+
+    async def metrics(self) -> dict:
+        return await self._call("Metrics", "MetricsRequest", {})
 
     async def pairing_uri(self, ttl_s: float = 600.0) -> str:
         return (await self._call("PairingCreate", "PairingRequest", {"ttl_s": ttl_s}))["uri"]

@@ -25,6 +25,7 @@ from dataclasses import dataclass, field
 import torch
 
 from ..protocol import stage_ring as sr
+from ..telemetry.metrics import METRICS
 from ..transport.stage_ring_net import ConnectionPool, TransportError
 from ..transport.tensor_codec import pack_tensor, unpack_tensor
 from .executors import StageExecutor
@@ -140,6 +141,7 @@ class StageOwner:
 
     def _error(self, req: sr.StageMessage, exc: Exception) -> list[sr.StageMessage]:
         self.stats.rejected += 1
+        METRICS.inc("stage_rejected_frames", stage=self.spec.stage_id, error=type(exc).__name__)
         self.stats.errors.append(f"{type(exc).__name__}: {exc}")
         return [self._reply(req, sr.Operation.ERROR, status="ERROR",
                             attrs={"error": type(exc).__name__, "detail": str(exc)})]
@@ -188,8 +190,10 @@ class StageOwner:
                 self.seq_in.check(msg)
         except (sr.SessionError, sr.SequenceError) as exc:
             return self._error(msg, exc)
+        METRICS.inc("stage_frames", stage=self.spec.stage_id, op=op.name)
         if self._inflight >= self.max_queue:
             self.stats.rejected += 1
+            METRICS.inc("stage_backpressure", stage=self.spec.stage_id)
             return [self._reply(msg, sr.Operation.ERROR, status="ERROR", attrs={
                 "error": "BackpressureError", "detail": f"execution queue full ({self.max_queue})",
                 "retry_after_ms": 5})]
@@ -246,7 +250,9 @@ class StageOwner:
         t0 = time.perf_counter()
         async with self._lock:
             y = await asyncio.to_thread(self.ex.forward, msg.session_id, x, msg.token_position)
-        self.stats.forward_ms += (time.perf_counter() - t0) * 1e3
+        dt_ms = (time.perf_counter() - t0) * 1e3
+        self.stats.forward_ms += dt_ms
+        METRICS.observe("stage_forward_ms", dt_ms, stage=self.spec.stage_id)
         if self.spec.is_last:
             last = y[-1].float()
             token = int(torch.argmax(last))  # lowest id on ties

@@ -32,6 +32,7 @@ from dataclasses import dataclass
 import torch
 
 from ..protocol import stage_ring as sr
+from ..telemetry.metrics import METRICS
 from ..transport.grpc_control import GrpcControlClient, GrpcControlServer
 from ..transport.stage_ring_net import StageRingServer
 from .executors import ReferenceStageExecutor, StageSpec
@@ -164,12 +165,13 @@ class WorkerRuntime:
                     "generation": self.owner.route.generation if self.owner else 0,
                     "deployment_id": self.deployment_id, "at": time.time()})
                 self.heartbeats += 1
+                METRICS.inc("worker_heartbeats")
                 if rep.get("reregister"):
                     await self.register()
             except asyncio.CancelledError:
                 raise
             except Exception:  # noqa: BLE001 - the coordinator may be restarting
-                pass
+                METRICS.inc("worker_heartbeat_failures")
 
     async def stop(self) -> None:
         if self._hb_task is not None:
@@ -298,4 +300,5 @@ class WorkerRuntime:
              "deployment_id": self.deployment_id}
         if self.owner is not None:
             h.update(self.owner.health())
+        h["metrics"] = METRICS.snapshot()
         return "WorkerHealth", h

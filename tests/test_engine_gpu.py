@@ -6,28 +6,35 @@ pytestmark = pytest.mark.gpu
 
 
 def test_tiny_llama_generate_matches_reference():
+    """Greedy tokens of the bf16 kernels against an fp32 oracle, teacher-forced on the
+    engine's own output: every emitted token is within the bf16 error bound of the fp32
+    maximum, and wherever the fp32 top-2 margin exceeds that bound it is the fp32 argmax."""
     from swarm_inference_lab_b200.engine.engine import LLMEngine, SamplingParams
     from swarm_inference_lab_b200.models.config import TINY_LLAMA_GPU
+    from swarm_inference_lab_b200.models.dense import DenseWeights, TPInfo
     from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
     cfg = TINY_LLAMA_GPU
-    eng = LLMEngine(cfg, device="cuda", seed=3, max_batch=8, max_seq_len=512, kv_pages=64)
+    w = DenseWeights.random(cfg, TPInfo(), "cuda", seed=3, std=0.06)
+    eng = LLMEngine(cfg, device="cuda", weights=w, max_batch=8, max_seq_len=512, kv_pages=64)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (5, 70, 130)]
-    outs, m = eng.generate(prompts, SamplingParams(max_new_tokens=12))
-    ref = ReferenceDecoder(cfg, random_source(3, device="cuda"), device="cuda", dtype=torch.bfloat16)
-    agree = 0
-    total = 0
+    outs, m = eng.generate(prompts, SamplingParams(max_new_tokens=16))
+    ref = ReferenceDecoder(cfg, random_source(3, std=0.06, device="cuda"), device="cuda",
+                           dtype=torch.float32)
+    decisive = total = 0
     for p, o in zip(prompts, outs):
-        toks, _ = ref.greedy_generate(p, 12)
-        # bf16 kernels vs bf16 eager torch: allow a late divergence, require a long common prefix
-        n = 0
-        while n < len(toks) and toks[n] == o.token_ids[n]:
-            n += 1
-        agree += n
-        total += len(toks)
-        assert n >= 4, (toks, o.token_ids)
+        seq = torch.tensor(p + o.token_ids, device="cuda")
+        lg = ref.forward(seq).float()[len(p) - 1:len(p) - 1 + len(o.token_ids)]
+        tol = 0.02 * lg.abs().max().item() + 1e-3
+        top2 = lg.topk(2, dim=-1).values
+        for i, t in enumerate(o.token_ids):
+            assert lg[i, t].item() >= top2[i, 0].item() - tol, (i, t, lg[i].argmax().item())
+            if (top2[i, 0] - top2[i, 1]).item() > tol:
+                decisive += 1
+                assert t == int(lg[i].argmax()), (i, t, int(lg[i].argmax()))
+            total += 1
     assert m.decode_steps > 0
-    assert agree / total > 0.6
+    assert decisive >= total // 4, (decisive, total)
 
 
 def test_tiny_llama_logits_close():
@@ -52,7 +59,7 @@ def test_tiny_llama_logits_close():
     ref = ReferenceDecoder(cfg, random_source(5, device="cuda"), device="cuda", dtype=torch.float32)
     rl = ref.forward(ids)
     err = (logits - rl).abs().max().item()
-    assert err < 0.05 * rl.abs().max().item() + 0.02, err
+    assert err < 0.02 * rl.abs().max().item() + 2e-3, err
 
 
 def test_speculative_decoding_is_exact_wrt_its_verifier():
