@@ -130,7 +130,8 @@ class MLAWeights:
             return random_tensor(shape, seed, name, dev, dtype, std)
 
         def fp8w(name, shape):
-            return random_fp8(shape, seed, name, dev)
+            # Rows padded to a whole 128-row scale block (the padding rows are never read).
+            return random_fp8((_pad128(shape[0]), shape[1]), seed, name, dev)
 
         return cls.from_source(cfg, ep, get, fp8w, dev, num_layers=num_layers)
 
