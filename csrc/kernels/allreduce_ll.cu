@@ -200,7 +200,93 @@ __global__ void __launch_bounds__(1024) ll_allreduce_norm_kernel(const LLArgs a)
   }
 }
 
+// Distributed greedy selection over a vocabulary-parallel LM head: every rank holds the
+// argmax of its vocabulary shard per row; each rank sends {value, epoch, global id, epoch}
+// (one 16-byte word) per row to every peer and picks, per row, the largest value over the
+// ranks with the lowest global id on ties -- the same answer on every rank.  Its own epoch
+// counter lives at byte 8 of the state block.
+__global__ void __launch_bounds__(128) ll_argmax_exchange_kernel(
+    const LLArgs a, const float* __restrict__ logits, long long ld, const long long* __restrict__ idx,
+    long long vocab_start, int rows, long long slot_off, long long* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  uint32_t* st = reinterpret_cast<uint32_t*>(a.peers[a.rank]) + 2;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(st) + 1u;
+  const int par = epoch & 1;
+  const uint64_t limit = wait_limit_ns(a.status);
+  bool ok = load_status(a.status) == 0;
+  for (int r = threadIdx.x; r < rows && ok; r += blockDim.x) {
+    const long long li = idx[r];
+    const float v = logits[(long long)r * ld + li];
+    const uint32_t gid = static_cast<uint32_t>(vocab_start + li);
+    const uint4 w = make_uint4(__float_as_uint(v), epoch, gid, epoch);
+    for (int p = 0; p < a.world; ++p) {
+      if (p == a.rank) continue;
+      uint4* dst = reinterpret_cast<uint4*>(a.peers[p] + slot_off) +
+                   ((long long)par * kLLMaxRanks + a.rank) * a.max_elems + r;
+      st_vol_v4(dst, w);
+    }
+    float best = v;
+    uint32_t best_id = gid;
+    for (int p = 0; p < a.world; ++p) {
+      if (p == a.rank) continue;
+      const uint4* src = reinterpret_cast<const uint4*>(a.peers[a.rank] + slot_off) +
+                         ((long long)par * kLLMaxRanks + p) * a.max_elems + r;
+      uint4 q = ld_vol_v4(src);
+      if (q.y != epoch || q.w != epoch) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t it = 0;
+        while (q.y != epoch || q.w != epoch) {
+          if ((++it & 255u) == 0 && (load_status(a.status) != 0 || globaltimer_ns() - t0 > limit)) {
+            raise_status(a.status, kStatusTimeoutPeer);
+            ok = false;
+            break;
+          }
+          q = ld_vol_v4(src);
+        }
+        if (!ok) break;
+      }
+      const float qv = __uint_as_float(q.x);
+      if (qv > best || (qv == best && q.z < best_id)) {
+        best = qv;
+        best_id = q.z;
+      }
+    }
+    if (ok) out[r] = best_id;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(st) = epoch;
+}
+
 }  // namespace
+
+// out[r] = global id of the largest logit of row r over every rank's vocabulary shard
+// (lowest id on ties); idx holds this rank's local argmax per row.
+void ll_argmax_exchange(const at::Tensor& logits, const at::Tensor& idx, int64_t vocab_start,
+                        const std::vector<int64_t>& peers, int64_t rank, int64_t slot_off,
+                        int64_t max_rows, at::Tensor& out, const at::Tensor& status) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "ll_argmax_exchange: fp32 logits [B, V]");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && out.scalar_type() == at::kLong,
+              "ll_argmax_exchange: int64 ids");
+  const int world = static_cast<int>(peers.size());
+  const int B = static_cast<int>(logits.size(0));
+  TORCH_CHECK(world >= 1 && world <= kLLMaxRanks && rank >= 0 && rank < world && B <= max_rows &&
+                  idx.numel() >= B && out.numel() >= B && slot_off % 16 == 0,
+              "ll_argmax_exchange: group / rows");
+  if (B == 0) return;
+  c10::cuda::CUDAGuard guard(logits.device());
+  LLArgs a{};
+  for (int i = 0; i < world; ++i) a.peers[i] = peers[i];
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  a.max_elems = max_rows;  // 16-byte words per (parity, source) slot
+  a.status = status.data_ptr<int>();
+  launch_pdl(ll_argmax_exchange_kernel, dim3(1), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+             "ll_argmax_exchange launch", a, logits.data_ptr<float>(), (long long)logits.stride(0),
+             reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), (long long)vocab_start, B,
+             (long long)slot_off, reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
+}
 
 // h [T, H] += sum over ranks of each rank's partial (bf16 at byte offset partial_off of its
 // symmetric buffer); with norm_w defined also x_out = rmsnorm(h) * norm_w.

@@ -97,10 +97,17 @@ void oneshot_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, in
                             const at::Tensor& norm_w, double eps, at::Tensor& x_out,
                             const at::Tensor& status);
 at::Tensor symm_tensor(int64_t ptr, int64_t offset, int64_t rows, int64_t cols, int64_t device);
+void paged_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      const at::Tensor& block_table, const at::Tensor& seq_lens,
+                      const at::Tensor& cu_q, at::Tensor& out, double scale, int64_t max_q_len,
+                      const at::Tensor& status);
 void decode_advance(const at::Tensor& tok, at::Tensor& ids, at::Tensor& out, at::Tensor& meta,
                     const at::Tensor& valid, const at::Tensor& block_table,
                     const c10::optional<at::Tensor>& offsets, const c10::optional<at::Tensor>& history,
                     const c10::optional<at::Tensor>& hist_len);
+void ll_argmax_exchange(const at::Tensor& logits, const at::Tensor& idx, int64_t vocab_start,
+                        const std::vector<int64_t>& peers, int64_t rank, int64_t slot_off,
+                        int64_t max_rows, at::Tensor& out, const at::Tensor& status);
 void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
                        int64_t ll_off, int64_t partial_off, int64_t max_elems,
                        const c10::optional<at::Tensor>& norm_w, double eps,
@@ -115,7 +122,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: tcgen05 GEMM, paged attention, norms, RoPE, sampling";
   m.def("gemm_bf16", &sil::gemm_bf16, "tcgen05 bf16 GEMM with fused epilogue");
   m.def("paged_decode", &sil::paged_decode, "paged GQA decode attention (split-KV)");
-  m.def("paged_prefill", &sil::paged_prefill, "paged causal prefill attention");
+  m.def("paged_prefill", &sil::paged_prefill, "paged causal prefill attention (mma.sync)");
+  m.def("paged_prefill_tc", &sil::paged_prefill_tc,
+        "paged causal prefill attention on tcgen05 (S and O accumulators in TMEM)");
   m.def("rmsnorm", &sil::rmsnorm, "RMSNorm (+ residual add)");
   m.def("rope_kv_write", &sil::rope_kv_write, "q/k-norm + RoPE + paged KV write");
   m.def("embedding", &sil::embedding, "token embedding gather");
@@ -159,6 +168,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_advance", &sil::decode_advance,
         "advance a captured decode step's static inputs (ids, positions, slots, lengths, "
         "sampling offsets and history) from the step's tokens");
+  m.def("ll_argmax_exchange", &sil::ll_argmax_exchange,
+        "distributed greedy selection over a vocabulary-parallel LM head (peer-memory words "
+        "carrying their epoch; lowest global id on ties)");
   m.def("ll_allreduce_norm", &sil::ll_allreduce_norm,
         "one-shot all-reduce with the flag inside every 8-byte word (no fence, no flag round "
         "trip) into h, optionally fused with the next RMSNorm");

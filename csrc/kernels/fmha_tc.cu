@@ -1,0 +1,425 @@
+// Causal paged prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// One CTA per (128-query tile, query head, sequence); 192 threads in three roles:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 tokens (two 64-token
+//               pages of the paged cache) into a two-stage ring;
+//   warp 1      MMA issuer (one elected thread) and TMEM owner:
+//                 S[b] = Q K_j^T           (M=128 queries, N=128 keys, K=128 dims)
+//                 O   += P_{j-1} V_{j-1}   (M=128 queries, N=128 dims, K=128 keys)
+//               with S double buffered in TMEM so the next tile's QK^T runs while the
+//               softmax warps work on the current one;
+//   warps 2..5  softmax and epilogue: thread i owns query row i (TMEM lane i).  It reads its
+//               S row, applies the scale and the causal mask, keeps the running max m and sum
+//               l (exp2 domain), rescales its O row in TMEM only when m grew, writes its P row
+//               (bf16) into shared memory for the PV MMA, and after the last tile writes
+//               O / l as bf16.
+// TMEM: S0, S1, O = 3 x 128 fp32 columns (512 allocated).
+//
+// Shared-memory layouts (all 128-byte swizzled, 1024-byte aligned):
+//   Q  [dim half][128 rows][64 dims]             A operand, K-major
+//   K  [dim half][128 tokens][64 dims]           B operand of QK^T, K-major
+//   V  [dim half][128 tokens][64 dims]           B operand of PV, MN-major (dims contiguous)
+//   P  [token half][128 rows][64 tokens]         A operand of PV, K-major
+// A 64-token page of one KV head is two [64 x 64] TMA boxes; page p of a tile lands at
+// rows 64p..64p+63 of both dim halves.  A tile's second page past the end of the sequence is
+// replaced by its first page (finite values that the mask zeroes).
+//
+// Every wait is bounded (the status word); a CTA whose wait gave up lets its own loads in
+// flight land, frees its TMEM and returns.
+//
+// Replaces the reference's SDPA / FlashAttention-2 prefill (si/model/qwen3.py:916-996).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "sil/host.h"
+#include "sil/ptx.cuh"
+
+namespace sil {
+namespace {
+
+constexpr int kPage = 64;
+constexpr int kD = 128;
+constexpr int kBM = 128;                     // queries per CTA
+constexpr int kBN = 128;                     // keys per tile
+constexpr int kHalf = 128 * 64 * 2;          // one [128 rows x 64] bf16 half-tile: 16 KB
+constexpr int kTile = 2 * kHalf;             // 32 KB
+constexpr int kBox = 64 * 64 * 2;            // one TMA box: 8 KB
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+
+// smem map (offsets from the 1024-aligned base)
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTile;         // 2 stages
+constexpr int kOffV = kOffK + 2 * kTile;     // 2 stages
+constexpr int kOffP = kOffV + 2 * kTile;
+constexpr int kOffBar = kOffP + kTile;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+
+struct FmhaArgs {
+  __nv_bfloat16* out;
+  long long o_stride;      // elements between consecutive tokens of out
+  const int* block_table;
+  long long bt_stride;
+  const int* seq_lens;     // context length incl. the new tokens
+  const int* cu_q;         // [B+1]
+  int Hq, Hkv, G;
+  int num_pages;
+  float scale_log2;
+  int* status;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory descriptor of an MN-major operand with the 128-byte swizzle: 64 MN
+// elements (128 bytes) per row, consecutive K rows 128 bytes apart; `mn_stride` bytes from
+// MN elements 0..63 to 64..127, 1024 bytes per 8 K rows.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t mn_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFFu) << 16;   // LBO: along MN
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;                     // SBO: 8 K rows
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// K-major A/B with 128 rows per dim half (1024-byte 8-row atoms stacked along M/N).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kslice) {
+  return umma_desc_sw128(base + (kslice >> 2) * kHalf + (kslice & 3) * 32);
+}
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
+  return mbar_wait(bar, parity, status, kStatusTimeoutFull);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                           const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const FmhaArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [2]
+  uint64_t* s_empty = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* mma_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  int* sflag = reinterpret_cast<int*>(bars + 13);
+
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int h = hq / args.G;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_wait();  // q and the KV cache come from earlier kernels
+  const int q_begin = args.cu_q[b];
+  const int q_len = args.cu_q[b + 1] - q_begin;
+  const int n_qt = (q_len + kBM - 1) / kBM;
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int kv_len = args.seq_lens[b];
+  const int pos0 = kv_len - q_len;
+  const int q0 = qt * kBM;
+  const bool active_cta = qt < n_qt && load_status(args.status) == 0;
+  const int last_q = min(q0 + kBM - 1, q_len - 1);
+  const int n_keys = active_cta ? min(pos0 + last_q + 1, kv_len) : 0;
+  const int n_tiles = (n_keys + kBN - 1) / kBN;
+  const int n_pages = (kv_len + kPage - 1) / kPage;
+  const int* bt = args.block_table + (long long)b * args.bt_stride;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0 && n_tiles > 0) {
+      // Q: two [128 x 64] boxes of head hq at rows q_begin + q0.
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_2d(smem + kOffQ, &tmQ, q_full, hq * kD, q_begin + q0);
+      tma_load_2d(smem + kOffQ + kHalf, &tmQ, q_full, hq * kD + 64, q_begin + q0);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_bar(&kv_empty[s], ((j >> 1) - 1) & 1, args.status)) {
+          ok = false;
+          break;
+        }
+        int pg[2];
+        for (int p = 0; p < 2; ++p) {
+          const int page = 2 * j + p < n_pages ? 2 * j + p : 2 * j;
+          int pid = bt[page];
+          if (static_cast<unsigned>(pid) >= static_cast<unsigned>(args.num_pages)) {
+            raise_status(args.status, kStatusBadArgument);
+            ok = false;
+          }
+          pg[p] = pid;
+        }
+        if (!ok) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTile);
+        uint8_t* kd = smem + kOffK + s * kTile;
+        uint8_t* vd = smem + kOffV + s * kTile;
+        for (int p = 0; p < 2; ++p) {
+          const int row = (pg[p] * args.Hkv + h) * kPage;
+          for (int d = 0; d < 2; ++d) {
+            tma_load_2d(kd + d * kHalf + p * kBox, &tmK, &kv_full[s], d * 64, row);
+            tma_load_2d(vd + d * kHalf + p * kBox, &tmV, &kv_full[s], d * 64, row);
+          }
+        }
+        issued = j + 1;
+      }
+      sflag[0] = issued;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t idesc_s = umma_idesc_bf16(kBM, kBN);
+      const uint32_t idesc_o = umma_idesc_bf16(kBM, kD) | (1u << 16);  // B (V) MN-major
+      bool ok = wait_bar(q_full, 0, args.status);
+      const uint32_t qa = sbase + kOffQ;
+      const uint32_t pa = sbase + kOffP;
+      for (int j = 0; j <= n_tiles && ok; ++j) {
+        if (j < n_tiles) {
+          const int s = j & 1;
+          if (!wait_bar(&kv_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
+          if (j >= 2 && !wait_bar(&s_empty[s], ((j >> 1) - 1) & 1, args.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t kb = sbase + kOffK + s * kTile;
+          const uint32_t dS = tmem + (s ? kColS1 : kColS0);
+#pragma unroll
+          for (int k = 0; k < kD / 16; ++k)
+            umma_f16(dS, kmajor_desc(qa, k), kmajor_desc(kb, k), idesc_s, k > 0 ? 1u : 0u);
+          umma_commit(&s_full[s]);
+        }
+        if (j >= 1) {
+          const int jp = j - 1, sp = jp & 1;
+          if (!wait_bar(p_full, jp & 1, args.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t vb = sbase + kOffV + sp * kTile;
+#pragma unroll
+          for (int k = 0; k < kBN / 16; ++k)
+            umma_f16(tmem + kColO, kmajor_desc(pa, k),
+                     umma_desc_sw128_mn(vb + k * 2048, kHalf), idesc_o,
+                     (jp > 0 || k > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&kv_empty[sp]);
+        }
+      }
+      // Every MMA this thread issued has finished before TMEM is released (also when a wait
+      // above gave up): one more commit, waited for regardless of the status word.
+      umma_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+  } else {
+    // Softmax / epilogue warps: thread t owns query row t == TMEM lane t.
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const int qi = q0 + row;                 // query index within the sequence
+    const int qpos = pos0 + qi;              // its absolute position
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* prow = smem + kOffP + row * 128;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int s = j & 1;
+      if (!wait_bar(&s_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
+      tc_fence_after();
+      float sv[kBN];
+      const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off;
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32_sync(sa + c * 32, r);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      const int key0 = j * kBN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < kBN; ++t) {
+        const int key = key0 + t;
+        float v = sv[t] * args.scale_log2;
+        if (key > qpos || key >= kv_len) v = -INFINITY;
+        sv[t] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      float rs = 0.f;
+#pragma unroll
+      for (int t = 0; t < kBN; ++t) {
+        const float p = exp2f(sv[t] - m_use);
+        sv[t] = p;
+        rs += p;
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      if (j >= 1) {
+        // PV of the previous tile must be done before O is rescaled and P is overwritten.
+        if (!wait_bar(o_done, (j - 1) & 1, args.status)) { ok = false; break; }
+        tc_fence_after();
+        if (alpha != 1.f) {
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+            tmem_st32(tmem + kColO + lane_off + c * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row -> shared memory, 128-byte swizzle: token half, 16-byte chunk c at c ^ (row & 7).
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float* src = sv + hh * 64 + c * 8;
+          uint4 v;
+          v.x = pack_bf16x2(src[0], src[1]);
+          v.y = pack_bf16x2(src[2], src[3]);
+          v.z = pack_bf16x2(src[4], src[5]);
+          v.w = pack_bf16x2(src[6], src[7]);
+          *reinterpret_cast<uint4*>(prow + hh * kHalf + ((c ^ (row & 7)) << 4)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool store = qi < q_len;
+      __nv_bfloat16* orow = args.out + (long long)(q_begin + qi) * args.o_stride + (long long)hq * kD;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
+        if (store) {
+#pragma unroll
+          for (int t = 0; t < 32; t += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(r[t + 0]) * inv, __uint_as_float(r[t + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(r[t + 2]) * inv, __uint_as_float(r[t + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(r[t + 4]) * inv, __uint_as_float(r[t + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(r[t + 6]) * inv, __uint_as_float(r[t + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + t) = v;
+          }
+        }
+      }
+    }
+  }
+  // Teardown: a producer that gave up lets its own loads land before the CTA exits.
+  __syncthreads();
+  if (warp == 0 && lane == 0 && n_tiles > 0 && load_status(args.status) != 0) {
+    mbar_drain(q_full, 0);
+    const int issued = sflag[0];
+    for (int j = max(0, issued - 2); j < issued; ++j) mbar_drain(&kv_full[j & 1], (j >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+// q: packed [T, Hq, 128] (token stride q.stride(0)); k/v cache [pages, Hkv, 64, 128];
+// cu_q [B+1]; seq_lens [B] (context after append); out [T, Hq*128].
+void paged_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      const at::Tensor& block_table, const at::Tensor& seq_lens,
+                      const at::Tensor& cu_q, at::Tensor& out, double scale, int64_t max_q_len,
+                      const at::Tensor& status) {
+  for (const at::Tensor* c : {&k_cache, &v_cache})
+    TORCH_CHECK(c->is_cuda() && c->scalar_type() == at::kBFloat16 && c->is_contiguous() &&
+                    c->dim() == 4 && c->size(2) == kPage && c->size(3) == kD,
+                "paged_prefill_tc: KV cache must be contiguous bf16 [pages, Hkv, 64, 128]");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.size(2) == kD &&
+                  q.stride(2) == 1 && q.stride(1) == kD && q.stride(0) % 8 == 0,
+              "paged_prefill_tc: q must be [T, Hq, 128] with contiguous heads, 16-byte row pitch");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.stride(0) % 8 == 0,
+              "paged_prefill_tc: out [T, Hq*128] bf16 with a 16-byte row pitch");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  cu_q.scalar_type() == at::kInt,
+              "paged_prefill_tc: int32 block table / seq lens / cu_q");
+  TORCH_CHECK(status.numel() >= 4, "paged_prefill_tc: status block");
+  const int B = seq_lens.size(0), Hq = q.size(1), Hkv = k_cache.size(1);
+  TORCH_CHECK(Hq % Hkv == 0, "paged_prefill_tc: Hq must be a multiple of Hkv");
+  if (B == 0 || max_q_len <= 0) return;
+  c10::cuda::CUDAGuard guard(q.device());
+  FmhaArgs a{};
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.o_stride = out.stride(0);
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = block_table.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.cu_q = cu_q.data_ptr<int>();
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.num_pages = static_cast<int>(k_cache.size(0));
+  a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  a.status = status.data_ptr<int>();
+  const uint64_t T = q.size(0);
+  CUtensorMap tq = make_tmap_2d(q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T,
+                                (uint64_t)Hq * kD, q.stride(0), kBM, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint64_t rows = (uint64_t)k_cache.size(0) * Hkv * kPage;
+  CUtensorMap tk = make_tmap_2d(k_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kD,
+                                kD, kPage, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, kD,
+                                kD, kPage, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  set_smem_limit(reinterpret_cast<const void*>(fmha_prefill_tc_kernel), kSmemBytes,
+                 "cudaFuncSetAttribute(fmha)");
+  dim3 grid((max_q_len + kBM - 1) / kBM, Hq, B);
+  launch_pdl(fmha_prefill_tc_kernel, grid, dim3(kThreads), kSmemBytes,
+             at::cuda::getCurrentCUDAStream(), "paged_prefill_tc launch", tq, tk, tv, a);
+}
+
+}  // namespace sil

@@ -334,6 +334,11 @@ class DenseModel:
         idx = sampling.argmax(logits)
         if self.tp.size == 1:
             return idx
+        exchange = getattr(self.comm, "argmax_exchange", None)
+        if exchange is not None:
+            out = exchange(logits, idx, self.w.vocab_start)
+            if out is not None:
+                return out
         val = logits.gather(1, idx[:, None]).squeeze(1)
         gid = (idx + self.w.vocab_start).to(torch.float32)
         pair = torch.stack([val, gid], dim=1)  # [B, 2] (ids < 2^24 are exact in fp32)

@@ -74,6 +74,7 @@ class ReferenceDecoder:
         for li in range(lo, hi):
             p = f"model.layers.{li}."
             L = {
+                "index": li,
                 "ln1": t(p + "input_layernorm.weight", (H,)),
                 "wq": t(p + "self_attn.q_proj.weight", (cfg.num_heads * D, H)),
                 "wk": t(p + "self_attn.k_proj.weight", (cfg.num_kv_heads * D, H)),
@@ -108,6 +109,9 @@ class ReferenceDecoder:
         mp = max_positions or cfg.max_position_embeddings
         self.cos_sin = rope_cos_sin_table(mp, D, cfg.rope_theta, cfg.rope_scaling).to(self.device)
 
+    # Where the routed experts run (``runtime/moe_backends.py``); None: the experts held here.
+    moe_backend = None
+
     def _moe(self, L, m: torch.Tensor) -> torch.Tensor:
         from ..ops.moe import MODE_SIGMOID_GROUP, MODE_SOFTMAX, route_reference
         cfg = self.cfg
@@ -117,6 +121,13 @@ class ReferenceDecoder:
                                  renorm=cfg.norm_topk_prob, n_group=cfg.n_group,
                                  topk_group=cfg.topk_group,
                                  scale=cfg.routed_scaling_factor if sig else 1.0)
+        if self.moe_backend is not None:
+            out = self.moe_backend.experts(L["index"], m.float().cpu(), ids.cpu(), w.float().cpu())
+            out = out.to(m.device)
+            if "shared" in L:
+                g, u, d = L["shared"]
+                out += ((torch.nn.functional.silu(m @ g.T) * (m @ u.T)) @ d.T).float()
+            return out.to(m.dtype)
         out = torch.zeros_like(m, dtype=torch.float32)
         for e in torch.unique(ids).tolist():
             sel = (ids == e)

@@ -5,6 +5,7 @@ KV cache per layer: ``[num_pages, num_kv_heads, 64, 128]`` bf16 for K and V.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -41,18 +42,30 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return out
 
 
+PREFILL_KERNEL = os.environ.get("SIL_PREFILL_ATTN", "mma")  # tc (tcgen05) | mma (mma.sync)
+
+
 def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   block_table: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor,
                   max_q_len: int, *, out: torch.Tensor | None = None,
-                  scale: float | None = None) -> torch.Tensor:
-    """q: packed [T, Hq, 128]; cu_q: [B+1] int32 query offsets -> out [T, Hq*128]."""
+                  scale: float | None = None, kernel: str | None = None) -> torch.Tensor:
+    """q: packed [T, Hq, 128]; cu_q: [B+1] int32 query offsets -> out [T, Hq*128].
+
+    ``kernel`` "tc" runs the tcgen05 kernel (S and O in TMEM, 128 queries x 128 keys per
+    step); "mma" the earlier ``mma.sync`` kernel (64-query tiles).  Short query chunks (at
+    most 16 queries per sequence: speculative verification, small chunks) use "mma"."""
     T, Hq, D = q.shape
     if out is None:
         out = torch.empty((T, Hq * D), dtype=q.dtype, device=q.device)
     ws = get_workspace(q.device)
-    ext().paged_prefill(q, k_cache, v_cache, block_table, seq_lens, cu_q, out,
-                        scale if scale is not None else 1.0 / math.sqrt(D), int(max_q_len),
-                        ws.status)
+    sc = scale if scale is not None else 1.0 / math.sqrt(D)
+    kind = kernel or PREFILL_KERNEL
+    if kind == "tc" and max_q_len > 16 and q.stride(0) % 8 == 0:
+        ext().paged_prefill_tc(q, k_cache, v_cache, block_table, seq_lens, cu_q, out, sc,
+                               int(max_q_len), ws.status)
+    else:
+        ext().paged_prefill(q, k_cache, v_cache, block_table, seq_lens, cu_q, out, sc,
+                            int(max_q_len), ws.status)
     return out
 
 

@@ -43,7 +43,9 @@ class LLTPComm:
         self.ll_off = 256
         # ll[2 parities][8 sources][max_elems / 2 words of 8 bytes]
         self.partial_off = self.ll_off + 2 * MAX_RANKS * self.max_elems * 4
-        nbytes = self.partial_off + self.max_elems * 2
+        # argmax words [2 parities][8 sources][max_tokens] x 16 bytes
+        self.argmax_off = ((self.partial_off + self.max_elems * 2 + 255) // 256) * 256
+        nbytes = self.argmax_off + 2 * MAX_RANKS * max_tokens * 16
         self.local, self.peers, self._opened = open_symmetric(base, self.device, nbytes)
         self._views: dict[tuple[int, int], torch.Tensor] = {}
         torch.cuda.synchronize(self.device)
@@ -100,6 +102,18 @@ class LLTPComm:
         ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
                                 self.max_elems, norm_w, float(eps), x_out,
                                 get_workspace(x.device).status)
+
+    def argmax_exchange(self, logits: torch.Tensor, idx: torch.Tensor, vocab_start: int) -> torch.Tensor:
+        """Global greedy token per row from each rank's local argmax over its vocabulary shard
+        (largest logit, lowest global id on ties), exchanged through peer memory."""
+        B = logits.shape[0]
+        if B > self.max_tokens:
+            return None
+        out = torch.empty(B, dtype=torch.int64, device=logits.device)
+        ext().ll_argmax_exchange(logits, idx, int(vocab_start), self.peers, self.rank,
+                                 self.argmax_off, self.max_tokens, out,
+                                 get_workspace(logits.device).status)
+        return out
 
     fused_gemm_allreduce = None
 

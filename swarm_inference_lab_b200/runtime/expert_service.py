@@ -98,6 +98,7 @@ class ExpertService:
         self._cache_n = cache_entries
         self.stats = {"requests": 0, "rejected": 0, "cache_hits": 0, "rows": 0}
         self._server = None
+        self._writers: set = set()
 
     def accept_lease(self, lease_hash: str) -> None:
         self.accepted_leases.add(lease_hash)
@@ -110,9 +111,12 @@ class ExpertService:
     async def close(self):
         if self._server is not None:
             self._server.close()
+            for w in list(self._writers):
+                w.close()
             await self._server.wait_closed()
 
     async def _conn(self, reader, writer):
+        self._writers.add(writer)
         try:
             while True:
                 req = await read_packet(reader, timeout=None)
@@ -122,6 +126,7 @@ class ExpertService:
         except (asyncio.IncompleteReadError, ConnectionError):
             pass
         finally:
+            self._writers.discard(writer)
             writer.close()
 
     def _error(self, req: ExpertPacket, msg: str) -> ExpertPacket:
