@@ -126,6 +126,7 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
                 top_p: float = typer.Option(1.0, "--top-p"),
                 repetition_penalty: float = typer.Option(1.0, "--repetition-penalty"),
                 stages: int = typer.Option(None, "--stages"),
+                replicas: int = typer.Option(1, "--replicas"),
                 return_logits: bool = typer.Option(False, "--return-logits"),
                 state: str = typer.Option(STATE, "--state-dir")):
     """Resolve, plan and run MODEL (on this box, or across the cluster), streaming tokens."""
@@ -141,7 +142,7 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
     ids, tok_kind = _prompt_ids(prompt, prompt_ids, cfg.vocab_size, tokenizer)
     if require_distributed:
         _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
-                         as_json, ndjson, return_logits, state)
+                         as_json, ndjson, return_logits, state, replicas)
         return
     caps = _gpu_caps(gpus)
     comp = EngineRegistry().compete(cfg, caps, RequestShape(
@@ -213,7 +214,7 @@ def _model_desc(model: str, cfg, ckpt: str | None, seed: int) -> dict:
 
 
 def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
-                     as_json, ndjson, return_logits, state):
+                     as_json, ndjson, return_logits, state, replicas=1):
     """Deploy MODEL across the cluster's joined nodes through the coordinator and stream
     the request's tokens (the coordinator replays the request on a replacement node if a
     node fails mid-request)."""
@@ -228,7 +229,7 @@ def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, 
         cli = coordinator_client(st)
         try:
             desc = _model_desc(model, cfg, ckpt, seed)
-            dep = await cli.deploy(desc, stages=stages)
+            dep = await cli.deploy(desc, stages=stages, replicas=replicas)
             name = dep["model"]
             events, tokens, logits = [], [], []
             async for ev in cli.submit_stream(name, ids, max_tokens, return_logits=return_logits):

@@ -115,12 +115,19 @@ class GrpcWorkerAgent:
 
 @dataclass
 class ActiveModel:
+    """A deployed model: one pipeline per replica, and the scheduler that places requests
+    on them (least predicted completion time among replicas with free capacity)."""
     name: str
     model: dict
     revision: str
-    deployment: Deployment
+    replicas: dict          # route id -> Deployment
     num_layers: int
     topology_id: str
+    scheduler: object = None
+
+    @property
+    def deployment(self) -> Deployment:
+        return next(iter(self.replicas.values()))
 
 
 @dataclass
@@ -228,25 +235,38 @@ class CoordinatorCore:
         return sorted(out, key=lambda d: d["worker_id"])
 
     # ------------------------------------------------------------ planning / deployment
-    def plan(self, model: dict, stages: int | None = None) -> list[dict]:
+    def plan(self, model: dict, stages: int | None = None, replicas: int = 1) -> list[dict]:
+        """Stage plans of every replica (``replica`` key): contiguous equal layer intervals,
+        one stage per free healthy worker; replicas are balanced by the workers' measured
+        speed (``place_replicas``)."""
         from ..models.config import preset
+        from .replicas import place_replicas
         if "checkpoint" in model:
             from ..model_io.loader import checkpoint_config
             cfg = checkpoint_config(model["checkpoint"])
         else:
             cfg = preset(model["preset"])
         healthy = sorted(self.registry.healthy(), key=lambda w: w.worker_id)
-        busy = {sp.worker_id for m in self.models.values() for sp in m.deployment.stages}
+        busy = {sp.worker_id for m in self.models.values() for d in m.replicas.values()
+                for sp in d.stages}
         free = [w for w in healthy if w.worker_id not in busy]
-        n = stages or len(free)
+        replicas = max(1, int(replicas))
+        n = stages or max(1, len(free) // replicas)
         n = min(n, cfg.num_layers)
-        if n < 1 or len(free) < n:
-            raise DeploymentError(f"{n} stages need {n} free healthy workers; {len(free)} available")
+        if n < 1 or len(free) < n * replicas:
+            raise DeploymentError(f"{replicas} replica(s) of {n} stages need {n * replicas} free "
+                                  f"healthy workers; {len(free)} available")
+        speed = {w.worker_id: float(w.capabilities.get("stage_tokens_per_s", 1.0)) for w in free}
+        routes = place_replicas(speed, replicas, n)
         from ..runtime.worker import equal_layer_ranges
+        ranges = equal_layer_ranges(cfg.num_layers, n)
         out = []
-        for i, (lo, hi) in enumerate(equal_layer_ranges(cfg.num_layers, n)):
-            out.append({"stage_id": i, "worker_id": free[i].worker_id, "layer_start": lo,
-                        "layer_end": hi, "artifact_id": artifact_id_for(model, lo, hi)})
+        for r in routes:
+            workers = sorted(r.workers) if len(set(speed.values())) == 1 else r.workers
+            for i, (lo, hi) in enumerate(ranges):
+                out.append({"replica": r.route_id, "stage_id": i, "worker_id": workers[i],
+                            "layer_start": lo, "layer_end": hi,
+                            "artifact_id": artifact_id_for(model, lo, hi)})
         return out
 
     async def deploy(self, req: dict) -> dict:
@@ -256,49 +276,72 @@ class CoordinatorCore:
             if name in self.models:
                 m = self.models[name]
                 return self._model_status(m)
-            plan = self.plan(model, req.get("stages"))
+            from .replicas import AtomicRouteAllocator, ReplicaRoute, ReplicaScheduler
+            plan = self.plan(model, req.get("stages"), int(req.get("replicas") or 1))
             rev = model_revision(model)
+            by_rep: dict[str, list[dict]] = {}
             for p in plan:
-                ag = self.agents[p["worker_id"]]
-                ag.model, ag.model_revision, ag.num_stages = model, rev, len(plan)
-            stages = [StagePlan(p["stage_id"], p["worker_id"], p["layer_start"], p["layer_end"],
-                                p["artifact_id"]) for p in plan]
+                by_rep.setdefault(p["replica"], []).append(p)
+            deployed: dict[str, Deployment] = {}
             topology = f"{name}:{uuid.uuid4().hex[:8]}"
-            d = await self.deployer.deploy(stages, model_revision=rev, topology_id=topology)
-            m = ActiveModel(name, model, rev, d, plan[-1]["layer_end"], topology)
+            try:
+                for rid, ps in by_rep.items():
+                    for p in ps:
+                        ag = self.agents[p["worker_id"]]
+                        ag.model, ag.model_revision, ag.num_stages = model, rev, len(ps)
+                    stages = [StagePlan(p["stage_id"], p["worker_id"], p["layer_start"],
+                                        p["layer_end"], p["artifact_id"]) for p in ps]
+                    deployed[rid] = await self.deployer.deploy(
+                        stages, model_revision=rev, topology_id=f"{topology}:{rid}")
+            except Exception:
+                for d in deployed.values():
+                    await self.deployer.unload(d.deployment_id)
+                raise
+            cap = int(req.get("capacity") or 8)
+            routes = [ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0)
+                      for rid, d in deployed.items()]
+            m = ActiveModel(name, model, rev, deployed, plan[-1]["layer_end"], topology,
+                            ReplicaScheduler(AtomicRouteAllocator(routes)))
             self.models[name] = m
-            self.events.append({"event": "model_deployed", "model": name,
-                                "generation": d.generation, "at": time.time()})
+            self.events.append({"event": "model_deployed", "model": name, "replicas": len(deployed),
+                                "generation": m.deployment.generation, "at": time.time()})
             return self._model_status(m)
 
     def _model_status(self, m: ActiveModel) -> dict:
         d = m.deployment
+
+        def stages(dep):
+            return [{"stage_id": s.stage_id, "worker_id": s.worker_id,
+                     "layers": [s.layer_start, s.layer_end]} for s in dep.stages]
         return {"model": m.name, "deployment_id": d.deployment_id, "phase": d.phase.value,
                 "generation": d.generation, "topology_id": d.topology_id, "revision": m.revision,
-                "stages": [{"stage_id": s.stage_id, "worker_id": s.worker_id,
-                            "layers": [s.layer_start, s.layer_end]} for s in d.stages]}
+                "stages": stages(d),
+                "replicas": {rid: {"deployment_id": dep.deployment_id, "phase": dep.phase.value,
+                                   "generation": dep.generation, "stages": stages(dep)}
+                             for rid, dep in m.replicas.items()}}
 
     async def unload(self, req: dict) -> dict:
         async with self._lock:
             m = self.models.pop(req["model"], None)
             if m is None:
                 return {"unloaded": False}
-            await self.deployer.unload(m.deployment.deployment_id)
+            for d in m.replicas.values():
+                await self.deployer.unload(d.deployment_id)
             return {"unloaded": True}
 
-    def _route(self, m: ActiveModel) -> Route:
-        d = m.deployment
+    def _route(self, m: ActiveModel, d: Deployment | None = None) -> Route:
+        d = d or m.deployment
         s0 = d.stages[0]
         host, port = self.agents[s0.worker_id].endpoint.rsplit(":", 1)
         return Route((host, int(port)), d.generation, d.topology_id, m.revision,
                      (s0.layer_start, s0.layer_end))
 
-    async def _failed_workers(self, m: ActiveModel) -> list[str]:
+    async def _failed_workers(self, m: ActiveModel, d: Deployment) -> list[str]:
         """Workers of the route that do not answer a HEALTH frame (or are marked dead)."""
         failed = []
         pool = ConnectionPool()
         try:
-            for sp in m.deployment.stages:
+            for sp in d.stages:
                 rec = self.registry.workers.get(sp.worker_id)
                 if rec is None or not rec.healthy:
                     failed.append(sp.worker_id)
@@ -318,24 +361,24 @@ class CoordinatorCore:
             await pool.close()
         return failed
 
-    async def _recover(self, m: ActiveModel, route: Route, exc: Exception) -> Route:
+    async def _recover(self, m: ActiveModel, d: Deployment, route: Route, exc: Exception) -> Route:
         async with self._lock:
-            if m.deployment.generation != route.generation:
-                return self._route(m)  # another request already recovered this deployment
-            failed = await self._failed_workers(m)
+            if d.generation != route.generation:
+                return self._route(m, d)  # another request already recovered this replica
+            failed = await self._failed_workers(m, d)
             if not failed:
                 raise exc
             for ag in self.agents.values():   # any healthy worker may become the replacement
                 ag.model, ag.model_revision = m.model, m.revision
-                ag.num_stages = len(m.deployment.stages)
+                ag.num_stages = len(d.stages)
             for wid in failed:
                 self.registry.mark_unhealthy(wid)
                 self.events.append({"event": "stage_failed", "worker": wid, "at": time.time()})
-                await self.deployer.recover(m.deployment.deployment_id, wid)
+                await self.deployer.recover(d.deployment_id, wid)
             self.events.append({"event": "route_recovered", "model": m.name,
-                                "generation": m.deployment.generation, "at": time.time()})
+                                "generation": d.generation, "at": time.time()})
             METRICS.inc("coordinator_recoveries")
-            return self._route(m)
+            return self._route(m, d)
 
     # ------------------------------------------------------------ requests
     async def submit_stream(self, req: dict):
@@ -352,14 +395,22 @@ class CoordinatorCore:
         self.requests[rid] = rec
         if self.state is not None:
             self.state.record_request(rid, prompt, {"max_tokens": req.get("max_tokens")})
-        ctl = SessionController(self._route(m), recover=lambda r, e: self._recover(m, r, e),
+        max_tokens = int(req.get("max_tokens", 16))
+        try:
+            grant = m.scheduler.submit(len(prompt), max_tokens)
+        except Exception as exc:  # noqa: BLE001 - every replica is at capacity
+            yield {"event": "failed", "request_id": rid, "error": f"{type(exc).__name__}: {exc}"}
+            return
+        d = m.replicas[grant.route_id]
+        ctl = SessionController(self._route(m, d), recover=lambda r, e: self._recover(m, d, r, e),
                                 return_logits=bool(req.get("return_logits")))
-        yield {"event": "accepted", "request_id": rid, "generation": m.deployment.generation}
+        yield {"event": "accepted", "request_id": rid, "generation": d.generation,
+               "replica": grant.route_id}
         METRICS.inc("coordinator_requests")
         t0 = time.perf_counter()
         t_last = t0
         try:
-            async for ev in ctl.stream(prompt, int(req.get("max_tokens", 16)), rid):
+            async for ev in ctl.stream(prompt, max_tokens, rid):
                 if ev["event"] == "token":
                     now = time.perf_counter()
                     METRICS.observe("coordinator_ttft_ms" if ev["index"] == 0
@@ -388,6 +439,7 @@ class CoordinatorCore:
                 METRICS.inc("coordinator_transport_errors")
             yield {"event": "failed", "request_id": rid, "error": f"{type(exc).__name__}: {exc}"}
         finally:
+            m.scheduler.allocator.release(grant.lease_id)
             if self.state is not None:
                 self.state.set_state(rid, rec.state)
             await ctl.pool.close()
@@ -442,7 +494,7 @@ class CoordinatorRpcServer:
             return {"snapshot": METRICS.snapshot(), "prometheus": METRICS.prometheus()}
 
         async def plan(obj):
-            return {"plan": core.plan(obj["model"], obj.get("stages"))}
+            return {"plan": core.plan(obj["model"], obj.get("stages"), int(obj.get("replicas") or 1))}
 
         async def pairing_create(obj):
             if core.pairing is None:
@@ -490,9 +542,11 @@ class CoordinatorClient:
         _, rep = await self.client.call(COORDINATOR_SERVICE, method, kind, obj)
         return rep
 
-    async def deploy(self, model: dict, *, name: str | None = None, stages: int | None = None) -> dict:
+    async def deploy(self, model: dict, *, name: str | None = None, stages: int | None = None,
+                     replicas: int = 1) -> dict:
         return await self._call("DeployModel", "DeployRequest",
-                                {"model": model, "name": name, "stages": stages})
+                                {"model": model, "name": name, "stages": stages,
+                                 "replicas": replicas})
 
     async def unload(self, name: str) -> dict:
         return await self._call("UnloadModel", "UnloadRequest", {"model": name})

@@ -214,3 +214,72 @@ def test_worker_killed_mid_decode_recovers_on_a_spare(tmp_path, single_process):
     assert m.deployment.generation == gen0 + 1
     assert spare in {s.worker_id for s in m.deployment.stages}
     assert victim not in {s.worker_id for s in m.deployment.stages}
+
+
+def test_replica_pipelines_share_concurrent_requests(tmp_path, single_process):
+    """Two replicas of a 2-stage pipeline on four nodes; four concurrent requests are
+    placed by the replica scheduler on both replicas and all return the reference tokens."""
+    from swarm_inference_lab_b200.cluster.control import (channel_credentials, coordinator_tls,
+                                                          server_credentials)
+    from swarm_inference_lab_b200.cluster.pairing import PairingManager
+    from swarm_inference_lab_b200.cluster.state import ClusterStateStore
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+
+    toks_ref, _ = single_process
+    n_new = 16
+    port = _free_pair()
+    coord = tmp_path / "coord"
+    _swarm("cluster", "create", "demo", "--host", "127.0.0.1", "--port", str(port),
+           "--state-dir", str(coord), "--json")
+    store = ClusterStateStore(coord)
+
+    async def go():
+        ca, crt, key = coordinator_tls(store)
+        core = CoordinatorCore(store.identity("coordinator"), state_dir=coord, cluster_store=store,
+                               worker_credentials=channel_credentials(ca, crt, key))
+        pm = PairingManager(store, f"127.0.0.1:{port}")
+        await pm.start("127.0.0.1", port)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=port + 1,
+                                   credentials=server_credentials(ca, crt, key))
+        await rpc.start()
+        agents = []
+        try:
+            names = ["r1", "r2", "r3", "r4"]
+            for name in names:
+                st = tmp_path / name
+                proc = await asyncio.create_subprocess_exec(
+                    sys.executable, "-m", "swarm_inference_lab_b200.cli", "node", "join",
+                    pm.invite().uri(), "--name", name, "--state-dir", str(st), env=_env(), cwd=ROOT,
+                    stdout=asyncio.subprocess.DEVNULL, stderr=asyncio.subprocess.PIPE)
+                _, err = await asyncio.wait_for(proc.communicate(), 120)
+                assert proc.returncode == 0, err.decode()[-2000:]
+                agents.append(_start_agent(st, tmp_path / f"{name}.ready"))
+            t0 = time.time()
+            while len(core.registry.healthy()) < 4:
+                assert time.time() - t0 < 120
+                await asyncio.sleep(0.1)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2,
+                                     "replicas": 2})
+            assert len(dep["replicas"]) == 2
+
+            async def one(i):
+                toks, rep = [], None
+                async for ev in core.submit_stream({"model": dep["model"], "prompt_ids": PROMPT,
+                                                    "max_tokens": n_new, "request_id": f"q{i}"}):
+                    if ev["event"] == "accepted":
+                        rep = ev["replica"]
+                    elif ev["event"] == "token":
+                        toks.append(ev["token"])
+                    elif ev["event"] == "failed":
+                        raise AssertionError(ev)
+                return rep, toks
+            return await asyncio.gather(*[one(i) for i in range(4)])
+        finally:
+            _stop(agents)
+            await rpc.stop()
+            await pm.close()
+
+    results = asyncio.run(go())
+    assert {rep for rep, _ in results} == {"replica0", "replica1"}
+    for _, toks in results:
+        assert toks == toks_ref[:n_new]
