@@ -183,5 +183,14 @@ class MoEModel(DenseModel):
         if self.tp.size == 1:
             moe_ops.combine(y, rows, w, k, residual=h, shared=shared, out=h, row_limit=limit)
             return None
+        buf = getattr(self.comm, "partial_buffer", None)
+        dst = buf(T, x.shape[1]) if buf is not None and h.is_contiguous() else None
+        if dst is not None:
+            # Expert parallelism over NVLink: the combine of this rank's experts lands in its
+            # symmetric partial buffer and the low-latency all-reduce adds every rank's
+            # partial to the residual stream in rank order.
+            moe_ops.combine(y, rows, w, k, shared=shared, row_limit=limit, out=dst)
+            self.comm.allreduce_partial_residual(h)
+            return None
         part = moe_ops.combine(y, rows, w, k, shared=shared, row_limit=limit)
         return self._reduce(part)

@@ -103,6 +103,21 @@ class LLTPComm:
                                 self.max_elems, norm_w, float(eps), x_out,
                                 get_workspace(x.device).status)
 
+    def partial_buffer(self, T: int, H: int) -> torch.Tensor | None:
+        """This rank's partial-sum buffer [T, H] (bf16) for a producer that writes its
+        row-parallel output there directly (the MoE combine), or None when it does not fit."""
+        if T * H > self.max_elems or H != self.hidden:
+            return None
+        return self._partial(T, H)
+
+    def allreduce_partial_residual(self, h: torch.Tensor, norm_w: torch.Tensor | None = None,
+                                   eps: float = 0.0, x_out: torch.Tensor | None = None) -> None:
+        """h += sum over ranks of the partial in ``partial_buffer``; with ``norm_w`` also
+        x_out = rmsnorm(h) * norm_w."""
+        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
+                                self.max_elems, norm_w, float(eps), x_out,
+                                get_workspace(h.device).status)
+
     def argmax_exchange(self, logits: torch.Tensor, idx: torch.Tensor, vocab_start: int) -> torch.Tensor:
         """Global greedy token per row from each rank's local argmax over its vocabulary shard
         (largest logit, lowest global id on ties), exchanged through peer memory."""

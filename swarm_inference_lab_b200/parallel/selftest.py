@@ -91,6 +91,42 @@ def main():
             ref = a[:, v0:v0 + b.shape[1]]
             errs.append((ref - b).abs().max().item() / (ref.abs().max().item() + 1e-6))
         results[name] = {"max_rel_err": max(errs), "tokens_equal": bool(torch.equal(tok, tok_full))}
+    # bf16 MoE (TP attention + EP experts) at EP=world against EP=1, through NCCL and through
+    # the low-latency all-reduce of the expert combine.
+    from ..models.config import ModelConfig
+    from ..models.moe import MoEModel, MoEWeights
+    mcfg = ModelConfig(name="tiny-moe", family="qwen3_moe", vocab_size=2048, hidden_size=cfg.hidden_size,
+                       num_layers=2, num_heads=max(4, 2 * world), num_kv_heads=max(2, world),
+                       head_dim=128, intermediate_size=1024, qk_norm=True, num_experts=8,
+                       num_experts_per_tok=2, moe_intermediate_size=256, rms_norm_eps=1e-6)
+
+    def run_moe(tp, comm):
+        w = MoEWeights.random(mcfg, tp, dev, seed=11)
+        model = MoEModel(w, dev, comm=comm, max_positions=512)
+        T = 24
+        kv = PagedKVCache(mcfg.num_layers, model.num_kv_local, 4, dev)
+        ids_m = torch.randint(0, mcfg.vocab_size, (T,), generator=torch.Generator().manual_seed(5)).to(dev)
+        fb = ForwardBatch(ids=ids_m, positions=torch.arange(T, dtype=torch.int32, device=dev),
+                          slots=torch.arange(T, dtype=torch.int32, device=dev),
+                          seq_lens=torch.tensor([T], dtype=torch.int32, device=dev),
+                          block_table=torch.arange(4, dtype=torch.int32, device=dev)[None],
+                          last_idx=torch.arange(T, device=dev), is_decode=False,
+                          cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), max_q_len=T)
+        lg = model.logits(model.forward_hidden(fb, kv), fb)
+        torch.cuda.synchronize()
+        return lg
+
+    moe_full = run_moe(TPInfo(), LocalComm())
+    for name, comm in (("moe_ep_nccl", nccl), ("moe_ep_ll", ll)):
+        shard = run_moe(TPInfo(rank, world), comm)
+        v0, _ = TPInfo(rank, world).split(mcfg.vocab_size)
+        ref = moe_full[:, v0:v0 + shard.shape[1]]
+        row = ((shard.float() - ref.float()).norm(dim=1) / ref.float().norm(dim=1)).cpu()
+        agree = (shard.argmax(-1) == ref.argmax(-1)).float().mean().item()
+        # a routing near-tie may send a token to another expert: most rows must agree closely
+        results[name] = {"max_rel_err": float(row.median().item()),
+                         "tokens_equal": bool(agree > 0.8 and (row < 0.1).float().mean().item() > 0.9)}
+
     # Bit-equality of one row-parallel all-reduce: the low-latency kernel against NCCL in
     # deterministic mode (all-gather, fp32 rank-ordered sum, one rounding), at 1, 32 and
     # 128 tokens.
@@ -112,7 +148,9 @@ def main():
     results["ll_vs_deterministic_nccl_bit_equal"] = {"max_rel_err": 0.0 if bit_equal else 1.0,
                                                      "tokens_equal": bit_equal}
     get_workspace(dev).check()
-    ok = all(r["max_rel_err"] < 0.05 for r in results.values())
+    ok = all(r["max_rel_err"] < 0.05 for r in results.values()) and \
+        results["ll_vs_deterministic_nccl_bit_equal"]["tokens_equal"] and \
+        results["moe_ep_nccl"]["tokens_equal"] and results["moe_ep_ll"]["tokens_equal"]
     out = torch.tensor([1.0 if ok else 0.0], device=dev)
     dist.all_reduce(out, op=dist.ReduceOp.MIN)
     if rank == 0:
