@@ -78,3 +78,40 @@ def test_name_mapping_and_fp8_dequantisation():
 def test_tokenizer_absent_is_none(tmp_path):
     from swarm_inference_lab_b200.model_io.loader import load_tokenizer
     assert load_tokenizer(tmp_path) is None
+
+
+def test_deepseek_v3_checkpoint_builds_mla_weights(tmp_path):
+    """A tiny HF DeepSeek-V3 checkpoint maps onto the MLA model's weights (names, shapes,
+    the padded fused q_a / kv_a projection, fp8 128x128 quantisation of bf16 tensors)."""
+    from transformers import DeepseekV3Config, DeepseekV3ForCausalLM
+
+    from swarm_inference_lab_b200.model_io.loader import (checkpoint_config, fp8_source,
+                                                          safetensors_source)
+    from swarm_inference_lab_b200.models.deepseek import MLAWeights
+    from swarm_inference_lab_b200.models.dense import TPInfo
+    c = DeepseekV3Config(vocab_size=512, hidden_size=256, intermediate_size=384,
+                         moe_intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                         num_key_value_heads=4, n_shared_experts=1, n_routed_experts=8,
+                         num_experts_per_tok=2, n_group=2, topk_group=1, first_k_dense_replace=1,
+                         q_lora_rank=256, kv_lora_rank=512, qk_nope_head_dim=128,
+                         qk_rope_head_dim=64, v_head_dim=128, max_position_embeddings=1024,
+                         tie_word_embeddings=False)
+    torch.manual_seed(0)
+    DeepseekV3ForCausalLM(c).save_pretrained(tmp_path, safe_serialization=True)
+    cfg = checkpoint_config(tmp_path)
+    assert cfg.mla and cfg.num_experts == 8 and cfg.first_k_dense == 1
+    get = safetensors_source(tmp_path)
+
+    def getd(name, shape, dt=torch.bfloat16):
+        return get(name, shape).to(dt)
+
+    w = MLAWeights.from_source(cfg, TPInfo(0, 2), getd, fp8_source(get), "cpu")
+    L0, L1 = w.layers
+    assert L0.dense and not L1.dense
+    assert L0.w_qkv_a[0].shape == (896, 256)            # pad128(256 + 512 + 64) rows
+    assert L1.experts_gate_up[0].shape == (4 * 2 * 128, 256)   # 4 local experts (EP 2)
+    assert L1.router_bias.dtype == torch.float32 and L1.router_bias.shape == (8,)
+    ref = get("model.layers.1.mlp.experts.0.gate_proj.weight", (128, 256))  # rank 0 owns 0..3
+    q, s = L1.experts_gate_up
+    deq = (q[:128].view(torch.float8_e4m3fn).float() * s[0].repeat_interleave(128)[None, :256])
+    assert (deq - ref).abs().max().item() <= ref.abs().max().item() * 0.07
