@@ -262,9 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     uint8_t* prow = smem + kOffP + row * 128;
+    // tcgen05.ld / st are warp-collective (.sync.aligned): every branch around them below
+    // is made uniform across the warp (__all_sync / __any_sync).
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int s = j & 1;
-      if (!wait_bar(&s_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
+      ok = __all_sync(0xffffffffu, wait_bar(&s_full[s], (j >> 1) & 1, args.status));
+      if (!ok) break;
       tc_fence_after();
       float sv[kBN];
       const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off;
@@ -301,9 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       m = m_new;
       if (j >= 1) {
         // PV of the previous tile must be done before O is rescaled and P is overwritten.
-        if (!wait_bar(o_done, (j - 1) & 1, args.status)) { ok = false; break; }
+        ok = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, args.status));
+        if (!ok) break;
         tc_fence_after();
-        if (alpha != 1.f) {
+        // Rows whose max did not grow multiply by 1; the warp skips only if none grew.
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             uint32_t r[32];
@@ -333,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status)) {
+    const bool done = ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status);
+    if (__all_sync(0xffffffffu, done)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool store = qi < q_len;
@@ -366,7 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is warp-collective: lane 0 ran the MMA loop alone
+    tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
 }  // namespace

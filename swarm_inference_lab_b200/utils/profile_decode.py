@@ -3,6 +3,7 @@
     python -m swarm_inference_lab_b200.utils.profile_decode --batch 32 --ctx 2048 [--steps 5]
     python -m swarm_inference_lab_b200.utils.profile_decode --op gemm --m 28672 --n 32 --k 4096 --swiglu
     python -m swarm_inference_lab_b200.utils.profile_decode --op decode_attn --batch 32 --ctx 2048
+    python -m swarm_inference_lab_b200.utils.profile_decode --op prefill_attn --batch 32 --ctx 2048 --kernel tc
     python -m swarm_inference_lab_b200.utils.profile_decode --op mla_decode --batch 32 --ctx 4096
     python -m swarm_inference_lab_b200.utils.profile_decode --op fp8_grouped --groups 48 --n 6 --m 7168 --k 2048
 
@@ -100,6 +101,31 @@ def op_decode_attn(a):
     pk = _peaks()
     return {"op": "paged_decode", "batch": B, "ctx": ctx, "splits": splits, "ms": ms,
             "GBps": bytes_ / ms / 1e6, "frac_hbm_of_measured": bytes_ / ms / 1e6 / pk["hbm_gbs"]}
+
+
+def op_prefill_attn(a):
+    """Causal paged prefill attention of ``batch`` sequences of ``ctx`` tokens (all new):
+    the tcgen05 kernel or the mma.sync kernel (``--kernel``); FLOPs count the causal half."""
+    from ..ops import attention as A
+    B, ctx, hq, hkv = a.batch, a.ctx, a.hq, a.hkv
+    pages_per = (ctx + 63) // 64
+    P = B * pages_per
+    kc = torch.randn(P, hkv, 64, 128, device="cuda").bfloat16()
+    vc = torch.randn_like(kc)
+    bt = torch.arange(P, dtype=torch.int32, device="cuda").view(B, pages_per)
+    sl = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    T = B * ctx
+    qkv = torch.randn(T, (hq + 2 * hkv) * 128, device="cuda").bfloat16()
+    q = qkv.as_strided((T, hq, 128), (qkv.stride(0), 128, 1))
+    cu = torch.arange(0, T + 1, ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, hq * 128, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: A.paged_prefill(q, kc, vc, bt, sl, cu, ctx, out=out, kernel=a.kernel),
+                 a.iters, graph=not a.eager)
+    flops = 4.0 * B * hq * 128 * ctx * (ctx + 1) / 2
+    pk = _peaks()
+    return {"op": "paged_prefill", "kernel": a.kernel, "batch": B, "ctx": ctx, "heads": hq,
+            "ms": ms, "TFLOPs": flops / ms / 1e9,
+            "frac_bf16_of_measured": flops / ms / 1e9 / pk["bf16_tflops"]}
 
 
 def op_launch_floor(a):
@@ -229,8 +255,8 @@ def decode_steps(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "mla_decode", "fp8_grouped",
-                                     "gemm_ar1", "launch_floor"],
+    ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "prefill_attn", "mla_decode",
+                                     "fp8_grouped", "gemm_ar1", "launch_floor"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
     ap.add_argument("--hq", type=int, default=32, help="decode_attn: query heads")
@@ -248,8 +274,10 @@ def main():
     ap.add_argument("--swiglu", action="store_true")
     ap.add_argument("--splits", type=int, default=0, help="force K splits (0 = heuristic)")
     ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
+    ap.add_argument("--kernel", default="tc", help="prefill_attn: tc (tcgen05) or mma (mma.sync)")
     a = ap.parse_args()
     out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn,
+           "prefill_attn": op_prefill_attn,
            "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped,
            "gemm_ar1": op_gemm_ar1, "launch_floor": op_launch_floor}[a.op](a)
     print(json.dumps(out))
