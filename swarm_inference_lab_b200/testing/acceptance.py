@@ -92,3 +92,73 @@ def write_evidence(record: dict, out_dir: str | Path) -> Path:
     p = out / f"{record.get('gate', 'evidence')}-{int(record['recorded_at'])}.json"
     p.write_text(json.dumps(record, indent=1, default=str))
     return p
+
+
+# ---------------------------------------------------------------- frozen contracts
+CONTRACTS = Path(__file__).resolve().parent / "contracts"
+
+
+def _field(d: dict, path: str):
+    cur = d
+    for part in path.split("."):
+        if not isinstance(cur, dict) or part not in cur:
+            raise KeyError(path)
+        cur = cur[part]
+    return cur
+
+
+def load_contract(name_or_path: str) -> dict:
+    import yaml
+    p = Path(name_or_path)
+    if not p.exists():
+        p = CONTRACTS / f"{name_or_path}.yaml"
+    return yaml.safe_load(p.read_text())
+
+
+def check_contract(contract: dict, evidence: dict) -> dict:
+    """Evaluates every required field and gate of a frozen contract against an evidence
+    record; returns ``{"contract", "ok", "results": [...]}`` (missing fields fail)."""
+    ops = {"==": lambda a, b: a == b, ">=": lambda a, b: a >= b, ">": lambda a, b: a > b,
+           "<=": lambda a, b: a <= b, "<": lambda a, b: a < b,
+           "excludes_any": lambda a, b: not (set(a or []) & set(b))}
+    results = []
+    for f, want in (contract.get("required") or {}).items():
+        try:
+            got = _field(evidence, f)
+            results.append({"field": f, "ok": got == want, "got": got, "want": want})
+        except KeyError:
+            results.append({"field": f, "ok": False, "got": None, "want": want})
+    for g in contract.get("gates") or []:
+        try:
+            got = _field(evidence, g["field"])
+            ok = bool(ops[g["op"]](got, g["value"]))
+        except (KeyError, TypeError):
+            got, ok = None, False
+        results.append({"field": g["field"], "op": g["op"], "ok": ok, "got": got, "want": g["value"]})
+    return {"contract": contract.get("name"), "ok": all(r["ok"] for r in results),
+            "results": results}
+
+
+def main(argv=None):
+    """``python -m swarm_inference_lab_b200.testing.acceptance CONTRACT EVIDENCE.json``: checks
+    the last JSON object of the evidence file against the contract; exit 1 on failure."""
+    import sys
+    args = list(sys.argv[1:] if argv is None else argv)
+    if len(args) != 2:
+        print("usage: acceptance CONTRACT EVIDENCE.json", file=sys.stderr)
+        return 2
+    text = Path(args[1]).read_text().strip()
+    ev = None
+    for line in text.splitlines()[::-1]:
+        if line.startswith("{"):
+            ev = json.loads(line)
+            break
+    if ev is None:
+        ev = json.loads(text)
+    rep = check_contract(load_contract(args[0]), ev)
+    print(json.dumps(rep, indent=1, default=str))
+    return 0 if rep["ok"] else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
