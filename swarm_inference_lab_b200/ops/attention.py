@@ -42,7 +42,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     return out
 
 
-PREFILL_KERNEL = os.environ.get("SIL_PREFILL_ATTN", "mma")  # tc (tcgen05) | mma (mma.sync)
+PREFILL_KERNEL = os.environ.get("SIL_PREFILL_ATTN", "tc")  # tc (tcgen05) | mma (mma.sync)
 
 
 def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

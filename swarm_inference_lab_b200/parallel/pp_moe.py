@@ -47,7 +47,7 @@ class PPMoERank:
     """One rank of the pp x ep grid with its stage model, paged KV and micro-batch metadata."""
 
     def __init__(self, cfg: ModelConfig, pp: int, *, batch: int, max_seq: int, micro_batches: int,
-                 device, seed: int = 0):
+                 device, seed: int = 0, comm: str = "nccl"):
         rank, world = dist.get_rank(), dist.get_world_size()
         if world % pp:
             raise ValueError(f"world {world} not divisible by pp {pp}")
@@ -72,6 +72,14 @@ class PPMoERank:
         w = MoEWeights.random(cfg, tp, self.device, seed=seed, layer_range=(lo, hi),
                               with_embed=self.first, with_head=self.last)
         self.comm = NcclComm(self.ep_group) if ep > 1 else None
+        self.comm_kind = "nccl" if ep > 1 else "none"
+        if ep > 1 and comm == "ll":
+            # The EP group's two reductions per layer (attention output, expert combine) go
+            # through the low-latency NVLink all-reduce for decode micro-batches; prefill-sized
+            # ones fall back to NCCL.
+            from .ll_tp import LLTPComm
+            self.comm = LLTPComm(self.comm, self.device, max_tokens=128, hidden=cfg.hidden_size)
+            self.comm_kind = "ll_allreduce (attention output + expert combine) + nccl (prefill)"
         self.model = MoEModel(w, self.device, comm=self.comm, max_positions=max_seq + PAGE)
         self.cfg = cfg
         self.batch = batch
@@ -138,7 +146,9 @@ def run_pp_bench(args, cfg: ModelConfig, rank: int, world: int, local: int) -> d
     B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
     M = max(1, args.micro_batches)
     dev = torch.device("cuda", local)
-    r = PPMoERank(cfg, pp, batch=B, max_seq=P + K + W + 8, micro_batches=M, device=dev)
+    comm = getattr(args, "comm", "nccl")
+    r = PPMoERank(cfg, pp, batch=B, max_seq=P + K + W + 8, micro_batches=M, device=dev,
+                  comm="ll" if comm in ("ll", "auto_ll") else "nccl")
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
 
@@ -195,6 +205,7 @@ def run_pp_bench(args, cfg: ModelConfig, rank: int, world: int, local: int) -> d
         "config": {"model": cfg.name, "global_batch": B, "seq_len": P, "decode_tokens": K,
                    "parallelism": f"pp{pp}x(tp{world // pp}-attention+ep{world // pp})",
                    "micro_batches": len(r.mb_sizes), "stage_boundary": "nccl p2p, micro-batch overlap",
+                   "comm": r.comm_kind,
                    "l2": "weights per stage exceed L2; no flush needed"},
         "ttft_ms_p50": ttft, "tpot_ms_p50": tpot,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
