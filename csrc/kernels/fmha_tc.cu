@@ -105,6 +105,17 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kslice) {
   return umma_desc_sw128(base + (kslice >> 2) * kHalf + (kslice & 3) * 32);
 }
 
+// 2^x with the hardware approximation (MUFU.EX2; flushes denormals), one instruction.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A running max may lag the true one by up to 2^8 before O is rescaled: P values stay
+// below 256 (fine in bf16) and most tiles skip the TMEM round trip of the rescale.
+constexpr float kRescaleThreshold = 8.0f;
+
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
   return mbar_wait(bar, parity, status, kStatusTimeoutFull);
 }
@@ -281,33 +292,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
       const int key0 = j * kBN;
-      float mx = -INFINITY;
+      // Masks are needed only on tiles that reach past the CTA's first query position
+      // (the causal diagonal) or past the end of the context (uniform per CTA).
+      if (key0 + kBN - 1 > pos0 + q0 || key0 + kBN > kv_len) {
 #pragma unroll
-      for (int t = 0; t < kBN; ++t) {
-        const int key = key0 + t;
-        float v = sv[t] * args.scale_log2;
-        if (key > qpos || key >= kv_len) v = -INFINITY;
-        sv[t] = v;
-        mx = fmaxf(mx, v);
+        for (int t = 0; t < kBN; ++t)
+          if (key0 + t > qpos || key0 + t >= kv_len) sv[t] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - m_use);
+      float mx = sv[0];
+#pragma unroll
+      for (int t = 1; t < kBN; ++t) mx = fmaxf(mx, sv[t]);
+      // Running max in the scaled exp2 domain; it moves only when the tile's max exceeds it by
+      // the threshold (or on the first tile with a finite score).
+      const float mx_s = mx * args.scale_log2;
+      float alpha = 1.f;
+      if (m == -INFINITY || mx_s > m + kRescaleThreshold) {
+        const float m_new = fmaxf(m, mx_s);
+        alpha = m == -INFINITY ? 0.f : ex2_approx(m - m_new);
+        m = m_new;
+      }
+      const float m_use = m == -INFINITY ? 0.f : m;
       float rs = 0.f;
 #pragma unroll
       for (int t = 0; t < kBN; ++t) {
-        const float p = exp2f(sv[t] - m_use);
+        const float p = ex2_approx(fmaf(sv[t], args.scale_log2, -m_use));
         sv[t] = p;
         rs += p;
       }
       l = l * alpha + rs;
-      m = m_new;
       if (j >= 1) {
         // PV of the previous tile must be done before O is rescaled and P is overwritten.
         ok = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, args.status));
         if (!ok) break;
         tc_fence_after();
-        // Rows whose max did not grow multiply by 1; the warp skips only if none grew.
+        // Rows whose max did not move multiply by 1; the warp skips only if none moved.
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
