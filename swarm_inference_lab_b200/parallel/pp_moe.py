@@ -148,7 +148,7 @@ def run_pp_bench(args, cfg: ModelConfig, rank: int, world: int, local: int) -> d
     dev = torch.device("cuda", local)
     comm = getattr(args, "comm", "nccl")
     r = PPMoERank(cfg, pp, batch=B, max_seq=P + K + W + 8, micro_batches=M, device=dev,
-                  comm="ll" if comm in ("ll", "auto_ll") else "nccl")
+                  comm="ll" if comm in ("ll", "auto") else "nccl")
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
 
