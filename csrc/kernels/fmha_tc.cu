@@ -1,6 +1,6 @@
 // Causal paged prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// One CTA per (128-query tile, query head, sequence); 320 threads in three roles:
+// One CTA per (128-query tile, query head, sequence); 192 threads in three roles:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 tokens (two 64-token
 //               pages of the paged cache) into a two-stage ring;
 //   warp 1      MMA issuer (one elected thread) and TMEM owner:
@@ -8,14 +8,11 @@
 //                 O   += P_{j-1} V_{j-1}   (M=128 queries, N=128 dims, K=128 keys)
 //               with S double buffered in TMEM so the next tile's QK^T runs while the
 //               softmax warps work on the current one;
-//   warps 2..9  softmax and epilogue, two threads per query row (TMEM lane i): warps 2..5 own
-//               key / output columns 0..63 of their rows, warps 6..9 columns 64..127.  Per
-//               tile a thread reads its half of the S row, the two halves agree on the row max
-//               through shared memory, and each thread keeps its partial sum l, rescales its
-//               half of the O row in TMEM only when the running max moved by more than 2^8,
-//               writes its half of the P row (bf16) for the PV MMA, and at the end writes its
-//               half of O / (l_a + l_b) as bf16.  Loop exits are agreed by all 256 softmax
-//               threads through a reducing named barrier, so no warp is left at a barrier.
+//   warps 2..5  softmax and epilogue: thread i owns query row i (TMEM lane i).  It reads its
+//               S row, applies the scale and the causal mask, keeps the running max m and sum
+//               l (exp2 domain), rescales its O row in TMEM only when m grew, writes its P row
+//               (bf16) into shared memory for the PV MMA, and after the last tile writes
+//               O / l as bf16.
 // TMEM: S0, S1, O = 3 x 128 fp32 columns (512 allocated).
 //
 // Shared-memory layouts (all 128-byte swizzled, 1024-byte aligned):
@@ -48,8 +45,7 @@ constexpr int kBN = 128;                     // keys per tile
 constexpr int kHalf = 128 * 64 * 2;          // one [128 rows x 64] bf16 half-tile: 16 KB
 constexpr int kTile = 2 * kHalf;             // 32 KB
 constexpr int kBox = 64 * 64 * 2;            // one TMA box: 8 KB
-constexpr int kThreads = 320;
-constexpr int kSoftmaxThreads = 256;
+constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
 
@@ -59,8 +55,7 @@ constexpr int kOffK = kOffQ + kTile;         // 2 stages
 constexpr int kOffV = kOffK + 2 * kTile;     // 2 stages
 constexpr int kOffP = kOffV + 2 * kTile;
 constexpr int kOffBar = kOffP + kTile;
-constexpr int kOffRed = kOffBar + 256;  // float [3][2 halves][128 rows]: maxima of even / odd tiles, sums
-constexpr int kSmemBytes = kOffRed + 3 * 2 * 128 * 4 + 1024;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 struct FmhaArgs {
   __nv_bfloat16* out;
@@ -121,20 +116,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // below 256 (fine in bf16) and most tiles skip the TMEM round trip of the rescale.
 constexpr float kRescaleThreshold = 8.0f;
 
-// Named barrier over the softmax warps that also ANDs a predicate across them.
-__device__ __forceinline__ bool softmax_bar_and(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(kSoftmaxThreads)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
   return mbar_wait(bar, parity, status, kStatusTimeoutFull);
 }
@@ -169,9 +150,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], kSoftmaxThreads);
+      mbar_init(&s_empty[s], 128);
     }
-    mbar_init(p_full, kSoftmaxThreads);
+    mbar_init(p_full, 128);
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -283,55 +264,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(mma_done, 0);
     }
   } else {
-    // Softmax / epilogue warps: two threads per query row == TMEM lane.
+    // Softmax / epilogue warps: thread t owns query row t == TMEM lane t.
     const int q4 = warp & 3;
-    const int half = (warp - 2) >> 2;        // 0: columns 0..63, 1: columns 64..127
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const uint32_t col0 = static_cast<uint32_t>(half * 64);
     const int qi = q0 + row;                 // query index within the sequence
     const int qpos = pos0 + qi;              // its absolute position
-    float* red = reinterpret_cast<float*>(smem + kOffRed);   // [3][2][128]
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow = smem + kOffP + half * kHalf + row * 128;
-    // tcgen05.ld / st are warp-collective: the branches around them are warp-uniform
-    // (__all_sync / __any_sync); loop exits are agreed by all softmax threads.
-    for (int j = 0; j < n_tiles; ++j) {
+    uint8_t* prow = smem + kOffP + row * 128;
+    // tcgen05.ld / st are warp-collective (.sync.aligned): every branch around them below
+    // is made uniform across the warp (__all_sync / __any_sync).
+    for (int j = 0; j < n_tiles && ok; ++j) {
       const int s = j & 1;
-      const bool okw = __all_sync(0xffffffffu, wait_bar(&s_full[s], (j >> 1) & 1, args.status));
+      ok = __all_sync(0xffffffffu, wait_bar(&s_full[s], (j >> 1) & 1, args.status));
+      if (!ok) break;
       tc_fence_after();
-      float sv[64];
-      if (okw) {
-        const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off + col0;
+      float sv[kBN];
+      const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t r[32];
-          tmem_ld32_sync(sa + c * 32, r);
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32_sync(sa + c * 32, r);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]);
-        }
-      } else {
-#pragma unroll
-        for (int t = 0; t < 64; ++t) sv[t] = -INFINITY;
+        for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      const int key0 = j * kBN + half * 64;
-      if (j * kBN + kBN - 1 > pos0 + q0 || j * kBN + kBN > kv_len) {
+      const int key0 = j * kBN;
+      // Masks are needed only on tiles that reach past the CTA's first query position
+      // (the causal diagonal) or past the end of the context (uniform per CTA).
+      if (key0 + kBN - 1 > pos0 + q0 || key0 + kBN > kv_len) {
 #pragma unroll
-        for (int t = 0; t < 64; ++t)
+        for (int t = 0; t < kBN; ++t)
           if (key0 + t > qpos || key0 + t >= kv_len) sv[t] = -INFINITY;
       }
       float mx = sv[0];
 #pragma unroll
-      for (int t = 1; t < 64; ++t) mx = fmaxf(mx, sv[t]);
-      red[(s * 2 + half) * 128 + row] = mx;
-      ok = softmax_bar_and(ok && okw);       // also publishes the partial maxima
-      if (!ok) break;
-      mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * 128 + row]);
-      // Running max in the scaled exp2 domain; it moves only when the tile's max exceeds it
-      // by the threshold (or on the first tile with a finite score).
+      for (int t = 1; t < kBN; ++t) mx = fmaxf(mx, sv[t]);
+      // Running max in the scaled exp2 domain; it moves only when the tile's max exceeds it by
+      // the threshold (or on the first tile with a finite score).
       const float mx_s = mx * args.scale_log2;
       float alpha = 1.f;
       if (m == -INFINITY || mx_s > m + kRescaleThreshold) {
@@ -342,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_use = m == -INFINITY ? 0.f : m;
       float rs = 0.f;
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
+      for (int t = 0; t < kBN; ++t) {
         const float p = ex2_approx(fmaf(sv[t], args.scale_log2, -m_use));
         sv[t] = p;
         rs += p;
@@ -350,52 +322,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       l = l * alpha + rs;
       if (j >= 1) {
         // PV of the previous tile must be done before O is rescaled and P is overwritten.
-        const bool okd = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, args.status));
-        ok = ok && okd;                      // agreed at the next barrier
+        ok = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, args.status));
+        if (!ok) break;
         tc_fence_after();
-        if (okd && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // Rows whose max did not move multiply by 1; the warp skips only if none moved.
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < kD / 32; ++c) {
             uint32_t r[32];
-            const uint32_t oa = tmem + kColO + lane_off + col0 + c * 32;
-            tmem_ld32_sync(oa, r);
+            tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
 #pragma unroll
             for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-            tmem_st32(oa, r);
+            tmem_st32(tmem + kColO + lane_off + c * 32, r);
           }
           tmem_st_wait();
         }
       }
-      // This thread's half of the P row -> shared memory, 128-byte swizzle: 16-byte chunk c
-      // at c ^ (row & 7).
+      // P row -> shared memory, 128-byte swizzle: token half, 16-byte chunk c at c ^ (row & 7).
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float* src = sv + c * 8;
-        uint4 v;
-        v.x = pack_bf16x2(src[0], src[1]);
-        v.y = pack_bf16x2(src[2], src[3]);
-        v.z = pack_bf16x2(src[4], src[5]);
-        v.w = pack_bf16x2(src[6], src[7]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = v;
+      for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float* src = sv + hh * 64 + c * 8;
+          uint4 v;
+          v.x = pack_bf16x2(src[0], src[1]);
+          v.y = pack_bf16x2(src[2], src[3]);
+          v.z = pack_bf16x2(src[4], src[5]);
+          v.w = pack_bf16x2(src[6], src[7]);
+          *reinterpret_cast<uint4*>(prow + hh * kHalf + ((c ^ (row & 7)) << 4)) = v;
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    bool done = ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status);
-    red[(4 + half) * 128 + row] = l;        // own slots: the maxima may still be read
-    done = softmax_bar_and(done);
-    if (done) {
+    const bool done = ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status);
+    if (__all_sync(0xffffffffu, done)) {
       tc_fence_after();
-      const float lt = l + red[(4 + (half ^ 1)) * 128 + row];
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool store = qi < q_len;
-      __nv_bfloat16* orow = args.out + (long long)(q_begin + qi) * args.o_stride +
-                            (long long)hq * kD + col0;
+      __nv_bfloat16* orow = args.out + (long long)(q_begin + qi) * args.o_stride + (long long)hq * kD;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kD / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32_sync(tmem + kColO + lane_off + col0 + c * 32, r);
+        tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
         if (store) {
 #pragma unroll
           for (int t = 0; t < 32; t += 8) {
