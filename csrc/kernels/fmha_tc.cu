@@ -19,7 +19,7 @@
 //   Q  [dim half][128 rows][64 dims]             A operand, K-major
 //   K  [dim half][128 tokens][64 dims]           B operand of QK^T, K-major
 //   V  [dim half][128 tokens][64 dims]           B operand of PV, MN-major (dims contiguous)
-//   P  [token half][128 rows][64 tokens]         A operand of PV, K-major
+//   P  [2][token half][128 rows][64 tokens]      A operand of PV, K-major, double buffered
 // A 64-token page of one KV head is two [64 x 64] TMA boxes; page p of a tile lands at
 // rows 64p..64p+63 of both dim halves.  A tile's second page past the end of the sequence is
 // replaced by its first page (finite values that the mask zeroes).
@@ -53,8 +53,8 @@ constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;         // 2 stages
 constexpr int kOffV = kOffK + 2 * kTile;     // 2 stages
-constexpr int kOffP = kOffV + 2 * kTile;
-constexpr int kOffBar = kOffP + kTile;
+constexpr int kOffP = kOffV + 2 * kTile;     // 2 buffers: P of tile j+1 is written while
+constexpr int kOffBar = kOffP + 2 * kTile;   // PV of tile j still reads P of tile j
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 struct FmhaArgs {
@@ -134,10 +134,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 5;     // [2]
   uint64_t* s_empty = bars + 7;    // [2]
   uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* mma_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  int* sflag = reinterpret_cast<int*>(bars + 13);
+  uint64_t* pv_done = bars + 10;   // [2]: PV of tiles with that parity finished
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  int* sflag = reinterpret_cast<int*>(bars + 14);
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_empty[s], 128);
     }
     mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -249,12 +250,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wait_bar(p_full, jp & 1, args.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t vb = sbase + kOffV + sp * kTile;
+          const uint32_t pb = pa + sp * kTile;
 #pragma unroll
           for (int k = 0; k < kBN / 16; ++k)
-            umma_f16(tmem + kColO, kmajor_desc(pa, k),
+            umma_f16(tmem + kColO, kmajor_desc(pb, k),
                      umma_desc_sw128_mn(vb + k * 2048, kHalf), idesc_o,
                      (jp > 0 || k > 0) ? 1u : 0u);
-          umma_commit(o_done);
+          umma_commit(&pv_done[sp]);
           umma_commit(&kv_empty[sp]);
         }
       }
@@ -320,13 +322,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         rs += p;
       }
       l = l * alpha + rs;
-      if (j >= 1) {
-        // PV of the previous tile must be done before O is rescaled and P is overwritten.
-        ok = __all_sync(0xffffffffu, wait_bar(o_done, (j - 1) & 1, args.status));
+      // P buffer j & 1 is free once PV of tile j - 2 has finished reading it.
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, wait_bar(&pv_done[s], ((j >> 1) - 1) & 1, args.status));
+        if (!ok) break;
+      }
+      // Rows whose max did not move multiply by 1; the warp skips only if none moved.  A
+      // rescale needs O stable: PV of tile j - 1 finished.
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        ok = __all_sync(0xffffffffu, wait_bar(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, args.status));
         if (!ok) break;
         tc_fence_after();
-        // Rows whose max did not move multiply by 1; the warp skips only if none moved.
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             uint32_t r[32];
@@ -339,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // P row -> shared memory, 128-byte swizzle: token half, 16-byte chunk c at c ^ (row & 7).
+      uint8_t* prow_j = prow + s * kTile;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
@@ -349,14 +357,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           v.y = pack_bf16x2(src[2], src[3]);
           v.z = pack_bf16x2(src[4], src[5]);
           v.w = pack_bf16x2(src[6], src[7]);
-          *reinterpret_cast<uint4*>(prow + hh * kHalf + ((c ^ (row & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(prow_j + hh * kHalf + ((c ^ (row & 7)) << 4)) = v;
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    const bool done = ok && n_tiles > 0 && wait_bar(o_done, (n_tiles - 1) & 1, args.status);
+    const bool done = ok && n_tiles > 0 &&
+                      wait_bar(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, args.status);
     if (__all_sync(0xffffffffu, done)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
