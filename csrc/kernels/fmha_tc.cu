@@ -2,7 +2,11 @@
 //
 // One CTA per (128-query tile, query head, sequence); 192 threads in three roles:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 tokens (two 64-token
-//               pages of the paged cache) into a two-stage ring;
+//               pages of the paged cache) into two separate two-stage rings.  K runs one tile
+//               ahead of V: a K buffer is free as soon as its QK^T has finished, a V buffer
+//               only after its PV, so K_{j+1} is already loading while the softmax warps
+//               still work on tile j - 1 (one shared K+V ring would start that load only
+//               after PV_{j-1}, leaving the tensor cores idle for a load latency per tile);
 //   warp 1      MMA issuer (one elected thread) and TMEM owner:
 //                 S[b] = Q K_j^T           (M=128 queries, N=128 keys, K=128 dims)
 //                 O   += P_{j-1} V_{j-1}   (M=128 queries, N=128 dims, K=128 keys)
@@ -129,15 +133,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [2]
-  uint64_t* s_empty = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;   // [2]: PV of tiles with that parity finished
-  uint64_t* mma_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-  int* sflag = reinterpret_cast<int*>(bars + 14);
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2]
+  uint64_t* v_full = bars + 5;     // [2]
+  uint64_t* v_empty = bars + 7;    // [2]
+  uint64_t* s_full = bars + 9;     // [2]
+  uint64_t* s_empty = bars + 11;   // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;   // [2]: PV of tiles with that parity finished
+  uint64_t* mma_done = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  int* sflag = reinterpret_cast<int*>(bars + 18);  // [2]: K / V tiles issued
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,8 +153,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 128);
     }
@@ -192,38 +200,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(q_full, kTile);
       tma_load_2d(smem + kOffQ, &tmQ, q_full, hq * kD, q_begin + q0);
       tma_load_2d(smem + kOffQ + kHalf, &tmQ, q_full, hq * kD + 64, q_begin + q0);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !wait_bar(&kv_empty[s], ((j >> 1) - 1) & 1, args.status)) {
-          ok = false;
-          break;
-        }
-        int pg[2];
+      // Page ids of tile j (a second page past the context repeats the first).
+      auto tile_pages = [&](int j, int (&pg)[2]) -> bool {
+        bool good = true;
         for (int p = 0; p < 2; ++p) {
           const int page = 2 * j + p < n_pages ? 2 * j + p : 2 * j;
-          int pid = bt[page];
+          const int pid = bt[page];
           if (static_cast<unsigned>(pid) >= static_cast<unsigned>(args.num_pages)) {
             raise_status(args.status, kStatusBadArgument);
-            ok = false;
+            good = false;
           }
           pg[p] = pid;
         }
-        if (!ok) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kTile);
-        uint8_t* kd = smem + kOffK + s * kTile;
-        uint8_t* vd = smem + kOffV + s * kTile;
+        return good;
+      };
+      // One [128 x 128] tile: two pages x two dim halves, four [64 x 64] boxes.
+      auto load_tile = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, const int (&pg)[2]) {
+        mbar_arrive_expect_tx(bar, kTile);
         for (int p = 0; p < 2; ++p) {
           const int row = (pg[p] * args.Hkv + h) * kPage;
-          for (int d = 0; d < 2; ++d) {
-            tma_load_2d(kd + d * kHalf + p * kBox, &tmK, &kv_full[s], d * 64, row);
-            tma_load_2d(vd + d * kHalf + p * kBox, &tmV, &kv_full[s], d * 64, row);
-          }
+          for (int d = 0; d < 2; ++d) tma_load_2d(dst + d * kHalf + p * kBox, tm, bar, d * 64, row);
         }
-        issued = j + 1;
+      };
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      // Order K_0, K_1, V_0, K_2, V_1, ...: K one tile ahead of V.
+      for (int i = 0; i <= n_tiles && ok; ++i) {
+        if (i < n_tiles) {
+          const int s = i & 1;
+          if (i >= 2 && !wait_bar(&k_empty[s], ((i >> 1) - 1) & 1, args.status)) break;
+          int pg[2];
+          if (!tile_pages(i, pg)) break;
+          load_tile(&tmK, smem + kOffK + s * kTile, &k_full[s], pg);
+          k_issued = i + 1;
+        }
+        if (i >= 1) {
+          const int j = i - 1, s = j & 1;
+          if (j >= 2 && !wait_bar(&v_empty[s], ((j >> 1) - 1) & 1, args.status)) break;
+          int pg[2];
+          if (!tile_pages(j, pg)) break;
+          load_tile(&tmV, smem + kOffV + s * kTile, &v_full[s], pg);
+          v_issued = j + 1;
+        }
       }
-      sflag[0] = issued;
+      sflag[0] = k_issued;
+      sflag[1] = v_issued;
     }
   } else if (warp == 1) {
     if (lane == 0 && n_tiles > 0) {
@@ -235,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j <= n_tiles && ok; ++j) {
         if (j < n_tiles) {
           const int s = j & 1;
-          if (!wait_bar(&kv_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
+          if (!wait_bar(&k_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
           if (j >= 2 && !wait_bar(&s_empty[s], ((j >> 1) - 1) & 1, args.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t kb = sbase + kOffK + s * kTile;
@@ -244,10 +265,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < kD / 16; ++k)
             umma_f16(dS, kmajor_desc(qa, k), kmajor_desc(kb, k), idesc_s, k > 0 ? 1u : 0u);
           umma_commit(&s_full[s]);
+          umma_commit(&k_empty[s]);
         }
         if (j >= 1) {
           const int jp = j - 1, sp = jp & 1;
           if (!wait_bar(p_full, jp & 1, args.status)) { ok = false; break; }
+          if (!wait_bar(&v_full[sp], (jp >> 1) & 1, args.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t vb = sbase + kOffV + sp * kTile;
           const uint32_t pb = pa + sp * kTile;
@@ -257,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      umma_desc_sw128_mn(vb + k * 2048, kHalf), idesc_o,
                      (jp > 0 || k > 0) ? 1u : 0u);
           umma_commit(&pv_done[sp]);
-          umma_commit(&kv_empty[sp]);
+          umma_commit(&v_empty[sp]);
         }
       }
       // Every MMA this thread issued has finished before TMEM is released (also when a wait
@@ -284,12 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       float sv[kBN];
       const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off;
+      {
+        uint32_t r[kBN];  // one x128 load and one wait: a single TMEM round trip
+        tmem_ld128_sync(sa, r);
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32_sync(sa + c * 32, r);
-#pragma unroll
-        for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(r[t]);
+        for (int t = 0; t < kBN; ++t) sv[t] = __uint_as_float(r[t]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
@@ -301,9 +323,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kBN; ++t)
           if (key0 + t > qpos || key0 + t >= kv_len) sv[t] = -INFINITY;
       }
-      float mx = sv[0];
+      // Eight independent partial maxima / sums: short dependency chains.
+      float mxp[8];
 #pragma unroll
-      for (int t = 1; t < kBN; ++t) mx = fmaxf(mx, sv[t]);
+      for (int u = 0; u < 8; ++u) mxp[u] = sv[u];
+#pragma unroll
+      for (int t = 8; t < kBN; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], sv[t]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       // Running max in the scaled exp2 domain; it moves only when the tile's max exceeds it by
       // the threshold (or on the first tile with a finite score).
       const float mx_s = mx * args.scale_log2;
@@ -314,13 +341,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      float rs = 0.f;
+      float rsp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
 #pragma unroll
       for (int t = 0; t < kBN; ++t) {
         const float p = ex2_approx(fmaf(sv[t], args.scale_log2, -m_use));
         sv[t] = p;
-        rs += p;
+        rsp[t & 7] += p;
       }
+      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       l = l * alpha + rs;
       // P buffer j & 1 is free once PV of tile j - 2 has finished reading it.
       if (j >= 2) {
@@ -393,8 +423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0 && lane == 0 && n_tiles > 0 && load_status(args.status) != 0) {
     mbar_drain(q_full, 0);
-    const int issued = sflag[0];
-    for (int j = max(0, issued - 2); j < issued; ++j) mbar_drain(&kv_full[j & 1], (j >> 1) & 1);
+    for (int kv = 0; kv < 2; ++kv) {
+      const int issued = sflag[kv];
+      uint64_t* full = kv ? v_full : k_full;
+      for (int j = max(0, issued - 2); j < issued; ++j) mbar_drain(&full[j & 1], (j >> 1) & 1);
+    }
   }
   tc_fence_before();
   __syncthreads();
