@@ -1,29 +1,34 @@
 // Causal paged prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// One CTA per (128-query tile, query head, sequence); 192 threads in three roles:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 tokens (two 64-token
+// One CTA per (pair of 128-query tiles, query head, sequence): queries q0..q0+255 of one head
+// as two tiles A (q0..q0+127) and B (q0+128..q0+255) that share every K / V tile the CTA
+// loads, so a 64 KB K+V tile feeds 2 x 8.4 MFLOP of MMA (one tile per CTA needed twice the
+// shared-memory fill rate per FLOP and left the tensor cores waiting on L2).  Three
+// warpgroups (384 threads); warpgroup 0 gives registers to the two softmax warpgroups
+// (setmaxnreg: 56 / 224 / 224 registers per thread, launched with 168):
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128 tokens (two 64-token
 //               pages of the paged cache) into two separate two-stage rings.  K runs one tile
-//               ahead of V: a K buffer is free as soon as its QK^T has finished, a V buffer
-//               only after its PV, so K_{j+1} is already loading while the softmax warps
-//               still work on tile j - 1 (one shared K+V ring would start that load only
-//               after PV_{j-1}, leaving the tensor cores idle for a load latency per tile);
-//   warp 1      MMA issuer (one elected thread) and TMEM owner:
-//                 S[b] = Q K_j^T           (M=128 queries, N=128 keys, K=128 dims)
-//                 O   += P_{j-1} V_{j-1}   (M=128 queries, N=128 dims, K=128 keys)
-//               with S double buffered in TMEM so the next tile's QK^T runs while the
-//               softmax warps work on the current one;
-//   warps 2..5  softmax and epilogue: thread i owns query row i (TMEM lane i).  It reads its
-//               S row, applies the scale and the causal mask, keeps the running max m and sum
-//               l (exp2 domain), rescales its O row in TMEM only when m grew, writes its P row
-//               (bf16) into shared memory for the PV MMA, and after the last tile writes
-//               O / l as bf16.
-// TMEM: S0, S1, O = 3 x 128 fp32 columns (512 allocated).
+//               ahead of V: a K buffer is free once its QK^T MMAs finished, a V buffer only
+//               after its PVs;
+//   warp 1      MMA issuer (one elected thread) and TMEM owner.  Per key tile j, for X = A, B:
+//                 O_X += P_X(j) V_j              (A = P from TMEM, M=128, N=128 dims, K=128 keys)
+//                 S_X  = Q_X K_{j+1}^T           (M=128 queries, N=128 keys, K=128 dims)
+//               so the tensor cores work on one tile's MMAs while the other tile's softmax runs
+//               (ping-pong).  S_X(j+1) overwrites the TMEM columns that P_X(j) occupies, and
+//               MMAs with different accumulators are not ordered by the hardware, so the issuer
+//               waits for PV_X(j) to complete before it issues S_X(j+1);
+//   warps 2, 3  idle (they only complete warpgroup 0 for the register hand-over);
+//   warps 4..7  softmax and epilogue of tile A, warps 8..11 of tile B: thread i of a group owns
+//               query row i (TMEM lane i).  It reads its S row, applies the scale and the causal
+//               mask, keeps the running max m and sum l (exp2 domain), rescales its O row in
+//               TMEM only when m grew, writes its P row as packed bf16 over its S row, and after
+//               the last tile writes O / l as bf16.
+// TMEM (512 columns): S_A 0..127 (P_A in 0..63), S_B 128..255 (P_B), O_A 256..383, O_B 384..511.
 //
 // Shared-memory layouts (all 128-byte swizzled, 1024-byte aligned):
-//   Q  [dim half][128 rows][64 dims]             A operand, K-major
-//   K  [dim half][128 tokens][64 dims]           B operand of QK^T, K-major
-//   V  [dim half][128 tokens][64 dims]           B operand of PV, MN-major (dims contiguous)
-//   P  [2][token half][128 rows][64 tokens]      A operand of PV, K-major, double buffered
+//   Q  [tile][dim half][128 rows][64 dims]      A operand of QK^T, K-major
+//   K  [stage][dim half][128 tokens][64 dims]   B operand of QK^T, K-major
+//   V  [stage][dim half][128 tokens][64 dims]   B operand of PV, MN-major (dims contiguous)
 // A 64-token page of one KV head is two [64 x 64] TMA boxes; page p of a tile lands at
 // rows 64p..64p+63 of both dim halves.  A tile's second page past the end of the sequence is
 // replaced by its first page (finite values that the mask zeroes).
@@ -44,21 +49,25 @@ namespace {
 
 constexpr int kPage = 64;
 constexpr int kD = 128;
-constexpr int kBM = 128;                     // queries per CTA
+constexpr int kBM = 128;                     // queries per tile
+constexpr int kQT = 2;                       // query tiles per CTA
 constexpr int kBN = 128;                     // keys per tile
 constexpr int kHalf = 128 * 64 * 2;          // one [128 rows x 64] bf16 half-tile: 16 KB
 constexpr int kTile = 2 * kHalf;             // 32 KB
 constexpr int kBox = 64 * 64 * 2;            // one TMA box: 8 KB
-constexpr int kThreads = 192;
+constexpr int kThreads = 128 + kQT * 128;   // warpgroup 0 (producer, MMA) + one per tile
+constexpr int kLaunchRegs = 168;             // 65536 / 384, rounded down to 8
+constexpr int kRegsWg0 = 56, kRegsSoftmax = 224;
+static_assert(128 * kRegsWg0 + kQT * 128 * kRegsSoftmax <= kThreads * kLaunchRegs,
+              "register split above the launch allocation");
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr uint32_t kColO = 256;              // O_X at kColO + 128 X; S_X / P_X at 128 X
 
 // smem map (offsets from the 1024-aligned base)
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;         // 2 stages
+constexpr int kOffQ = 0;                     // kQT tiles
+constexpr int kOffK = kOffQ + kQT * kTile;   // 2 stages
 constexpr int kOffV = kOffK + 2 * kTile;     // 2 stages
-constexpr int kOffP = kOffV + 2 * kTile;     // 2 buffers: P of tile j+1 is written while
-constexpr int kOffBar = kOffP + 2 * kTile;   // PV of tile j still reads P of tile j
+constexpr int kOffBar = kOffV + 2 * kTile;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 struct FmhaArgs {
@@ -91,6 +100,18 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// D (TMEM) (+)= A (TMEM) x B (shared memory descriptor), kind::f16.  A is M x K with row i in
+// lane i and two 16-bit K elements per 32-bit column (lower K index in the low half).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory descriptor of an MN-major operand with the 128-byte swizzle: 64 MN
 // elements (128 bytes) per row, consecutive K rows 128 bytes apart; `mn_stride` bytes from
 // MN elements 0..63 to 64..127, 1024 bytes per 8 K rows.
@@ -120,6 +141,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // below 256 (fine in bf16) and most tiles skip the TMEM round trip of the rescale.
 constexpr float kRescaleThreshold = 8.0f;
 
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
   return mbar_wait(bar, parity, status, kStatusTimeoutFull);
 }
@@ -137,13 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = bars + 3;    // [2]
   uint64_t* v_full = bars + 5;     // [2]
   uint64_t* v_empty = bars + 7;    // [2]
-  uint64_t* s_full = bars + 9;     // [2]
-  uint64_t* s_empty = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;   // [2]: PV of tiles with that parity finished
-  uint64_t* mma_done = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  int* sflag = reinterpret_cast<int*>(bars + 18);  // [2]: K / V tiles issued
+  uint64_t* s_full = bars + 9;     // [kQT]: S_X(j) in TMEM
+  uint64_t* p_full = bars + 11;    // [kQT]: P_X(j) in TMEM (128 arrivals)
+  uint64_t* o_done = bars + 13;    // [kQT]: PV_X(j) finished
+  uint64_t* mma_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  int* sflag = reinterpret_cast<int*>(bars + 17);  // [2]: K / V tiles issued
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -157,12 +186,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
+    for (int x = 0; x < kQT; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], 128);
+      mbar_init(&o_done[x], 1);
+    }
     mbar_init(mma_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -181,25 +210,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // q and the KV cache come from earlier kernels
   const int q_begin = args.cu_q[b];
   const int q_len = args.cu_q[b + 1] - q_begin;
-  const int n_qt = (q_len + kBM - 1) / kBM;
-  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int n_qp = (q_len + kQT * kBM - 1) / (kQT * kBM);
+  const int qp = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest pairs first
   const int kv_len = args.seq_lens[b];
   const int pos0 = kv_len - q_len;
-  const int q0 = qt * kBM;
-  const bool active_cta = qt < n_qt && load_status(args.status) == 0;
-  const int last_q = min(q0 + kBM - 1, q_len - 1);
-  const int n_keys = active_cta ? min(pos0 + last_q + 1, kv_len) : 0;
-  const int n_tiles = (n_keys + kBN - 1) / kBN;
+  const int q0 = qp * kQT * kBM;
+  const bool active_cta = qp < n_qp && load_status(args.status) == 0;
+  int n_t[kQT];  // key tiles of query tile X (0 when the tile has no query)
+#pragma unroll
+  for (int x = 0; x < kQT; ++x) {
+    const int qx = q0 + x * kBM;
+    const int keys = (active_cta && qx < q_len) ? min(pos0 + min(qx + kBM, q_len), kv_len) : 0;
+    n_t[x] = (keys + kBN - 1) / kBN;
+  }
+  int n_tiles = 0;  // K / V tiles the CTA streams
+#pragma unroll
+  for (int x = 0; x < kQT; ++x) n_tiles = max(n_tiles, n_t[x]);
   const int n_pages = (kv_len + kPage - 1) / kPage;
   const int* bt = args.block_table + (long long)b * args.bt_stride;
   const uint32_t sbase = smem_u32(smem);
 
+  // Each setmaxnreg sits inside its own role branch: ptxas compiles the code it dominates
+  // with that register budget, so no softmax code may be reachable after the decrease.
+  if (warp < 4) {
+    regs_dec<kRegsWg0>();
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
-      // Q: two [128 x 64] boxes of head hq at rows q_begin + q0.
-      mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_2d(smem + kOffQ, &tmQ, q_full, hq * kD, q_begin + q0);
-      tma_load_2d(smem + kOffQ + kHalf, &tmQ, q_full, hq * kD + 64, q_begin + q0);
+      // Q: two [128 x 64] boxes per tile of head hq at rows q_begin + q0 + 128 X.  Rows past
+      // the end of q are filled with zeros by the TMA unit; rows of the next sequence are
+      // finite.  Neither is stored.
+      mbar_arrive_expect_tx(q_full, kQT * kTile);
+      for (int x = 0; x < kQT; ++x)
+        for (int d = 0; d < 2; ++d)
+          tma_load_2d(smem + kOffQ + x * kTile + d * kHalf, &tmQ, q_full, hq * kD + d * 64,
+                      q_begin + q0 + x * kBM);
       // Page ids of tile j (a second page past the context repeats the first).
       auto tile_pages = [&](int j, int (&pg)[2]) -> bool {
         bool good = true;
@@ -223,9 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       int k_issued = 0, v_issued = 0;
-      bool ok = true;
       // Order K_0, K_1, V_0, K_2, V_1, ...: K one tile ahead of V.
-      for (int i = 0; i <= n_tiles && ok; ++i) {
+      for (int i = 0; i <= n_tiles; ++i) {
         if (i < n_tiles) {
           const int s = i & 1;
           if (i >= 2 && !wait_bar(&k_empty[s], ((i >> 1) - 1) & 1, args.status)) break;
@@ -250,75 +293,92 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t idesc_s = umma_idesc_bf16(kBM, kBN);
       const uint32_t idesc_o = umma_idesc_bf16(kBM, kD) | (1u << 16);  // B (V) MN-major
-      bool ok = wait_bar(q_full, 0, args.status);
-      const uint32_t qa = sbase + kOffQ;
-      const uint32_t pa = sbase + kOffP;
-      for (int j = 0; j <= n_tiles && ok; ++j) {
-        if (j < n_tiles) {
-          const int s = j & 1;
-          if (!wait_bar(&k_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
-          if (j >= 2 && !wait_bar(&s_empty[s], ((j >> 1) - 1) & 1, args.status)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t kb = sbase + kOffK + s * kTile;
-          const uint32_t dS = tmem + (s ? kColS1 : kColS0);
+      auto issue_s = [&](int x, int j) {  // S_X = Q_X K_j^T
+        const uint32_t qa = sbase + kOffQ + x * kTile;
+        const uint32_t kb = sbase + kOffK + (j & 1) * kTile;
 #pragma unroll
-          for (int k = 0; k < kD / 16; ++k)
-            umma_f16(dS, kmajor_desc(qa, k), kmajor_desc(kb, k), idesc_s, k > 0 ? 1u : 0u);
-          umma_commit(&s_full[s]);
-          umma_commit(&k_empty[s]);
-        }
-        if (j >= 1) {
-          const int jp = j - 1, sp = jp & 1;
-          if (!wait_bar(p_full, jp & 1, args.status)) { ok = false; break; }
-          if (!wait_bar(&v_full[sp], (jp >> 1) & 1, args.status)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t vb = sbase + kOffV + sp * kTile;
-          const uint32_t pb = pa + sp * kTile;
+        for (int k = 0; k < kD / 16; ++k)
+          umma_f16(tmem + x * 128, kmajor_desc(qa, k), kmajor_desc(kb, k), idesc_s, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {  // O_X += P_X V_j, 16 keys (8 TMEM columns) per MMA
+        const uint32_t vb = sbase + kOffV + (j & 1) * kTile;
 #pragma unroll
-          for (int k = 0; k < kBN / 16; ++k)
-            umma_f16(tmem + kColO, kmajor_desc(pb, k),
-                     umma_desc_sw128_mn(vb + k * 2048, kHalf), idesc_o,
-                     (jp > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&pv_done[sp]);
-          umma_commit(&v_empty[sp]);
+        for (int k = 0; k < kBN / 16; ++k)
+          umma_f16_ts(tmem + kColO + x * 128, tmem + x * 128 + k * 8,
+                      umma_desc_sw128_mn(vb + k * 2048, kHalf), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&o_done[x]);
+      };
+      bool ok = wait_bar(q_full, 0, args.status) && wait_bar(&k_full[0], 0, args.status);
+      if (ok) {
+        tc_fence_after();
+        for (int x = 0; x < kQT; ++x)
+          if (n_t[x] > 0) issue_s(x, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j & 1;
+        bool v_ready = false, k_ready = false;
+        for (int x = 0; x < kQT && ok; ++x) {
+          if (j >= n_t[x]) continue;
+          if (!wait_bar(&p_full[x], j & 1, args.status)) { ok = false; break; }
+          if (!v_ready && !wait_bar(&v_full[s], (j >> 1) & 1, args.status)) { ok = false; break; }
+          v_ready = true;
+          tc_fence_after();
+          issue_pv(x, j);
+          if (j + 1 < n_t[x]) {
+            // S_X(j+1) overwrites P_X(j): PV_X(j) must have read it.
+            if (!wait_bar(&o_done[x], j & 1, args.status)) { ok = false; break; }
+            if (!k_ready && !wait_bar(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, args.status)) {
+              ok = false;
+              break;
+            }
+            k_ready = true;
+            tc_fence_after();
+            issue_s(x, j + 1);
+          }
         }
+        if (!ok) break;
+        umma_commit(&v_empty[s]);                              // V_j's PVs are issued
+        if (j + 1 < n_tiles) umma_commit(&k_empty[(j + 1) & 1]);  // K_{j+1}'s QK^Ts are issued
       }
       // Every MMA this thread issued has finished before TMEM is released (also when a wait
       // above gave up): one more commit, waited for regardless of the status word.
       umma_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
+  }
   } else {
-    // Softmax / epilogue warps: thread t owns query row t == TMEM lane t.
-    const int q4 = warp & 3;
+    regs_inc<kRegsSoftmax>();
+    const int x = (warp - 4) >> 2;          // query tile of this warpgroup
+    const int q4 = warp & 3;                // TMEM lane quarter this warp may access
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const int qi = q0 + row;                 // query index within the sequence
-    const int qpos = pos0 + qi;              // its absolute position
+    const int n_x = n_t[x];
+    const int qx0 = q0 + x * kBM;
+    const int qi = qx0 + row;               // query index within the sequence
+    const int qpos = pos0 + qi;             // its absolute position
+    const uint32_t tS = tmem + x * 128 + lane_off;
+    const uint32_t tO = tmem + kColO + x * 128 + lane_off;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow = smem + kOffP + row * 128;
     // tcgen05.ld / st are warp-collective (.sync.aligned): every branch around them below
     // is made uniform across the warp (__all_sync / __any_sync).
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j & 1;
-      ok = __all_sync(0xffffffffu, wait_bar(&s_full[s], (j >> 1) & 1, args.status));
+    for (int j = 0; j < n_x && ok; ++j) {
+      ok = __all_sync(0xffffffffu, wait_bar(&s_full[x], j & 1, args.status));
       if (!ok) break;
       tc_fence_after();
       float sv[kBN];
-      const uint32_t sa = tmem + (s ? kColS1 : kColS0) + lane_off;
       {
         uint32_t r[kBN];  // one x128 load and one wait: a single TMEM round trip
-        tmem_ld128_sync(sa, r);
+        tmem_ld128_sync(tS, r);
 #pragma unroll
         for (int t = 0; t < kBN; ++t) sv[t] = __uint_as_float(r[t]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);
       const int key0 = j * kBN;
-      // Masks are needed only on tiles that reach past the CTA's first query position
-      // (the causal diagonal) or past the end of the context (uniform per CTA).
-      if (key0 + kBN - 1 > pos0 + q0 || key0 + kBN > kv_len) {
+      // Masks are needed only on tiles that reach past the tile's first query position
+      // (the causal diagonal) or past the end of the context (uniform per warpgroup).
+      if (key0 + kBN - 1 > pos0 + qx0 || key0 + kBN > kv_len) {
 #pragma unroll
         for (int t = 0; t < kBN; ++t)
           if (key0 + t > qpos || key0 + t >= kv_len) sv[t] = -INFINITY;
@@ -352,50 +412,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       l = l * alpha + rs;
-      // P buffer j & 1 is free once PV of tile j - 2 has finished reading it.
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, wait_bar(&pv_done[s], ((j >> 1) - 1) & 1, args.status));
-        if (!ok) break;
-      }
-      // Rows whose max did not move multiply by 1; the warp skips only if none moved.  A
-      // rescale needs O stable: PV of tile j - 1 finished.
+      // Rows whose max did not move multiply by 1; the warp skips only if none moved.  O_X is
+      // stable here: S_X(j) was issued after PV_X(j - 1) had completed.
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        ok = __all_sync(0xffffffffu, wait_bar(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, args.status));
-        if (!ok) break;
-        tc_fence_after();
-        {
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32_sync(tO + c * 32, r);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-            tmem_st32(tmem + kColO + lane_off + c * 32, r);
-          }
-          tmem_st_wait();
+          for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+          tmem_st32(tO + c * 32, r);
         }
       }
-      // P row -> shared memory, 128-byte swizzle: token half, 16-byte chunk c at c ^ (row & 7).
-      uint8_t* prow_j = prow + s * kTile;
+      // P row -> TMEM over the S row: 64 columns of bf16 pairs (keys 2c, 2c+1 in column c).
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
+        uint32_t w[32];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float* src = sv + hh * 64 + c * 8;
-          uint4 v;
-          v.x = pack_bf16x2(src[0], src[1]);
-          v.y = pack_bf16x2(src[2], src[3]);
-          v.z = pack_bf16x2(src[4], src[5]);
-          v.w = pack_bf16x2(src[6], src[7]);
-          *reinterpret_cast<uint4*>(prow_j + hh * kHalf + ((c ^ (row & 7)) << 4)) = v;
-        }
+        for (int c = 0; c < 32; ++c) w[c] = pack_bf16x2(sv[hh * 64 + 2 * c], sv[hh * 64 + 2 * c + 1]);
+        tmem_st32(tS + hh * 32, w);
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[x]);
     }
-    const bool done = ok && n_tiles > 0 &&
-                      wait_bar(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, args.status);
+    const bool done = ok && n_x > 0 && wait_bar(&o_done[x], (n_x - 1) & 1, args.status);
     if (__all_sync(0xffffffffu, done)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -404,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32_sync(tmem + kColO + lane_off + c * 32, r);
+        tmem_ld32_sync(tO + c * 32, r);
         if (store) {
 #pragma unroll
           for (int t = 0; t < 32; t += 8) {
@@ -486,7 +527,19 @@ void paged_prefill_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::
                                 kD, kPage, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   set_smem_limit(reinterpret_cast<const void*>(fmha_prefill_tc_kernel), kSmemBytes,
                  "cudaFuncSetAttribute(fmha)");
-  dim3 grid((max_q_len + kBM - 1) / kBM, Hq, B);
+  {
+    // setmaxnreg.inc waits for registers that warpgroup 0 hands back; the split adds up to
+    // the launch allocation only if the kernel was compiled with kLaunchRegs registers.
+    static const int regs = [] {
+      cudaFuncAttributes fa{};
+      check_cuda(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(fmha_prefill_tc_kernel)),
+                 "cudaFuncGetAttributes(fmha)");
+      return fa.numRegs;
+    }();
+    TORCH_CHECK(regs == kLaunchRegs, "paged_prefill_tc: kernel compiled with ", regs,
+                " registers per thread, the register split needs ", kLaunchRegs);
+  }
+  dim3 grid((max_q_len + kQT * kBM - 1) / (kQT * kBM), Hq, B);
   launch_pdl(fmha_prefill_tc_kernel, grid, dim3(kThreads), kSmemBytes,
              at::cuda::getCurrentCUDAStream(), "paged_prefill_tc launch", tq, tk, tv, a);
 }
