@@ -150,14 +150,17 @@ class DenseWeights:
         return cls.from_full(cfg, tp, get, device, dtype, **kw)
 
     def nbytes(self) -> int:
-        n = 0
-        for t in [self.embed, self.final_norm, self.lm_head]:
-            if t is not None:
-                n += t.numel() * t.element_size()
+        """Bytes of every weight tensor held, including (codes, scales) pairs of quantized
+        weights; flags and other non-tensor layer attributes are skipped."""
+        def size(t) -> int:
+            if isinstance(t, torch.Tensor):
+                return t.numel() * t.element_size()
+            if isinstance(t, (tuple, list)):
+                return sum(size(u) for u in t)
+            return 0
+        n = sum(size(t) for t in [self.embed, self.final_norm, self.lm_head])
         for L in self.layers:
-            for t in vars(L).values():
-                if t is not None:
-                    n += t.numel() * t.element_size()
+            n += sum(size(t) for t in vars(L).values())
         return n
 
 

@@ -169,3 +169,28 @@ def test_cli_feasibility_and_variants(tmp_path):
                                  "--objective", "capacity"])
     assert r.exit_code == 0, r.output
     assert json.loads(r.output)["selected"] == "Q4_K_M"
+
+
+def test_weight_bytes_count_tensors_and_skip_flags():
+    """``nbytes`` of MoE weights counts every tensor (also inside (codes, scales) pairs) and
+    skips the per-layer flags that sit beside them."""
+    import dataclasses
+
+    import torch
+
+    from swarm_inference_lab_b200.models import config as C
+    from swarm_inference_lab_b200.models.dense import TPInfo
+    from swarm_inference_lab_b200.models.moe import MoEWeights
+    cfg = dataclasses.replace(C.preset("mixtral-8x7b-shape"), hidden_size=256,
+                              intermediate_size=512, moe_intermediate_size=512, num_layers=2,
+                              vocab_size=1024, num_heads=4, num_kv_heads=2, head_dim=64)
+    w = MoEWeights.random(cfg, TPInfo(0, 2), "cpu")
+    expect = 0
+    for t in [w.embed, w.final_norm, w.lm_head]:
+        expect += t.numel() * t.element_size() if t is not None else 0
+    for L in w.layers:
+        for v in vars(L).values():
+            if isinstance(v, torch.Tensor):
+                expect += v.numel() * v.element_size()
+    assert any(isinstance(v, bool) for v in vars(w.layers[0]).values())
+    assert w.nbytes() == expect > 0
