@@ -5,7 +5,7 @@
 // loads, so a 64 KB K+V tile feeds 2 x 8.4 MFLOP of MMA (one tile per CTA needed twice the
 // shared-memory fill rate per FLOP and left the tensor cores waiting on L2).  Three
 // warpgroups (384 threads); warpgroup 0 gives registers to the two softmax warpgroups
-// (setmaxnreg: 56 / 224 / 224 registers per thread, launched with 168):
+// (setmaxnreg: 72 / 216 / 216 registers per thread, launched with 168):
 //   warp 0      TMA producer: both Q tiles once, then K and V tiles of 128 tokens (two 64-token
 //               pages of the paged cache) into two separate two-stage rings.  K runs one tile
 //               ahead of V: a K buffer is free once its QK^T MMAs finished, a V buffer only
@@ -16,7 +16,8 @@
 //               so the tensor cores work on one tile's MMAs while the other tile's softmax runs
 //               (ping-pong).  S_X(j+1) overwrites the TMEM columns that P_X(j) occupies, and
 //               MMAs with different accumulators are not ordered by the hardware, so the issuer
-//               waits for PV_X(j) to complete before it issues S_X(j+1);
+//               waits for PV_X(j) to complete before it issues S_X(j+1) (issuing the half of
+//               S beside P ahead of that wait, as two N=64 MMAs, measured slower);
 //   warps 2, 3  idle (they only complete warpgroup 0 for the register hand-over);
 //   warps 4..7  softmax and epilogue of tile A, warps 8..11 of tile B: thread i of a group owns
 //               query row i (TMEM lane i).  It reads its S row, applies the scale and the causal
@@ -57,7 +58,7 @@ constexpr int kTile = 2 * kHalf;             // 32 KB
 constexpr int kBox = 64 * 64 * 2;            // one TMA box: 8 KB
 constexpr int kThreads = 128 + kQT * 128;   // warpgroup 0 (producer, MMA) + one per tile
 constexpr int kLaunchRegs = 168;             // 65536 / 384, rounded down to 8
-constexpr int kRegsWg0 = 56, kRegsSoftmax = 224;
+constexpr int kRegsWg0 = 72, kRegsSoftmax = 216;
 static_assert(128 * kRegsWg0 + kQT * 128 * kRegsSoftmax <= kThreads * kLaunchRegs,
               "register split above the launch allocation");
 constexpr int kTmemCols = 512;
@@ -148,6 +149,31 @@ __device__ __forceinline__ void regs_dec() {
 template <int N>
 __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Packed fp32 pairs (sm_100 f32x2 instructions: two lanes of work per issue slot).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
@@ -291,8 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && n_tiles > 0) {
-      const uint32_t idesc_s = umma_idesc_bf16(kBM, kBN);
+      const uint32_t idesc_s = umma_idesc_bf16(kBM, kBN);  // one 64-key half of S
       const uint32_t idesc_o = umma_idesc_bf16(kBM, kD) | (1u << 16);  // B (V) MN-major
+      // Half `hf` of S_X = Q_X K_j^T: keys 64 hf .. 64 hf + 63 (K rows 64 hf.., 8 KB further
+      // into each dim half) into TMEM columns 64 hf ...  P_X occupies columns 0..63 only.
       auto issue_s = [&](int x, int j) {  // S_X = Q_X K_j^T
         const uint32_t qa = sbase + kOffQ + x * kTile;
         const uint32_t kb = sbase + kOffK + (j & 1) * kTile;
@@ -383,14 +411,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kBN; ++t)
           if (key0 + t > qpos || key0 + t >= kv_len) sv[t] = -INFINITY;
       }
-      // Eight independent partial maxima / sums: short dependency chains.
+      // Eight independent partial maxima (3-input max: two keys per instruction).
       float mxp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mxp[u] = sv[u];
+      for (int u = 0; u < 8; ++u) mxp[u] = fmaxf(sv[2 * u], sv[2 * u + 1]);
 #pragma unroll
-      for (int t = 8; t < kBN; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], sv[t]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      for (int t = 16; t < kBN; t += 16)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mxp[u] = max3f(mxp[u], sv[t + 2 * u], sv[t + 2 * u + 1]);
+      const float mx = max3f(max3f(mxp[0], mxp[1], mxp[2]), max3f(mxp[3], mxp[4], mxp[5]),
+                             fmaxf(mxp[6], mxp[7]));
       // Running max in the scaled exp2 domain; it moves only when the tile's max exceeds it by
       // the threshold (or on the first tile with a finite score).
       const float mx_s = mx * args.scale_log2;
@@ -401,16 +431,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
       }
       const float m_use = m == -INFINITY ? 0.f : m;
-      float rsp[8];
+      // p = 2^(s * scale - m) for key pairs (one f32x2 FMA), sums in four packed accumulators.
+      // P_X(j) goes to TMEM over columns 0..63 of the S row (keys 2c, 2c+1 in column c), the
+      // first 64 keys stored while the second half's exponentials are computed.
+      const uint64_t sc2 = f2(args.scale_log2, args.scale_log2), nm2 = f2(-m_use, -m_use);
+      uint64_t acc[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t w[32];
 #pragma unroll
-      for (int t = 0; t < kBN; ++t) {
-        const float p = ex2_approx(fmaf(sv[t], args.scale_log2, -m_use));
-        sv[t] = p;
-        rsp[t & 7] += p;
+        for (int c = 0; c < 32; ++c) {
+          const int t = hh * 64 + 2 * c;
+          float x0, x1;
+          f2_split(fma_f2(f2(sv[t], sv[t + 1]), sc2, nm2), x0, x1);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          acc[c & 3] = add_f2(acc[c & 3], f2(p0, p1));
+          w[c] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(tS + hh * 32, w);
       }
-      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+      float rsl[4], rsh[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f2_split(acc[u], rsl[u], rsh[u]);
+      const float rs = ((rsl[0] + rsh[0]) + (rsl[1] + rsh[1])) + ((rsl[2] + rsh[2]) + (rsl[3] + rsh[3]));
       l = l * alpha + rs;
       // Rows whose max did not move multiply by 1; the warp skips only if none moved.  O_X is
       // stable here: S_X(j) was issued after PV_X(j - 1) had completed.
@@ -423,14 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
           tmem_st32(tO + c * 32, r);
         }
-      }
-      // P row -> TMEM over the S row: 64 columns of bf16 pairs (keys 2c, 2c+1 in column c).
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t w[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) w[c] = pack_bf16x2(sv[hh * 64 + 2 * c], sv[hh * 64 + 2 * c + 1]);
-        tmem_st32(tS + hh * 32, w);
       }
       tmem_st_wait();
       tc_fence_before();
