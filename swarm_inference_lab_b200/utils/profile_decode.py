@@ -6,6 +6,7 @@
     python -m swarm_inference_lab_b200.utils.profile_decode --op prefill_attn --batch 32 --ctx 2048 --kernel tc
     python -m swarm_inference_lab_b200.utils.profile_decode --op mla_decode --batch 32 --ctx 4096
     python -m swarm_inference_lab_b200.utils.profile_decode --op fp8_grouped --groups 48 --n 6 --m 7168 --k 2048
+    python -m swarm_inference_lab_b200.utils.profile_decode --op prefill_gemms --n 65536 --layers 32
 
 The decode mode builds the Llama-3-8B-shaped model with random weights and
 a KV cache whose pages hold random values (attention cost depends only on
@@ -253,10 +254,55 @@ def decode_steps(a):
             "frac_of_roofline": (wbytes + kvbytes) / pk["hbm_gbs"] / 1e6 / ms}
 
 
+def op_prefill_gemms(a):
+    """The projection GEMMs of one batch prefill of the 8B shape (``--n`` tokens: QKV, o_proj,
+    gate/up with the SwiGLU epilogue, down), ``--layers`` layers back to back, with the
+    repo's tcgen05 GEMMs and with cuBLAS (``torch.matmul``, SwiGLU as separate ops), each
+    sequence timed with CUDA events while the SM clock and throttle reasons are sampled: a
+    seconds-long dense phase is where the 1 kW power cap sets the clock."""
+    from ..ops import gemm
+    from .timing import ClockSampler
+    T, H, I, QKV = a.n, 4096, 14336, 6144
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    W = {"qkv": (QKV, H), "o": (H, H), "gu": (2 * I, H), "d": (H, I)}
+    W = {k: (torch.randn(*v, device="cuda", generator=g) * 0.02).bfloat16() for k, v in W.items()}
+    flops = 2 * T * sum(w.shape[0] * w.shape[1] for w in W.values()) * a.layers
+
+    def ours():
+        for _ in range(a.layers):
+            gemm.linear(x, W["qkv"])
+            gemm.linear(x, W["o"])
+            act = gemm.linear(x, W["gu"], swiglu=True)
+            gemm.linear(act, W["d"])
+
+    def cublas():
+        for _ in range(a.layers):
+            torch.matmul(x, W["qkv"].t())
+            torch.matmul(x, W["o"].t())
+            gu = torch.matmul(x, W["gu"].t())
+            act = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+            torch.matmul(act, W["d"].t())
+
+    out = {"op": "prefill_gemms", "tokens": T, "layers": a.layers, "TFLOP": flops / 1e12}
+    for name, fn in (("ours", ours), ("cublas", cublas), ("ours_again", ours)):
+        fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device(), period_ms=100) as clk:
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+        out[name] = {"ms": ms, "TFLOPs": flops / ms / 1e9, "clocks": clk.summary()}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", choices=["step", "gemm", "decode_attn", "prefill_attn", "mla_decode",
-                                     "fp8_grouped", "gemm_ar1", "launch_floor"],
+                                     "fp8_grouped", "gemm_ar1", "launch_floor", "prefill_gemms"],
                     default="step")
     ap.add_argument("--groups", type=int, default=48)
     ap.add_argument("--hq", type=int, default=32, help="decode_attn: query heads")
@@ -279,7 +325,8 @@ def main():
     out = {"step": decode_steps, "gemm": op_gemm, "decode_attn": op_decode_attn,
            "prefill_attn": op_prefill_attn,
            "mla_decode": op_mla_decode, "fp8_grouped": op_fp8_grouped,
-           "gemm_ar1": op_gemm_ar1, "launch_floor": op_launch_floor}[a.op](a)
+           "gemm_ar1": op_gemm_ar1, "launch_floor": op_launch_floor,
+           "prefill_gemms": op_prefill_gemms}[a.op](a)
     print(json.dumps(out))
 
 
