@@ -129,7 +129,8 @@ def run_ours(args, rank, world, local):
             from swarm_inference_lab_b200.parallel.ll_tp import LLTPComm
             comm = LLTPComm(comm, torch.device("cuda", local), max_tokens=128,
                             hidden=cfg.hidden_size)
-            comm_kind = ("gemm + ll_allreduce_norm (decode: one-shot NVLink all-reduce fused with the "
+            shot = "two-shot (reduce-scatter + all-gather)" if comm.two_shot else "one-shot"
+            comm_kind = (f"gemm + ll_allreduce_norm (decode: {shot} NVLink all-reduce fused with the "
                          "next RMSNorm, flag inside each word; distributed argmax over peer memory) "
                          "+ nccl (prefill)")
         elif args.comm == "oneshot":

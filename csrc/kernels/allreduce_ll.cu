@@ -25,6 +25,16 @@
 //      bit-identical sums);
 //   3. add the residual row, store it, and (when a norm weight is given) write the next
 //      block's input rmsnorm(h) * w.
+// Two-shot variant (reduce-scatter + all-gather, for larger groups): the row splits into
+// `world` equal slices and rank o owns slice o.  A thread whose 8 elements lie in another
+// rank's slice sends them to that owner only (ll[parity][rank] of the owner) and then waits
+// for the owner's finished values in ll[parity][owner] of its own buffer; an owning thread
+// sums every rank's words for its elements in rank order, adds the residual and sends the
+// bf16 result to every peer.  Each rank sends 2 x (world-1)/world of a row per token instead
+// of (world-1) rows, at the cost of a second NVLink crossing; the sums are the same fp32
+// rank-ordered sums, so both variants give bit-identical results.  The reduce-scatter words
+// a rank receives sit in its own slice's positions and the all-gather words in the other
+// slices' positions, so the two share the slots without overlap.
 // Slots alternate by epoch parity.  A peer can only write epoch e+2 into the parity a
 // reader uses at epoch e after it has received the reader's epoch e+1 words, which the
 // reader sends after it finished reading epoch e, so no second exchange is needed.  No
@@ -81,6 +91,27 @@ __device__ __forceinline__ uint4* ll_slot(const LLArgs& a, int owner, int par, i
          ((long long)par * kLLMaxRanks + src) * (a.max_elems / 4);
 }
 
+// Polls the two 16-byte LL words at `src` until both carry `epoch` (bounded by the status
+// word's limit); false when the wait gave up.
+__device__ __forceinline__ bool ll_recv(const uint4* src, uint32_t epoch, uint64_t limit,
+                                        int* status, uint4& v0, uint4& v1) {
+  v0 = ld_vol_v4(src);
+  v1 = ld_vol_v4(src + 1);
+  if (v0.y == epoch && v0.w == epoch && v1.y == epoch && v1.w == epoch) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (v0.y != epoch || v0.w != epoch || v1.y != epoch || v1.w != epoch) {
+    if ((++it & 255u) == 0 && (load_status(status) != 0 || globaltimer_ns() - t0 > limit)) {
+      raise_status(status, kStatusTimeoutPeer);
+      return false;
+    }
+    v0 = ld_vol_v4(src);
+    v1 = ld_vol_v4(src + 1);
+  }
+  return true;
+}
+
+template <bool kTwoShot>
 __global__ void __launch_bounds__(1024) ll_allreduce_norm_kernel(const LLArgs a) {
   __shared__ float red[32];
   __shared__ int s_ok;
@@ -95,53 +126,66 @@ __global__ void __launch_bounds__(1024) ll_allreduce_norm_kernel(const LLArgs a)
   __syncthreads();
   const bool active = u < units && s_ok;
   const long long widx = ((long long)t * units + u) * 2;  // first 16-byte LL word
-  float s[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) s[j] = 0.f;
   bool ok = true;
-  uint4 mine = make_uint4(0, 0, 0, 0);
+  uint4 o = make_uint4(0, 0, 0, 0);  // this thread's 8 elements of the new residual row
   if (active) {
-    mine = reinterpret_cast<const uint4*>(a.peers[a.rank] + a.partial_off)[(long long)t * units + u];
+    const uint4 mine =
+        reinterpret_cast<const uint4*>(a.peers[a.rank] + a.partial_off)[(long long)t * units + u];
     const uint4 w0 = make_uint4(mine.x, epoch, mine.y, epoch);
     const uint4 w1 = make_uint4(mine.z, epoch, mine.w, epoch);
-#pragma unroll
-    for (int p = 0; p < kLLMaxRanks; ++p) {
-      if (p < a.world && p != a.rank) {
-        uint4* dst = ll_slot(a, p, par, a.rank) + widx;
-        st_vol_v4(dst, w0);
-        st_vol_v4(dst + 1, w1);
-      }
-    }
     const uint64_t limit = wait_limit_ns(a.status);
-#pragma unroll 1
-    for (int p = 0; p < a.world && ok; ++p) {
-      uint4 v0, v1;
-      if (p == a.rank) {
-        v0 = make_uint4(mine.x, epoch, mine.y, epoch);
-        v1 = make_uint4(mine.z, epoch, mine.w, epoch);
-      } else {
-        const uint4* src = ll_slot(a, a.rank, par, p) + widx;
-        v0 = ld_vol_v4(src);
-        v1 = ld_vol_v4(src + 1);
-        if (v0.y != epoch || v0.w != epoch || v1.y != epoch || v1.w != epoch) {
-          const uint64_t t0 = globaltimer_ns();
-          uint32_t it = 0;
-          while (v0.y != epoch || v0.w != epoch || v1.y != epoch || v1.w != epoch) {
-            if ((++it & 255u) == 0 &&
-                (load_status(a.status) != 0 || globaltimer_ns() - t0 > limit)) {
-              raise_status(a.status, kStatusTimeoutPeer);
-              ok = false;
-              break;
-            }
-            v0 = ld_vol_v4(src);
-            v1 = ld_vol_v4(src + 1);
+    const int owner = kTwoShot ? u / (units / a.world) : a.rank;
+    if (kTwoShot && owner != a.rank) {
+      uint4* dst = ll_slot(a, owner, par, a.rank) + widx;  // reduce-scatter: to the owner only
+      st_vol_v4(dst, w0);
+      st_vol_v4(dst + 1, w1);
+      uint4 v0, v1;  // all-gather: the owner's finished values
+      ok = ll_recv(ll_slot(a, a.rank, par, owner) + widx, epoch, limit,
+                   a.status, v0, v1);
+      o = make_uint4(v0.x, v0.z, v1.x, v1.z);
+    } else {
+      if (!kTwoShot) {
+#pragma unroll
+        for (int p = 0; p < kLLMaxRanks; ++p) {
+          if (p < a.world && p != a.rank) {
+            uint4* dst = ll_slot(a, p, par, a.rank) + widx;
+            st_vol_v4(dst, w0);
+            st_vol_v4(dst + 1, w1);
           }
         }
       }
-      s[0] += bf16_lo(v0.x); s[1] += bf16_hi(v0.x);
-      s[2] += bf16_lo(v0.z); s[3] += bf16_hi(v0.z);
-      s[4] += bf16_lo(v1.x); s[5] += bf16_hi(v1.x);
-      s[6] += bf16_lo(v1.z); s[7] += bf16_hi(v1.z);
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] = 0.f;
+#pragma unroll 1
+      for (int p = 0; p < a.world && ok; ++p) {
+        uint4 v0 = w0, v1 = w1;
+        if (p != a.rank) ok = ll_recv(ll_slot(a, a.rank, par, p) + widx, epoch, limit, a.status, v0, v1);
+        if (!ok) break;
+        s[0] += bf16_lo(v0.x); s[1] += bf16_hi(v0.x);
+        s[2] += bf16_lo(v0.z); s[3] += bf16_hi(v0.z);
+        s[4] += bf16_lo(v1.x); s[5] += bf16_hi(v1.x);
+        s[6] += bf16_lo(v1.z); s[7] += bf16_hi(v1.z);
+      }
+      if (ok) {
+        const uint4 r = reinterpret_cast<const uint4*>(a.h)[(long long)t * units + u];
+        o.x = pack_bf16x2(bf16_lo(r.x) + s[0], bf16_hi(r.x) + s[1]);
+        o.y = pack_bf16x2(bf16_lo(r.y) + s[2], bf16_hi(r.y) + s[3]);
+        o.z = pack_bf16x2(bf16_lo(r.z) + s[4], bf16_hi(r.z) + s[5]);
+        o.w = pack_bf16x2(bf16_lo(r.w) + s[6], bf16_hi(r.w) + s[7]);
+        if (kTwoShot) {  // all-gather: the finished slice to every peer
+          const uint4 g0 = make_uint4(o.x, epoch, o.y, epoch);
+          const uint4 g1 = make_uint4(o.z, epoch, o.w, epoch);
+#pragma unroll
+          for (int p = 0; p < kLLMaxRanks; ++p) {
+            if (p < a.world && p != a.rank) {
+              uint4* dst = ll_slot(a, p, par, a.rank) + widx;
+              st_vol_v4(dst, g0);
+              st_vol_v4(dst + 1, g1);
+            }
+          }
+        }
+      }
     }
   }
   if (active && !ok) s_ok = 0;
@@ -150,14 +194,7 @@ __global__ void __launch_bounds__(1024) ll_allreduce_norm_kernel(const LLArgs a)
   float ss = 0.f;
   float hv[8];
   if (write) {
-    uint4* hp = reinterpret_cast<uint4*>(a.h) + (long long)t * units + u;
-    const uint4 r = *hp;
-    uint4 o;
-    o.x = pack_bf16x2(bf16_lo(r.x) + s[0], bf16_hi(r.x) + s[1]);
-    o.y = pack_bf16x2(bf16_lo(r.y) + s[2], bf16_hi(r.y) + s[3]);
-    o.z = pack_bf16x2(bf16_lo(r.z) + s[4], bf16_hi(r.z) + s[5]);
-    o.w = pack_bf16x2(bf16_lo(r.w) + s[6], bf16_hi(r.w) + s[7]);
-    *hp = o;
+    reinterpret_cast<uint4*>(a.h)[(long long)t * units + u] = o;
     // The norm sees the bf16-rounded residual stream, as the unfused RMSNorm would.
     hv[0] = bf16_lo(o.x); hv[1] = bf16_hi(o.x); hv[2] = bf16_lo(o.y); hv[3] = bf16_hi(o.y);
     hv[4] = bf16_lo(o.z); hv[5] = bf16_hi(o.z); hv[6] = bf16_lo(o.w); hv[7] = bf16_hi(o.w);
@@ -289,11 +326,13 @@ void ll_argmax_exchange(const at::Tensor& logits, const at::Tensor& idx, int64_t
 }
 
 // h [T, H] += sum over ranks of each rank's partial (bf16 at byte offset partial_off of its
-// symmetric buffer); with norm_w defined also x_out = rmsnorm(h) * norm_w.
+// symmetric buffer); with norm_w defined also x_out = rmsnorm(h) * norm_w.  two_shot picks
+// the reduce-scatter + all-gather exchange (H / 8 must be a multiple of the group size).
 void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
                        int64_t ll_off, int64_t partial_off, int64_t max_elems,
                        const c10::optional<at::Tensor>& norm_w, double eps,
-                       const c10::optional<at::Tensor>& x_out, const at::Tensor& status) {
+                       const c10::optional<at::Tensor>& x_out, const at::Tensor& status,
+                       bool two_shot) {
   TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.dim() == 2,
               "ll_allreduce_norm: h [T, H] bf16 contiguous");
   const int world = static_cast<int>(peers.size());
@@ -301,6 +340,8 @@ void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t
               "ll_allreduce_norm: group of 1..8 ranks");
   const int T = h.size(0), H = h.size(1);
   TORCH_CHECK(H % 8 == 0 && H / 8 <= 1024, "ll_allreduce_norm: H must be a multiple of 8, <= 8192");
+  TORCH_CHECK(!two_shot || (H / 8) % world == 0,
+              "ll_allreduce_norm: two-shot needs H / 8 to be a multiple of the group size");
   TORCH_CHECK((long long)T * H <= max_elems && max_elems % 8 == 0,
               "ll_allreduce_norm: T * H exceeds the buffer");
   TORCH_CHECK(ll_off % 16 == 0 && partial_off % 16 == 0 &&
@@ -331,8 +372,12 @@ void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t
   a.x_out = with_norm ? reinterpret_cast<__nv_bfloat16*>(x_out->data_ptr()) : nullptr;
   a.status = status.data_ptr<int>();
   const int threads = ((H / 8 + 31) / 32) * 32;
-  launch_pdl(ll_allreduce_norm_kernel, dim3(T), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
-             "ll_allreduce_norm launch", a);
+  if (two_shot)
+    launch_pdl(ll_allreduce_norm_kernel<true>, dim3(T), dim3(threads), 0,
+               at::cuda::getCurrentCUDAStream(), "ll_allreduce_norm launch", a);
+  else
+    launch_pdl(ll_allreduce_norm_kernel<false>, dim3(T), dim3(threads), 0,
+               at::cuda::getCurrentCUDAStream(), "ll_allreduce_norm launch", a);
 }
 
 }  // namespace sil

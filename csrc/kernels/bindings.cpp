@@ -111,7 +111,8 @@ void ll_argmax_exchange(const at::Tensor& logits, const at::Tensor& idx, int64_t
 void ll_allreduce_norm(at::Tensor& h, const std::vector<int64_t>& peers, int64_t rank,
                        int64_t ll_off, int64_t partial_off, int64_t max_elems,
                        const c10::optional<at::Tensor>& norm_w, double eps,
-                       const c10::optional<at::Tensor>& x_out, const at::Tensor& status);
+                       const c10::optional<at::Tensor>& x_out, const at::Tensor& status,
+                       bool two_shot);
 void nvls_allreduce(at::Tensor& h, const std::vector<int64_t>& peers, int64_t mc, int64_t rank,
                     int64_t flags1_off, int64_t flags2_off, int64_t partial_off, int64_t sum_off,
                     int64_t max_elems, const c10::optional<at::Tensor>& norm_w, double eps,

@@ -106,15 +106,17 @@ def main():
                                          one.partial_off, one.max_elems, nw, 1e-5, x, st)
         ll._partial(T, H).copy_(part)
 
-        def f_ll():
+        def f_ll(two=False):
             ext().ll_allreduce_norm(h, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
-                                    None, 0.0, None, st)
+                                    None, 0.0, None, st, two)
 
-        def f_ll_norm():
+        def f_ll_norm(two=False):
             ext().ll_allreduce_norm(h, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
-                                    nw, 1e-5, x, st)
+                                    nw, 1e-5, x, st, two)
         paths = [("nccl", f_nccl), ("oneshot", f_one), ("oneshot_norm", f_norm), ("ll", f_ll),
                  ("ll_norm", f_ll_norm)]
+        if world > 1 and (H // 8) % world == 0:
+            paths += [("ll_twoshot", lambda: f_ll(True)), ("ll_twoshot_norm", lambda: f_ll_norm(True))]
         if nv is not None:
             nv._partial(T, H).copy_(part)
             paths += [("nvls", lambda: nv._reduce(h)), ("nvls_norm", lambda: nv._reduce(h, nw, 1e-5, x))]

@@ -12,10 +12,19 @@ exchange costs one NVLink crossing.  Prefill-sized calls (more tokens than the b
 holds) use GEMM + NCCL.  ``all_reduce`` / ``all_gather`` / ``reduce_scatter`` forward to
 NCCL.
 
+In groups of more than two ranks the same kernel also has a two-shot exchange
+(reduce-scatter to the owner of each 1/world slice of the row, then the owner's finished
+slice to every peer): (world-1)/world x 2 of a row leaves each rank per token instead of
+(world-1) rows, for a second NVLink crossing.  Which one a group uses is measured once at
+set-up on a decode-sized call (the timings are summed over the ranks, so every rank picks
+the same); ``SIL_LL_MODE=oneshot|twoshot`` overrides it.
+
 Reference semantics: deterministic rank-ordered all-reduce of row-parallel projections,
 si/microsharding/dense.py:600-708.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -28,7 +37,8 @@ from .oneshot_tp import MAX_RANKS, open_symmetric
 class LLTPComm:
     kernel = "ll_allreduce_norm"
 
-    def __init__(self, base, device: torch.device, *, max_tokens: int = 128, hidden: int = 4096):
+    def __init__(self, base, device: torch.device, *, max_tokens: int = 128, hidden: int = 4096,
+                 mode: str | None = None):
         self.base = base
         self.rank = base.rank
         self.size = base.size
@@ -50,6 +60,46 @@ class LLTPComm:
         self._views: dict[tuple[int, int], torch.Tensor] = {}
         torch.cuda.synchronize(self.device)
         base.barrier()
+        mode = mode or os.environ.get("SIL_LL_MODE", "auto")
+        if mode not in ("auto", "oneshot", "twoshot"):
+            raise ValueError(f"SIL_LL_MODE must be auto, oneshot or twoshot, not {mode!r}")
+        two_ok = self.size > 1 and (hidden // 8) % self.size == 0
+        if mode == "twoshot" and not two_ok:
+            raise ValueError("the two-shot exchange needs hidden / 8 divisible by the group size")
+        self.two_shot = mode == "twoshot"
+        self.tuning: dict | None = None
+        if mode == "auto" and two_ok and self.size > 2:
+            self.two_shot = self._pick_two_shot()
+
+    def _pick_two_shot(self, tokens: int = 32, iters: int = 20) -> bool:
+        """Times both exchanges on a ``tokens``-row call (this rank's CUDA events, summed over
+        the group so that every rank takes the same decision); True if two-shot is faster."""
+        T = min(tokens, self.max_tokens)
+        part = self._partial(T, self.hidden)
+        part.zero_()
+        h = torch.zeros(T, self.hidden, dtype=torch.bfloat16, device=self.device)
+        status = get_workspace(self.device).status
+        ms = []
+        for two in (False, True):
+            for _ in range(3):
+                self._exchange(h, None, 0.0, None, status, two)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(iters):
+                self._exchange(h, None, 0.0, None, status, two)
+            e.record()
+            torch.cuda.synchronize(self.device)
+            ms.append(s.elapsed_time(e) / iters)
+        t = torch.tensor(ms, dtype=torch.float32, device=self.device)
+        self.base.all_reduce(t)
+        tot = t.tolist()
+        self.tuning = {"tokens": T, "oneshot_ms_sum": tot[0], "twoshot_ms_sum": tot[1]}
+        return tot[1] < 0.95 * tot[0]
+
+    def _exchange(self, h, norm_w, eps, x_out, status, two_shot=None):
+        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
+                                self.max_elems, norm_w, float(eps), x_out, status,
+                                self.two_shot if two_shot is None else two_shot)
 
     # NCCL collectives (prefill path and plumbing)
     def all_reduce(self, x):
@@ -84,8 +134,7 @@ class LLTPComm:
             return None
         part = self._partial(T, H)
         gemm.linear(x, w, out=part)
-        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
-                                self.max_elems, None, 0.0, None, get_workspace(x.device).status)
+        self._exchange(h, None, 0.0, None, get_workspace(x.device).status)
         return None
 
     def fused_gemm_allreduce_residual_norm(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor,
@@ -99,9 +148,7 @@ class LLTPComm:
             return
         part = self._partial(T, H)
         gemm.linear(x, w, out=part)
-        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
-                                self.max_elems, norm_w, float(eps), x_out,
-                                get_workspace(x.device).status)
+        self._exchange(h, norm_w, eps, x_out, get_workspace(x.device).status)
 
     def partial_buffer(self, T: int, H: int) -> torch.Tensor | None:
         """This rank's partial-sum buffer [T, H] (bf16) for a producer that writes its
@@ -114,9 +161,7 @@ class LLTPComm:
                                    eps: float = 0.0, x_out: torch.Tensor | None = None) -> None:
         """h += sum over ranks of the partial in ``partial_buffer``; with ``norm_w`` also
         x_out = rmsnorm(h) * norm_w."""
-        ext().ll_allreduce_norm(h, self.peers, self.rank, self.ll_off, self.partial_off,
-                                self.max_elems, norm_w, float(eps), x_out,
-                                get_workspace(h.device).status)
+        self._exchange(h, norm_w, eps, x_out, get_workspace(h.device).status)
 
     def argmax_exchange(self, logits: torch.Tensor, idx: torch.Tensor, vocab_start: int) -> torch.Tensor:
         """Global greedy token per row from each rank's local argmax over its vocabulary shard

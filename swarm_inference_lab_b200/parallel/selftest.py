@@ -130,21 +130,29 @@ def main():
     # Bit-equality of one row-parallel all-reduce: the low-latency kernel against NCCL in
     # deterministic mode (all-gather, fp32 rank-ordered sum, one rounding), at 1, 32 and
     # 128 tokens.
+    # Both exchanges of the kernel (one-shot, and two-shot reduce-scatter + all-gather where
+    # H / 8 divides by the group size) must give the same bits.
     det = NcclComm(deterministic=True)
     bit_equal = True
     H = cfg.hidden_size
+    modes = [False] + ([True] if (H // 8) % world == 0 else [])
     for T in (1, 32, 128):
         g = torch.Generator(device=dev).manual_seed(100 + rank * 10 + T)
         part = (torch.randn(T, H, device=dev, generator=g) * 0.5).bfloat16()
         h0 = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(T)).bfloat16()
-        h_ll, h_det = h0.clone(), h0.clone()
-        ll._partial(T, H).copy_(part)
-        from ..ops._ext import ext
-        ext().ll_allreduce_norm(h_ll, ll.peers, ll.rank, ll.ll_off, ll.partial_off, ll.max_elems,
-                                None, 0.0, None, get_workspace(dev).status)
+        h_det = h0.clone()
         det.all_reduce_residual(part.clone(), h_det)
-        torch.cuda.synchronize()
-        bit_equal &= bool(torch.equal(h_ll, h_det))
+        from ..ops._ext import ext
+        for two in modes:
+            h_ll = h0.clone()
+            ll._partial(T, H).copy_(part)
+            ext().ll_allreduce_norm(h_ll, ll.peers, ll.rank, ll.ll_off, ll.partial_off,
+                                    ll.max_elems, None, 0.0, None, get_workspace(dev).status, two)
+            torch.cuda.synchronize()
+            bit_equal &= bool(torch.equal(h_ll, h_det))
+    results["ll_modes_checked"] = {"max_rel_err": 0.0, "tokens_equal": True,
+                                   "two_shot_checked": len(modes) == 2,
+                                   "model_path_two_shot": bool(getattr(ll, "two_shot", False))}
     results["ll_vs_deterministic_nccl_bit_equal"] = {"max_rel_err": 0.0 if bit_equal else 1.0,
                                                      "tokens_equal": bit_equal}
     get_workspace(dev).check()
