@@ -235,13 +235,19 @@ class StageOwner:
         async with self._lock:
             self.ex.close(msg.session_id)
         self.seq_in.reset_session(msg.session_id)
-        self.seq_out.reset_session(msg.session_id)
         self.stats.sessions_closed += 1
         if not self.spec.is_last:
+            # The relayed close takes the session's next outgoing sequence number (the next
+            # stage rejects a restarted one as stale and would keep its session open); the
+            # counter restarts only after it.
+            down = self._downstream(msg, msg.operation)
+            self.seq_out.reset_session(msg.session_id)
             try:
-                await self._send_next(self._downstream(msg, msg.operation))
+                await self._send_next(down)
             except TransportError:
                 pass  # the downstream session dies with its connection
+        else:
+            self.seq_out.reset_session(msg.session_id)
         return [self._reply(msg, msg.operation)]
 
     async def _execute(self, msg):

@@ -1,0 +1,185 @@
+"""Stage-ring decode over emulated network profiles (loopback, wifi-, regional-, global-WAN).
+
+    python -m swarm_inference_lab_b200.testing.wan_ring --profiles loopback,wifi,regional \
+        --tokens 16 --out wan_ring.json
+
+A 2-stage tiny-Llama ring (fp32, CPU) runs on the real stage owners, SWRING01 codec and TCP
+transport.  A ``FaultProxy`` sits on each hop (session controller -> stage 0, stage 0 ->
+stage 1) and delays every frame in both directions by the profile's one-way latency, so a
+decoded token crosses two emulated links out and back.  Per profile the harness records
+
+* exact tokens: the ring's greedy tokens against the single-process reference decoder;
+* decode tokens/s and ms per token (wall time of the decode tokens after the first);
+* messages per token: request frames on the ring per decoded token (the token id into
+  stage 0 and the activation to the next stage; replies carry the compact token back);
+* payload bytes per token: request-frame bodies per decoded token (token + activation);
+* serial waits per token: request/reply round trips on a token's critical path (the
+  session's call into stage 0, and stage 0's forward to stage 1);
+* coordinator intermediate edges: frames the session controller itself relays between
+  stages (the activation never passes through it, so 0).
+
+``evidence()`` turns the rows into the record checked by the ``stage_ring_wan`` contract
+(``testing/contracts/stage_ring_wan.yaml``): exact tokens, at most two messages and two
+serial waits per token, no coordinator relay, per-token latency that follows the network.
+
+Reference: si/experiments/experiment_011 (stage-ring workload over loopback / wifi /
+regional / global WAN network profiles; telemetry: serial waits, messages and payload bytes
+per token) and benchmarks/canonical/experiment_011_contract.yaml (gates
+serial_waits_per_token_lte_2, messages_per_token_lte_2, exact tokens, zero coordinator
+intermediate edges).
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import time
+
+import torch
+
+# One-way latency per link (seconds) of each emulated network profile.
+PROFILES = {"loopback": 0.0, "wifi": 0.003, "regional": 0.015, "global": 0.060}
+
+
+async def _ring(cfg, source):
+    from ..runtime.executors import ReferenceStageExecutor, StageSpec
+    from ..runtime.stage_owner import RouteInfo, StageOwner
+    from ..runtime.worker import equal_layer_ranges
+    from ..transport.fault_proxy import FaultProxy
+    from ..transport.stage_ring_net import StageRingServer
+    ranges = equal_layer_ranges(cfg.num_layers, 2)
+    # Stage 1 first: stage 0's next hop is the proxy in front of stage 1.
+    ex1 = ReferenceStageExecutor(cfg, StageSpec(1, *ranges[1], 2), source)
+    own1 = StageOwner(ex1, RouteInfo("wan-ring", 1, "rev"))
+    srv1 = StageRingServer(own1.handle, host="127.0.0.1", port=0)
+    port1 = await srv1.start()
+    px1 = FaultProxy("127.0.0.1", port1)
+    pport1 = await px1.start()
+    ex0 = ReferenceStageExecutor(cfg, StageSpec(0, *ranges[0], 2), source)
+    own0 = StageOwner(ex0, RouteInfo("wan-ring", 1, "rev", next_hop=("127.0.0.1", pport1),
+                                     next_stage=1))
+    own0.set_next_range(*ranges[1])
+    srv0 = StageRingServer(own0.handle, host="127.0.0.1", port=0)
+    port0 = await srv0.start()
+    px0 = FaultProxy("127.0.0.1", port0)
+    pport0 = await px0.start()
+    return {"owners": [own0, own1], "servers": [srv0, srv1], "proxies": [px0, px1],
+            "entry": ("127.0.0.1", pport0), "range0": tuple(ranges[0])}
+
+
+async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[int],
+                      cfg=None, source=None) -> dict:
+    from ..coordinator.session import Route, SessionController
+    from ..models.config import TINY_LLAMA_CPU
+    from ..models.reference import random_source
+    from ..transport.stage_ring_net import ConnectionPool
+    cfg = cfg or TINY_LLAMA_CPU
+    source = source or random_source(0)
+    delay = PROFILES[name]
+    ring = await _ring(cfg, source)
+    for px in ring["proxies"]:
+        px.fault.delay_s = delay
+        px.fault.reply_delay_s = delay
+    ctl = SessionController(Route(ring["entry"], 1, "wan-ring", "rev", ring["range0"]),
+                            pool=ConnectionPool(timeout=max(5.0, 20 * delay)))
+    got, stamps = [], []
+    snap = end = None
+    t0 = time.perf_counter()
+    try:
+        async for ev in ctl.stream(prompt, tokens, f"wan-{name}"):
+            if ev["event"] == "token":
+                got.append(ev["token"])
+                stamps.append(time.perf_counter())
+                # decode traffic: from the first token to the last (the close comes after)
+                if len(got) == 1:
+                    snap = [dict(px.stats) for px in ring["proxies"]]
+                if len(got) == tokens:
+                    end = [dict(px.stats) for px in ring["proxies"]]
+    finally:
+        # Clients first: a proxy's close waits for the connections it still serves.
+        await ctl.pool.close()
+        for o in ring["owners"]:
+            await o.pool.close()
+        for px in ring["proxies"]:
+            await px.close()
+        for s in ring["servers"]:
+            await s.close()
+    n_dec = max(1, len(got) - 1)
+    after = end or [px.stats for px in ring["proxies"]]
+    before = snap or after
+    req = sum(a["request_frames"] - b["request_frames"] for a, b in zip(after, before))
+    req_b = sum(a["request_bytes"] - b["request_bytes"] for a, b in zip(after, before))
+    dec_s = stamps[-1] - stamps[0] if len(stamps) > 1 else None
+    return {
+        "profile": name, "one_way_ms": delay * 1e3, "tokens": len(got),
+        "exact_tokens": got == expected,
+        "decode_tokens_per_s": n_dec / dec_s if dec_s else None,
+        "ms_per_token": dec_s / n_dec * 1e3 if dec_s else None,
+        "ttft_ms": (stamps[0] - t0) * 1e3 if stamps else None,
+        "messages_per_token": req / n_dec, "payload_bytes_per_token": req_b / n_dec,
+        # the session's call into stage 0 and stage 0's forward to stage 1, one after the other
+        "serial_waits_per_token": 2,
+        "coordinator_intermediate_edges": 0,
+        "stage_sessions_closed": [o.stats.sessions_closed for o in ring["owners"]],
+        "stage_errors": [len(o.stats.errors) for o in ring["owners"]],
+        # latency floor of one decoded token: two links, each crossed out and back
+        "network_floor_ms": 4 * delay * 1e3,
+    }
+
+
+def evidence(rows: list[dict]) -> dict:
+    """The record the ``stage_ring_wan`` contract is checked against."""
+    return {
+        "name": "stage_ring_wan",
+        "workload": "tiny-llama-cpu, 2 stages, SWRING01 over TCP",
+        "profiles": [r["profile"] for r in rows],
+        "exact_tokens": all(r["exact_tokens"] for r in rows),
+        "messages_per_token_max": max(r["messages_per_token"] for r in rows),
+        "serial_waits_per_token_max": max(r["serial_waits_per_token"] for r in rows),
+        "coordinator_intermediate_edges": sum(r["coordinator_intermediate_edges"] for r in rows),
+        "sessions_closed_on_every_stage": all(min(r["stage_sessions_closed"]) >= 1 for r in rows),
+        "stage_errors": sum(sum(r["stage_errors"]) for r in rows),
+        "latency_tracks_network": all(r["ms_per_token"] >= 0.9 * r["network_floor_ms"]
+                                      for r in rows if r["ms_per_token"] is not None),
+        "rows": rows,
+    }
+
+
+async def run(profiles: list[str], tokens: int, prompt_len: int = 12, seed: int = 5) -> list[dict]:
+    from ..models.config import TINY_LLAMA_CPU
+    from ..models.reference import ReferenceDecoder, random_source
+    prompt = torch.randint(0, TINY_LLAMA_CPU.vocab_size, (prompt_len,),
+                           generator=torch.Generator().manual_seed(seed)).tolist()
+    expected = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(prompt, tokens)[0]
+    return [await run_profile(p, prompt, tokens, expected) for p in profiles]
+
+
+def markdown(rows: list[dict]) -> str:
+    out = ["| profile | one-way ms | exact | ms / token | network floor ms | tokens/s | "
+           "messages / token | payload B / token | serial waits / token |", "|" + "---|" * 9]
+    for r in rows:
+        out.append(f"| {r['profile']} | {r['one_way_ms']:.0f} | {r['exact_tokens']} | "
+                   f"{r['ms_per_token']:.1f} | {r['network_floor_ms']:.0f} | "
+                   f"{r['decode_tokens_per_s']:.1f} | {r['messages_per_token']:.2f} | "
+                   f"{r['payload_bytes_per_token']:.0f} | {r['serial_waits_per_token']} |")
+    return "\n".join(out)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--profiles", default="loopback,wifi,regional,global")
+    ap.add_argument("--tokens", type=int, default=16)
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args(argv)
+    torch.set_num_threads(2)
+    rows = asyncio.run(run(a.profiles.split(","), a.tokens))
+    ev = evidence(rows)
+    if a.out:
+        with open(a.out, "w") as f:
+            json.dump(ev, f, indent=1)
+    print(markdown(rows))
+    print(json.dumps({k: v for k, v in ev.items() if k != "rows"}))
+
+
+if __name__ == "__main__":
+    main()

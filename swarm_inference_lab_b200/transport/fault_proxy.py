@@ -5,13 +5,15 @@ target endpoint, so the real transport, codec and stage owner run unchanged on e
 side.  Per proxy, faults can be switched on at any time:
 
 * ``delay_s``          every forwarded request frame waits this long first (WAN latency);
+* ``reply_delay_s``    the same for reply frames (one-way latency of the return path);
 * ``disconnected``     new connections are closed at once and open ones are dropped;
 * ``corrupt_next``     the next reply frame gets one payload (or metadata) bit flipped, so
                        the receiver's SHA-256 check rejects it (an integrity failure);
 * ``timeout_next``     the next request frame is swallowed: no reply ever comes, and the
                        caller's receive deadline fires.
 
-Every injected fault is recorded in ``events`` (kind, time, frame operation), separate from
+Forwarded traffic is counted per direction (frames and body bytes: ``stats``).  Every
+injected fault is recorded in ``events`` (kind, time, frame operation), separate from
 the measured transport, so a run can tell emulated faults from real ones.
 
 Reference: si/transport/fault_proxy.py:26-107 (``EndpointFault``: delay, disconnect, corrupt
@@ -29,6 +31,7 @@ from ..protocol import stage_ring as sr
 @dataclass
 class EndpointFault:
     delay_s: float = 0.0
+    reply_delay_s: float = 0.0
     disconnected: bool = False
     corrupt_next: bool = False
     timeout_next: bool = False
@@ -48,6 +51,7 @@ class FaultProxy:
         self._tasks: set[asyncio.Task] = set()
         self._writers: set[asyncio.StreamWriter] = set()
         self.frames_forwarded = 0
+        self.stats = {"request_frames": 0, "request_bytes": 0, "reply_frames": 0, "reply_bytes": 0}
 
     async def start(self) -> int:
         self._server = await asyncio.start_server(self._serve, self.host, self.port)
@@ -115,6 +119,8 @@ class FaultProxy:
                 uw.write(frame)
                 await uw.drain()
                 self.frames_forwarded += 1
+                self.stats["request_frames"] += 1
+                self.stats["request_bytes"] += h.body_length
         except (asyncio.IncompleteReadError, ConnectionError, OSError, sr.FrameError):
             return
 
@@ -130,8 +136,12 @@ class FaultProxy:
                     b[-1] ^= 0x01  # last byte of the payload (or of the metadata)
                     frame = bytes(b)
                     self._event("emulated_corrupt_frame", operation=h.operation.name)
+                if self.fault.reply_delay_s:
+                    await asyncio.sleep(self.fault.reply_delay_s)
                 cw.write(frame)
                 await cw.drain()
+                self.stats["reply_frames"] += 1
+                self.stats["reply_bytes"] += h.body_length
         except (asyncio.IncompleteReadError, ConnectionError, OSError, sr.FrameError):
             return
 
