@@ -84,11 +84,25 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
-// A waiting thread may be suspended by the hardware for up to 20 us (it resumes as soon as
-// the phase completes): waiters then stop issuing poll instructions, which in a seconds-long
-// GEMM phase under the 1 kW power cap measured 11% faster (a higher SM clock) than the
-// default suspend limit.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// The same test, but a waiting thread may be suspended by the hardware for up to 20 us (it
+// resumes when the phase completes): waiters stop issuing poll instructions.  Used by the
+// large (prefill) GEMM, where 128 epilogue threads wait through each tile's whole mainloop:
+// in a seconds-long GEMM phase under the 1 kW power cap that measured 11% faster (a higher
+// SM clock).  Short latency-bound kernels keep the plain test (decode measured 0.7% slower
+// with the suspend limit).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -103,15 +117,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // Wait for the phase with the given parity to complete.  Returns false if the
 // wait gave up (deadline or an already-raised status); the caller must then
 // skip dependent work and head for the kernel's exit.
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
                                           int code) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
+  auto test = [a, parity]() {
+    return kSleep ? mbar_try_wait_sleep(a, parity) : mbar_try_wait(a, parity);
+  };
+  if (test()) return true;
   const uint64_t t0 = globaltimer_ns();
   const uint64_t limit = wait_limit_ns(status);
   uint32_t it = 0;
   while (true) {
-    if (mbar_try_wait(a, parity)) return true;
+    if (test()) return true;
     if ((++it & 63u) == 0) {
       if (load_status(status) != 0) return false;
       if (globaltimer_ns() - t0 > limit) {

@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               pdl_wait();
               waited = true;
             }
-            if (!mbar_wait(&empty[s], (r & 1) ^ 1, args.status, kStatusTimeoutEmpty)) {
+            if (!mbar_wait<!SWAP>(&empty[s], (r & 1) ^ 1, args.status, kStatusTimeoutEmpty)) {
               ok = false;
               break;
             }
@@ -546,12 +546,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         Segment sg;
         while (ok && sch.next(args, sg)) {
           const int b = j & 1;
-          if (!mbar_wait(&acc_empty[b], ((j >> 1) & 1) ^ 1, args.status, kStatusTimeoutAccum)) break;
+          if (!mbar_wait<!SWAP>(&acc_empty[b], ((j >> 1) & 1) ^ 1, args.status, kStatusTimeoutAccum)) break;
           tc_fence_after();
           const uint32_t acc = tmem_base + b * C::ACC_COLS;
           for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
             const int s = i % STAGES;
-            if (!mbar_wait(&full[s], (i / STAGES) & 1, args.status, kStatusTimeoutFull)) {
+            if (!mbar_wait<!SWAP>(&full[s], (i / STAGES) & 1, args.status, kStatusTimeoutFull)) {
               ok = false;
               break;
             }
@@ -594,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const TileCtx tc = make_ctx<GROUPED, SWAP>(args, sg.tile, s_pref);
         const int nt = tc.nt;
         const int m_glob = tc.mt * BM + row;
-        if (!mbar_wait(&acc_full[b], (j >> 1) & 1, args.status, kStatusTimeoutAccum)) break;
+        if (!mbar_wait<!SWAP>(&acc_full[b], (j >> 1) & 1, args.status, kStatusTimeoutAccum)) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + b * C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
         const bool whole = sg.kb0 == 0 && sg.kb1 == nkb;
