@@ -102,3 +102,47 @@ def test_ll_exchange_against_emulated_peer(two_shot):
         e.symm_free(mine)
         e.symm_free(peer)
         get_workspace().reset()
+
+
+def test_set_up_timing_picks_a_mode_in_a_group_of_one():
+    """The set-up timing that chooses between the exchanges (run at construction in groups of
+    more than two ranks) runs both kernels, sums the timings over the group and leaves the
+    communicator usable; here in a one-rank NCCL group."""
+    import socket
+
+    import torch.distributed as dist
+
+    from swarm_inference_lab_b200.parallel.comm import NcclComm
+    from swarm_inference_lab_b200.parallel.ll_tp import LLTPComm
+    from swarm_inference_lab_b200.ops.workspace import get_workspace
+
+    created = not dist.is_initialized()
+    if created:
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0,
+                                world_size=1, device_id=torch.device("cuda", torch.cuda.current_device()))
+    comm = None
+    try:
+        comm = LLTPComm(NcclComm(), torch.device("cuda", torch.cuda.current_device()),
+                        max_tokens=32, hidden=512)
+        assert comm.two_shot is False and comm.tuning is None  # a group of one: one-shot
+        pick = comm._pick_two_shot(tokens=32, iters=5)
+        assert isinstance(pick, bool)
+        assert comm.tuning["oneshot_ms_sum"] > 0 and comm.tuning["twoshot_ms_sum"] > 0
+        get_workspace().check()
+        # still usable: h += partial with the group's own (single) contribution
+        g = torch.Generator(device="cuda").manual_seed(3)
+        part = comm.partial_buffer(8, 512)
+        part.copy_(torch.randn(8, 512, device="cuda", generator=g).bfloat16())
+        h = torch.randn(8, 512, device="cuda", generator=g).bfloat16()
+        expect = (h.float() + part.float()).bfloat16()
+        comm.allreduce_partial_residual(h)
+        torch.cuda.synchronize()
+        assert torch.equal(h, expect)
+    finally:
+        if comm is not None:
+            comm.close()
+        if created:
+            dist.destroy_process_group()
