@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-PUBLISHED = None  # the reference publishes no B200 / Llama-3-8B number
+PUBLISHED = None  # the reference publishes no B200 / Llama-3-8B-shape decode number
 METRIC = "decode tokens/s/box + p50 TTFT/TPOT, K2-shape fp8 EP & 8B TP at 1/2/4/8 GPU"
 
 
