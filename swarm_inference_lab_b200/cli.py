@@ -428,6 +428,59 @@ def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids
     asyncio.run(go())
 
 
+@app.command("status")
+def status_command(state: str = typer.Option(STATE, "--state-dir"),
+                   json_output: bool = typer.Option(False, "--json")):
+    """Coordinator identity, uptime, workers, active requests, tokens, throughput,
+    recoveries and the last error, from the running coordinator."""
+    from .cluster.control import coordinator_client
+
+    async def go():
+        cli = coordinator_client(_store(state))
+        try:
+            return await cli.status()
+        finally:
+            await cli.close()
+    st = asyncio.run(go())
+    if json_output:
+        typer.echo(json.dumps(st, indent=1, default=str))
+        return
+    typer.echo(f"coordinator={st['coordinator_fingerprint'][:16]} uptime_s={st['uptime_s']:.1f}")
+    typer.echo(f"workers={st['healthy_workers']}/{st['workers']} models={','.join(st['models']) or '-'} "
+               f"active_requests={st['active_requests']}")
+    typer.echo(f"tokens={st['generated_tokens']} throughput_tokens_s={st['throughput_tokens_s']:.3f} "
+               f"recoveries={st['recoveries']}")
+    for name, m in st["models"].items():
+        typer.echo(f"model {name}: {json.dumps(m, default=str)}")
+    if st.get("last_error"):
+        typer.echo(f"last_error={st['last_error']}")
+
+
+@app.command("sessions")
+def sessions_command(state: str = typer.Option(STATE, "--state-dir"),
+                     include_terminal: bool = typer.Option(False, "--include-terminal"),
+                     json_output: bool = typer.Option(False, "--json")):
+    """Requests known to the running coordinator: state, model, prompt and generated tokens,
+    route generations (more than one: recovered), and errors."""
+    from .cluster.control import coordinator_client
+
+    async def go():
+        cli = coordinator_client(_store(state))
+        try:
+            return await cli.status()
+        finally:
+            await cli.close()
+    reqs = asyncio.run(go())["requests"]
+    rows = {k: v for k, v in reqs.items() if include_terminal or v["state"] == "RUNNING"}
+    if json_output:
+        typer.echo(json.dumps(rows, indent=1, default=str))
+        return
+    for rid, r in rows.items():
+        typer.echo(f"{rid} state={r['state']} model={r['model']} prompt={r['prompt_tokens']} "
+                   f"tokens={r['tokens']} generations={r['generations']}"
+                   + (f" error={r['error']}" if r.get("error") else ""))
+
+
 # ------------------------------------------------------------------ node
 @node_app.command("agent")
 def node_agent(state: str = typer.Option(STATE, "--state-dir"), host: str = typer.Option(None, "--host"),

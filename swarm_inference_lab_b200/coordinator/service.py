@@ -138,6 +138,9 @@ class RequestRecord:
     published: list[dict] = field(default_factory=list)
     generations: list[int] = field(default_factory=list)
     state: str = "RUNNING"
+    model: str = ""
+    started_at: float = 0.0
+    error: str | None = None
 
 
 def model_revision(model: dict) -> str:
@@ -161,6 +164,8 @@ class CoordinatorCore:
         self.models: dict[str, ActiveModel] = {}
         self.requests: dict[str, RequestRecord] = {}
         self.events: list[dict] = []
+        self.started_at = time.time()
+        self.last_error: str | None = None
         self.pairing = None          # PairingManager when serving a cluster
         self._sweeper: asyncio.Task | None = None
         self._lock = asyncio.Lock()
@@ -391,7 +396,7 @@ class CoordinatorCore:
             return
         rid = req.get("request_id") or uuid.uuid4().hex[:12]
         prompt = [int(t) for t in req["prompt_ids"]]
-        rec = RequestRecord(rid, prompt)
+        rec = RequestRecord(rid, prompt, model=name, started_at=time.time())
         self.requests[rid] = rec
         if self.state is not None:
             self.state.record_request(rid, prompt, {"max_tokens": req.get("max_tokens")})
@@ -399,7 +404,9 @@ class CoordinatorCore:
         try:
             grant = m.scheduler.submit(len(prompt), max_tokens)
         except Exception as exc:  # noqa: BLE001 - every replica is at capacity
-            yield {"event": "failed", "request_id": rid, "error": f"{type(exc).__name__}: {exc}"}
+            rec.state = "REJECTED"
+            rec.error = f"{type(exc).__name__}: {exc}"
+            yield {"event": "failed", "request_id": rid, "error": rec.error}
             return
         d = m.replicas[grant.route_id]
         ctl = SessionController(self._route(m, d), recover=lambda r, e: self._recover(m, d, r, e),
@@ -434,6 +441,7 @@ class CoordinatorCore:
                    "generations": rec.generations, "seconds": time.perf_counter() - t0}
         except Exception as exc:  # noqa: BLE001 - reported to the caller as an event
             rec.state = "FAILED"
+            rec.error = self.last_error = f"{type(exc).__name__}: {exc}"
             METRICS.inc("coordinator_requests_failed")
             if isinstance(exc, TransportError):
                 METRICS.inc("coordinator_transport_errors")
@@ -453,12 +461,24 @@ class CoordinatorCore:
         return {"ok": True}
 
     def status(self) -> dict:
+        """Identity, uptime, capacity, request counts, throughput and recoveries, plus one
+        record per deployed model and per request (the ``status`` / ``sessions`` commands)."""
+        uptime = time.time() - self.started_at
+        tokens = sum(len(r.tokens) for r in self.requests.values())
         return {"coordinator_fingerprint": self.identity.fingerprint,
+                "uptime_s": uptime,
                 "workers": len(self.registry.workers),
                 "healthy_workers": len(self.registry.healthy()),
+                "active_requests": sum(r.state == "RUNNING" for r in self.requests.values()),
+                "generated_tokens": tokens,
+                "throughput_tokens_s": tokens / uptime if uptime > 0 else 0.0,
+                "recoveries": sum(max(0, len(r.generations) - 1) for r in self.requests.values()),
+                "last_error": self.last_error,
                 "models": {k: self._model_status(v) for k, v in self.models.items()},
-                "requests": {k: {"state": r.state, "tokens": len(r.tokens),
-                                 "published": len(r.published), "generations": r.generations}
+                "requests": {k: {"state": r.state, "model": r.model, "prompt_tokens": len(r.prompt),
+                                 "tokens": len(r.tokens), "published": len(r.published),
+                                 "generations": r.generations, "started_at": r.started_at,
+                                 "error": r.error}
                              for k, r in self.requests.items()}}
 
     async def close(self) -> None:

@@ -134,6 +134,14 @@ def test_cluster_create_join_and_run_distributed(tmp_path, single_process):
         # The coordinator saw both workers register and heartbeat.
         status = _swarm("cluster", "status", "--state-dir", str(coord), "--json").stdout
         assert json.loads(status.strip().splitlines()[-1])["members"] == 2
+        # The running coordinator's own view: workers, generated tokens, finished sessions.
+        st = json.loads(_swarm("status", "--state-dir", str(coord), "--json").stdout)
+        assert st["healthy_workers"] == 2 and st["generated_tokens"] >= NEW
+        assert st["uptime_s"] > 0 and st["recoveries"] == 0 and st["last_error"] is None
+        sess = json.loads(_swarm("sessions", "--include-terminal", "--state-dir", str(coord),
+                                 "--json").stdout)
+        assert any(r["state"] == "COMPLETED" and r["tokens"] == NEW and
+                   r["prompt_tokens"] == len(PROMPT) for r in sess.values())
     finally:
         _stop(agents)
         _swarm("cluster", "stop", "--state-dir", str(coord), check=False)
@@ -201,6 +209,10 @@ def test_worker_killed_mid_decode_recovers_on_a_spare(tmp_path, single_process):
                 elif ev["event"] == "failed":
                     raise AssertionError(ev)
             m = core.models[dep["model"]]
+            st = core.status()
+            assert st["recoveries"] == 1 and st["generated_tokens"] == NEW
+            req = next(iter(st["requests"].values()))
+            assert req["state"] == "COMPLETED" and req["generations"] == [gen0, gen0 + 1]
             return tokens, recovered, gen0, m, victim, spare
         finally:
             _stop(list(agents.values()))
