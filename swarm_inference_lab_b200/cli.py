@@ -42,7 +42,7 @@ import typer
 app = typer.Typer(add_completion=False, help="Blackwell-native distributed inference runtime")
 cluster_app = typer.Typer(help="cluster lifecycle")
 node_app = typer.Typer(help="this node")
-model_app = typer.Typer(help="model inspection")
+model_app = typer.Typer(help="model inspection and deployment")
 identity_app = typer.Typer(help="node identity")
 probe_app = typer.Typer(help="measurements")
 app.add_typer(cluster_app, name="cluster")
@@ -481,6 +481,41 @@ def sessions_command(state: str = typer.Option(STATE, "--state-dir"),
                    + (f" error={r['error']}" if r.get("error") else ""))
 
 
+def _with_coordinator(state: str, fn):
+    """Runs ``fn(client)`` against the cluster's running coordinator."""
+    from .cluster.control import coordinator_client
+
+    async def go():
+        cli = coordinator_client(_store(state))
+        try:
+            return await fn(cli)
+        finally:
+            await cli.close()
+    return asyncio.run(go())
+
+
+@app.command("cancel")
+def cancel_command(request_id: str, state: str = typer.Option(STATE, "--state-dir")):
+    """Cancel a running request: its stream ends with a ``cancelled`` event before the next
+    token and every stage drops the session and its KV cache."""
+    rep = _with_coordinator(state, lambda c: c.cancel(request_id))
+    typer.echo(json.dumps(rep))
+    if not rep.get("ok"):
+        raise typer.Exit(1)
+
+
+@app.command("workers")
+def workers_command(state: str = typer.Option(STATE, "--state-dir"),
+                    json_output: bool = typer.Option(False, "--json")):
+    """Workers registered with the running coordinator and their last heartbeat."""
+    ws = _with_coordinator(state, lambda c: c.workers())
+    if json_output:
+        typer.echo(json.dumps(ws, indent=1, default=str))
+        return
+    for w in ws:
+        typer.echo(" ".join(f"{k}={v}" for k, v in w.items() if not isinstance(v, (dict, list))))
+
+
 # ------------------------------------------------------------------ node
 @node_app.command("agent")
 def node_agent(state: str = typer.Option(STATE, "--state-dir"), host: str = typer.Option(None, "--host"),
@@ -578,6 +613,37 @@ def node_leave(state: str = typer.Option(STATE, "--state-dir"), yes: bool = type
 
 
 # ------------------------------------------------------------------ model / plan
+@model_app.command("deploy")
+def model_deploy(model: str, stages: int = typer.Option(None, "--stages"),
+                 replicas: int = typer.Option(1, "--replicas"), seed: int = typer.Option(0, "--seed"),
+                 name: str = typer.Option(None, "--name"),
+                 state: str = typer.Option(STATE, "--state-dir")):
+    """Deploy MODEL (a preset or a local checkpoint) across the cluster's nodes through the
+    running coordinator: placement, stage loads, signed routes; prints the deployment."""
+    cfg, res = _resolve_model(model)
+    desc = _model_desc(model, cfg, _checkpoint_dir(model, res), seed)
+    dep = _with_coordinator(state, lambda c: c.deploy(desc, name=name, stages=stages,
+                                                      replicas=replicas))
+    typer.echo(json.dumps(dep, indent=1, default=str))
+
+
+@model_app.command("unload")
+def model_unload(name: str, state: str = typer.Option(STATE, "--state-dir")):
+    """Unload a deployed model: routes withdrawn, stages released on every node."""
+    typer.echo(json.dumps(_with_coordinator(state, lambda c: c.unload(name)), default=str))
+
+
+@model_app.command("plan")
+def model_plan(model: str, stages: int = typer.Option(None, "--stages"),
+               seed: int = typer.Option(0, "--seed"), state: str = typer.Option(STATE, "--state-dir")):
+    """The running coordinator's placement of MODEL on the cluster's healthy nodes (nothing
+    is deployed)."""
+    cfg, res = _resolve_model(model)
+    desc = _model_desc(model, cfg, _checkpoint_dir(model, res), seed)
+    typer.echo(json.dumps(_with_coordinator(state, lambda c: c.plan(desc, stages)), indent=1,
+                          default=str))
+
+
 @model_app.command("inspect")
 def model_inspect(path: str, as_json: bool = typer.Option(True, "--json/--text")):
     from .model_io.resolver import ModelSourceResolver

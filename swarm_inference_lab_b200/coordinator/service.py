@@ -141,6 +141,7 @@ class RequestRecord:
     model: str = ""
     started_at: float = 0.0
     error: str | None = None
+    cancel_requested: bool = False
 
 
 def model_revision(model: dict) -> str:
@@ -416,8 +417,11 @@ class CoordinatorCore:
         METRICS.inc("coordinator_requests")
         t0 = time.perf_counter()
         t_last = t0
+        agen = ctl.stream(prompt, max_tokens, rid)
         try:
-            async for ev in ctl.stream(prompt, max_tokens, rid):
+            async for ev in agen:
+                if rec.cancel_requested:
+                    break
                 if ev["event"] == "token":
                     now = time.perf_counter()
                     METRICS.observe("coordinator_ttft_ms" if ev["index"] == 0
@@ -436,6 +440,13 @@ class CoordinatorCore:
                     if ev["event"] == "recovered":
                         yield {"event": "recovered", "generation": ev["generation"],
                                "replayed": ev["replayed"]}
+            if rec.cancel_requested:
+                await agen.aclose()
+                await ctl.cancel_current()  # every stage drops the session and its KV
+                rec.state = "CANCELLED"
+                METRICS.inc("coordinator_requests_cancelled")
+                yield {"event": "cancelled", "request_id": rid, "tokens": rec.tokens}
+                return
             rec.state = "COMPLETED"
             yield {"event": "completed", "request_id": rid, "tokens": rec.tokens,
                    "generations": rec.generations, "seconds": time.perf_counter() - t0}
@@ -459,6 +470,15 @@ class CoordinatorCore:
             return {"ok": False}
         rec.published.append(pub)
         return {"ok": True}
+
+    def cancel(self, req: dict) -> dict:
+        """Stops a running request before its next token; its stream ends with a
+        ``cancelled`` event and every stage drops the session."""
+        rec = self.requests.get(req.get("request_id", ""))
+        if rec is None or rec.state != "RUNNING":
+            return {"ok": False, "state": rec.state if rec else None}
+        rec.cancel_requested = True
+        return {"ok": True, "state": rec.state}
 
     def status(self) -> dict:
         """Identity, uptime, capacity, request counts, throughput and recoveries, plus one
@@ -507,6 +527,9 @@ class CoordinatorRpcServer:
         async def workers(obj):
             return {"workers": core.workers()}
 
+        async def cancel(obj):
+            return core.cancel(obj)
+
         async def status(obj):
             return core.status()
 
@@ -535,6 +558,7 @@ class CoordinatorRpcServer:
             ("UnloadModel", "UnloadReply", core.unload),
             ("PublishToken", "PublishReply", core.publish_token),
             ("Workers", "WorkersReply", workers),
+            ("CancelRequest", "CancelReply", cancel),
             ("Status", "CoordinatorStatus", status),
             ("PlanModel", "PlanReply", plan),
             ("PairingCreate", "PairingInvitation", pairing_create),
@@ -570,6 +594,9 @@ class CoordinatorClient:
 
     async def unload(self, name: str) -> dict:
         return await self._call("UnloadModel", "UnloadRequest", {"model": name})
+
+    async def cancel(self, request_id: str) -> dict:
+        return await self._call("CancelRequest", "CancelRequestMsg", {"request_id": request_id})
 
     async def workers(self) -> list[dict]:
         return (await self._call("Workers", "WorkersRequest", {}))["workers"]

@@ -150,6 +150,7 @@ class SessionController:
         tokens: list[int] = []
         recoveries = 0
         session_id = f"{request_id}:g{self.route.generation}"
+        self.current = (session_id, request_id)
         yield {"event": "started", "request": request_id, "generation": self.route.generation}
         need_open = True
         recovering = False
@@ -198,6 +199,18 @@ class SessionController:
                 await self._close(session_id, request_id, cancel=True)
                 self.route = await self.recover_cb(self.route, exc)
                 session_id = f"{request_id}:g{self.route.generation}:r{recoveries}"
+                self.current = (session_id, request_id)
                 need_open = True
                 recovering = True
         await self._close(session_id, request_id)
+        self.current = None
+
+    async def cancel_current(self) -> bool:
+        """Cancels the session of the stream this controller ran last, on every stage (for a
+        consumer that stopped reading the stream before its end).  False if none is open."""
+        if getattr(self, "current", None) is None:
+            return False
+        session_id, request_id = self.current
+        self.current = None
+        await self._close(session_id, request_id, cancel=True)
+        return True

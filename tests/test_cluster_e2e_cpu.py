@@ -142,6 +142,16 @@ def test_cluster_create_join_and_run_distributed(tmp_path, single_process):
                                  "--json").stdout)
         assert any(r["state"] == "COMPLETED" and r["tokens"] == NEW and
                    r["prompt_tokens"] == len(PROMPT) for r in sess.values())
+        ws = json.loads(_swarm("workers", "--state-dir", str(coord), "--json").stdout)
+        assert {w["worker_id"] for w in ws} == {"n1", "n2"}
+        name = res["deployment"]["model"]
+        _swarm("model", "unload", name, "--state-dir", str(coord))
+        st = json.loads(_swarm("status", "--state-dir", str(coord), "--json").stdout)
+        assert name not in st["models"]
+        # with the workers free again, the coordinator places a new 2-stage plan on them
+        plan = json.loads(_swarm("model", "plan", "tiny-llama-cpu", "--stages", "2",
+                                 "--state-dir", str(coord)).stdout)
+        assert len(plan) == 2 and {p["worker_id"] for p in plan} == {"n1", "n2"}
     finally:
         _stop(agents)
         _swarm("cluster", "stop", "--state-dir", str(coord), check=False)
