@@ -285,6 +285,8 @@ def cluster_create(name: str, host: str = "127.0.0.1", port: int = 7651,
 
 @cluster_app.command("status")
 def cluster_status(state: str = typer.Option(STATE, "--state-dir"), as_json: bool = typer.Option(False, "--json")):
+    """This node's view of the cluster record: name, role, coordinator endpoint, member and
+    revoked counts."""
     st = _store(state)
     doc = st.load_cluster()
     _out({"cluster": doc["name"], "role": doc["role"], "coordinator": doc["coordinator_endpoint"],
@@ -293,18 +295,21 @@ def cluster_status(state: str = typer.Option(STATE, "--state-dir"), as_json: boo
 
 @cluster_app.command("nodes")
 def cluster_nodes(state: str = typer.Option(STATE, "--state-dir")):
+    """Members of the cluster (name, fingerprint, endpoints, capabilities)."""
     doc = _store(state).load_cluster()
     typer.echo(json.dumps(doc["members"], indent=1, default=str))
 
 
 @cluster_app.command("revoke")
 def cluster_revoke(node: str, state: str = typer.Option(STATE, "--state-dir")):
+    """Revoke NODE: its fingerprint is refused by the coordinator from now on."""
     fp = _store(state).revoke(node)
     typer.echo(f"revoked {node} ({fp})")
 
 
 @cluster_app.command("delete")
 def cluster_delete(state: str = typer.Option(STATE, "--state-dir"), yes: bool = typer.Option(False, "--yes")):
+    """Delete this node's cluster state (needs --yes)."""
     if not yes:
         typer.echo("refusing to delete cluster state without --yes", err=True)
         raise typer.Exit(EXIT_USAGE)
@@ -577,6 +582,8 @@ def node_update(state: str = typer.Option(STATE, "--state-dir"),
 @node_app.command("join")
 def node_join(uri: str, node_id: str = typer.Option(None, "--name"),
               state: str = typer.Option(STATE, "--state-dir")):
+    """Join a cluster with a pairing URI from `swarm cluster pair`: this node's identity is
+    enrolled and it receives its TLS certificate."""
     from .cluster.pairing import join
     from .worker_caps import local_capabilities
     caps = local_capabilities(benchmark=False)
@@ -586,6 +593,7 @@ def node_join(uri: str, node_id: str = typer.Option(None, "--name"),
 
 @node_app.command("status")
 def node_status(state: str = typer.Option(STATE, "--state-dir"), as_json: bool = typer.Option(False, "--json")):
+    """This node's identity, state directory and cluster membership."""
     st = _store(state)
     info = {"identity": st.identity().fingerprint, "state_dir": str(st.root)}
     if st.has_cluster():
@@ -596,6 +604,8 @@ def node_status(state: str = typer.Option(STATE, "--state-dir"), as_json: bool =
 
 @node_app.command("doctor")
 def node_doctor(as_json: bool = typer.Option(False, "--json")):
+    """Check this host: torch and CUDA, GPU model and compute capability (sm_100a), driver
+    and memory (nvidia-smi, read-only), and the built kernel and native libraries."""
     from .doctor import run_doctor
     rep = run_doctor()
     _out(rep, as_json)
@@ -605,6 +615,7 @@ def node_doctor(as_json: bool = typer.Option(False, "--json")):
 
 @node_app.command("leave")
 def node_leave(state: str = typer.Option(STATE, "--state-dir"), yes: bool = typer.Option(False, "--yes")):
+    """Leave the cluster: remove this node's local cluster state (needs --yes)."""
     if not yes:
         typer.echo("refusing to leave without --yes", err=True)
         raise typer.Exit(EXIT_USAGE)
@@ -646,6 +657,8 @@ def model_plan(model: str, stages: int = typer.Option(None, "--stages"),
 
 @model_app.command("inspect")
 def model_inspect(path: str, as_json: bool = typer.Option(True, "--json/--text")):
+    """Inspect a model source (preset, local checkpoint or GGUF): format, revision, size and
+    architecture profile."""
     from .model_io.resolver import ModelSourceResolver
     res = ModelSourceResolver().inspect(path)
     _out({"source": res.source, "revision": res.revision, "format": res.format,
@@ -682,6 +695,8 @@ def model_variants(directory: str, memory_gb: float = 180.0, objective: str = "b
 @app.command("plan")
 def plan_command(model: str, gpus: int = 8, batch: int = 32, ctx: int = 2304, prompt: int = 2048,
                  mode: str = "throughput", as_json: bool = typer.Option(False, "--json")):
+    """Plan MODEL on one box of GPUS B200s: candidate layouts (TP / EP / PP / DP) ranked by
+    predicted throughput from the measured peaks."""
     from .planner.box_planner import explain, plan_box, plan_json
     cfg, _ = _resolve_model(model)
     caps = _gpu_caps(gpus)
@@ -696,6 +711,7 @@ def plan_command(model: str, gpus: int = 8, batch: int = 32, ctx: int = 2304, pr
 def worker_command(stage: int, stages: int, preset: str = "tiny-llama-cpu", port: int = 0,
                    next_hop: str = typer.Option("", "--next"), seed: int = 0,
                    backend: str = "reference"):
+    """Run one stage-ring worker process (stage STAGE of STAGES) on this host."""
     from .runtime.worker import main as worker_main
     worker_main(["--preset", preset, "--stage", str(stage), "--stages", str(stages), "--port",
                  str(port), "--next", next_hop, "--seed", str(seed), "--backend", backend])
@@ -703,6 +719,8 @@ def worker_command(stage: int, stages: int, preset: str = "tiny-llama-cpu", port
 
 @probe_app.command("nvlink")
 def probe_nvlink(out: str = "nvlink_probe.json"):
+    """Measure GPU-to-GPU copy bandwidth and latency on this box (one process per GPU under
+    torchrun)."""
     from .parallel.nvlink_probe import main as probe_main
     sys.argv = ["nvlink_probe", "--out", out]
     probe_main()
@@ -710,6 +728,7 @@ def probe_nvlink(out: str = "nvlink_probe.json"):
 
 @identity_app.command("show")
 def identity_show(state: str = typer.Option(STATE, "--state-dir")):
+    """This node's Ed25519 identity: name and fingerprint."""
     ident = _store(state).identity()
     typer.echo(json.dumps({"name": ident.name, "fingerprint": ident.fingerprint}))
 
