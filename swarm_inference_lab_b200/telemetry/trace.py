@@ -4,7 +4,9 @@ lifecycle events, and NVTX ranges.
 * ``TraceWriter``: thread-safe JSONL writer of spans (``with tw.span(name, **attrs)``)
   and instant events; every record carries a monotonic timestamp, process
   and thread ids and optional causal parents (``after=[span ids]``).
-* ``merge_traces`` merges per-process files by timestamp.
+* ``merge_traces`` merges per-process files by timestamp; ``chrome_trace`` converts records
+  to the Chrome trace-event format (chrome://tracing, Perfetto): one row per process and
+  thread, causal ``after`` links as flow arrows.
 * ``critical_path`` walks the dependency graph backwards from the latest
   span and reports the chain that bounds end-to-end latency, counting
   token-critical receives (spans named ``recv*`` on the path).
@@ -99,6 +101,49 @@ def critical_path(records: list[dict]) -> dict:
     total = (path[-1]["end_ns"] - path[0]["start_ns"]) / 1e6
     recv = sum(1 for s in path if s["name"].startswith("recv"))
     return {"path": [s["name"] for s in path], "total_ms": total, "token_critical_receives": recv}
+
+
+def chrome_trace(records: list[dict]) -> dict:
+    """Chrome trace-event JSON of span / event records: spans become complete events ("X",
+    microseconds), events instant events ("i"), each process a ``pid`` with its name, and each
+    ``after`` dependency a flow arrow ("s" / "f") from the predecessor's end to the span."""
+    pids: dict[str, int] = {}
+    out: list[dict] = []
+    spans = {r["id"]: r for r in records if r.get("kind") == "span"}
+    for r in records:
+        proc = r.get("process", "")
+        if proc not in pids:
+            pids[proc] = len(pids) + 1
+            out.append({"ph": "M", "name": "process_name", "pid": pids[proc],
+                        "args": {"name": proc}})
+        base = {"name": r["name"], "pid": pids[proc], "tid": r.get("thread", 0),
+                "args": dict(r.get("attrs") or {}, id=r["id"])}
+        if r.get("kind") == "span":
+            out.append(dict(base, ph="X", ts=r["start_ns"] / 1e3,
+                            dur=(r["end_ns"] - r["start_ns"]) / 1e3))
+        else:
+            out.append(dict(base, ph="i", s="t", ts=r["ts_ns"] / 1e3))
+    flow = 0
+    for r in spans.values():
+        for dep in r.get("after", []):
+            src = spans.get(dep)
+            if src is None:
+                continue
+            flow += 1
+            out.append({"ph": "s", "id": flow, "name": "after", "cat": "dep",
+                        "pid": pids[src.get("process", "")], "tid": src.get("thread", 0),
+                        "ts": src["end_ns"] / 1e3})
+            out.append({"ph": "f", "bp": "e", "id": flow, "name": "after", "cat": "dep",
+                        "pid": pids[r.get("process", "")], "tid": r.get("thread", 0),
+                        "ts": r["start_ns"] / 1e3})
+    return {"traceEvents": out, "displayTimeUnit": "ms"}
+
+
+def write_chrome_trace(paths, out_path) -> Path:
+    """Merges JSONL trace files and writes them as one Chrome trace JSON file."""
+    out = Path(out_path)
+    out.write_text(json.dumps(chrome_trace(merge_traces(paths))))
+    return out
 
 
 class LifecycleObserver:

@@ -134,6 +134,33 @@ def test_trace_critical_path(tmp_path):
     assert cp["path"] == ["prefill", "recv_token"] and cp["token_critical_receives"] == 1
 
 
+def test_chrome_trace_export(tmp_path):
+    """Two processes' JSONL traces merge into one Chrome trace: complete events in
+    microseconds, instant events, process names and a flow arrow for the causal link."""
+    import json as _json
+
+    from swarm_inference_lab_b200.telemetry.trace import TraceWriter, write_chrome_trace
+    a = TraceWriter(tmp_path / "a.jsonl", "stage0")
+    b = TraceWriter(tmp_path / "b.jsonl", "stage1")
+    with a.span("forward", layers=16) as sa:
+        time.sleep(0.002)
+    with b.span("recv_activation", after=[sa]):
+        time.sleep(0.001)
+    b.event("token", index=0)
+    a.close()
+    b.close()
+    out = write_chrome_trace([tmp_path / "a.jsonl", tmp_path / "b.jsonl"], tmp_path / "t.json")
+    ev = _json.loads(out.read_text())["traceEvents"]
+    names = {e["args"]["name"] for e in ev if e["ph"] == "M"}
+    assert names == {"stage0", "stage1"}
+    fwd = next(e for e in ev if e["ph"] == "X" and e["name"] == "forward")
+    rcv = next(e for e in ev if e["ph"] == "X" and e["name"] == "recv_activation")
+    assert fwd["dur"] >= 2000 and fwd["args"]["layers"] == 16 and rcv["ts"] >= fwd["ts"] + fwd["dur"]
+    assert any(e["ph"] == "i" and e["name"] == "token" for e in ev)
+    s_, f_ = [e for e in ev if e["ph"] == "s"], [e for e in ev if e["ph"] == "f"]
+    assert len(s_) == len(f_) == 1 and s_[0]["pid"] != f_[0]["pid"]
+
+
 def test_box_planner_refit_changes_choice():
     from swarm_inference_lab_b200.models.config import LLAMA3_8B
     from swarm_inference_lab_b200.planner.box_planner import BoxMeasurements, plan_box
