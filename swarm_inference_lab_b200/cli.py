@@ -563,6 +563,25 @@ def node_install_service(state: str = typer.Option(STATE, "--state-dir"),
         typer.echo(unit)
 
 
+@node_app.command("uninstall-service")
+def node_uninstall_service(path: str = typer.Option(..., "--path"),
+                           yes: bool = typer.Option(False, "--yes")):
+    """Remove a unit file written by ``install-service --path`` (needs --yes).  Stopping and
+    disabling the running service is left to the service manager (``systemctl``)."""
+    p = Path(path).expanduser()
+    if not p.is_file():
+        typer.echo(f"no unit file at {p}", err=True)
+        raise typer.Exit(EXIT_USAGE)
+    if "swarm_inference_lab_b200" not in p.read_text() or "node" not in p.read_text():
+        typer.echo(f"{p} is not a unit written by install-service; left in place", err=True)
+        raise typer.Exit(EXIT_USAGE)
+    if not yes:
+        typer.echo("refusing to remove the unit file without --yes", err=True)
+        raise typer.Exit(EXIT_USAGE)
+    p.unlink()
+    typer.echo(f"removed {p}")
+
+
 @node_app.command("update")
 def node_update(state: str = typer.Option(STATE, "--state-dir"),
                 as_json: bool = typer.Option(True, "--json/--text")):
@@ -731,6 +750,29 @@ def identity_show(state: str = typer.Option(STATE, "--state-dir")):
     """This node's Ed25519 identity: name and fingerprint."""
     ident = _store(state).identity()
     typer.echo(json.dumps({"name": ident.name, "fingerprint": ident.fingerprint}))
+
+
+@identity_app.command("create")
+def identity_create(name: str = typer.Option("node", "--name"),
+                    out: str = typer.Option(..., "--out"),
+                    force: bool = typer.Option(False, "--force")):
+    """Create an Ed25519 identity document at OUT (refuses to overwrite without --force)."""
+    from .security.identity import Identity
+    p = Path(out).expanduser()
+    if p.exists() and not force:
+        typer.echo(f"{p} exists; pass --force to replace it", err=True)
+        raise typer.Exit(EXIT_USAGE)
+    ident = Identity.generate(name)
+    ident.save(p)
+    typer.echo(json.dumps({"name": ident.name, "fingerprint": ident.fingerprint, "path": str(p)}))
+
+
+@identity_app.command("fingerprint")
+def identity_fingerprint(path: str):
+    """The fingerprint of the identity document at PATH (what cluster membership and signed
+    route leases are bound to)."""
+    from .security.identity import Identity
+    typer.echo(Identity.load(Path(path).expanduser()).fingerprint)
 
 
 def main():  # console entry point

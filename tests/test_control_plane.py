@@ -215,3 +215,31 @@ def test_cli_dry_run_and_inspect(tmp_path):
     assert json.loads(r.output)["pairing_uri"].startswith("swarm-pair://")
     r = CliRunner().invoke(app, ["cluster", "create", "lab", "--state-dir", str(st)])
     assert r.exit_code == 3
+
+
+def test_cli_identity_and_service_files(tmp_path):
+    """``identity create`` / ``fingerprint`` round trip (no overwrite without --force) and
+    ``node install-service`` / ``uninstall-service`` (only its own unit, only with --yes)."""
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    run = CliRunner().invoke
+    idp = tmp_path / "id.json"
+    r = run(app, ["identity", "create", "--name", "w7", "--out", str(idp)])
+    assert r.exit_code == 0, r.output
+    fp = json.loads(r.output)["fingerprint"]
+    r = run(app, ["identity", "fingerprint", str(idp)])
+    assert r.exit_code == 0 and r.output.strip() == fp
+    assert run(app, ["identity", "create", "--out", str(idp)]).exit_code != 0
+    st, unit = tmp_path / "st", tmp_path / "agent.service"
+    assert run(app, ["cluster", "create", "lab", "--state-dir", str(st), "--json"]).exit_code == 0
+    r = run(app, ["node", "install-service", "--state-dir", str(st), "--path", str(unit)])
+    assert r.exit_code == 0 and unit.is_file()
+    assert run(app, ["node", "uninstall-service", "--path", str(unit)]).exit_code != 0
+    assert unit.is_file()
+    other = tmp_path / "other.service"
+    other.write_text("[Service]\nExecStart=/bin/true\n")
+    assert run(app, ["node", "uninstall-service", "--path", str(other), "--yes"]).exit_code != 0
+    assert other.is_file()
+    r = run(app, ["node", "uninstall-service", "--path", str(unit), "--yes"])
+    assert r.exit_code == 0 and not unit.exists()
