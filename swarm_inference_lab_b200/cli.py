@@ -45,9 +45,11 @@ node_app = typer.Typer(help="this node")
 model_app = typer.Typer(help="model inspection and deployment")
 identity_app = typer.Typer(help="node identity")
 probe_app = typer.Typer(help="measurements")
+experiment_app = typer.Typer(help="research harnesses on the real control plane (CPU)")
 app.add_typer(cluster_app, name="cluster")
 app.add_typer(node_app, name="node")
 app.add_typer(model_app, name="model")
+app.add_typer(experiment_app, name="experiment")
 app.add_typer(identity_app, name="identity")
 app.add_typer(probe_app, name="probe")
 
@@ -773,6 +775,70 @@ def identity_fingerprint(path: str):
     route leases are bound to)."""
     from .security.identity import Identity
     typer.echo(Identity.load(Path(path).expanduser()).fingerprint)
+
+
+@experiment_app.command("loopback-matrix")
+def experiment_loopback_matrix(workers: str = "2,4,8", concurrency: str = "1,16,64",
+                               stages: int = 1, tokens: int = 16,
+                               out: str = "loopback_matrix.json", csv_out: str = typer.Option(None, "--csv")):
+    """Replica scaling x concurrency and worker fan-out (cold / warm deploy, lease economics)
+    with verified tokens, on in-process workers."""
+    from .testing.loopback_matrix import main as lm_main
+    args = ["--workers", workers, "--concurrency", concurrency, "--stages", str(stages),
+            "--tokens", str(tokens), "--out", out]
+    lm_main(args + (["--csv", csv_out] if csv_out else []))
+
+
+@experiment_app.command("wan-ring")
+def experiment_wan_ring(profiles: str = "loopback,wifi,regional,global", tokens: int = 16,
+                        out: str = typer.Option(None, "--out")):
+    """Stage-ring decode through delaying proxies at emulated network profiles: exact tokens,
+    messages, payload bytes and serial waits per token."""
+    from .testing.wan_ring import main as wan_main
+    wan_main(["--profiles", profiles, "--tokens", str(tokens)] + (["--out", out] if out else []))
+
+
+@app.command("validate-run")
+def validate_run(contract: str, evidence: str):
+    """Check EVIDENCE (a JSON record, or the last JSON line of a log) against a frozen
+    CONTRACT (a name under testing/contracts or a YAML path); exit 1 when a gate fails."""
+    from .testing.acceptance import main as acc_main
+    raise typer.Exit(acc_main([contract, evidence]))
+
+
+@app.command("simulate")
+def simulate_command(stages: int = 2, requests: int = 32, prompt_tokens: int = 128,
+                     output_tokens: int = 64, decode_ms: float = 5.0, prefill_us_per_token: float = 50.0,
+                     latency_ms: float = 1.0, bandwidth_mbps: float = 1000.0, jitter_ms: float = 0.0,
+                     loss: float = 0.0, hidden_bytes: int = 8192, arrival_ms: float = 0.0,
+                     seed: int = 0, as_json: bool = typer.Option(False, "--json")):
+    """Discrete-event simulation of a pipeline ring: STAGES equal stages, one link profile,
+    REQUESTS arriving every ARRIVAL_MS; prints tokens/s, p50 TTFT / TPOT and resends."""
+    from .testing.simulation import Link, StageNode, simulate_ring
+    nodes = [StageNode(f"s{i}", decode_ms / 1e3 / stages, prefill_us_per_token / 1e6 / stages)
+             for i in range(stages)]
+    link = Link(latency_s=latency_ms / 1e3, bandwidth_Bps=bandwidth_mbps * 1e6 / 8,
+                jitter_s=jitter_ms / 1e3, loss=loss)
+    rep = simulate_ring(nodes, link, requests=requests, prompt_tokens=prompt_tokens,
+                        output_tokens=output_tokens, hidden_bytes=hidden_bytes,
+                        arrival_s=arrival_ms / 1e3, seed=seed)
+    _out(rep, as_json)
+
+
+@app.command("topology")
+def topology_command(rtt_ms: float = typer.Option(None, "--rtt-ms"),
+                     bandwidth_mbps: float = typer.Option(None, "--bandwidth-mbps"),
+                     jitter_ms: float = 0.0, stability: float = 1.0,
+                     nvlink: bool = typer.Option(False, "--nvlink"),
+                     message_bytes: int = 8192, as_json: bool = typer.Option(False, "--json")):
+    """Classify a link (NVLink, local-fast, regional, WAN, unknown) from its measured RTT,
+    bandwidth, jitter and stability, and the one-way time of a MESSAGE_BYTES message."""
+    from .planner.topology import LinkProfile, classify, transfer_ms
+    link = LinkProfile("a", "b", rtt_ms, bandwidth_mbps / 8 if bandwidth_mbps else None,
+                       jitter_ms=jitter_ms, stability=stability, kind="nvlink" if nvlink else "tcp",
+                       measured=rtt_ms is not None or nvlink)
+    _out({"domain": classify(link).value, "message_bytes": message_bytes,
+          "one_way_ms": transfer_ms(link, message_bytes)}, as_json)
 
 
 def main():  # console entry point

@@ -243,3 +243,25 @@ def test_cli_identity_and_service_files(tmp_path):
     assert other.is_file()
     r = run(app, ["node", "uninstall-service", "--path", str(unit), "--yes"])
     assert r.exit_code == 0 and not unit.exists()
+
+
+def test_cli_topology_simulate_and_validate_run(tmp_path):
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    run = CliRunner().invoke
+    r = run(app, ["topology", "--rtt-ms", "20", "--bandwidth-mbps", "200", "--json"])
+    assert r.exit_code == 0 and json.loads(r.output)["domain"] == "regional"
+    r = run(app, ["topology", "--json"])
+    assert json.loads(r.output)["domain"] == "unknown"
+    r = run(app, ["simulate", "--requests", "8", "--json"])
+    d = json.loads(r.output)
+    assert r.exit_code == 0 and d["completed"] == 8 and d["tokens_per_s"] > 0
+    good = {"exact_tokens": True, "messages_per_token_max": 2.0, "serial_waits_per_token_max": 2,
+            "coordinator_intermediate_edges": 0, "sessions_closed_on_every_stage": True,
+            "stage_errors": 0, "latency_tracks_network": True}
+    ev = tmp_path / "ev.json"
+    ev.write_text(json.dumps(good))
+    assert run(app, ["validate-run", "stage_ring_wan", str(ev)]).exit_code == 0
+    ev.write_text(json.dumps(dict(good, messages_per_token_max=3.0)))
+    assert run(app, ["validate-run", "stage_ring_wan", str(ev)]).exit_code == 1
