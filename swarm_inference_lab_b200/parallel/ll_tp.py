@@ -73,27 +73,40 @@ class LLTPComm:
 
     def _pick_two_shot(self, tokens: int = 32, iters: int = 20) -> bool:
         """Times both exchanges on a ``tokens``-row call (this rank's CUDA events, summed over
-        the group so that every rank takes the same decision); True if two-shot is faster."""
+        the group so that every rank takes the same decision); True if two-shot is faster.
+        An exchange whose calls left an error in the status word (a bounded peer wait ran
+        out) counts as infinitely slow on this rank, so the sum steers every rank to the
+        other one; the code is cleared and reported as a warning."""
+        import warnings
         T = min(tokens, self.max_tokens)
         part = self._partial(T, self.hidden)
         part.zero_()
         h = torch.zeros(T, self.hidden, dtype=torch.bfloat16, device=self.device)
-        status = get_workspace(self.device).status
+        ws = get_workspace(self.device)
         ms = []
         for two in (False, True):
             for _ in range(3):
-                self._exchange(h, None, 0.0, None, status, two)
+                self._exchange(h, None, 0.0, None, ws.status, two)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             for _ in range(iters):
-                self._exchange(h, None, 0.0, None, status, two)
+                self._exchange(h, None, 0.0, None, ws.status, two)
             e.record()
             torch.cuda.synchronize(self.device)
-            ms.append(s.elapsed_time(e) / iters)
+            code = ws.code()
+            if code:
+                warnings.warn(f"LL all-reduce set-up: the {'two' if two else 'one'}-shot exchange "
+                              f"reported status {code}; it will not be used", RuntimeWarning)
+                ws.clear_status()
+                ms.append(float("inf"))
+            else:
+                ms.append(s.elapsed_time(e) / iters)
         t = torch.tensor(ms, dtype=torch.float32, device=self.device)
         self.base.all_reduce(t)
         tot = t.tolist()
         self.tuning = {"tokens": T, "oneshot_ms_sum": tot[0], "twoshot_ms_sum": tot[1]}
+        if tot[0] == float("inf") and tot[1] == float("inf"):
+            raise RuntimeError("LL all-reduce set-up: both exchanges failed on some rank")
         return tot[1] < 0.95 * tot[0]
 
     def _exchange(self, h, norm_w, eps, x_out, status, two_shot=None):

@@ -146,3 +146,47 @@ def test_set_up_timing_picks_a_mode_in_a_group_of_one():
             comm.close()
         if created:
             dist.destroy_process_group()
+
+
+def test_set_up_timing_skips_an_exchange_that_reports_an_error():
+    """If one exchange leaves an error code while it is timed (here a fake of the two-shot
+    call that writes a peer-timeout code after the real call; no device fault), set-up counts
+    it as infinitely slow, keeps the other one and clears the status word."""
+    import socket
+
+    import torch.distributed as dist
+
+    from swarm_inference_lab_b200.ops.workspace import get_workspace
+    from swarm_inference_lab_b200.parallel.comm import NcclComm
+    from swarm_inference_lab_b200.parallel.ll_tp import LLTPComm
+
+    created = not dist.is_initialized()
+    if created:
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0,
+                                world_size=1, device_id=torch.device("cuda", torch.cuda.current_device()))
+    comm = None
+    try:
+        comm = LLTPComm(NcclComm(), torch.device("cuda", torch.cuda.current_device()),
+                        max_tokens=32, hidden=512)
+        real = comm._exchange
+
+        def failing(h, norm_w, eps, x_out, status, two_shot=None):
+            real(h, norm_w, eps, x_out, status, two_shot)
+            if two_shot:
+                status[0].fill_(4)  # what a peer wait that ran out records
+        comm._exchange = failing
+        with pytest.warns(RuntimeWarning, match="two-shot"):
+            pick = comm._pick_two_shot(tokens=32, iters=3)
+        assert pick is False
+        assert comm.tuning["twoshot_ms_sum"] == float("inf") and comm.tuning["oneshot_ms_sum"] > 0
+        assert get_workspace().code() == 0
+    finally:
+        if comm is not None:
+            comm.__dict__.pop("_exchange", None)
+            comm.close()
+        if created:
+            dist.destroy_process_group()
+        get_workspace().reset()
