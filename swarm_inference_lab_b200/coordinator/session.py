@@ -24,6 +24,7 @@ from typing import Awaitable, Callable
 
 import torch
 
+from ..engine.speculative import prompt_lookup_draft
 from ..protocol import stage_ring as sr
 from ..transport.stage_ring_net import ConnectionPool, TransportError
 from ..transport.tensor_codec import pack_tensor, unpack_tensor
@@ -69,12 +70,18 @@ Recover = Callable[[Route, Exception], Awaitable[Route]]
 class SessionController:
     def __init__(self, route: Route, *, pool: ConnectionPool | None = None,
                  recover: Recover | None = None, max_recoveries: int = 3,
-                 return_logits: bool = False):
+                 return_logits: bool = False, speculate_k: int = 0):
         self.route = route
         self.pool = pool or ConnectionPool()
         self.recover_cb = recover
         self.max_recoveries = max_recoveries
         self.return_logits = return_logits
+        # Exact speculation (off by default): up to ``speculate_k`` prompt-lookup draft tokens
+        # are verified in one VERIFY_CANDIDATES pass through the ring; the longest prefix that
+        # equals the greedy predictions is accepted plus one token, so the output is exactly
+        # the greedy output.  Not combined with per-token logits.
+        self.speculate_k = 0 if return_logits else int(speculate_k)
+        self.spec_stats = {"verify_calls": 0, "drafted": 0, "accepted": 0}
         self.seq = sr.SequenceAllocator()
         self.events: list[dict] = []
 
@@ -99,9 +106,12 @@ class SessionController:
         return rep
 
     async def _run_tokens(self, session_id, request_id, ids: list[int], position: int,
-                          op: sr.Operation, replay: bool) -> tuple[int, torch.Tensor | None]:
+                          op: sr.Operation, replay: bool,
+                          truncate_to: int | None = None) -> tuple[int, torch.Tensor | None]:
         pk = pack_tensor(torch.tensor(ids, dtype=torch.int64))
         attrs = {"tensor": pk.attributes, "replay": replay}
+        if truncate_to is not None:
+            attrs["truncate_to"] = int(truncate_to)
         if self.return_logits:
             attrs["return_logits"] = True
         rep = await self._call(self._msg(op, session_id, request_id, position, pk.payload, attrs,
@@ -110,6 +120,18 @@ class SessionController:
         if rep.payload and "tensor" in rep.attributes:
             logits = unpack_tensor(rep.payload, rep.attributes["tensor"])
         return int(rep.attributes["token"]), logits
+
+    async def _verify(self, session_id, request_id, ids: list[int], position: int,
+                      truncate_to: int | None) -> list[int]:
+        """One VERIFY_CANDIDATES pass of ``ids`` (the last accepted token then the draft) at
+        ``position``: the greedy token after every row."""
+        pk = pack_tensor(torch.tensor(ids, dtype=torch.int64))
+        attrs = {"tensor": pk.attributes, "replay": False}
+        if truncate_to is not None:
+            attrs["truncate_to"] = int(truncate_to)
+        rep = await self._call(self._msg(sr.Operation.VERIFY_CANDIDATES, session_id, request_id,
+                                         position, pk.payload, attrs, pk.shape, "int64"))
+        return [int(t) for t in rep.attributes["tokens"]]
 
     async def _open(self, session_id, request_id):
         await self._call(self._msg(sr.Operation.OPEN_SESSION, session_id, request_id, -1))
@@ -181,10 +203,33 @@ class SessionController:
                                     f"replay diverged at output {i + 1}: {t2} != {tokens[i + 1]}")
                         self.events.append({"event": "replay_complete", "request": request_id,
                                             "tokens": len(tokens)})
+                # Cache length the stages must roll back to before the next frame (rejected
+                # candidates of the last verification), or None.
+                trunc = None
                 while len(tokens) < max_new_tokens:
                     pos = len(prompt) + len(tokens) - 1
+                    draft = []
+                    if self.speculate_k:
+                        draft = prompt_lookup_draft(prompt + tokens, self.speculate_k)
+                        draft = draft[:max(0, max_new_tokens - len(tokens) - 1)]
+                    if draft:
+                        preds = await self._verify(session_id, request_id, [tokens[-1]] + draft,
+                                                   pos, trunc)
+                        m = 0
+                        while m < len(draft) and draft[m] == preds[m]:
+                            m += 1
+                        trunc = pos + 1 + m if m < len(draft) else None
+                        self.spec_stats["verify_calls"] += 1
+                        self.spec_stats["drafted"] += len(draft)
+                        self.spec_stats["accepted"] += m
+                        for tok in preds[:m + 1]:
+                            tokens.append(tok)
+                            yield {"event": "token", "index": len(tokens) - 1, "token": tok,
+                                   "logits": None}
+                        continue
                     tok, lg = await self._run_tokens(session_id, request_id, [tokens[-1]], pos,
-                                                     sr.Operation.DECODE, False)
+                                                     sr.Operation.DECODE, False, trunc)
+                    trunc = None
                     tokens.append(tok)
                     yield {"event": "token", "index": len(tokens) - 1, "token": tok, "logits": lg}
                 break

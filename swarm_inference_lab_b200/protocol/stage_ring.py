@@ -323,7 +323,8 @@ class SessionValidator:
             raise SessionError("tokenizer revision mismatch")
         if p.stage_id is not None and msg.destination_stage not in (p.stage_id, COORDINATOR):
             raise SessionError("frame addressed to another stage")
-        if p.layer_range is not None and msg.operation in (Operation.PREFILL, Operation.DECODE):
+        if p.layer_range is not None and msg.operation in (Operation.PREFILL, Operation.DECODE,
+                                                           Operation.VERIFY_CANDIDATES):
             if (msg.layer_start, msg.layer_end) != tuple(p.layer_range):
                 raise SessionError("layer interval mismatch")
         op = msg.operation

@@ -185,8 +185,8 @@ class StageOwner:
             if (self.verifier is not None and self.spec.stage_id > 0
                     and self.hello_ok_generation != self.route.generation):
                 raise sr.SessionError("no completed peer handshake for the installed route")
-            if op in (sr.Operation.PREFILL, sr.Operation.DECODE, sr.Operation.CLOSE_SESSION,
-                      sr.Operation.CANCEL_SESSION):
+            if op in (sr.Operation.PREFILL, sr.Operation.DECODE, sr.Operation.VERIFY_CANDIDATES,
+                      sr.Operation.CLOSE_SESSION, sr.Operation.CANCEL_SESSION):
                 self.seq_in.check(msg)
         except (sr.SessionError, sr.SequenceError) as exc:
             return self._error(msg, exc)
@@ -211,10 +211,8 @@ class StageOwner:
                     return await self._open(msg)
                 if op in (sr.Operation.CLOSE_SESSION, sr.Operation.CANCEL_SESSION):
                     return await self._close(msg)
-                if op in (sr.Operation.PREFILL, sr.Operation.DECODE):
+                if op in (sr.Operation.PREFILL, sr.Operation.DECODE, sr.Operation.VERIFY_CANDIDATES):
                     return await self._execute(msg)
-                if op == sr.Operation.VERIFY_CANDIDATES:
-                    raise NotImplementedError("speculative verification is not enabled on stage owners")
                 raise sr.FrameError(f"unexpected operation {op.name}")
             except TransportError:
                 raise
@@ -251,10 +249,18 @@ class StageOwner:
         return [self._reply(msg, msg.operation)]
 
     async def _execute(self, msg):
+        """PREFILL / DECODE / VERIFY_CANDIDATES: run this stage's layers on the frame's rows at
+        its position and forward the activations (the last stage answers with the greedy
+        token; for VERIFY_CANDIDATES with the greedy token after every row, ``tokens``).  A
+        ``truncate_to`` attribute first rolls the session's cache back to that length (the
+        candidates of an earlier verification that the client rejected); it travels down the
+        ring with the frame."""
         attrs = msg.attributes
         x = unpack_tensor(msg.payload, attrs["tensor"])
         t0 = time.perf_counter()
         async with self._lock:
+            if attrs.get("truncate_to") is not None:
+                self.ex.truncate(msg.session_id, int(attrs["truncate_to"]))
             y = await asyncio.to_thread(self.ex.forward, msg.session_id, x, msg.token_position)
         dt_ms = (time.perf_counter() - t0) * 1e3
         self.stats.forward_ms += dt_ms
@@ -264,6 +270,10 @@ class StageOwner:
             token = int(torch.argmax(last))  # lowest id on ties
             self.stats.tokens += 1
             out_attrs = {"token": token, "replay": bool(attrs.get("replay", False))}
+            if msg.operation == sr.Operation.VERIFY_CANDIDATES:
+                preds = [int(t) for t in torch.argmax(y.float(), dim=-1).tolist()]
+                out_attrs["tokens"] = preds
+                out_attrs["token"] = preds[0]
             payload, shape, dtype = b"", (), "none"
             if attrs.get("return_logits"):
                 pk = pack_tensor(last.cpu())
@@ -273,7 +283,7 @@ class StageOwner:
                                 shape=shape, dtype=dtype)]
         pk = pack_tensor(y, compression=self.compression)
         fwd_attrs = {"tensor": pk.attributes, "codec": pk.attributes["codec"]}
-        for k in ("return_logits", "replay"):
+        for k in ("return_logits", "replay", "truncate_to"):
             if k in attrs:
                 fwd_attrs[k] = attrs[k]
         rep = await self._send_next(self._downstream(msg, msg.operation, payload=pk.payload,

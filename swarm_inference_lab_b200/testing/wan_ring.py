@@ -14,7 +14,9 @@ decoded token crosses two emulated links out and back.  Per profile the harness 
   stage 0 and the activation to the next stage; replies carry the compact token back);
 * payload bytes per token: request-frame bodies per decoded token (token + activation);
 * serial waits per token: request/reply round trips on a token's critical path (the
-  session's call into stage 0, and stage 0's forward to stage 1);
+  session's call into stage 0, and stage 0's forward to stage 1, nested), measured from the
+  frames: with ``--speculate K`` (exact prompt-lookup speculation, one VERIFY_CANDIDATES pass
+  for up to K draft tokens) accepted drafts bring it below 2;
 * coordinator intermediate edges: frames the session controller itself relays between
   stages (the activation never passes through it, so 0).
 
@@ -68,7 +70,7 @@ async def _ring(cfg, source):
 
 
 async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[int],
-                      cfg=None, source=None) -> dict:
+                      cfg=None, source=None, speculate_k: int = 0) -> dict:
     from ..coordinator.session import Route, SessionController
     from ..models.config import TINY_LLAMA_CPU
     from ..models.reference import random_source
@@ -81,7 +83,8 @@ async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[
         px.fault.delay_s = delay
         px.fault.reply_delay_s = delay
     ctl = SessionController(Route(ring["entry"], 1, "wan-ring", "rev", ring["range0"]),
-                            pool=ConnectionPool(timeout=max(5.0, 20 * delay)))
+                            pool=ConnectionPool(timeout=max(5.0, 20 * delay)),
+                            speculate_k=speculate_k)
     got, stamps = [], []
     snap = end = None
     t0 = time.perf_counter()
@@ -111,19 +114,20 @@ async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[
     req_b = sum(a["request_bytes"] - b["request_bytes"] for a, b in zip(after, before))
     dec_s = stamps[-1] - stamps[0] if len(stamps) > 1 else None
     return {
-        "profile": name, "one_way_ms": delay * 1e3, "tokens": len(got),
+        "profile": name, "one_way_ms": delay * 1e3, "speculate_k": speculate_k,
+        "speculation": dict(ctl.spec_stats), "tokens": len(got),
         "exact_tokens": got == expected,
         "decode_tokens_per_s": n_dec / dec_s if dec_s else None,
         "ms_per_token": dec_s / n_dec * 1e3 if dec_s else None,
         "ttft_ms": (stamps[0] - t0) * 1e3 if stamps else None,
         "messages_per_token": req / n_dec, "payload_bytes_per_token": req_b / n_dec,
-        # the session's call into stage 0 and stage 0's forward to stage 1, one after the other
-        "serial_waits_per_token": 2,
+        # every request frame on this ring is a nested request / reply wait on the token path
+        "serial_waits_per_token": req / n_dec,
         "coordinator_intermediate_edges": 0,
         "stage_sessions_closed": [o.stats.sessions_closed for o in ring["owners"]],
         "stage_errors": [len(o.stats.errors) for o in ring["owners"]],
-        # latency floor of one decoded token: two links, each crossed out and back
-        "network_floor_ms": 4 * delay * 1e3,
+        # latency floor of one decoded token: each serial wait crosses a link out and back
+        "network_floor_ms": 2 * (req / n_dec) * delay * 1e3,
     }
 
 
@@ -145,13 +149,15 @@ def evidence(rows: list[dict]) -> dict:
     }
 
 
-async def run(profiles: list[str], tokens: int, prompt_len: int = 12, seed: int = 5) -> list[dict]:
+async def run(profiles: list[str], tokens: int, prompt_len: int = 12, seed: int = 5,
+              speculate_k: int = 0) -> list[dict]:
     from ..models.config import TINY_LLAMA_CPU
     from ..models.reference import ReferenceDecoder, random_source
     prompt = torch.randint(0, TINY_LLAMA_CPU.vocab_size, (prompt_len,),
                            generator=torch.Generator().manual_seed(seed)).tolist()
     expected = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(prompt, tokens)[0]
-    return [await run_profile(p, prompt, tokens, expected) for p in profiles]
+    return [await run_profile(p, prompt, tokens, expected, speculate_k=speculate_k)
+            for p in profiles]
 
 
 def markdown(rows: list[dict]) -> str:
@@ -161,7 +167,7 @@ def markdown(rows: list[dict]) -> str:
         out.append(f"| {r['profile']} | {r['one_way_ms']:.0f} | {r['exact_tokens']} | "
                    f"{r['ms_per_token']:.1f} | {r['network_floor_ms']:.0f} | "
                    f"{r['decode_tokens_per_s']:.1f} | {r['messages_per_token']:.2f} | "
-                   f"{r['payload_bytes_per_token']:.0f} | {r['serial_waits_per_token']} |")
+                   f"{r['payload_bytes_per_token']:.0f} | {r['serial_waits_per_token']:.2f} |")
     return "\n".join(out)
 
 
@@ -169,10 +175,12 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--profiles", default="loopback,wifi,regional,global")
     ap.add_argument("--tokens", type=int, default=16)
+    ap.add_argument("--speculate", type=int, default=0,
+                    help="exact prompt-lookup speculation with up to K draft tokens per pass")
     ap.add_argument("--out", default=None)
     a = ap.parse_args(argv)
     torch.set_num_threads(2)
-    rows = asyncio.run(run(a.profiles.split(","), a.tokens))
+    rows = asyncio.run(run(a.profiles.split(","), a.tokens, speculate_k=a.speculate))
     ev = evidence(rows)
     if a.out:
         with open(a.out, "w") as f:
