@@ -420,7 +420,9 @@ def coordinator_command(state: str = typer.Option(STATE, "--state-dir"),
 def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids"),
                    max_tokens: int = typer.Option(16, "--max-tokens"),
                    state: str = typer.Option(STATE, "--state-dir"),
-                   return_logits: bool = typer.Option(False, "--return-logits")):
+                   return_logits: bool = typer.Option(False, "--return-logits"),
+                   speculate: int = typer.Option(0, "--speculate",
+                                                 help="exact prompt-lookup speculation, up to K draft tokens")):
     """Stream one request of an already deployed MODEL through the coordinator (NDJSON)."""
     from .cluster.control import coordinator_client
     ids = [int(x) for x in prompt_ids.split(",") if x.strip()]
@@ -428,7 +430,8 @@ def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids
     async def go():
         cli = coordinator_client(_store(state))
         try:
-            async for ev in cli.submit_stream(model, ids, max_tokens, return_logits=return_logits):
+            async for ev in cli.submit_stream(model, ids, max_tokens, return_logits=return_logits,
+                                              speculate_k=speculate):
                 typer.echo(json.dumps(ev))
         finally:
             await cli.close()

@@ -411,7 +411,8 @@ class CoordinatorCore:
             return
         d = m.replicas[grant.route_id]
         ctl = SessionController(self._route(m, d), recover=lambda r, e: self._recover(m, d, r, e),
-                                return_logits=bool(req.get("return_logits")))
+                                return_logits=bool(req.get("return_logits")),
+                                speculate_k=int(req.get("speculate_k") or 0))
         yield {"event": "accepted", "request_id": rid, "generation": d.generation,
                "replica": grant.route_id}
         METRICS.inc("coordinator_requests")
@@ -614,11 +615,13 @@ class CoordinatorClient:
         return (await self._call("PairingCreate", "PairingRequest", {"ttl_s": ttl_s}))["uri"]
 
     async def submit_stream(self, model: str, prompt_ids: list[int], max_tokens: int, *,
-                            return_logits: bool = False, request_id: str | None = None):
+                            return_logits: bool = False, request_id: str | None = None,
+                            speculate_k: int = 0):
         async for _, ev in self.client.call_stream(
                 COORDINATOR_SERVICE, "SubmitStream", "SubmitRequest",
                 {"model": model, "prompt_ids": list(prompt_ids), "max_tokens": max_tokens,
-                 "return_logits": return_logits, "request_id": request_id}):
+                 "return_logits": return_logits, "request_id": request_id,
+                 "speculate_k": speculate_k}):
             yield ev
 
     async def close(self) -> None:

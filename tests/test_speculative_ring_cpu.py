@@ -54,3 +54,42 @@ def test_speculative_ring_decode_is_exact_and_sends_fewer_messages():
     assert frames_spec < frames_plain, (frames_spec, frames_plain)
     assert err0 == [[], []] and err1 == [[], []]
     assert closed == [1, 1]
+
+
+def test_speculation_through_the_coordinator_is_exact():
+    """``speculate_k`` on a request submitted to the coordinator (in-process, two worker
+    runtimes serving the 2-stage tiny Llama) gives the greedy tokens."""
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(PROMPT, NEW)[0]
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = []
+        try:
+            for i in range(2):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=1.0,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2})
+            toks = [ev["token"] async for ev in core.submit_stream(
+                {"model": dep["model"], "prompt_ids": PROMPT, "max_tokens": NEW, "speculate_k": 4})
+                if ev["event"] == "token"]
+            frames = [w.owner.stats.frames for w in ws]
+            return toks, frames
+        finally:
+            for w in ws:
+                await w.stop()
+            await rpc.stop()
+
+    toks, frames = asyncio.run(go())
+    assert toks == expect
+    assert frames[0] < NEW + 2  # fewer stage-0 frames than one per token (plus open / close)
