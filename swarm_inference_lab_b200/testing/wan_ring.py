@@ -20,6 +20,12 @@ decoded token crosses two emulated links out and back.  Per profile the harness 
 * coordinator intermediate edges: frames the session controller itself relays between
   stages (the activation never passes through it, so 0).
 
+``plan_strategy`` (``--plan``) measures the exact candidate strategies of the ring (plain,
+lossless payload compression, speculation) on a profile and selects the fastest; an option is
+kept only where it measures faster (the reference's planner gates
+compression_positive_utility_only / speculation_positive_utility_only,
+si/experiments/experiment_011/planner.py).
+
 ``evidence()`` turns the rows into the record checked by the ``stage_ring_wan`` contract
 (``testing/contracts/stage_ring_wan.yaml``): exact tokens, at most two messages and two
 serial waits per token, no coordinator relay, per-token latency that follows the network.
@@ -43,7 +49,7 @@ import torch
 PROFILES = {"loopback": 0.0, "wifi": 0.003, "regional": 0.015, "global": 0.060}
 
 
-async def _ring(cfg, source):
+async def _ring(cfg, source, compression: str = "none"):
     from ..runtime.executors import ReferenceStageExecutor, StageSpec
     from ..runtime.stage_owner import RouteInfo, StageOwner
     from ..runtime.worker import equal_layer_ranges
@@ -52,14 +58,14 @@ async def _ring(cfg, source):
     ranges = equal_layer_ranges(cfg.num_layers, 2)
     # Stage 1 first: stage 0's next hop is the proxy in front of stage 1.
     ex1 = ReferenceStageExecutor(cfg, StageSpec(1, *ranges[1], 2), source)
-    own1 = StageOwner(ex1, RouteInfo("wan-ring", 1, "rev"))
+    own1 = StageOwner(ex1, RouteInfo("wan-ring", 1, "rev"), compression=compression)
     srv1 = StageRingServer(own1.handle, host="127.0.0.1", port=0)
     port1 = await srv1.start()
     px1 = FaultProxy("127.0.0.1", port1)
     pport1 = await px1.start()
     ex0 = ReferenceStageExecutor(cfg, StageSpec(0, *ranges[0], 2), source)
     own0 = StageOwner(ex0, RouteInfo("wan-ring", 1, "rev", next_hop=("127.0.0.1", pport1),
-                                     next_stage=1))
+                                     next_stage=1), compression=compression)
     own0.set_next_range(*ranges[1])
     srv0 = StageRingServer(own0.handle, host="127.0.0.1", port=0)
     port0 = await srv0.start()
@@ -70,7 +76,8 @@ async def _ring(cfg, source):
 
 
 async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[int],
-                      cfg=None, source=None, speculate_k: int = 0) -> dict:
+                      cfg=None, source=None, speculate_k: int = 0,
+                      compression: str = "none") -> dict:
     from ..coordinator.session import Route, SessionController
     from ..models.config import TINY_LLAMA_CPU
     from ..models.reference import random_source
@@ -78,7 +85,7 @@ async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[
     cfg = cfg or TINY_LLAMA_CPU
     source = source or random_source(0)
     delay = PROFILES[name]
-    ring = await _ring(cfg, source)
+    ring = await _ring(cfg, source, compression)
     for px in ring["proxies"]:
         px.fault.delay_s = delay
         px.fault.reply_delay_s = delay
@@ -115,6 +122,7 @@ async def run_profile(name: str, prompt: list[int], tokens: int, expected: list[
     dec_s = stamps[-1] - stamps[0] if len(stamps) > 1 else None
     return {
         "profile": name, "one_way_ms": delay * 1e3, "speculate_k": speculate_k,
+        "compression": compression,
         "speculation": dict(ctl.spec_stats), "tokens": len(got),
         "exact_tokens": got == expected,
         "decode_tokens_per_s": n_dec / dec_s if dec_s else None,
@@ -160,6 +168,43 @@ async def run(profiles: list[str], tokens: int, prompt_len: int = 12, seed: int 
             for p in profiles]
 
 
+# Exact candidate strategies of the ring: payload compression and speculation are options
+# that a strategy keeps only where they measure faster.
+CANDIDATES = ({"name": "plain", "speculate_k": 0, "compression": "none"},
+              {"name": "compressed", "speculate_k": 0, "compression": "shuffle+zlib"},
+              {"name": "speculative", "speculate_k": 4, "compression": "none"})
+
+
+async def plan_strategy(profile: str, tokens: int = 12, candidates=CANDIDATES, prompt_len: int = 12,
+                        seed: int = 5) -> dict:
+    """Measures every candidate on the emulated ``profile`` and selects the exact one with the
+    lowest measured ms per token; non-exact candidates are excluded.  Returns the decision
+    with each candidate's measured latency, serial waits, wire bytes and exclusion reasons."""
+    from ..models.config import TINY_LLAMA_CPU
+    from ..models.reference import ReferenceDecoder, random_source
+    prompt = torch.randint(0, TINY_LLAMA_CPU.vocab_size, (prompt_len,),
+                           generator=torch.Generator().manual_seed(seed)).tolist()
+    expected = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(prompt, tokens)[0]
+    scores = []
+    for c in candidates:
+        r = await run_profile(profile, prompt, tokens, expected, speculate_k=c["speculate_k"],
+                              compression=c["compression"])
+        reasons = [] if r["exact_tokens"] else ["tokens differ from the greedy reference"]
+        if r["ms_per_token"] is None:
+            reasons.append("no decode timing")
+        scores.append({"candidate": c["name"], **c, "feasible": not reasons,
+                       "exclusion_reasons": reasons, "ms_per_token": r["ms_per_token"],
+                       "serial_waits_per_token": r["serial_waits_per_token"],
+                       "payload_bytes_per_token": r["payload_bytes_per_token"],
+                       "speculation": r["speculation"]})
+    feasible = [x for x in scores if x["feasible"]]
+    best = min(feasible, key=lambda x: (x["ms_per_token"], x["serial_waits_per_token"],
+                                        x["payload_bytes_per_token"], x["candidate"])) if feasible else None
+    for x in scores:
+        x["selected"] = best is not None and x["candidate"] == best["candidate"]
+    return {"profile": profile, "selected": best["candidate"] if best else None, "scores": scores}
+
+
 def markdown(rows: list[dict]) -> str:
     out = ["| profile | one-way ms | exact | ms / token | network floor ms | tokens/s | "
            "messages / token | payload B / token | serial waits / token |", "|" + "---|" * 9]
@@ -177,9 +222,22 @@ def main(argv=None):
     ap.add_argument("--tokens", type=int, default=16)
     ap.add_argument("--speculate", type=int, default=0,
                     help="exact prompt-lookup speculation with up to K draft tokens per pass")
+    ap.add_argument("--plan", action="store_true",
+                    help="measure the candidate strategies (plain, compressed, speculative) per "
+                         "profile and select the fastest exact one")
     ap.add_argument("--out", default=None)
     a = ap.parse_args(argv)
     torch.set_num_threads(2)
+    if a.plan:
+        decisions = [asyncio.run(plan_strategy(p, a.tokens)) for p in a.profiles.split(",")]
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(decisions, f, indent=1)
+        for d in decisions:
+            print(json.dumps({"profile": d["profile"], "selected": d["selected"],
+                              "ms_per_token": {x["candidate"]: round(x["ms_per_token"], 2)
+                                               for x in d["scores"] if x["ms_per_token"]}}))
+        return
     rows = asyncio.run(run(a.profiles.split(","), a.tokens, speculate_k=a.speculate))
     ev = evidence(rows)
     if a.out:

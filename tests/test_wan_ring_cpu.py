@@ -22,3 +22,15 @@ def test_wan_ring_profiles_meet_the_contract():
     assert wifi["ms_per_token"] >= wifi["network_floor_ms"], wifi
     rep = check_contract(load_contract("stage_ring_wan"), evidence(rows))
     assert rep["ok"], rep
+
+
+def test_strategy_planner_keeps_only_faster_exact_options():
+    from swarm_inference_lab_b200.testing.wan_ring import plan_strategy
+    torch.set_num_threads(2)
+    d = asyncio.run(plan_strategy("wifi", tokens=8))
+    scores = {x["candidate"]: x for x in d["scores"]}
+    assert set(scores) == {"plain", "compressed", "speculative"}
+    assert all(x["feasible"] for x in scores.values())          # every candidate is exact
+    best = min(scores.values(), key=lambda x: x["ms_per_token"])
+    assert d["selected"] == best["candidate"] and scores[d["selected"]]["selected"]
+    assert scores["speculative"]["serial_waits_per_token"] < scores["plain"]["serial_waits_per_token"]
