@@ -44,6 +44,10 @@ class RouteInfo:
     next_fingerprint: str | None = None
 
 
+# Rows of one VERIFY_CANDIDATES frame (the last accepted token plus the draft).
+MAX_VERIFY_ROWS = 64
+
+
 class BackpressureError(RuntimeError):
     """The stage's bounded execution queue is full; the caller should retry later."""
 
@@ -257,10 +261,16 @@ class StageOwner:
         ring with the frame."""
         attrs = msg.attributes
         x = unpack_tensor(msg.payload, attrs["tensor"])
+        if msg.operation == sr.Operation.VERIFY_CANDIDATES and x.shape[0] > MAX_VERIFY_ROWS:
+            raise sr.FrameError(f"{x.shape[0]} candidate rows (at most {MAX_VERIFY_ROWS})")
         t0 = time.perf_counter()
         async with self._lock:
             if attrs.get("truncate_to") is not None:
-                self.ex.truncate(msg.session_id, int(attrs["truncate_to"]))
+                keep = int(attrs["truncate_to"])
+                have = self.ex.length(msg.session_id)
+                if not 0 <= keep <= have:
+                    raise sr.FrameError(f"truncate_to {keep} outside the session's {have} tokens")
+                self.ex.truncate(msg.session_id, keep)
             y = await asyncio.to_thread(self.ex.forward, msg.session_id, x, msg.token_position)
         dt_ms = (time.perf_counter() - t0) * 1e3
         self.stats.forward_ms += dt_ms

@@ -93,3 +93,39 @@ def test_speculation_through_the_coordinator_is_exact():
     toks, frames = asyncio.run(go())
     assert toks == expect
     assert frames[0] < NEW + 2  # fewer stage-0 frames than one per token (plus open / close)
+
+
+def test_out_of_range_rollback_is_refused():
+    """A frame whose ``truncate_to`` lies beyond the session's cache is answered with an
+    ERROR frame (StageError at the controller) and leaves the session usable."""
+    import pytest
+
+    from swarm_inference_lab_b200.coordinator.session import StageError
+    from swarm_inference_lab_b200.protocol import stage_ring as sr
+
+    async def go():
+        ring = await _ring(TINY_LLAMA_CPU, random_source(0))
+        ctl = SessionController(Route(ring["entry"], 1, "wan-ring", "rev", ring["range0"]),
+                                pool=ConnectionPool(timeout=10.0))
+        try:
+            await ctl._open("s1", "r1")
+            tok, _ = await ctl._run_tokens("s1", "r1", PROMPT, 0, sr.Operation.PREFILL, False)
+            with pytest.raises(StageError, match="truncate_to"):
+                await ctl._run_tokens("s1", "r1", [tok], len(PROMPT), sr.Operation.DECODE, False,
+                                      truncate_to=len(PROMPT) + 5)
+            # the session still decodes from where it was
+            tok2, _ = await ctl._run_tokens("s1", "r1", [tok], len(PROMPT), sr.Operation.DECODE,
+                                            False)
+            return tok, tok2
+        finally:
+            await ctl.pool.close()
+            for o in ring["owners"]:
+                await o.pool.close()
+            for px in ring["proxies"]:
+                await px.close()
+            for s in ring["servers"]:
+                await s.close()
+
+    tok, tok2 = asyncio.run(go())
+    expect = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(PROMPT, 2)[0]
+    assert [tok, tok2] == expect
