@@ -679,6 +679,55 @@ def model_plan(model: str, stages: int = typer.Option(None, "--stages"),
                           default=str))
 
 
+def _layer_bytes(res) -> list[float]:
+    """Bytes of every decoder layer's tensors (from the checkpoint headers)."""
+    n = res.profile.config.num_layers
+    out = [0.0] * n
+    for name, d in res.profile.tensors.items():
+        if d.layer is not None and 0 <= d.layer < n:
+            out[d.layer] += float(res.tensor_bytes.get(name, 0))
+    return out
+
+
+@model_app.command("partition")
+def model_partition(checkpoint: str, stages: int = typer.Option(..., "--stages"),
+                    as_json: bool = typer.Option(True, "--json/--text")):
+    """Contiguous layer intervals for STAGES pipeline stages of a local checkpoint, balanced
+    by the layers' weight bytes (the largest stage is as small as possible); the embedding
+    goes with stage 0 and the final norm / LM head with the last stage."""
+    from .model_io.partition import balanced_ranges
+    from .model_io.resolver import ModelSourceResolver
+    res = ModelSourceResolver().inspect(checkpoint)
+    if res.profile.config is None:
+        raise typer.BadParameter(f"{checkpoint}: no runnable configuration")
+    costs = _layer_bytes(res)
+    ranges = balanced_ranges([c or 1.0 for c in costs], stages)
+    _out({"layers": len(costs), "stages": [
+        {"stage": i, "layers": [a, b], "bytes": sum(costs[a:b]), "embed": i == 0,
+         "head": i == len(ranges) - 1} for i, (a, b) in enumerate(ranges)]}, as_json)
+
+
+@model_app.command("shard")
+def model_shard(checkpoint: str, stages: int = typer.Option(..., "--stages"),
+                out: str = typer.Option(..., "--out")):
+    """Write one content-addressed stage artifact per pipeline stage of a local checkpoint
+    (safetensors with exactly that stage's tensors, and a manifest with the source revision,
+    layer interval, tensor list and SHA-256), layer intervals balanced by weight bytes."""
+    from .cluster.artifacts import build_stage_artifact
+    from .model_io.partition import balanced_ranges
+    from .model_io.resolver import ModelSourceResolver
+    res = ModelSourceResolver().inspect(checkpoint)
+    if res.profile.config is None:
+        raise typer.BadParameter(f"{checkpoint}: no runnable configuration")
+    costs = _layer_bytes(res)
+    ranges = balanced_ranges([c or 1.0 for c in costs], stages)
+    mans = []
+    for i, (a, b) in enumerate(ranges):
+        m = build_stage_artifact(res, out, a, b, embed=i == 0, head=i == len(ranges) - 1)
+        mans.append(m.to_json())
+    typer.echo(json.dumps(mans, indent=1))
+
+
 @model_app.command("inspect")
 def model_inspect(path: str, as_json: bool = typer.Option(True, "--json/--text")):
     """Inspect a model source (preset, local checkpoint or GGUF): format, revision, size and

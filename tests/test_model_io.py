@@ -182,3 +182,37 @@ def test_stage_artifact_build_transfer_resume_and_evict(tmp_path):
     src.budget = 1
     gone = src.evict()
     assert man.artifact_id in gone and other.artifact_id not in gone
+
+
+def test_cli_model_partition_and_shard(tmp_path):
+    """``swarm model partition`` / ``shard`` on a tiny HF Llama checkpoint: contiguous
+    intervals covering every layer, one artifact per stage holding exactly its tensors (the
+    embedding on stage 0, norm and head on the last), each with a verified SHA-256."""
+    import json
+
+    import pytest
+    transformers = pytest.importorskip("transformers")
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    from swarm_inference_lab_b200.cluster.artifacts import ArtifactStore
+    cfg = transformers.LlamaConfig(vocab_size=256, hidden_size=64, intermediate_size=96,
+                                   num_hidden_layers=5, num_attention_heads=4,
+                                   num_key_value_heads=2, tie_word_embeddings=False)
+    ck = tmp_path / "ck"
+    transformers.LlamaForCausalLM(cfg).save_pretrained(ck, safe_serialization=True)
+    r = CliRunner().invoke(app, ["model", "partition", str(ck), "--stages", "2"])
+    assert r.exit_code == 0, r.output
+    st = json.loads(r.output)["stages"]
+    assert [s["layers"] for s in st] in ([[0, 3], [3, 5]], [[0, 2], [2, 5]])
+    out = tmp_path / "arts"
+    r = CliRunner().invoke(app, ["model", "shard", str(ck), "--stages", "2", "--out", str(out)])
+    assert r.exit_code == 0, r.output
+    mans = json.loads(r.output)
+    assert len(mans) == 2 and mans[0]["embed"] and mans[1]["head"]
+    assert [m["layer_start"] for m in mans] == [s["layers"][0] for s in st]
+    assert any("embed_tokens" in n for n in mans[0]["tensors"])
+    assert any("lm_head" in n for n in mans[1]["tensors"])
+    assert not any("embed_tokens" in n for n in mans[1]["tensors"])
+    store = ArtifactStore(out)
+    assert all(store.verify(m["artifact_id"]) for m in mans)
