@@ -265,3 +265,23 @@ def test_cli_topology_simulate_and_validate_run(tmp_path):
     assert run(app, ["validate-run", "stage_ring_wan", str(ev)]).exit_code == 0
     ev.write_text(json.dumps(dict(good, messages_per_token_max=3.0)))
     assert run(app, ["validate-run", "stage_ring_wan", str(ev)]).exit_code == 1
+
+
+def test_cli_report_renders_evidence(tmp_path):
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    from swarm_inference_lab_b200.testing.acceptance import check_contract, load_contract
+    bench = {"metric": "m", "value": 6400.5, "unit": "tokens/s", "n_gpus": 1, "ms_per_step": 4.95,
+             "ttft_ms_p50": 1190.0, "config": {"model": "llama-3-8b-shape", "parallelism": "tp1"},
+             "clocks": {"sm_mhz": 1965.0}, "e2e": {"value": 6300.0}, "impl": "ours"}
+    log = tmp_path / "bench.log"
+    log.write_text("some text\n" + json.dumps(bench) + "\n")
+    rep = check_contract(load_contract("stage_ring_wan"), {"exact_tokens": True})
+    res = tmp_path / "contract.json"
+    res.write_text(json.dumps(rep))
+    r = CliRunner().invoke(app, ["report", str(log), str(res)])
+    assert r.exit_code == 0, r.output
+    assert "| ours | llama-3-8b-shape | tp1 | 1 | 6400.5 tokens/s |" in r.output
+    assert "contract `stage_ring_wan`: FAIL" in r.output   # gates without evidence fail
+    assert "| exact_tokens | True |" in r.output
