@@ -689,6 +689,18 @@ def _layer_bytes(res) -> list[float]:
     return out
 
 
+@model_app.command("validate")
+def model_validate(checkpoint: str, as_json: bool = typer.Option(True, "--json/--text")):
+    """Check a local safetensors checkpoint against its config without reading tensor data:
+    every tensor the model needs is present with the shape the config implies; lists the
+    problems and the tensors no layer uses.  Exit 1 when a problem is found."""
+    from .model_io.loader import validate_checkpoint
+    rep = validate_checkpoint(checkpoint)
+    _out(rep, as_json)
+    if not rep["ok"]:
+        raise typer.Exit(1)
+
+
 @model_app.command("partition")
 def model_partition(checkpoint: str, stages: int = typer.Option(..., "--stages"),
                     as_json: bool = typer.Option(True, "--json/--text")):

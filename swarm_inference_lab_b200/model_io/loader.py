@@ -97,6 +97,18 @@ class SafetensorsIndex:
             self._open[f] = h
         return h.get_tensor(name)
 
+    def meta(self, name: str) -> tuple[str, tuple[int, ...]]:
+        """(dtype string, shape) of a tensor from the file header, without reading its data."""
+        f = self.where.get(name)
+        if f is None:
+            raise CheckpointError(f"tensor {name} not in the checkpoint")
+        h = self._open.get(f)
+        if h is None:
+            h = self._safe_open(str(self.root / f), framework="pt")
+            self._open[f] = h
+        sl = h.get_slice(name)
+        return str(sl.get_dtype()), tuple(int(x) for x in sl.get_shape())
+
     def close(self) -> None:
         self._open.clear()
 
@@ -186,6 +198,73 @@ def load_weights(cfg: ModelConfig, path: str | Path, tp=None, device="cuda", *,
         from ..models.moe import MoEWeights
         return MoEWeights.from_full(cfg, tp, get, device, dtype)
     return DenseWeights.from_full(cfg, tp, get, device, dtype)
+
+
+def validate_checkpoint(path: str | Path) -> dict:
+    """Header-only check of a checkpoint against its config: the model's weight builder runs on
+    the ``meta`` device with a source that looks up every tensor it asks for (canonical name
+    mapped to the checkpoint's) and compares the header shape with the shape the config
+    implies; no tensor data is read.  Returns the problems found (missing tensors, shape
+    mismatches) and the checkpoint tensors no layer used."""
+    from ..models.dense import DenseWeights, TPInfo
+    cfg = checkpoint_config(path)
+    idx = SafetensorsIndex(path)
+    fam = cfg.family
+    tie = False
+    try:
+        tie = bool(json.loads((Path(path) / "config.json").read_text()).get("tie_word_embeddings"))
+    except Exception:  # noqa: BLE001
+        pass
+    problems: list[str] = []
+    used: set[str] = set()
+
+    def resolve(name):
+        real = checkpoint_name(fam, name)
+        if real not in idx and name == "lm_head.weight" and tie:
+            real = "model.embed_tokens.weight"
+        return real
+
+    def check(name, shape):
+        real = resolve(name)
+        if real not in idx:
+            problems.append(f"missing {real}")
+            return
+        used.add(real)
+        if _scale_name(real) in idx:
+            used.add(_scale_name(real))
+        _, sh = idx.meta(real)
+        if sh != tuple(shape):
+            problems.append(f"{real}: shape {sh}, expected {tuple(shape)}")
+
+    def get(name, shape, dtype=None):
+        check(name, shape)
+        return torch.empty(tuple(shape), dtype=dtype or torch.float32, device="meta")
+
+    get.index = idx
+    get.family = fam
+    try:
+        if cfg.mla:
+            from ..models.deepseek import MLAWeights
+
+            def getd(name, shape, dt=torch.bfloat16):
+                return get(name, shape, dt)
+
+            def fp8d(name, shape):
+                check(name, shape)
+                rows = -(-shape[0] // 128) * 128
+                return (torch.empty((rows, shape[1]), dtype=torch.uint8, device="meta"),
+                        torch.empty((rows // 128, -(-shape[1] // 128)), device="meta"))
+            MLAWeights.from_source(cfg, TPInfo(), getd, fp8d, torch.device("meta"))
+        elif cfg.is_moe:
+            from ..models.moe import MoEWeights
+            MoEWeights.from_full(cfg, TPInfo(), get, "meta", torch.bfloat16)
+        else:
+            DenseWeights.from_full(cfg, TPInfo(), get, "meta", torch.bfloat16)
+    finally:
+        idx.close()
+    unused = sorted(n for n in idx.where if n not in used)
+    return {"family": fam, "layers": cfg.num_layers, "ok": not problems,
+            "problems": problems[:50], "tensors_checked": len(used), "unused": unused[:50]}
 
 
 def load_tokenizer(path: str | Path):

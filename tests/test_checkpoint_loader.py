@@ -115,3 +115,31 @@ def test_deepseek_v3_checkpoint_builds_mla_weights(tmp_path):
     q, s = L1.experts_gate_up
     deq = (q[:128].view(torch.float8_e4m3fn).float() * s[0].repeat_interleave(128)[None, :256])
     assert (deq - ref).abs().max().item() <= ref.abs().max().item() * 0.07
+
+
+@pytest.mark.parametrize("model_type", ["llama", "qwen3_moe"])
+def test_validate_checkpoint_headers_only(tmp_path, model_type):
+    """``swarm model validate``: a complete checkpoint passes with every tensor used; a
+    dropped tensor and a resized one are both reported, and the command exits 1."""
+    import json
+
+    from safetensors.torch import load_file, save_file
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    torch.manual_seed(0)
+    _tiny(model_type).save_pretrained(tmp_path, safe_serialization=True)
+    r = CliRunner().invoke(app, ["model", "validate", str(tmp_path)])
+    rep = json.loads(r.output)
+    assert r.exit_code == 0 and rep["ok"] and rep["unused"] == [] and rep["tensors_checked"] > 10
+    f = tmp_path / "model.safetensors"
+    t = load_file(str(f))
+    t.pop("model.layers.1.mlp.gate.weight" if model_type == "qwen3_moe"
+          else "model.layers.1.mlp.down_proj.weight")
+    t["model.layers.0.self_attn.o_proj.weight"] = t["model.layers.0.self_attn.o_proj.weight"][:, :8].contiguous()
+    save_file(t, str(f), metadata={"format": "pt"})
+    r = CliRunner().invoke(app, ["model", "validate", str(tmp_path)])
+    rep = json.loads(r.output)
+    assert r.exit_code == 1 and not rep["ok"]
+    assert any(p.startswith("missing model.layers.1.mlp") for p in rep["problems"])
+    assert any("o_proj.weight: shape" in p for p in rep["problems"])
