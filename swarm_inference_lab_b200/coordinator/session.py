@@ -70,7 +70,8 @@ Recover = Callable[[Route, Exception], Awaitable[Route]]
 class SessionController:
     def __init__(self, route: Route, *, pool: ConnectionPool | None = None,
                  recover: Recover | None = None, max_recoveries: int = 3,
-                 return_logits: bool = False, speculate_k: int = 0):
+                 return_logits: bool = False, speculate_k: int = 0,
+                 spec_min_accept: float = 0.1, spec_warmup: int = 8):
         self.route = route
         self.pool = pool or ConnectionPool()
         self.recover_cb = recover
@@ -80,8 +81,13 @@ class SessionController:
         # are verified in one VERIFY_CANDIDATES pass through the ring; the longest prefix that
         # equals the greedy predictions is accepted plus one token, so the output is exactly
         # the greedy output.  Not combined with per-token logits.
+        # Drafting stops for the rest of a stream once, after ``spec_warmup`` verifications,
+        # fewer than ``spec_min_accept`` of the drafted tokens were accepted (a verification
+        # that rarely pays costs a frame per token like plain decode, with bigger frames).
         self.speculate_k = 0 if return_logits else int(speculate_k)
-        self.spec_stats = {"verify_calls": 0, "drafted": 0, "accepted": 0}
+        self.spec_min_accept = spec_min_accept
+        self.spec_warmup = spec_warmup
+        self.spec_stats = {"verify_calls": 0, "drafted": 0, "accepted": 0, "disabled": False}
         self.seq = sr.SequenceAllocator()
         self.events: list[dict] = []
 
@@ -206,10 +212,13 @@ class SessionController:
                 # Cache length the stages must roll back to before the next frame (rejected
                 # candidates of the last verification), or None.
                 trunc = None
+                calls0, drafted0, accepted0 = (self.spec_stats["verify_calls"],
+                                               self.spec_stats["drafted"], self.spec_stats["accepted"])
+                drafting = bool(self.speculate_k)
                 while len(tokens) < max_new_tokens:
                     pos = len(prompt) + len(tokens) - 1
                     draft = []
-                    if self.speculate_k:
+                    if drafting:
                         draft = prompt_lookup_draft(prompt + tokens, self.speculate_k)
                         draft = draft[:max(0, max_new_tokens - len(tokens) - 1)]
                     if draft:
@@ -222,6 +231,12 @@ class SessionController:
                         self.spec_stats["verify_calls"] += 1
                         self.spec_stats["drafted"] += len(draft)
                         self.spec_stats["accepted"] += m
+                        calls = self.spec_stats["verify_calls"] - calls0
+                        drafted = self.spec_stats["drafted"] - drafted0
+                        accepted = self.spec_stats["accepted"] - accepted0
+                        if calls >= self.spec_warmup and accepted < self.spec_min_accept * drafted:
+                            drafting = False
+                            self.spec_stats["disabled"] = True
                         for tok in preds[:m + 1]:
                             tokens.append(tok)
                             yield {"event": "token", "index": len(tokens) - 1, "token": tok,

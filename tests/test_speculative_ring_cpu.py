@@ -129,3 +129,33 @@ def test_out_of_range_rollback_is_refused():
     tok, tok2 = asyncio.run(go())
     expect = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(PROMPT, 2)[0]
     assert [tok, tok2] == expect
+
+
+def test_speculation_turns_itself_off_when_drafts_fail(monkeypatch):
+    """Drafts that are always wrong: after the warm-up verifications the controller stops
+    drafting for the rest of the stream; the tokens stay exact."""
+    import swarm_inference_lab_b200.coordinator.session as S
+
+    monkeypatch.setattr(S, "prompt_lookup_draft", lambda toks, k, *a, **kw: [0] * k)
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(PROMPT, NEW)[0]
+
+    async def go():
+        ring = await _ring(TINY_LLAMA_CPU, random_source(0))
+        ctl = SessionController(Route(ring["entry"], 1, "wan-ring", "rev", ring["range0"]),
+                                pool=ConnectionPool(timeout=10.0), speculate_k=3, spec_warmup=4)
+        try:
+            toks = [ev["token"] async for ev in ctl.stream(PROMPT, NEW, "bad") if ev["event"] == "token"]
+        finally:
+            await ctl.pool.close()
+            for o in ring["owners"]:
+                await o.pool.close()
+            for px in ring["proxies"]:
+                await px.close()
+            for s in ring["servers"]:
+                await s.close()
+        return toks, ctl.spec_stats
+
+    toks, st = asyncio.run(go())
+    assert toks == expect
+    assert st["disabled"] and st["verify_calls"] == 4 and st["accepted"] == 0
