@@ -150,6 +150,16 @@ def run_reference_arm(args, rank, world, local, metric):
     if B_total % world:
         return {"impl": "reference", "unavailable": "batch not divisible by the replica count"}
     B = B_total // world
+
+    def agree(ok: bool) -> bool:
+        """True on every rank iff ``ok`` on every rank (each rank takes the same collective
+        steps whether or not its own phase failed)."""
+        if world == 1:
+            return ok
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
+
     # One checkpoint for every replica: rank 0 writes it (16 GB), the others wait at a barrier.
     root = os.environ.get("SIL_REF_CKPT_DIR") or os.path.join(tempfile.gettempdir(),
                                                               f"sil_ref_ckpt_{os.getuid()}")
@@ -192,25 +202,41 @@ def run_reference_arm(args, rank, world, local, metric):
                 errors.append(f"{cache}+{compile_mode}: {type(exc).__name__}: {exc}"[:200])
                 loaded = None
                 torch.cuda.empty_cache()
-        if loaded is None:
-            return {"impl": "reference", "unavailable": " | ".join(errors)[:500]}
+        if not agree(loaded is not None):
+            return {"impl": "reference", "unavailable": (" | ".join(errors)
+                                                         or "the engine failed to load on another rank")[:500]}
         eng = loaded.engine
         g = torch.Generator().manual_seed(rank)
         inputs = torch.randint(0, 128256, (B, P), generator=g, dtype=torch.long)
-        eng.generate_batch(inputs, request_ids=tuple(f"w{i}" for i in range(B)),
-                           output_tokens=max(W, 2), scheduler_policy="throughput")
-        if world > 1:
-            dist.barrier()
+        err = None
+        try:
+            eng.generate_batch(inputs, request_ids=tuple(f"w{i}" for i in range(B)),
+                               output_tokens=max(W, 2), scheduler_policy="throughput")
+        except Exception as exc:  # noqa: BLE001 - agreed on below
+            err = f"warm-up: {type(exc).__name__}: {exc}"
+        if not agree(err is None):
+            return {"impl": "reference", "unavailable": (err or "warm-up failed on another rank")[:400]}
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        res = eng.generate_batch(inputs, request_ids=tuple(f"m{i}" for i in range(B)),
-                                 output_tokens=K + 1, scheduler_policy="throughput")
-        torch.cuda.synchronize()
+        res = None
+        try:
+            res = eng.generate_batch(inputs, request_ids=tuple(f"m{i}" for i in range(B)),
+                                     output_tokens=K + 1, scheduler_policy="throughput")
+            torch.cuda.synchronize()
+        except Exception as exc:  # noqa: BLE001 - agreed on below
+            err = f"timed run: {type(exc).__name__}: {exc}"
         wall_ms = (time.perf_counter() - t0) * 1e3
-        m = res.metrics
-        decode_ms = float(m.decode_ms)
-        ttft = float(m.ttft_ms)
-        tpot = float(m.inter_token_latency_ms_p50)
+        m = None
+        if err is None:
+            try:
+                m = res.metrics
+                decode_ms = float(m.decode_ms)
+                ttft = float(m.ttft_ms)
+                tpot = float(m.inter_token_latency_ms_p50)
+            except Exception as exc:  # noqa: BLE001 - agreed on below
+                err = f"metrics: {type(exc).__name__}: {exc}"
+        if not agree(err is None):
+            return {"impl": "reference", "unavailable": (err or "timed run failed on another rank")[:400]}
         vals = torch.tensor([decode_ms, ttft, tpot, float(B * K)], dtype=torch.float64, device=device)
         if world > 1:
             mx = vals.clone()
