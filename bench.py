@@ -229,6 +229,11 @@ def run_ours(args, rank, world, local):
     if per_step is None:
         per_step = _count_launches_per_step(eng, dg)
     _ = launches_before
+    # Release the captured decode graphs now: with an NCCL communicator they hold NCCL
+    # calls, and a graph that outlives destroy_process_group makes the exit wait.
+    torch.cuda.synchronize()
+    eng.runner.graphs.clear()
+    dg = None
     value = B * K / (total_ms / 1e3)
     clk = clocks.summary()
     fp8w = cfg.weight_dtype.startswith("fp8")
