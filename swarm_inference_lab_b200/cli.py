@@ -957,6 +957,42 @@ def topology_command(rtt_ms: float = typer.Option(None, "--rtt-ms"),
           "one_way_ms": transfer_ms(link, message_bytes)}, as_json)
 
 
+def _fingerprint_arg(value: str) -> str:
+    """A fingerprint given directly (``sha256:...``) or read from an identity document."""
+    if value.startswith("sha256:"):
+        return value
+    from .security.identity import Identity
+    return Identity.load(Path(value).expanduser()).fingerprint
+
+
+@identity_app.command("trust")
+def identity_trust(identity: str, label: str = typer.Option("", "--label"),
+                   notes: str = typer.Option("", "--notes"),
+                   state: str = typer.Option(STATE, "--state-dir")):
+    """Let the coordinator of this cluster admit a worker identity at registration without
+    pairing (IDENTITY: a ``sha256:`` fingerprint or an identity document).  A revoked identity
+    stays refused; with mutual TLS on, the worker still needs a certificate of the cluster CA."""
+    fp = _fingerprint_arg(identity)
+    added = _store(state).trust(fp, label=label, notes=notes)
+    typer.echo(json.dumps({"status": "trusted" if added else "updated", "fingerprint": fp}))
+
+
+@identity_app.command("untrust")
+def identity_untrust(identity: str, state: str = typer.Option(STATE, "--state-dir")):
+    """Remove a worker identity from the trust list."""
+    fp = _fingerprint_arg(identity)
+    gone = _store(state).untrust(fp)
+    typer.echo(json.dumps({"status": "removed" if gone else "absent", "fingerprint": fp}))
+    if not gone:
+        raise typer.Exit(1)
+
+
+@identity_app.command("list-trusted")
+def identity_list_trusted(state: str = typer.Option(STATE, "--state-dir")):
+    """Worker identities on the trust list, with their labels."""
+    typer.echo(json.dumps(_store(state).trusted(), indent=1, default=str))
+
+
 def main():  # console entry point
     app()
 

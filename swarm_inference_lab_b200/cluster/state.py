@@ -116,6 +116,28 @@ class ClusterStateStore:
         self.save_cluster(doc)
         return m["fingerprint"]
 
+    # worker trust list: identities the coordinator admits at registration besides the
+    # paired members (a revoked fingerprint stays refused)
+    def trust(self, fingerprint: str, label: str = "", notes: str = "") -> bool:
+        """Adds or updates a trusted worker fingerprint; True if it was new."""
+        doc = self.load_cluster()
+        if fingerprint in doc["revoked"]:
+            raise StateError("node identity is revoked")
+        trusted = doc.setdefault("trusted", {})
+        added = fingerprint not in trusted
+        trusted[fingerprint] = {"label": label, "notes": notes, "at": time.time()}
+        self.save_cluster(doc)
+        return added
+
+    def untrust(self, fingerprint: str) -> bool:
+        doc = self.load_cluster()
+        gone = doc.setdefault("trusted", {}).pop(fingerprint, None) is not None
+        self.save_cluster(doc)
+        return gone
+
+    def trusted(self) -> dict:
+        return dict(self.load_cluster().get("trusted", {}))
+
     def delete(self) -> None:
         for p in sorted(self.root.rglob("*"), reverse=True):
             if p.is_file():

@@ -177,9 +177,11 @@ class CoordinatorCore:
             return
         doc = self.cluster_store.load_cluster()
         members = {m["fingerprint"] for m in doc.get("members", {}).values()}
+        members |= set(doc.get("trusted", {}))       # `swarm identity trust`
         revoked = set(doc.get("revoked", []))
         if fingerprint not in members or fingerprint in revoked:
-            raise PermissionError("worker is not a paired member of this cluster (or is revoked)")
+            raise PermissionError("worker is neither a paired member nor trusted by this "
+                                  "cluster (or is revoked)")
 
     def _check_caller(self, claimed: str) -> None:
         peer = PEER_FINGERPRINT.get()

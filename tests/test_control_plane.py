@@ -285,3 +285,47 @@ def test_cli_report_renders_evidence(tmp_path):
     assert "| ours | llama-3-8b-shape | tp1 | 1 | 6400.5 tokens/s |" in r.output
     assert "contract `stage_ring_wan`: FAIL" in r.output   # gates without evidence fail
     assert "| exact_tokens | True |" in r.output
+
+
+def test_identity_trust_list_admits_and_refuses_registration(tmp_path):
+    """``identity trust`` lets the coordinator admit an unpaired worker identity at
+    registration; ``untrust`` removes it again; ``list-trusted`` shows the label."""
+    import asyncio
+
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    from swarm_inference_lab_b200.cluster.state import ClusterStateStore
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore
+    from swarm_inference_lab_b200.security.identity import Identity
+    run = CliRunner().invoke
+    st = tmp_path / "st"
+    assert run(app, ["cluster", "create", "lab", "--state-dir", str(st), "--json"]).exit_code == 0
+    store = ClusterStateStore(st)
+    core = CoordinatorCore(store.identity("coordinator"), cluster_store=store)
+    w = Identity.generate("w9")
+    idp = tmp_path / "w9.json"
+    w.save(idp)
+    req = {"worker_id": "w9", "fingerprint": w.fingerprint, "ring_endpoint": "127.0.0.1:1",
+           "control_endpoint": "127.0.0.1:2", "capabilities": {}}
+
+    async def register():
+        try:
+            await core.register(dict(req))
+            return True
+        except PermissionError:
+            return False
+        finally:
+            for ag in core.agents.values():
+                await ag.close()
+            core.agents.clear()
+
+    assert asyncio.run(register()) is False
+    r = run(app, ["identity", "trust", str(idp), "--label", "lab box", "--state-dir", str(st)])
+    assert r.exit_code == 0 and json.loads(r.output)["status"] == "trusted"
+    lst = json.loads(run(app, ["identity", "list-trusted", "--state-dir", str(st)]).output)
+    assert lst[w.fingerprint]["label"] == "lab box"
+    assert asyncio.run(register()) is True
+    r = run(app, ["identity", "untrust", w.fingerprint, "--state-dir", str(st)])
+    assert r.exit_code == 0
+    assert asyncio.run(register()) is False
