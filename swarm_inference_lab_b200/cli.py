@@ -701,6 +701,33 @@ def model_validate(checkpoint: str, as_json: bool = typer.Option(True, "--json/-
         raise typer.Exit(1)
 
 
+@model_app.command("build-microshards")
+def model_build_microshards(checkpoint: str, out: str = typer.Option(..., "--out"),
+                           layers: str = typer.Option(..., "--layers"),
+                           experts: str = typer.Option(None, "--experts"),
+                           parts: int = typer.Option(2, "--parts")):
+    """Split routed experts of a local MoE checkpoint into PARTS microshards each (contiguous
+    intermediate slices: gate / up rows, down columns), one file and manifest per shard."""
+    from .runtime.microshards import build_microshards
+    mans = build_microshards(checkpoint, out, layers=[int(x) for x in layers.split(",")],
+                             experts=[int(x) for x in experts.split(",")] if experts else None,
+                             parts=parts)
+    typer.echo(json.dumps({"microshards": len(mans), "out": out}))
+
+
+@model_app.command("validate-microshards")
+def model_validate_microshards(directory: str, checkpoint: str,
+                               as_json: bool = typer.Option(True, "--json/--text")):
+    """Check microshards against their manifests (SHA-256), that each expert's slices tile its
+    intermediate dimension, and that their fixed-order reduction reproduces the whole expert
+    from CHECKPOINT (fp32, random inputs).  Exit 1 on a problem."""
+    from .runtime.microshards import validate_microshards
+    rep = validate_microshards(directory, checkpoint)
+    _out(rep, as_json)
+    if not rep["ok"]:
+        raise typer.Exit(1)
+
+
 @model_app.command("partition")
 def model_partition(checkpoint: str, stages: int = typer.Option(..., "--stages"),
                     as_json: bool = typer.Option(True, "--json/--text")):

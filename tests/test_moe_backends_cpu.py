@@ -138,3 +138,46 @@ def test_unaccepted_lease_is_refused(setup):
             _run(get, ids, be)
     finally:
         be.close()
+
+
+def test_build_and_validate_microshards(tmp_path):
+    """``model build-microshards`` / ``validate-microshards`` on a tiny HF Qwen3-MoE
+    checkpoint: 3 microshards per expert reproduce each expert; a tampered file and a missing
+    slice are both reported."""
+    import json
+
+    import pytest
+    transformers = pytest.importorskip("transformers")
+    from safetensors.torch import load_file, save_file
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    cfg = transformers.Qwen3MoeConfig(vocab_size=256, hidden_size=64, intermediate_size=96,
+                                      moe_intermediate_size=40, num_hidden_layers=2,
+                                      num_attention_heads=4, num_key_value_heads=2, head_dim=16,
+                                      num_experts=4, num_experts_per_tok=2, decoder_sparse_step=1,
+                                      mlp_only_layers=[])
+    torch.manual_seed(0)
+    ck, out = tmp_path / "ck", tmp_path / "ms"
+    transformers.Qwen3MoeForCausalLM(cfg).save_pretrained(ck, safe_serialization=True)
+    run = CliRunner().invoke
+    r = run(app, ["model", "build-microshards", str(ck), "--out", str(out), "--layers", "0,1",
+                  "--experts", "1,3", "--parts", "3"])
+    assert r.exit_code == 0, r.output
+    assert json.loads(r.output)["microshards"] == 12
+    r = run(app, ["model", "validate-microshards", str(out), str(ck)])
+    rep = json.loads(r.output)
+    assert r.exit_code == 0 and rep["ok"] and rep["experts"] == 4 and rep["max_rel_err"] < 1e-5
+    # 40 channels in 3 parts: 14 + 13 + 13
+    m0 = json.loads((out / "l000_e0001_s00.json").read_text())
+    assert (m0["i0"], m0["i1"]) == (0, 14)
+    f = out / "l001_e0003_s01.safetensors"
+    t = load_file(str(f))
+    t["down"] = t["down"] * 1.01
+    save_file(t, str(f))
+    (out / "l000_e0001_s02.json").unlink()
+    r = run(app, ["model", "validate-microshards", str(out), str(ck)])
+    rep = json.loads(r.output)
+    assert r.exit_code == 1
+    assert any("SHA-256" in p for p in rep["problems"])
+    assert any("do not tile" in p for p in rep["problems"])
