@@ -889,6 +889,16 @@ def experiment_wan_ring(profiles: str = "loopback,wifi,regional,global", tokens:
     wan_main(["--profiles", profiles, "--tokens", str(tokens)] + (["--out", out] if out else []))
 
 
+@experiment_app.command("microsharding")
+def experiment_microsharding(tokens: int = 16, repeats: int = 3,
+                             out: str = typer.Option(None, "--out")):
+    """One MoE decoder with its experts local, whole on a remote expert worker, and as
+    microshards over 2 and 4 workers (SWARMEX1 over TCP): time per forward, remote requests
+    and rows, and exactness against local execution."""
+    from .testing.expert_backends import main as eb_main
+    eb_main(["--tokens", str(tokens), "--repeats", str(repeats)] + (["--out", out] if out else []))
+
+
 @app.command("validate-run")
 def validate_run(contract: str, evidence: str):
     """Check EVIDENCE (a JSON record, or the last JSON line of a log) against a frozen

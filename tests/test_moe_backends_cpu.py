@@ -181,3 +181,14 @@ def test_build_and_validate_microshards(tmp_path):
     assert r.exit_code == 1
     assert any("SHA-256" in p for p in rep["problems"])
     assert any("do not tile" in p for p in rep["problems"])
+
+
+def test_expert_backends_harness_is_exact():
+    from swarm_inference_lab_b200.testing.expert_backends import run
+    rows = {r["backend"]: r for r in run(tokens=8, repeats=1)}
+    assert set(rows) == {"local", "whole_remote", "microshard_2", "microshard_4"}
+    assert all(r["exact"] for r in rows.values())
+    assert rows["local"]["remote_rows_served"] == 0
+    # microshards: every routed row goes to every shard of its expert
+    assert rows["microshard_4"]["remote_rows_served"] == 2 * rows["microshard_2"]["remote_rows_served"] \
+        == 4 * rows["whole_remote"]["remote_rows_served"] > 0
