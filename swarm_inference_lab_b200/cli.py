@@ -33,6 +33,7 @@ from __future__ import annotations
 import asyncio
 import json
 import os
+import subprocess
 import sys
 import time
 from pathlib import Path
@@ -897,6 +898,44 @@ def experiment_microsharding(tokens: int = 16, repeats: int = 3,
     and rows, and exactness against local execution."""
     from .testing.expert_backends import main as eb_main
     eb_main(["--tokens", str(tokens), "--repeats", str(repeats)] + (["--out", out] if out else []))
+
+
+@experiment_app.command("node-roles")
+def experiment_node_roles(nodes: str, model_gb: float = typer.Option(..., "--model-gb"),
+                          expert_fraction: float = typer.Option(0.0, "--expert-fraction"),
+                          as_json: bool = typer.Option(True, "--json/--text")):
+    """Assign heterogeneous nodes (NODES: a JSON list of {node_id, decode_tok_s, memory_gb,
+    link_ms}) to pipeline-stage, expert-host, draft-host or idle roles by marginal gain in
+    aggregate tokens/s; a node that would slow the plan down stays idle."""
+    from .planner.roles import NodeCaps, assign_roles
+    doc = json.loads(Path(nodes).read_text())
+    caps = [NodeCaps(n["node_id"], float(n["decode_tok_s"]), float(n["memory_gb"]) * 1e9,
+                     float(n.get("link_ms", 0.0))) for n in doc]
+    roles = assign_roles(caps, model_gb * 1e9, expert_fraction=expert_fraction)
+    rows = [{"node_id": r.node_id, "role": r.role, "gain_tok_s": r.gain_tok_s} for r in roles]
+    if as_json:
+        typer.echo(json.dumps(rows, indent=1))
+    else:
+        for r in rows:
+            typer.echo(f"{r['node_id']}: {r['role']} (+{r['gain_tok_s']:.1f} tok/s)")
+
+
+@experiment_app.command("engine-performance")
+def experiment_engine_performance(gpus: int = 1, steps: int = 64, warmup: int = 3,
+                                  impl: str = typer.Option("ours", "--impl"),
+                                  model: str = typer.Option("llama-3-8b-shape", "--model")):
+    """The single-engine decode benchmark (``bench.py``: device-timed tokens/s, TTFT, TPOT, end
+    to end through ``LLMEngine.step``) on this box; ``--impl reference`` runs the reference's
+    own engine.  Multi-GPU runs use torchrun (127.0.0.1 rendezvous)."""
+    root = Path(__file__).resolve().parent.parent
+    args = ["bench.py", "--gpus", str(gpus), "--steps", str(steps), "--warmup", str(warmup),
+            "--impl", impl, "--model", model]
+    if gpus > 1:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={gpus}", "--master-addr", "127.0.0.1", "--master-port", "29555"] + args
+    else:
+        cmd = [sys.executable] + args
+    raise typer.Exit(subprocess.call(cmd, cwd=str(root)))
 
 
 @app.command("validate-run")

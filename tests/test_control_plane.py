@@ -329,3 +329,19 @@ def test_identity_trust_list_admits_and_refuses_registration(tmp_path):
     r = run(app, ["identity", "untrust", w.fingerprint, "--state-dir", str(st)])
     assert r.exit_code == 0
     assert asyncio.run(register()) is False
+
+
+def test_cli_node_roles(tmp_path):
+    from typer.testing import CliRunner
+
+    from swarm_inference_lab_b200.cli import app
+    nodes = [{"node_id": "a", "decode_tok_s": 50.0, "memory_gb": 24, "link_ms": 1},
+             {"node_id": "b", "decode_tok_s": 45.0, "memory_gb": 24, "link_ms": 1},
+             {"node_id": "c", "decode_tok_s": 2.0, "memory_gb": 8, "link_ms": 80}]
+    p = tmp_path / "nodes.json"
+    p.write_text(json.dumps(nodes))
+    r = CliRunner().invoke(app, ["experiment", "node-roles", str(p), "--model-gb", "40"])
+    assert r.exit_code == 0, r.output
+    roles = {x["node_id"]: x["role"] for x in json.loads(r.output)}
+    assert roles["a"] == roles["b"] == "stage"       # the two fast nodes hold the model
+    assert set(roles) == {"a", "b", "c"}
