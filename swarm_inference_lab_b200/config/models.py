@@ -116,6 +116,10 @@ class NetworkProfile(StrictModel):
     stability: float = 1.0
     loss: float = 0.0
 
+    @classmethod
+    def from_yaml(cls, path) -> "NetworkProfile":
+        return cls(**load_yaml(path))
+
 
 class StageDefinition(StrictModel):
     stage_id: int = Field(ge=0)

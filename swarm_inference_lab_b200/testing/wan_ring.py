@@ -45,8 +45,23 @@ import time
 
 import torch
 
-# One-way latency per link (seconds) of each emulated network profile.
+# One-way latency per link (seconds) of each emulated network profile: half the RTT of the
+# network profiles under configs/networks (these values when the files are not there).
 PROFILES = {"loopback": 0.0, "wifi": 0.003, "regional": 0.015, "global": 0.060}
+
+
+def _load_profiles() -> None:
+    from pathlib import Path
+
+    from ..config.models import NetworkProfile
+    d = Path(__file__).resolve().parents[2] / "configs" / "networks"
+    for f in sorted(d.glob("*.yaml")) if d.is_dir() else []:
+        prof = NetworkProfile.from_yaml(f)
+        if prof.name in PROFILES:
+            PROFILES[prof.name] = prof.rtt_ms / 2e3
+
+
+_load_profiles()
 
 
 async def _ring(cfg, source, compression: str = "none"):

@@ -513,3 +513,25 @@ def test_decode_split_heuristics():
     assert attention.decode_splits(1, 8, 6) == 3            # never below 2 pages per split
     assert attention.decode_splits(128, 8, 1) == 1
     assert mla.decode_splits(32, 4096) == 4 and mla.decode_splits(1, 4096) == 64
+
+
+def test_shipped_configs_validate():
+    """Every shipped network profile validates as a NetworkProfile (and classifies into the
+    expected topology domain), every node profile as a NodeProfile, the product config (with
+    its relative includes) as a ProductConfig, and the WAN harness uses the profiles' RTTs."""
+    from pathlib import Path
+
+    from swarm_inference_lab_b200.config import NetworkProfile, NodeProfile, ProductConfig, load_yaml
+    from swarm_inference_lab_b200.planner.topology import LinkProfile, classify
+    from swarm_inference_lab_b200.testing.wan_ring import PROFILES
+    root = Path(__file__).resolve().parents[1] / "configs"
+    nets = {p.stem: NetworkProfile.from_yaml(p) for p in (root / "networks").glob("*.yaml")}
+    assert {"nvlink5", "loopback", "wifi", "regional-wan", "global-wan"} <= set(nets)
+    dom = {k: classify(LinkProfile("a", "b", v.rtt_ms, v.bandwidth_mbps / 8, jitter_ms=v.jitter_ms,
+                                   stability=v.stability)).value for k, v in nets.items()}
+    assert dom["regional-wan"] == "regional" and dom["global-wan"] == "wan"
+    for p in (root / "nodes").glob("*.yaml"):
+        NodeProfile(**load_yaml(p))
+    for p in (root / "product").glob("b200-*.yaml"):
+        assert ProductConfig.from_yaml(p).max_recoveries == 3
+    assert PROFILES["global"] == nets["global-wan"].rtt_ms / 2e3
