@@ -535,3 +535,36 @@ def test_shipped_configs_validate():
     for p in (root / "product").glob("b200-*.yaml"):
         assert ProductConfig.from_yaml(p).max_recoveries == 3
     assert PROFILES["global"] == nets["global-wan"].rtt_ms / 2e3
+
+
+def test_cost_model_modes_and_unmeasured_penalty():
+    """Serial token path and bottleneck-bound aggregate; each unmeasured input costs 2% of the
+    score; the modes rank a fast-TTFT plan and a high-throughput plan differently."""
+    import math
+
+    from swarm_inference_lab_b200.planner.cost_model import PlanCostInputs, score_costs
+    c = PlanCostInputs(stage_compute_ms=[4.0, 6.0], boundary_ms=[1.0], prefill_ms=100.0, batch=8)
+    r = score_costs(c, "throughput")
+    assert r.tpot_ms == 11.0 and r.bottleneck_ms == 6.0 and r.ttft_ms == 101.0
+    assert math.isclose(r.decode_tok_s, 1000 / 11)
+    assert math.isclose(r.aggregate_tok_s, 8 * 1000 / max(6.0 * 2, 11.0))
+    pen = score_costs(PlanCostInputs([4.0, 6.0], [1.0], 100.0, batch=8, unmeasured=["a", "b"]),
+                      "throughput")
+    assert math.isclose(pen.score, r.score * 0.98 ** 2)
+    fast = PlanCostInputs([5.0], [], prefill_ms=50.0, batch=1)        # one stage, low latency
+    wide = PlanCostInputs([3.0] * 4, [0.5] * 3, prefill_ms=400.0, batch=32, replicas=2)
+    assert score_costs(fast, "speed").score > score_costs(wide, "speed").score
+    assert score_costs(wide, "throughput").score > score_costs(fast, "throughput").score
+    roomy = PlanCostInputs([5.0], [], 50.0, memory_fraction=0.2)
+    full = PlanCostInputs([5.0], [], 50.0, memory_fraction=0.9)
+    assert score_costs(roomy, "capacity").score > score_costs(full, "capacity").score
+
+
+def test_host_capabilities_and_doctor_report():
+    from swarm_inference_lab_b200.doctor import run_doctor
+    from swarm_inference_lab_b200.worker_caps import local_capabilities
+    caps = local_capabilities(benchmark=False)
+    assert caps["cpus"] and caps["os"] and caps["gpus"] == len(caps["devices"])
+    rep = run_doctor()
+    assert "checks" in rep and "torch" in rep["checks"] and "ok" in rep
+    assert rep["checks"]["kernel_library"] in ("built",) or rep["checks"]["kernel_library"].startswith("missing")
