@@ -568,3 +568,37 @@ def test_host_capabilities_and_doctor_report():
     rep = run_doctor()
     assert "checks" in rep and "torch" in rep["checks"] and "ok" in rep
     assert rep["checks"]["kernel_library"] in ("built",) or rep["checks"]["kernel_library"].startswith("missing")
+
+
+def test_torch_rank_backend_serves_the_worker_abi_exactly():
+    """The exact PyTorch backend behind ``UniversalWorker``: generate equals the reference
+    greedy decode; verify accepts the greedy continuation whole and a corrupted draft up to its
+    first wrong token (the same as the one-call-per-token ``GreedyVerifier``); draft proposes
+    from the context; an integrity audit finds a tampered continuation."""
+    from swarm_inference_lab_b200.models.config import TINY_LLAMA_CPU
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    from swarm_inference_lab_b200.runtime.abi import GreedyVerifier, UniversalWorker
+    from swarm_inference_lab_b200.runtime.torch_rank import TorchRankBackend
+    torch.set_num_threads(2)
+    prompt = [5, 9, 14, 5, 9, 22, 31]
+    expect = ReferenceDecoder(TINY_LLAMA_CPU, random_source(0)).greedy_generate(prompt, 6)[0]
+    be = TorchRankBackend({"preset": "tiny-llama-cpu", "seed": 0})
+    w = UniversalWorker(be, "torch-rank")
+    r = w.run({"kind": "generate", "prompt": prompt, "max_new_tokens": 6})
+    assert r["status"] == "OK" and r["result"]["tokens"] == expect
+    r = w.run({"kind": "verify", "context": prompt, "candidates": expect[:4]})
+    assert r["result"] == {"accepted": 4, "next": expect[4]}
+    bad = expect[:2] + [(expect[2] + 1) % 32000, expect[3]]
+    r = w.run({"kind": "verify", "context": prompt, "candidates": bad})
+    gv = GreedyVerifier(lambda ctx: be.generate(ctx, 1)["tokens"][0])
+    assert r["result"] == gv.verify(prompt, bad) == {"accepted": 2, "next": expect[2]}
+    # the trailing bigram (5, 9) last occurred at positions 3-4, followed by 22, 31, 5
+    r = w.run({"kind": "draft", "context": prompt + [5, 9], "k": 3})
+    assert r["result"]["draft"] == [22, 31, 5]
+    tampered = expect[:3] + [expect[3] + 1] + expect[4:]
+    r = w.run({"kind": "background", "name": "integrity_audit",
+               "args": {"prompt": prompt, "tokens": tampered}})
+    assert r["result"]["agreed"] is False and r["result"]["first_mismatch"] == 3
+    r = w.run({"kind": "background", "name": "integrity_audit",
+               "args": {"prompt": prompt, "tokens": expect}})
+    assert r["result"]["agreed"] is True
