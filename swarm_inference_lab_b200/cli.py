@@ -900,6 +900,17 @@ def experiment_microsharding(tokens: int = 16, repeats: int = 3,
     eb_main(["--tokens", str(tokens), "--repeats", str(repeats)] + (["--out", out] if out else []))
 
 
+@experiment_app.command("real-loopback")
+def experiment_real_loopback(checkpoint: str, stages: int = 4, tokens: int = 24,
+                             out: str = typer.Option(None, "--out")):
+    """A safetensors CHECKPOINT served as STAGES process-isolated pipeline stages on this host
+    (cluster create/start, pair + join + agent per node, ``run --require-distributed``),
+    checked token for token against the checkpoint's own greedy generation."""
+    from .testing.real_loopback import main as rl_main
+    raise typer.Exit(rl_main([checkpoint, "--stages", str(stages), "--tokens", str(tokens)]
+                             + (["--out", out] if out else [])))
+
+
 @experiment_app.command("node-roles")
 def experiment_node_roles(nodes: str, model_gb: float = typer.Option(..., "--model-gb"),
                           expert_fraction: float = typer.Option(0.0, "--expert-fraction"),

@@ -308,15 +308,13 @@ def test_replica_pipelines_share_concurrent_requests(tmp_path, single_process):
 
 
 def test_hf_qwen3_checkpoint_four_stages_matches_hf_generate(tmp_path):
-    """A Hugging Face Qwen3 checkpoint (tiny, random, fp32) deployed as 4 process-isolated
-    pipeline stages from its safetensors: greedy tokens equal HF's own ``generate``."""
+    """A Hugging Face Qwen3 checkpoint (tiny, random, fp32) served as 4 process-isolated
+    pipeline stages through the public commands (``testing/real_loopback.py``: cluster
+    create / start / pair, node join / agent, ``swarm run --require-distributed``): greedy
+    tokens equal HF's own ``generate``."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
-    from swarm_inference_lab_b200.cluster.control import (channel_credentials, coordinator_tls,
-                                                          server_credentials)
-    from swarm_inference_lab_b200.cluster.pairing import PairingManager
-    from swarm_inference_lab_b200.cluster.state import ClusterStateStore
-    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.testing.real_loopback import run
 
     torch.manual_seed(0)
     hf = Qwen3ForCausalLM(Qwen3Config(vocab_size=320, hidden_size=64, intermediate_size=96,
@@ -325,52 +323,8 @@ def test_hf_qwen3_checkpoint_four_stages_matches_hf_generate(tmp_path):
                                       max_position_embeddings=256, tie_word_embeddings=False)).eval()
     ckpt = tmp_path / "qwen3-tiny"
     hf.save_pretrained(ckpt, safe_serialization=True)
-    prompt = torch.randint(0, 320, (12,), generator=torch.Generator().manual_seed(2)).tolist()
-    with torch.no_grad():
-        gen = hf.generate(torch.tensor([prompt]), max_new_tokens=24, do_sample=False)[0, 12:].tolist()
-    port = _free_pair()
-    coord = tmp_path / "coord"
-    _swarm("cluster", "create", "demo", "--host", "127.0.0.1", "--port", str(port),
-           "--state-dir", str(coord), "--json")
-    store = ClusterStateStore(coord)
-
-    async def go():
-        ca, crt, key = coordinator_tls(store)
-        core = CoordinatorCore(store.identity("coordinator"), state_dir=coord, cluster_store=store,
-                               worker_credentials=channel_credentials(ca, crt, key))
-        pm = PairingManager(store, f"127.0.0.1:{port}")
-        await pm.start("127.0.0.1", port)
-        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=port + 1,
-                                   credentials=server_credentials(ca, crt, key))
-        await rpc.start()
-        agents = []
-        try:
-            for i in range(4):
-                st = tmp_path / f"s{i}"
-                proc = await asyncio.create_subprocess_exec(
-                    sys.executable, "-m", "swarm_inference_lab_b200.cli", "node", "join",
-                    pm.invite().uri(), "--name", f"s{i}", "--state-dir", str(st), env=_env(),
-                    cwd=ROOT, stdout=asyncio.subprocess.DEVNULL, stderr=asyncio.subprocess.PIPE)
-                _, err = await asyncio.wait_for(proc.communicate(), 120)
-                assert proc.returncode == 0, err.decode()[-2000:]
-                agents.append(_start_agent(st, tmp_path / f"s{i}.ready"))
-            t0 = time.time()
-            while len(core.registry.healthy()) < 4:
-                assert time.time() - t0 < 120
-                await asyncio.sleep(0.1)
-            dep = await core.deploy({"model": {"checkpoint": str(ckpt)}, "stages": 4})
-            assert [s["layers"] for s in dep["stages"]] == [[0, 1], [1, 2], [2, 3], [3, 4]]
-            toks = []
-            async for ev in core.submit_stream({"model": dep["model"], "prompt_ids": prompt,
-                                                "max_tokens": 24}):
-                if ev["event"] == "token":
-                    toks.append(ev["token"])
-                elif ev["event"] == "failed":
-                    raise AssertionError(ev)
-            return toks
-        finally:
-            _stop(agents)
-            await rpc.stop()
-            await pm.close()
-
-    assert asyncio.run(go()) == gen
+    rep = run(str(ckpt), stages=4, tokens=24, workdir=str(tmp_path / "run"))
+    assert rep["reference"].startswith("transformers")
+    assert [s["layers"] for s in rep["stages"]] == [[0, 1], [1, 2], [2, 3], [3, 4]]
+    assert len({s["worker"] for s in rep["stages"]}) == 4
+    assert rep["exact"], (rep["tokens"], rep["reference_tokens"])
