@@ -957,56 +957,33 @@ def validate_run(contract: str, evidence: str):
     raise typer.Exit(acc_main([contract, evidence]))
 
 
-def _report_markdown(records: list) -> str:
-    """Markdown for evidence records this repository writes: bench JSON lines, loopback
-    matrix rows, WAN ring evidence / strategy decisions and contract check results."""
-    out = []
-    for rec in records:
-        if isinstance(rec, dict) and "metric" in rec and "value" in rec:        # bench.py line
-            cfg = rec.get("config", {})
-            e2e = rec.get("e2e") or {}
-            out += ["| impl | model | parallelism | GPUs | value | ms/step | TTFT ms | e2e | clocks |",
-                    "|---|---|---|---|---|---|---|---|---|",
-                    f"| {rec.get('impl', '-')} | {cfg.get('model', '-')} | {cfg.get('parallelism', '-')} | "
-                    f"{rec.get('n_gpus')} | {rec['value']:.1f} {rec.get('unit', '')} | "
-                    f"{rec.get('ms_per_step', 0):.3f} | {rec.get('ttft_ms_p50') or '-'} | "
-                    f"{e2e.get('value', '-')} | {json.dumps(rec.get('clocks', {}))} |", ""]
-        elif isinstance(rec, dict) and "results" in rec and "contract" in rec:  # validate-run
-            out += [f"contract `{rec['contract']}`: {'pass' if rec['ok'] else 'FAIL'}", "",
-                    "| field | got | want | ok |", "|---|---|---|---|"]
-            out += [f"| {r['field']} | {r.get('got')} | {r.get('op', '==')} {r.get('want')} | "
-                    f"{r['ok']} |" for r in rec["results"]] + [""]
-        elif isinstance(rec, dict) and "scores" in rec and "selected" in rec:   # ring strategy
-            out += [f"profile `{rec['profile']}`: selected {rec['selected']}", "",
-                    "| candidate | exact | ms / token | serial waits / token | bytes / token |",
-                    "|---|---|---|---|---|"]
-            out += [f"| {x['candidate']} | {x['feasible']} | {x['ms_per_token']:.2f} | "
-                    f"{x['serial_waits_per_token']:.2f} | {x['payload_bytes_per_token']:.0f} |"
-                    for x in rec["scores"]] + [""]
-        elif isinstance(rec, dict) and "rows" in rec and rec.get("name") == "stage_ring_wan":
-            from .testing.wan_ring import markdown as wan_md
-            out += [wan_md(rec["rows"]), ""]
-        elif isinstance(rec, dict) and "concurrency" in rec and "workers" in rec:  # loopback row
-            from .testing.loopback_matrix import markdown as lm_md
-            out += [lm_md([rec]), ""]
-        else:
-            out += ["```", json.dumps(rec, indent=1, default=str)[:2000], "```", ""]
-    return "\n".join(out)
-
-
 @app.command("report")
-def report_command(evidence: list[str]):
-    """Render evidence files (JSON, JSON lines, or logs whose JSON lines are evidence) as
-    markdown tables: bench lines, contract results, ring strategies, WAN and loopback rows."""
-    records = []
-    for path in evidence:
-        text = Path(path).read_text()
-        try:
-            doc = json.loads(text)
-            records += doc if isinstance(doc, list) else [doc]
-        except ValueError:
-            records += [json.loads(l) for l in text.splitlines() if l.startswith("{")]
-    typer.echo(_report_markdown(records))
+def report_command(evidence: list[str],
+                   fmt: str = typer.Option("md", "--format", help="md, html or csv"),
+                   out: str = typer.Option(None, "--out", help="write a bundle to this directory"),
+                   title: str = typer.Option("Evidence report", "--title")):
+    """Render evidence files (JSON, JSON lines, or logs whose JSON lines are evidence: bench
+    lines, contract results, ring strategies, WAN, loopback, real-loopback and expert-backend
+    rows) as markdown, HTML with inline charts, or CSV, with scaling figures for bench lines
+    at several GPU counts.  ``--out DIR`` writes the whole bundle (report.html, report.md,
+    one CSV per kind, summary.json, records.jsonl) and exits 1 when a contract or an
+    exactness check failed."""
+    from .testing import reporting
+    records = reporting.load(evidence)
+    if out:
+        s = reporting.write_bundle(records, out, title)
+        typer.echo(json.dumps({k: s[k] for k in ("records", "kinds", "status", "failed")}))
+        raise typer.Exit(0 if s["status"] == "PASS" else 1)
+    if fmt == "html":
+        typer.echo(reporting.to_html(records, title))
+    elif fmt == "csv":
+        for k, rows in reporting.rows_by_kind(records).items():
+            typer.echo(f"# {k}")
+            typer.echo(reporting.to_csv(rows))
+    elif fmt == "md":
+        typer.echo(reporting.to_markdown(records))
+    else:
+        raise typer.BadParameter("--format must be md, html or csv")
 
 
 @app.command("simulate")
