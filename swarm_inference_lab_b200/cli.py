@@ -911,6 +911,18 @@ def experiment_real_loopback(checkpoint: str, stages: int = 4, tokens: int = 24,
                              + (["--out", out] if out else [])))
 
 
+@experiment_app.command("heterogeneous")
+def experiment_heterogeneous(seconds: float = 3.0, tokens: int = 16,
+                             out: str = typer.Option(None, "--out")):
+    """Whether a weaker node adds tokens/s, measured on this host: a background audit lane
+    beside a primary decode lane, planner-assigned node roles against their observed aggregate,
+    and a CPU expert host taking the experts local memory cannot hold (exact against
+    all-local execution)."""
+    from .testing.heterogeneous import main as het_main
+    raise typer.Exit(het_main(["--seconds", str(seconds), "--tokens", str(tokens)]
+                              + (["--out", out] if out else [])))
+
+
 @experiment_app.command("node-roles")
 def experiment_node_roles(nodes: str, model_gb: float = typer.Option(..., "--model-gb"),
                           expert_fraction: float = typer.Option(0.0, "--expert-fraction"),

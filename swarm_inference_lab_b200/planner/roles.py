@@ -47,6 +47,9 @@ def assign_roles(nodes: list[NodeCaps], model_bytes: float, *, expert_fraction: 
         replica_gain = n.decode_tok_s if n.memory_bytes >= model_bytes else 0.0
         expert_gain = expert_fraction * pipeline_rate * (1.0 / (1.0 + n.link_ms))
         latency_cost = pipeline_rate * n.link_ms / 100.0
-        best = max((replica_gain, "replica"), (expert_gain - latency_cost, "expert"), (0.0, "idle"))
-        out.append(RoleAssignment(n.node_id, best[1], max(best[0], 0.0)))
+        gain, role = max(((replica_gain, "replica"), (expert_gain - latency_cost, "expert")),
+                         key=lambda o: o[0])
+        if gain <= 0.0:              # nothing it could do adds tokens/s
+            gain, role = 0.0, "idle"
+        out.append(RoleAssignment(n.node_id, role, gain))
     return out

@@ -328,3 +328,5 @@ def test_hf_qwen3_checkpoint_four_stages_matches_hf_generate(tmp_path):
     assert [s["layers"] for s in rep["stages"]] == [[0, 1], [1, 2], [2, 3], [3, 4]]
     assert len({s["worker"] for s in rep["stages"]}) == 4
     assert rep["exact"], (rep["tokens"], rep["reference_tokens"])
+    from swarm_inference_lab_b200.testing.acceptance import check_contract, load_contract
+    assert check_contract(load_contract("real_loopback"), rep)["ok"]

@@ -27,5 +27,13 @@ def test_headline_contract_passes_and_fails(tmp_path):
 
 
 def test_every_shipped_contract_loads():
-    for name in ("dense_decode_8b", "cpu_plumbing", "tp_exactness", "promotion_manifest"):
+    from pathlib import Path
+
+    from swarm_inference_lab_b200.testing.acceptance import CONTRACTS
+    names = {p.stem for p in Path(CONTRACTS).glob("*.yaml")}
+    assert {"dense_decode_8b", "cpu_plumbing", "tp_exactness", "promotion_manifest",
+            "stage_ring_wan", "real_loopback", "heterogeneous_utility"} <= names
+    for name in names:
         assert load_contract(name)["contract_version"] == 1
+    listed = set(load_contract("promotion_manifest")["contracts"])
+    assert listed <= names
