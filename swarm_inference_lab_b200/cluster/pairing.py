@@ -31,7 +31,7 @@ from cryptography.hazmat.primitives.asymmetric.x25519 import X25519PrivateKey, X
 from cryptography.hazmat.primitives.ciphers.aead import AESGCM
 from cryptography.hazmat.primitives.kdf.hkdf import HKDF
 
-from ..security.identity import Identity, SignatureError, canonical, fingerprint, public_key
+from ..security.identity import SignatureError, canonical, fingerprint, public_key
 from ..security.tls import issue_node_cert
 from .state import ClusterStateStore
 

@@ -27,7 +27,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ..ops import gemm, moe as moe_ops, norm
+from ..ops import gemm, moe as moe_ops
 from .config import ModelConfig
 from .dense import DenseLayerWeights, DenseModel, DenseWeights, TPInfo, random_tensor
 

@@ -13,7 +13,6 @@ import shutil
 import statistics
 import subprocess
 import threading
-import time
 
 import torch
 
