@@ -305,9 +305,26 @@ def cluster_nodes(state: str = typer.Option(STATE, "--state-dir")):
 
 @cluster_app.command("revoke")
 def cluster_revoke(node: str, state: str = typer.Option(STATE, "--state-dir")):
-    """Revoke NODE: its fingerprint is refused by the coordinator from now on."""
-    fp = _store(state).revoke(node)
+    """Revoke NODE: its fingerprint is refused by the coordinator from now on; when the
+    coordinator is running, NODE's stages move to spares at once (running requests resume
+    on the new route by replay)."""
+    st = _store(state)
+    fp = st.revoke(node)
     typer.echo(f"revoked {node} ({fp})")
+    if "coordinator" in st.runtime():
+        rep = _with_coordinator(state, lambda c: c.remove_worker(node))
+        typer.echo(json.dumps(rep))
+
+
+@cluster_app.command("topology")
+def cluster_topology(state: str = typer.Option(STATE, "--state-dir")):
+    """The running coordinator's view: workers (health, draining, link class) and, per
+    deployed model and replica, which worker covers which layers and whether coverage is
+    complete; exits 1 when a deployed model has a gap or a stage on a dead worker."""
+    rep = _with_coordinator(state, lambda c: c.topology())
+    typer.echo(json.dumps(rep, indent=1))
+    if not all(m["complete"] for m in rep["models"].values()):
+        raise typer.Exit(1)
 
 
 @cluster_app.command("delete")
@@ -639,12 +656,37 @@ def node_doctor(as_json: bool = typer.Option(False, "--json")):
 
 
 @node_app.command("leave")
-def node_leave(state: str = typer.Option(STATE, "--state-dir"), yes: bool = typer.Option(False, "--yes")):
-    """Leave the cluster: remove this node's local cluster state (needs --yes)."""
+def node_leave(state: str = typer.Option(STATE, "--state-dir"), yes: bool = typer.Option(False, "--yes"),
+               force: bool = typer.Option(False, "--force"),
+               offline: bool = typer.Option(False, "--offline")):
+    """Leave the cluster (needs --yes): the coordinator moves this node's stages to spares
+    and forgets it (refused while a replica it serves has a running request, unless
+    --force), this node's agent is stopped, and the local cluster state is removed.
+    --offline skips the coordinator (it then finds the node silent and stops using it)."""
     if not yes:
         typer.echo("refusing to leave without --yes", err=True)
         raise typer.Exit(EXIT_USAGE)
-    _store(state).delete()
+    st = _store(state)
+    if st.has_cluster() and not offline:
+        doc = st.load_cluster()
+        if doc.get("role") == "coordinator":
+            typer.echo("the coordinator node deletes the cluster instead (cluster delete)", err=True)
+            raise typer.Exit(EXIT_USAGE)
+        node_id = doc.get("node_id") or st.identity().name
+        fp = st.identity(node_id).fingerprint
+        try:
+            rep = _with_coordinator(state, lambda c: c.leave(node_id, fp, force=force))
+        except Exception as exc:  # noqa: BLE001 - reported; --offline leaves anyway
+            typer.echo(f"coordinator unreachable ({type(exc).__name__}: {exc}); "
+                       "use --offline to leave without it", err=True)
+            raise typer.Exit(EXIT_RUNTIME)
+        if not rep.get("ok"):
+            typer.echo(json.dumps(rep), err=True)
+            raise typer.Exit(EXIT_STATE)
+        typer.echo(json.dumps(rep))
+    from .cluster.control import stop_local_agent
+    stop_local_agent(st)
+    st.delete()
     typer.echo("left the cluster; local state removed")
 
 

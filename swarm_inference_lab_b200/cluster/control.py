@@ -141,6 +141,10 @@ async def run_node_agent(store: ClusterStateStore, *, host: str | None = None, d
                        tls=TlsFiles(ca, crt, key), device=device or conf.get("device", "cpu"),
                        heartbeat_s=float(conf.get("heartbeat_s", 1.0)))
     await wr.start()
+    rt = store.runtime()
+    rt["agent"] = {"pid": os.getpid(), "worker_id": node_id, "ring": wr.ring_endpoint,
+                   "control": wr.control_endpoint, "started": time.time()}
+    store.save_runtime(rt)
     if ready_file:
         Path(ready_file).write_text(json.dumps({"worker_id": node_id, "ring": wr.ring_endpoint,
                                                 "control": wr.control_endpoint, "pid": os.getpid()}))
@@ -155,6 +159,39 @@ async def run_node_agent(store: ClusterStateStore, *, host: str | None = None, d
         await stop.wait()
     finally:
         await wr.stop()
+        if store.cluster_path().exists():        # gone after `node leave`
+            rt = store.runtime()
+            if rt.get("agent", {}).get("pid") == os.getpid():
+                rt.pop("agent")
+                store.save_runtime(rt)
+
+
+def stop_local_agent(store: ClusterStateStore, timeout_s: float = 20.0) -> bool:
+    """Stops this node's agent process, found by the pid it recorded (and only if that pid
+    still runs ``node agent``); True if one was stopped."""
+    pid = store.runtime().get("agent", {}).get("pid")
+    if not pid:
+        return False
+    try:
+        cmd = Path(f"/proc/{int(pid)}/cmdline").read_bytes().split(b"\0")
+    except OSError:
+        return False
+    if b"agent" not in cmd or not any(b"swarm_inference_lab_b200" in c or b"swarm" in c for c in cmd):
+        return False
+    try:
+        os.kill(int(pid), signal.SIGTERM)
+    except ProcessLookupError:
+        return False
+    t0 = time.time()
+    while time.time() - t0 < timeout_s:
+        try:
+            state = Path(f"/proc/{int(pid)}/stat").read_text().rsplit(")", 1)[1].split()[0]
+        except (OSError, IndexError):
+            break
+        if state == "Z":            # exited, not yet reaped by its parent
+            break
+        time.sleep(0.1)
+    return True
 
 
 SYSTEMD_UNIT = """[Unit]

@@ -116,6 +116,7 @@ class DeploymentManager:
         self.ttl = lease_ttl_s
         self.deployments: dict[str, Deployment] = {}
         self._generation = int(time.time())  # monotonic across coordinator restarts
+        self.excluded: set[str] = set()       # draining workers: never a replacement
 
     # ------------------------------------------------------------ helpers
     def _enter(self, d: Deployment, phase: Phase) -> None:
@@ -237,7 +238,7 @@ class DeploymentManager:
         used = {s.worker_id for s in d.stages}
         out = []
         for rec in self.registry.healthy():
-            if rec.worker_id in used or rec.worker_id not in self.agents:
+            if rec.worker_id in used or rec.worker_id not in self.agents or rec.worker_id in self.excluded:
                 continue
             if await self.agents[rec.worker_id].free_bytes() >= sp.artifact_bytes:
                 out.append(rec.worker_id)

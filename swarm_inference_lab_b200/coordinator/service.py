@@ -142,6 +142,7 @@ class RequestRecord:
     started_at: float = 0.0
     error: str | None = None
     cancel_requested: bool = False
+    replica: str | None = None
 
 
 def model_revision(model: dict) -> str:
@@ -168,6 +169,8 @@ class CoordinatorCore:
         self.started_at = time.time()
         self.last_error: str | None = None
         self.pairing = None          # PairingManager when serving a cluster
+        self.draining: set[str] = self.deployer.excluded   # leaving: no new stages, no spares
+        self.departed: set[str] = set()                    # left or removed: heartbeats refused
         self._sweeper: asyncio.Task | None = None
         self._lock = asyncio.Lock()
 
@@ -195,6 +198,8 @@ class CoordinatorCore:
         old = self.agents.pop(wid, None)
         if old is not None:
             await old.close()
+        self.departed.discard(wid)            # an explicit registration rejoins
+        self.draining.discard(wid)
         self.agents[wid] = GrpcWorkerAgent(wid, req["fingerprint"], req["ring_endpoint"],
                                            req["control_endpoint"],
                                            credentials=self.worker_credentials)
@@ -210,6 +215,8 @@ class CoordinatorCore:
     async def heartbeat(self, req: dict) -> dict:
         self._check_caller(req["fingerprint"])
         wid = req["worker_id"]
+        if wid in self.departed:
+            return {"ok": False, "left": True}
         if wid not in self.registry.workers:
             return {"ok": False, "reregister": True}
         self.registry.heartbeat(wid)
@@ -257,7 +264,7 @@ class CoordinatorCore:
         healthy = sorted(self.registry.healthy(), key=lambda w: w.worker_id)
         busy = {sp.worker_id for m in self.models.values() for d in m.replicas.values()
                 for sp in d.stages}
-        free = [w for w in healthy if w.worker_id not in busy]
+        free = [w for w in healthy if w.worker_id not in busy and w.worker_id not in self.draining]
         replicas = max(1, int(replicas))
         n = stages or max(1, len(free) // replicas)
         n = min(n, cfg.num_layers)
@@ -412,6 +419,7 @@ class CoordinatorCore:
             yield {"event": "failed", "request_id": rid, "error": rec.error}
             return
         d = m.replicas[grant.route_id]
+        rec.replica = grant.route_id
         ctl = SessionController(self._route(m, d), recover=lambda r, e: self._recover(m, d, r, e),
                                 return_logits=bool(req.get("return_logits")),
                                 speculate_k=int(req.get("speculate_k") or 0))
@@ -465,6 +473,135 @@ class CoordinatorCore:
             if self.state is not None:
                 self.state.set_state(rid, rec.state)
             await ctl.pool.close()
+
+    # ------------------------------------------------------------ membership changes
+    def _stages_on(self, wid: str) -> list[tuple["ActiveModel", str, Deployment]]:
+        return [(m, rid, d) for m in self.models.values() for rid, d in m.replicas.items()
+                if any(sp.worker_id == wid for sp in d.stages)]
+
+    async def _move_off(self, wid: str, *, force: bool) -> list[dict]:
+        """Moves every stage ``wid`` holds onto a spare (new generation per replica).  Without
+        ``force`` a replica with a running request, or a stage with no spare, refuses the
+        move before anything changes."""
+        hosted = self._stages_on(wid)
+        for m, rid, d in hosted:
+            if not force and any(r.state == "RUNNING" and r.model == m.name and r.replica == rid
+                                 for r in self.requests.values()):
+                raise DeploymentError(f"replica {rid} of {m.name} has running requests")
+            for sp in d.stages:
+                if sp.worker_id == wid and not await self.deployer.eligible_replacements(d, sp):
+                    raise DeploymentError(f"no spare worker for stage {sp.stage_id} of {m.name}")
+        moved = []
+        for m, rid, d in hosted:
+            for ag in self.agents.values():
+                ag.model, ag.model_revision, ag.num_stages = m.model, m.revision, len(d.stages)
+            old = d.deployment_id
+            await self.deployer.recover(old, wid)
+            self.events.append({"event": "stage_moved", "model": m.name, "replica": rid,
+                                "from": wid, "generation": d.generation, "at": time.time()})
+            moved.append({"model": m.name, "replica": rid, "generation": d.generation,
+                          "stages": [[sp.stage_id, sp.worker_id] for sp in d.stages]})
+            ag = self.agents.get(wid)
+            if ag is not None:            # best effort: the leaving worker frees its stage
+                try:
+                    await asyncio.wait_for(ag.unload_stage(old), timeout=5.0)
+                except Exception:  # noqa: BLE001 - it may already be gone
+                    pass
+        return moved
+
+    async def _drop(self, wid: str, event: str) -> None:
+        self.registry.workers.pop(wid, None)
+        self.draining.discard(wid)
+        self.departed.add(wid)
+        ag = self.agents.pop(wid, None)
+        if ag is not None:
+            await ag.close()
+        self.events.append({"event": event, "worker": wid, "at": time.time()})
+        METRICS.set("coordinator_workers_healthy", len(self.registry.healthy()))
+
+    async def leave(self, req: dict) -> dict:
+        """A worker leaves gracefully (``swarm node leave``): it is drained (no new stages,
+        never a spare), its stages move to spares under a new generation, it is removed from
+        the registry and, with a cluster state store, from the members.  Refused, with
+        nothing changed, while a replica it serves has a running request (unless ``force``)
+        or when a stage has no spare."""
+        self._check_caller(req["fingerprint"])
+        wid = req["worker_id"]
+        rec = self.registry.workers.get(wid)
+        if rec is None or rec.fingerprint != req["fingerprint"]:
+            return {"ok": False, "reason": f"{wid} is not registered with this identity"}
+        async with self._lock:
+            self.draining.add(wid)
+            try:
+                moved = await self._move_off(wid, force=bool(req.get("force")))
+            except DeploymentError as exc:
+                self.draining.discard(wid)
+                return {"ok": False, "reason": str(exc)}
+            await self._drop(wid, "worker_left")
+        if self.cluster_store is not None:
+            doc = self.cluster_store.load_cluster()
+            gone = [k for k, v in doc.get("members", {}).items() if v["fingerprint"] == req["fingerprint"]]
+            for k in gone:
+                doc["members"].pop(k)
+            self.cluster_store.save_cluster(doc)
+        return {"ok": True, "moved": moved}
+
+    async def remove_worker(self, req: dict) -> dict:
+        """Removes a worker now (``swarm cluster revoke`` on the coordinator): its stages move
+        to spares even under running requests, which resume on the new route by replay."""
+        wid = req["worker_id"]
+        if wid not in self.registry.workers and wid not in self.agents:
+            return {"ok": False, "reason": f"unknown worker {wid}"}
+        async with self._lock:
+            self.draining.add(wid)
+            try:
+                moved = await self._move_off(wid, force=True)
+            except DeploymentError as exc:
+                self.draining.discard(wid)
+                return {"ok": False, "reason": str(exc)}
+            await self._drop(wid, "worker_removed")
+        return {"ok": True, "moved": moved}
+
+    def topology(self) -> dict:
+        """Workers (health, draining, measured link class) and, per deployed model and
+        replica, which worker covers which layers and whether coverage is complete: every
+        layer held, by healthy workers that are not draining."""
+        from ..planner.topology import LinkProfile, classify
+        workers = []
+        for w in sorted(self.registry.workers.values(), key=lambda w: w.worker_id):
+            caps = w.capabilities
+            link = None
+            if caps.get("rtt_ms") is not None:
+                lp = LinkProfile("coordinator", w.worker_id, float(caps["rtt_ms"]),
+                                 caps.get("bandwidth_MBps"))
+                link = {"rtt_ms": caps["rtt_ms"], "bandwidth_MBps": caps.get("bandwidth_MBps"),
+                        "domain": str(getattr(classify(lp), "value", classify(lp)))}
+            workers.append({"worker_id": w.worker_id, "healthy": w.healthy,
+                            "draining": w.worker_id in self.draining,
+                            "ring_endpoint": w.endpoint, "link": link})
+        models = {}
+        for name, m in self.models.items():
+            reps = {}
+            for rid, d in m.replicas.items():
+                spans, gaps, at = [], [], 0
+                ok = True
+                for sp in sorted(d.stages, key=lambda s: s.layer_start):
+                    w = self.registry.workers.get(sp.worker_id)
+                    live = bool(w and w.healthy and sp.worker_id not in self.draining)
+                    ok &= live
+                    if sp.layer_start > at:
+                        gaps.append([at, sp.layer_start])
+                    at = max(at, sp.layer_end)
+                    spans.append({"layers": [sp.layer_start, sp.layer_end],
+                                  "worker_id": sp.worker_id, "live": live})
+                if at < m.num_layers:
+                    gaps.append([at, m.num_layers])
+                reps[rid] = {"generation": d.generation, "phase": d.phase.value, "stages": spans,
+                             "gaps": gaps, "complete": ok and not gaps}
+            models[name] = {"layers": m.num_layers, "replicas": reps,
+                            "complete": all(r["complete"] for r in reps.values())}
+        return {"workers": workers, "models": models,
+                "departed": sorted(self.departed), "draining": sorted(self.draining)}
 
     async def publish_token(self, pub: dict) -> dict:
         """Stage 0's copy of every token it relayed (checked against the accepted stream)."""
@@ -554,6 +691,14 @@ class CoordinatorRpcServer:
             async for ev in core.submit_stream(obj):
                 yield "StreamEvent", ev
 
+        async def topology(obj):
+            return core.topology()
+
+        async def remove_worker(obj):
+            if PEER_FINGERPRINT.get() not in (None, core.identity.fingerprint):
+                raise PermissionError("only the coordinator's own identity removes workers")
+            return await core.remove_worker(obj)
+
         handlers = {
             ("Register", "RegistrationAccepted", core.register),
             ("Heartbeat", "HeartbeatReply", core.heartbeat),
@@ -566,6 +711,9 @@ class CoordinatorRpcServer:
             ("PlanModel", "PlanReply", plan),
             ("PairingCreate", "PairingInvitation", pairing_create),
             ("Metrics", "MetricsReply", metrics),
+            ("NodeLeave", "NodeLeaveReply", core.leave),
+            ("RemoveWorker", "RemoveWorkerReply", remove_worker),
+            ("Topology", "TopologyStatus", topology),
         }
         self.server = GrpcControlServer(
             {(COORDINATOR_SERVICE, m): unary(fn, rk) for m, rk, fn in handlers},
@@ -612,6 +760,16 @@ class CoordinatorClient:
 
     async def metrics(self) -> dict:
         return await self._call("Metrics", "MetricsRequest", {})
+
+    async def topology(self) -> dict:
+        return await self._call("Topology", "TopologyRequest", {})
+
+    async def leave(self, worker_id: str, fingerprint: str, *, force: bool = False) -> dict:
+        return await self._call("NodeLeave", "NodeLeaveRequest",
+                                {"worker_id": worker_id, "fingerprint": fingerprint, "force": force})
+
+    async def remove_worker(self, worker_id: str) -> dict:
+        return await self._call("RemoveWorker", "RemoveWorkerRequest", {"worker_id": worker_id})
 
     async def pairing_uri(self, ttl_s: float = 600.0) -> str:
         return (await self._call("PairingCreate", "PairingRequest", {"ttl_s": ttl_s}))["uri"]

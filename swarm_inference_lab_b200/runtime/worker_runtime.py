@@ -166,12 +166,28 @@ class WorkerRuntime:
                     "deployment_id": self.deployment_id, "at": time.time()})
                 self.heartbeats += 1
                 METRICS.inc("worker_heartbeats")
+                if rep.get("left"):           # this worker left or was removed
+                    self.registered = False
+                    return
                 if rep.get("reregister"):
                     await self.register()
             except asyncio.CancelledError:
                 raise
             except Exception:  # noqa: BLE001 - the coordinator may be restarting
                 METRICS.inc("worker_heartbeat_failures")
+
+    async def leave(self, *, force: bool = False) -> dict:
+        """Leaves the cluster gracefully: the coordinator moves this worker's stages to spares
+        and forgets it; heartbeats stop.  Refused (nothing changes) while a replica it serves
+        has a running request, unless ``force``."""
+        _, rep = await self.client.call(COORDINATOR_SERVICE, "NodeLeave", "NodeLeaveRequest", {
+            "worker_id": self.worker_id, "fingerprint": self.identity.fingerprint,
+            "force": force})
+        if rep.get("ok"):
+            self.registered = False
+            if self._hb_task is not None:
+                self._hb_task.cancel()
+        return rep
 
     async def stop(self) -> None:
         if self._hb_task is not None:

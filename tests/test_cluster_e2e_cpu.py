@@ -152,6 +152,21 @@ def test_cluster_create_join_and_run_distributed(tmp_path, single_process):
         plan = json.loads(_swarm("model", "plan", "tiny-llama-cpu", "--stages", "2",
                                  "--state-dir", str(coord)).stdout)
         assert len(plan) == 2 and {p["worker_id"] for p in plan} == {"n1", "n2"}
+        # n2 leaves: the coordinator forgets it and drops its membership, its agent stops
+        # and its local state is gone; the topology view no longer lists it
+        r = _swarm("node", "leave", "--yes", "--state-dir", str(n2))
+        assert json.loads(r.stdout.strip().splitlines()[0])["ok"]
+        agents[1].wait(timeout=30)
+        assert not (n2 / "cluster.json").exists()
+        status = _swarm("cluster", "status", "--state-dir", str(coord), "--json").stdout
+        assert json.loads(status.strip().splitlines()[-1])["members"] == 1
+        topo = json.loads(_swarm("cluster", "topology", "--state-dir", str(coord)).stdout)
+        assert [w["worker_id"] for w in topo["workers"]] == ["n1"] and topo["departed"] == ["n2"]
+        # revoking n1 on the coordinator removes it from the running registry at once
+        r = _swarm("cluster", "revoke", "n1", "--state-dir", str(coord))
+        assert json.loads(r.stdout.strip().splitlines()[-1])["ok"]
+        topo = json.loads(_swarm("cluster", "topology", "--state-dir", str(coord)).stdout)
+        assert topo["workers"] == [] and topo["departed"] == ["n1", "n2"]
     finally:
         _stop(agents)
         _swarm("cluster", "stop", "--state-dir", str(coord), check=False)

@@ -1,0 +1,99 @@
+"""Membership changes on a running deployment (CPU): an in-process coordinator and three
+worker runtimes serve the 2-stage tiny Llama with two spares.  A stage worker that leaves
+gracefully (``NodeLeave``) is refused while its replica has a running request, then leaves:
+its stage moves to a spare under a new generation and the next request still produces the
+reference tokens.  ``RemoveWorker`` (``cluster revoke``) moves the other stage to the last
+spare; with no spare left it is refused and nothing changes.  The topology view reports
+coverage before and after."""
+import asyncio
+
+import torch
+
+PROMPT = list(range(3, 15))
+
+
+def test_leave_remove_and_topology():
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.models.config import preset
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(preset("tiny-llama-cpu"), random_source(0)).greedy_generate(PROMPT, 5)[0]
+
+    async def tokens(core, name):
+        return [ev["token"] async for ev in core.submit_stream(
+            {"model": name, "prompt_ids": PROMPT, "max_tokens": 5}) if ev["event"] == "token"]
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = {}
+        out = {}
+        try:
+            for i in range(4):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=0.2,
+                                  device="cpu")
+                await w.start()
+                ws[f"w{i}"] = w
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2})
+            name = dep["model"]
+            stage_workers = [s["worker_id"] for s in dep["stages"]]
+            spares = [w for w in ws if w not in stage_workers]
+            out["topo0"] = core.topology()
+            leaver = stage_workers[1]
+            # a running request on the replica blocks a graceful leave
+            agen = core.submit_stream({"model": name, "prompt_ids": PROMPT, "max_tokens": 5})
+            first = [await agen.__anext__(), await agen.__anext__()]      # accepted, token 0
+            out["refused"] = await ws[leaver].leave()
+            out["rest"] = first + [ev async for ev in agen]
+            gen0 = core.models[name].deployment.generation
+            out["left"] = await ws[leaver].leave()
+            out["gen_after_leave"] = core.models[name].deployment.generation > gen0
+            out["stages_after_leave"] = [sp.worker_id for sp in core.models[name].deployment.stages]
+            out["spares"], out["leaver"] = spares, leaver
+            out["tokens_after_leave"] = await tokens(core, name)
+            await asyncio.sleep(0.6)                                     # heartbeats stop
+            out["hb_stopped"] = not ws[leaver].registered and leaver not in core.registry.workers
+            out["topo1"] = core.topology()
+            # removal moves stage 0 to the last spare; the request after it is still exact
+            out["removed"] = await core.remove_worker({"worker_id": stage_workers[0]})
+            out["tokens_after_remove"] = await tokens(core, name)
+            out["stages_after_remove"] = [sp.worker_id for sp in core.models[name].deployment.stages]
+            # no spare left: removing a stage worker is refused and nothing changes
+            before = [sp.worker_id for sp in core.models[name].deployment.stages]
+            out["remove_refused"] = await core.remove_worker({"worker_id": before[0]})
+            out["unchanged"] = before == [sp.worker_id for sp in core.models[name].deployment.stages]
+            out["unknown"] = await core.remove_worker({"worker_id": "nobody"})
+            return out
+        finally:
+            for w in ws.values():
+                await w.stop()
+            await rpc.stop()
+
+    out = asyncio.run(go())
+    t0 = out["topo0"]
+    m0 = next(iter(t0["models"].values()))
+    assert m0["complete"] and m0["layers"] == 4
+    assert [s["layers"] for s in next(iter(m0["replicas"].values()))["stages"]] == [[0, 2], [2, 4]]
+    assert out["refused"]["ok"] is False and "running requests" in out["refused"]["reason"]
+    kinds = [e["event"] for e in out["rest"]]
+    assert kinds[-1] == "completed" and [e["token"] for e in out["rest"] if e["event"] == "token"] == expect
+    assert out["left"]["ok"] and out["gen_after_leave"]
+    taken = out["stages_after_leave"][1]
+    assert taken in out["spares"] and out["tokens_after_leave"] == expect
+    assert out["left"]["moved"][0]["stages"][1] == [1, taken]
+    assert out["hb_stopped"]
+    m1 = next(iter(out["topo1"]["models"].values()))
+    assert m1["complete"] and out["topo1"]["departed"] == [out["leaver"]]
+    assert len(out["topo1"]["workers"]) == 3
+    last = next(w for w in out["spares"] if w != taken)
+    assert out["removed"]["ok"] and out["stages_after_remove"] == [last, taken]
+    assert out["tokens_after_remove"] == expect
+    assert out["remove_refused"]["ok"] is False and "no spare" in out["remove_refused"]["reason"]
+    assert out["unchanged"]
+    assert out["unknown"]["ok"] is False
