@@ -705,6 +705,18 @@ def model_deploy(model: str, stages: int = typer.Option(None, "--stages"),
     typer.echo(json.dumps(dep, indent=1, default=str))
 
 
+@model_app.command("scale")
+def model_scale(name: str, replicas: int = typer.Option(..., "--replicas"),
+                state: str = typer.Option(STATE, "--state-dir")):
+    """Set deployed model NAME's replica count: new pipelines go onto free healthy workers and
+    join the scheduler when READY; shrinking unloads idle replicas only (exit 1 when the
+    change cannot be made; nothing changes then)."""
+    rep = _with_coordinator(state, lambda c: c.scale(name, replicas))
+    typer.echo(json.dumps(rep))
+    if not rep.get("ok"):
+        raise typer.Exit(1)
+
+
 @model_app.command("unload")
 def model_unload(name: str, state: str = typer.Option(STATE, "--state-dir")):
     """Unload a deployed model: routes withdrawn, stages released on every node."""

@@ -86,6 +86,21 @@ class AtomicRouteAllocator:
             self.leases[g.lease_id] = g
             return g
 
+    def add_route(self, route: ReplicaRoute) -> None:
+        with self._lock:
+            if route.route_id in self.routes:
+                raise ValueError(f"route {route.route_id} exists")
+            self.routes[route.route_id] = route
+
+    def remove_route(self, route_id: str) -> None:
+        """Removes an idle route (no live lease); a busy one raises ``CapacityExhausted``."""
+        with self._lock:
+            self._reclaim()
+            r = self.routes[route_id]
+            if r.active:
+                raise CapacityExhausted(f"route {route_id} has {r.active} live lease(s)")
+            del self.routes[route_id]
+
     def renew(self, lease_id: str) -> None:
         with self._lock:
             self.leases[lease_id].expires_at = self.clock() + self.ttl

@@ -297,21 +297,8 @@ class CoordinatorCore:
             by_rep: dict[str, list[dict]] = {}
             for p in plan:
                 by_rep.setdefault(p["replica"], []).append(p)
-            deployed: dict[str, Deployment] = {}
             topology = f"{name}:{uuid.uuid4().hex[:8]}"
-            try:
-                for rid, ps in by_rep.items():
-                    for p in ps:
-                        ag = self.agents[p["worker_id"]]
-                        ag.model, ag.model_revision, ag.num_stages = model, rev, len(ps)
-                    stages = [StagePlan(p["stage_id"], p["worker_id"], p["layer_start"],
-                                        p["layer_end"], p["artifact_id"]) for p in ps]
-                    deployed[rid] = await self.deployer.deploy(
-                        stages, model_revision=rev, topology_id=f"{topology}:{rid}")
-            except Exception:
-                for d in deployed.values():
-                    await self.deployer.unload(d.deployment_id)
-                raise
+            deployed = await self._deploy_replicas(model, rev, by_rep, topology)
             cap = int(req.get("capacity") or 8)
             routes = [ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0)
                       for rid, d in deployed.items()]
@@ -321,6 +308,77 @@ class CoordinatorCore:
             self.events.append({"event": "model_deployed", "model": name, "replicas": len(deployed),
                                 "generation": m.deployment.generation, "at": time.time()})
             return self._model_status(m)
+
+    async def _deploy_replicas(self, model: dict, rev: str, by_rep: dict[str, list[dict]],
+                               topology: str) -> dict[str, Deployment]:
+        """Deploys every replica's stage plans; on a failure unloads the ones it deployed."""
+        deployed: dict[str, Deployment] = {}
+        try:
+            for rid, ps in by_rep.items():
+                for p in ps:
+                    ag = self.agents[p["worker_id"]]
+                    ag.model, ag.model_revision, ag.num_stages = model, rev, len(ps)
+                stages = [StagePlan(p["stage_id"], p["worker_id"], p["layer_start"],
+                                    p["layer_end"], p["artifact_id"]) for p in ps]
+                deployed[rid] = await self.deployer.deploy(
+                    stages, model_revision=rev, topology_id=f"{topology}:{rid}")
+        except Exception:
+            for d in deployed.values():
+                await self.deployer.unload(d.deployment_id)
+            raise
+        return deployed
+
+    async def scale(self, req: dict) -> dict:
+        """Sets a deployed model's replica count.  Growing plans the new pipelines on free
+        healthy workers (same stage count, balanced by measured speed) and adds them to the
+        scheduler once they are READY; shrinking unloads idle replicas only -- with fewer idle
+        replicas than asked for, nothing changes."""
+        from .replicas import ReplicaRoute
+        name, want = req["model"], int(req["replicas"])
+        if want < 1:
+            raise ValueError("a deployed model keeps at least one replica")
+        async with self._lock:
+            m = self.models.get(name)
+            if m is None:
+                return {"ok": False, "reason": f"model {name} is not deployed"}
+            cur = len(m.replicas)
+            alloc = m.scheduler.allocator
+            if want > cur:
+                n_stages = len(m.deployment.stages)
+                try:
+                    plan = self.plan(m.model, n_stages, want - cur)
+                except DeploymentError as exc:
+                    return {"ok": False, "reason": str(exc)}
+                used = {int(r[len("replica"):]) for r in m.replicas if r.startswith("replica")
+                        and r[len("replica"):].isdigit()}
+                fresh = iter(i for i in range(10 ** 6) if i not in used)
+                rename: dict[str, str] = {}
+                by_rep: dict[str, list[dict]] = {}
+                for p in plan:
+                    rid = rename.setdefault(p["replica"], f"replica{next(fresh)}")
+                    by_rep.setdefault(rid, []).append(dict(p, replica=rid))
+                added = await self._deploy_replicas(m.model, m.revision, by_rep, m.topology_id)
+                cap = int(req.get("capacity") or max(r.capacity for r in alloc.routes.values()))
+                for rid, d in added.items():
+                    m.replicas[rid] = d
+                    alloc.add_route(ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0))
+                self.events.append({"event": "model_scaled", "model": name, "replicas": want,
+                                    "added": sorted(added), "at": time.time()})
+                return {"ok": True, "replicas": len(m.replicas), "added": sorted(added)}
+            if want < cur:
+                idle = sorted((rid for rid in m.replicas if alloc.routes[rid].active == 0),
+                              key=lambda r: (len(r), r), reverse=True)
+                if len(idle) < cur - want:
+                    return {"ok": False, "reason": f"only {len(idle)} idle replica(s); "
+                                                   f"{cur - want} must be removed"}
+                removed = idle[:cur - want]
+                for rid in removed:
+                    alloc.remove_route(rid)
+                    await self.deployer.unload(m.replicas.pop(rid).deployment_id)
+                self.events.append({"event": "model_scaled", "model": name, "replicas": want,
+                                    "removed": removed, "at": time.time()})
+                return {"ok": True, "replicas": len(m.replicas), "removed": removed}
+            return {"ok": True, "replicas": cur}
 
     def _model_status(self, m: ActiveModel) -> dict:
         d = m.deployment
@@ -694,6 +752,9 @@ class CoordinatorRpcServer:
         async def topology(obj):
             return core.topology()
 
+        async def scale(obj):
+            return await core.scale(obj)
+
         async def remove_worker(obj):
             if PEER_FINGERPRINT.get() not in (None, core.identity.fingerprint):
                 raise PermissionError("only the coordinator's own identity removes workers")
@@ -714,6 +775,7 @@ class CoordinatorRpcServer:
             ("NodeLeave", "NodeLeaveReply", core.leave),
             ("RemoveWorker", "RemoveWorkerReply", remove_worker),
             ("Topology", "TopologyStatus", topology),
+            ("ScaleModel", "ScaleReply", scale),
         }
         self.server = GrpcControlServer(
             {(COORDINATOR_SERVICE, m): unary(fn, rk) for m, rk, fn in handlers},
@@ -763,6 +825,9 @@ class CoordinatorClient:
 
     async def topology(self) -> dict:
         return await self._call("Topology", "TopologyRequest", {})
+
+    async def scale(self, name: str, replicas: int) -> dict:
+        return await self._call("ScaleModel", "ScaleRequest", {"model": name, "replicas": replicas})
 
     async def leave(self, worker_id: str, fingerprint: str, *, force: bool = False) -> dict:
         return await self._call("NodeLeave", "NodeLeaveRequest",

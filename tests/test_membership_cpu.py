@@ -97,3 +97,66 @@ def test_leave_remove_and_topology():
     assert out["remove_refused"]["ok"] is False and "no spare" in out["remove_refused"]["reason"]
     assert out["unchanged"]
     assert out["unknown"]["ok"] is False
+
+
+def test_scale_replicas_up_and_down():
+    """``ScaleModel``: 1 -> 2 replicas on free workers (concurrent requests then use both,
+    tokens exact), 2 -> 3 refused for lack of workers with nothing changed, 2 -> 1 unloads an
+    idle replica."""
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.models.config import preset
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(preset("tiny-llama-cpu"), random_source(0)).greedy_generate(PROMPT, 5)[0]
+
+    async def one(core, name):
+        rep, toks = None, []
+        async for ev in core.submit_stream({"model": name, "prompt_ids": PROMPT, "max_tokens": 5}):
+            if ev["event"] == "accepted":
+                rep = ev["replica"]
+            elif ev["event"] == "token":
+                toks.append(ev["token"])
+        return rep, toks
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws, out = [], {}
+        try:
+            for i in range(4):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=1.0,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2,
+                                     "capacity": 1})
+            name = dep["model"]
+            out["up"] = await core.scale({"model": name, "replicas": 2})
+            out["both"] = await asyncio.gather(one(core, name), one(core, name))
+            out["too_many"] = await core.scale({"model": name, "replicas": 3})
+            out["after_refusal"] = len(core.models[name].replicas)
+            out["down"] = await core.scale({"model": name, "replicas": 1})
+            out["left"] = sorted(core.models[name].replicas)
+            out["single"] = await one(core, name)
+            out["topo"] = core.topology()
+            return out
+        finally:
+            for w in ws:
+                await w.stop()
+            await rpc.stop()
+
+    out = asyncio.run(go())
+    assert out["up"] == {"ok": True, "replicas": 2, "added": ["replica1"]}
+    (ra, ta), (rb, tb) = out["both"]
+    assert {ra, rb} == {"replica0", "replica1"} and ta == tb == expect
+    assert out["too_many"]["ok"] is False and out["after_refusal"] == 2
+    assert out["down"]["ok"] and out["down"]["replicas"] == 1 and len(out["left"]) == 1
+    assert out["single"][1] == expect
+    m = next(iter(out["topo"]["models"].values()))
+    assert m["complete"] and list(m["replicas"]) == out["left"]
