@@ -131,8 +131,11 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
                 stages: int = typer.Option(None, "--stages"),
                 replicas: int = typer.Option(1, "--replicas"),
                 return_logits: bool = typer.Option(False, "--return-logits"),
+                ignore_eos: bool = typer.Option(False, "--ignore-eos",
+                                                help="generate MAX_TOKENS even past the model's EOS"),
                 state: str = typer.Option(STATE, "--state-dir")):
-    """Resolve, plan and run MODEL (on this box, or across the cluster), streaming tokens."""
+    """Resolve, plan and run MODEL (on this box, or across the cluster), streaming tokens;
+    generation ends after MAX_TOKENS or after the checkpoint's EOS token (which is emitted)."""
     from .engines import EngineRegistry, RequestShape
     if mode not in ("speed", "throughput", "capacity", "balanced"):
         raise typer.BadParameter("mode must be speed|throughput|capacity|balanced")
@@ -145,7 +148,7 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
     ids, tok_kind = _prompt_ids(prompt, prompt_ids, cfg.vocab_size, tokenizer)
     if require_distributed:
         _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
-                         as_json, ndjson, return_logits, state, replicas)
+                         as_json, ndjson, return_logits, state, replicas, ignore_eos)
         return
     caps = _gpu_caps(gpus)
     comp = EngineRegistry().compete(cfg, caps, RequestShape(
@@ -178,7 +181,8 @@ def run_command(model: str, prompt: str = typer.Option(None, "--prompt"),
     eng = LLMEngine(cfg, device="cuda", seed=seed, max_batch=1,
                     max_seq_len=len(ids) + max_tokens + 64, weights=weights)
     params = SamplingParams(max_new_tokens=max_tokens, temperature=temperature, top_k=top_k,
-                            top_p=top_p, repetition_penalty=repetition_penalty, seed=seed)
+                            top_p=top_p, repetition_penalty=repetition_penalty, seed=seed,
+                            stop_token_ids=() if ignore_eos else tuple(cfg.eos_token_ids))
     eng.add_request(ids, params, request_id="cli")
     out = []
     while eng.scheduler.has_work():
@@ -217,7 +221,7 @@ def _model_desc(model: str, cfg, ckpt: str | None, seed: int) -> dict:
 
 
 def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, tokenizer,
-                     as_json, ndjson, return_logits, state, replicas=1):
+                     as_json, ndjson, return_logits, state, replicas=1, ignore_eos=False):
     """Deploy MODEL across the cluster's joined nodes through the coordinator and stream
     the request's tokens (the coordinator replays the request on a replacement node if a
     node fails mid-request)."""
@@ -235,7 +239,8 @@ def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, 
             dep = await cli.deploy(desc, stages=stages, replicas=replicas)
             name = dep["model"]
             events, tokens, logits = [], [], []
-            async for ev in cli.submit_stream(name, ids, max_tokens, return_logits=return_logits):
+            async for ev in cli.submit_stream(name, ids, max_tokens, return_logits=return_logits,
+                                              ignore_eos=ignore_eos):
                 events.append(ev)
                 if ev["event"] == "token":
                     tokens.append(ev["token"])
@@ -254,7 +259,7 @@ def _run_distributed(model, cfg, ckpt, ids, tok_kind, max_tokens, stages, seed, 
         raise typer.Exit(EXIT_RUNTIME)
     result = {"tokens": tokens, "output_tokens": len(tokens), "deployment": dep,
               "generations": last.get("generations"), "prompt_tokenization": tok_kind,
-              "distributed": True}
+              "stop_reason": last.get("stop_reason"), "distributed": True}
     if return_logits:
         result["logits"] = logits
     if tokenizer is not None:
@@ -440,8 +445,11 @@ def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids
                    state: str = typer.Option(STATE, "--state-dir"),
                    return_logits: bool = typer.Option(False, "--return-logits"),
                    speculate: int = typer.Option(0, "--speculate",
-                                                 help="exact prompt-lookup speculation, up to K draft tokens")):
-    """Stream one request of an already deployed MODEL through the coordinator (NDJSON)."""
+                                                 help="exact prompt-lookup speculation, up to K draft tokens"),
+                   stop: str = typer.Option("", "--stop", help="extra stop token ids, comma separated"),
+                   ignore_eos: bool = typer.Option(False, "--ignore-eos")):
+    """Stream one request of an already deployed MODEL through the coordinator (NDJSON); it
+    ends after MAX_TOKENS, the model's EOS token or a --stop token (each emitted)."""
     from .cluster.control import coordinator_client
     ids = [int(x) for x in prompt_ids.split(",") if x.strip()]
 
@@ -449,7 +457,9 @@ def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids
         cli = coordinator_client(_store(state))
         try:
             async for ev in cli.submit_stream(model, ids, max_tokens, return_logits=return_logits,
-                                              speculate_k=speculate):
+                                              speculate_k=speculate, ignore_eos=ignore_eos,
+                                              stop_token_ids=[int(x) for x in stop.split(",")
+                                                              if x.strip()]):
                 typer.echo(json.dumps(ev))
         finally:
             await cli.close()

@@ -124,6 +124,7 @@ class ActiveModel:
     num_layers: int
     topology_id: str
     scheduler: object = None
+    eos_token_ids: tuple = ()
 
     @property
     def deployment(self) -> Deployment:
@@ -143,6 +144,15 @@ class RequestRecord:
     error: str | None = None
     cancel_requested: bool = False
     replica: str | None = None
+
+
+def _model_config(model: dict):
+    """The ``ModelConfig`` of a model description (a checkpoint directory or a preset)."""
+    if "checkpoint" in model:
+        from ..model_io.loader import checkpoint_config
+        return checkpoint_config(model["checkpoint"])
+    from ..models.config import preset
+    return preset(model["preset"])
 
 
 def model_revision(model: dict) -> str:
@@ -254,13 +264,8 @@ class CoordinatorCore:
         """Stage plans of every replica (``replica`` key): contiguous equal layer intervals,
         one stage per free healthy worker; replicas are balanced by the workers' measured
         speed (``place_replicas``)."""
-        from ..models.config import preset
         from .replicas import place_replicas
-        if "checkpoint" in model:
-            from ..model_io.loader import checkpoint_config
-            cfg = checkpoint_config(model["checkpoint"])
-        else:
-            cfg = preset(model["preset"])
+        cfg = _model_config(model)
         healthy = sorted(self.registry.healthy(), key=lambda w: w.worker_id)
         busy = {sp.worker_id for m in self.models.values() for d in m.replicas.values()
                 for sp in d.stages}
@@ -303,7 +308,8 @@ class CoordinatorCore:
             routes = [ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0)
                       for rid, d in deployed.items()]
             m = ActiveModel(name, model, rev, deployed, plan[-1]["layer_end"], topology,
-                            ReplicaScheduler(AtomicRouteAllocator(routes)))
+                            ReplicaScheduler(AtomicRouteAllocator(routes)),
+                            _model_config(model).eos_token_ids)
             self.models[name] = m
             self.events.append({"event": "model_deployed", "model": name, "replicas": len(deployed),
                                 "generation": m.deployment.generation, "at": time.time()})
@@ -469,6 +475,10 @@ class CoordinatorCore:
         if self.state is not None:
             self.state.record_request(rid, prompt, {"max_tokens": req.get("max_tokens")})
         max_tokens = int(req.get("max_tokens", 16))
+        stop_ids = {int(t) for t in (req.get("stop_token_ids") or ())}
+        if not req.get("ignore_eos"):
+            stop_ids |= set(m.eos_token_ids)
+        stop_reason = "length"
         try:
             grant = m.scheduler.submit(len(prompt), max_tokens)
         except Exception as exc:  # noqa: BLE001 - every replica is at capacity
@@ -504,6 +514,9 @@ class CoordinatorCore:
                     if ev.get("logits") is not None:
                         out["logits"] = [float(v) for v in ev["logits"].reshape(-1).tolist()]
                     yield out
+                    if ev["token"] in stop_ids:   # the stop token is the last one emitted
+                        stop_reason = "stop_token"
+                        break
                 elif ev["event"] in ("started", "recovered"):
                     rec.generations.append(ev["generation"])
                     if ev["event"] == "recovered":
@@ -516,9 +529,13 @@ class CoordinatorCore:
                 METRICS.inc("coordinator_requests_cancelled")
                 yield {"event": "cancelled", "request_id": rid, "tokens": rec.tokens}
                 return
+            if stop_reason == "stop_token":
+                await agen.aclose()
+                await ctl.cancel_current(finished=True)   # every stage closes the session
             rec.state = "COMPLETED"
             yield {"event": "completed", "request_id": rid, "tokens": rec.tokens,
-                   "generations": rec.generations, "seconds": time.perf_counter() - t0}
+                   "generations": rec.generations, "seconds": time.perf_counter() - t0,
+                   "stop_reason": stop_reason}
         except Exception as exc:  # noqa: BLE001 - reported to the caller as an event
             rec.state = "FAILED"
             rec.error = self.last_error = f"{type(exc).__name__}: {exc}"
@@ -841,12 +858,13 @@ class CoordinatorClient:
 
     async def submit_stream(self, model: str, prompt_ids: list[int], max_tokens: int, *,
                             return_logits: bool = False, request_id: str | None = None,
-                            speculate_k: int = 0):
+                            speculate_k: int = 0, stop_token_ids=(), ignore_eos: bool = False):
         async for _, ev in self.client.call_stream(
                 COORDINATOR_SERVICE, "SubmitStream", "SubmitRequest",
                 {"model": model, "prompt_ids": list(prompt_ids), "max_tokens": max_tokens,
                  "return_logits": return_logits, "request_id": request_id,
-                 "speculate_k": speculate_k}):
+                 "speculate_k": speculate_k, "stop_token_ids": list(stop_token_ids),
+                 "ignore_eos": ignore_eos}):
             yield ev
 
     async def close(self) -> None:

@@ -265,12 +265,14 @@ class SessionController:
         await self._close(session_id, request_id)
         self.current = None
 
-    async def cancel_current(self) -> bool:
-        """Cancels the session of the stream this controller ran last, on every stage (for a
-        consumer that stopped reading the stream before its end).  False if none is open."""
+    async def cancel_current(self, *, finished: bool = False) -> bool:
+        """Ends the session of the stream this controller ran last, on every stage (for a
+        consumer that stopped reading the stream before its end): a cancel, or with
+        ``finished`` an ordinary close (the request ended early, e.g. on a stop token).
+        False if none is open."""
         if getattr(self, "current", None) is None:
             return False
         session_id, request_id = self.current
         self.current = None
-        await self._close(session_id, request_id, cancel=True)
+        await self._close(session_id, request_id, cancel=not finished)
         return True

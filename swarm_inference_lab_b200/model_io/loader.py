@@ -26,7 +26,7 @@ from pathlib import Path
 
 import torch
 
-from ..models.config import ModelConfig, from_hf_config
+from ..models.config import ModelConfig, eos_ids, from_hf_config
 
 
 class CheckpointError(RuntimeError):
@@ -40,6 +40,11 @@ def checkpoint_config(path: str | Path) -> ModelConfig:
         raise CheckpointError(f"{p}: no config.json")
     raw = json.loads(cfg_file.read_text())
     cfg = from_hf_config(raw)
+    gen = p / "generation_config.json"          # what `generate` stops on takes precedence
+    if gen.is_file():
+        g = json.loads(gen.read_text())
+        if g.get("eos_token_id") is not None:
+            cfg = cfg.replace(eos_token_ids=eos_ids(g["eos_token_id"]))
     return cfg.replace(name=p.name)
 
 

@@ -55,6 +55,8 @@ class ModelConfig:
     v_head_dim: int = 0
     # weights
     weight_dtype: str = "bf16"        # bf16 | fp8_block128
+    # generation stops after emitting one of these (the checkpoint's eos_token_id)
+    eos_token_ids: tuple[int, ...] = ()
     extra: dict = field(default_factory=dict)
 
     @property
@@ -97,6 +99,15 @@ class ModelConfig:
         return dataclasses.asdict(self)
 
 
+def eos_ids(value) -> tuple[int, ...]:
+    """``eos_token_id`` of a Hugging Face config (an int, a list of ints or absent)."""
+    if value is None:
+        return ()
+    if isinstance(value, (list, tuple)):
+        return tuple(sorted({int(v) for v in value}))
+    return (int(value),)
+
+
 def from_hf_config(cfg: dict) -> ModelConfig:
     """Build a :class:`ModelConfig` from a Hugging Face ``config.json`` dictionary."""
     mt = cfg.get("model_type", "llama")
@@ -117,6 +128,7 @@ def from_hf_config(cfg: dict) -> ModelConfig:
         rope_scaling=cfg.get("rope_scaling"),
         tie_word_embeddings=bool(cfg.get("tie_word_embeddings", False)),
         max_position_embeddings=int(cfg.get("max_position_embeddings", 8192)),
+        eos_token_ids=eos_ids(cfg.get("eos_token_id")),
     )
     if mt in ("llama", "mistral"):
         return ModelConfig(family=mt, **common)

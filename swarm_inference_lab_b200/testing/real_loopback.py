@@ -72,8 +72,10 @@ def reference_tokens(checkpoint: str, prompt: list[int], tokens: int) -> tuple[l
     except ImportError:
         from ..model_io.loader import checkpoint_config, safetensors_source
         from ..models.reference import ReferenceDecoder
-        dec = ReferenceDecoder(checkpoint_config(checkpoint), safetensors_source(checkpoint))
-        return dec.greedy_generate(prompt, tokens)[0], "reference decoder (fp32)"
+        cfg = checkpoint_config(checkpoint)
+        out = ReferenceDecoder(cfg, safetensors_source(checkpoint)).greedy_generate(prompt, tokens)[0]
+        stop = next((i for i, t in enumerate(out) if t in cfg.eos_token_ids), None)
+        return (out if stop is None else out[:stop + 1]), "reference decoder (fp32)"
 
 
 def run(checkpoint: str, *, stages: int = 4, tokens: int = 24, prompt: list[int] | None = None,
@@ -136,7 +138,8 @@ def run(checkpoint: str, *, stages: int = 4, tokens: int = 24, prompt: list[int]
                 {"layers": s["layers"], "worker": s["worker_id"]} for s in res["deployment"]["stages"]],
             "prompt": prompt, "tokens": res["tokens"], "reference_tokens": ref,
             "reference": ref_kind, "exact": res["tokens"] == ref,
-            "distributed": res.get("distributed"), "seconds": time.perf_counter() - t0}
+            "stop_reason": res.get("stop_reason"), "distributed": res.get("distributed"),
+            "seconds": time.perf_counter() - t0}
 
 
 def main(argv=None):

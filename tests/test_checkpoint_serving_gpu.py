@@ -55,7 +55,7 @@ def test_swarm_run_serves_a_checkpoint_with_its_tokenizer(tmp_path, kind):
     prompt = " ".join(WORDS[i] for i in (5, 77, 300, 12, 999, 41, 8, 650, 123, 7))
     env = dict(os.environ, PYTHONPATH=ROOT)
     out = subprocess.run([sys.executable, "-m", "swarm_inference_lab_b200.cli", "run", str(tmp_path),
-                          "--prompt", prompt, "--max-tokens", "32", "--json"],
+                          "--prompt", prompt, "--max-tokens", "32", "--ignore-eos", "--json"],
                          capture_output=True, text=True, env=env, cwd=ROOT, timeout=600)
     assert out.returncode == 0, out.stderr[-3000:]
     res = json.loads(out.stdout.strip().splitlines()[-1])

@@ -326,7 +326,7 @@ def test_hf_qwen3_checkpoint_four_stages_matches_hf_generate(tmp_path):
     """A Hugging Face Qwen3 checkpoint (tiny, random, fp32) served as 4 process-isolated
     pipeline stages through the public commands (``testing/real_loopback.py``: cluster
     create / start / pair, node join / agent, ``swarm run --require-distributed``): greedy
-    tokens equal HF's own ``generate``."""
+    tokens equal HF's own ``generate``, both ending at the checkpoint's EOS token."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
     from swarm_inference_lab_b200.testing.real_loopback import run
@@ -336,12 +336,20 @@ def test_hf_qwen3_checkpoint_four_stages_matches_hf_generate(tmp_path):
                                       num_hidden_layers=4, num_attention_heads=4,
                                       num_key_value_heads=2, head_dim=16, initializer_range=0.2,
                                       max_position_embeddings=256, tie_word_embeddings=False)).eval()
+    prompt = torch.randint(0, 320, (12,), generator=torch.Generator().manual_seed(2)).tolist()
+    with torch.no_grad():
+        free = hf.generate(torch.tensor([prompt]), max_new_tokens=24, do_sample=False)[0, 12:].tolist()
+    # the checkpoint's EOS is a token greedy decoding reaches: both sides must stop after it
+    eos = free[10]
+    cut = free.index(eos) + 1
+    hf.generation_config.eos_token_id = eos
     ckpt = tmp_path / "qwen3-tiny"
     hf.save_pretrained(ckpt, safe_serialization=True)
-    rep = run(str(ckpt), stages=4, tokens=24, workdir=str(tmp_path / "run"))
+    rep = run(str(ckpt), stages=4, tokens=24, prompt=prompt, workdir=str(tmp_path / "run"))
     assert rep["reference"].startswith("transformers")
     assert [s["layers"] for s in rep["stages"]] == [[0, 1], [1, 2], [2, 3], [3, 4]]
     assert len({s["worker"] for s in rep["stages"]}) == 4
     assert rep["exact"], (rep["tokens"], rep["reference_tokens"])
+    assert rep["tokens"] == free[:cut] and rep["stop_reason"] == "stop_token"
     from swarm_inference_lab_b200.testing.acceptance import check_contract, load_contract
     assert check_contract(load_contract("real_loopback"), rep)["ok"]
