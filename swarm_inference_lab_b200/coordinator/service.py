@@ -179,8 +179,9 @@ class CoordinatorCore:
         self.started_at = time.time()
         self.last_error: str | None = None
         self.pairing = None          # PairingManager when serving a cluster
-        self.draining: set[str] = self.deployer.excluded   # leaving: no new stages, no spares
-        self.departed: set[str] = set()                    # left or removed: heartbeats refused
+        self.draining: set[str] = set()      # leaving: no new stages, never a spare
+        self.unreachable: set[str] = set()   # advertised control endpoint does not answer
+        self.departed: set[str] = set()      # left or removed: heartbeats refused
         self._sweeper: asyncio.Task | None = None
         self._lock = asyncio.Lock()
 
@@ -210,17 +211,44 @@ class CoordinatorCore:
             await old.close()
         self.departed.discard(wid)            # an explicit registration rejoins
         self.draining.discard(wid)
+        self._sync_excluded()
         self.agents[wid] = GrpcWorkerAgent(wid, req["fingerprint"], req["ring_endpoint"],
                                            req["control_endpoint"],
                                            credentials=self.worker_credentials)
         self.registry.register(WorkerRecord(wid, req["fingerprint"], req["ring_endpoint"],
                                             dict(req.get("capabilities", {}),
                                                  control_endpoint=req["control_endpoint"])))
-        self.events.append({"event": "worker_registered", "worker": wid, "at": time.time()})
+        reachable = await self._probe(wid)
+        self.events.append({"event": "worker_registered", "worker": wid, "reachable": reachable,
+                            "at": time.time()})
         METRICS.inc("coordinator_registrations")
         METRICS.set("coordinator_workers_healthy", len(self.registry.healthy()))
-        return {"accepted": True, "heartbeat_s": self.heartbeat_s,
+        return {"accepted": True, "heartbeat_s": self.heartbeat_s, "reachable": reachable,
                 "coordinator_fingerprint": self.identity.fingerprint}
+
+    def _sync_excluded(self) -> None:
+        self.deployer.excluded = self.draining | self.unreachable
+
+    async def _probe(self, wid: str, timeout_s: float = 1.0) -> bool:
+        """Reachability of a worker's advertised control endpoint from the coordinator: two
+        Health calls (the first sets up the channel); the second's round trip becomes the
+        worker's ``rtt_ms``.  An unreachable worker gets no stage and is never a spare."""
+        rec, ag = self.registry.workers.get(wid), self.agents.get(wid)
+        if rec is None or ag is None:
+            return False
+        try:
+            await asyncio.wait_for(ag.health(), timeout_s)
+            t0 = time.perf_counter()
+            await asyncio.wait_for(ag.health(), timeout_s)
+            rec.capabilities["rtt_ms"] = (time.perf_counter() - t0) * 1e3
+            ok = True
+        except Exception:  # noqa: BLE001 - any failure means not reachable
+            rec.capabilities["rtt_ms"] = None
+            ok = False
+        rec.capabilities["reachable"] = ok
+        (self.unreachable.discard if ok else self.unreachable.add)(wid)
+        self._sync_excluded()
+        return ok
 
     async def heartbeat(self, req: dict) -> dict:
         self._check_caller(req["fingerprint"])
@@ -230,6 +258,8 @@ class CoordinatorCore:
         if wid not in self.registry.workers:
             return {"ok": False, "reregister": True}
         self.registry.heartbeat(wid)
+        if wid in self.unreachable:           # re-checked until it answers
+            await self._probe(wid)
         METRICS.inc("coordinator_heartbeats")
         return {"ok": True}
 
@@ -269,7 +299,8 @@ class CoordinatorCore:
         healthy = sorted(self.registry.healthy(), key=lambda w: w.worker_id)
         busy = {sp.worker_id for m in self.models.values() for d in m.replicas.values()
                 for sp in d.stages}
-        free = [w for w in healthy if w.worker_id not in busy and w.worker_id not in self.draining]
+        free = [w for w in healthy if w.worker_id not in busy and w.worker_id not in self.draining
+                and w.worker_id not in self.unreachable]
         replicas = max(1, int(replicas))
         n = stages or max(1, len(free) // replicas)
         n = min(n, cfg.num_layers)
@@ -587,6 +618,8 @@ class CoordinatorCore:
     async def _drop(self, wid: str, event: str) -> None:
         self.registry.workers.pop(wid, None)
         self.draining.discard(wid)
+        self.unreachable.discard(wid)
+        self._sync_excluded()
         self.departed.add(wid)
         ag = self.agents.pop(wid, None)
         if ag is not None:
@@ -607,10 +640,12 @@ class CoordinatorCore:
             return {"ok": False, "reason": f"{wid} is not registered with this identity"}
         async with self._lock:
             self.draining.add(wid)
+            self._sync_excluded()
             try:
                 moved = await self._move_off(wid, force=bool(req.get("force")))
             except DeploymentError as exc:
                 self.draining.discard(wid)
+                self._sync_excluded()
                 return {"ok": False, "reason": str(exc)}
             await self._drop(wid, "worker_left")
         if self.cluster_store is not None:
@@ -629,10 +664,12 @@ class CoordinatorCore:
             return {"ok": False, "reason": f"unknown worker {wid}"}
         async with self._lock:
             self.draining.add(wid)
+            self._sync_excluded()
             try:
                 moved = await self._move_off(wid, force=True)
             except DeploymentError as exc:
                 self.draining.discard(wid)
+                self._sync_excluded()
                 return {"ok": False, "reason": str(exc)}
             await self._drop(wid, "worker_removed")
         return {"ok": True, "moved": moved}
@@ -653,6 +690,7 @@ class CoordinatorCore:
                         "domain": str(getattr(classify(lp), "value", classify(lp)))}
             workers.append({"worker_id": w.worker_id, "healthy": w.healthy,
                             "draining": w.worker_id in self.draining,
+                            "reachable": w.worker_id not in self.unreachable,
                             "ring_endpoint": w.endpoint, "link": link})
         models = {}
         for name, m in self.models.items():
@@ -662,7 +700,8 @@ class CoordinatorCore:
                 ok = True
                 for sp in sorted(d.stages, key=lambda s: s.layer_start):
                     w = self.registry.workers.get(sp.worker_id)
-                    live = bool(w and w.healthy and sp.worker_id not in self.draining)
+                    live = bool(w and w.healthy and sp.worker_id not in self.draining
+                                and sp.worker_id not in self.unreachable)
                     ok &= live
                     if sp.layer_start > at:
                         gaps.append([at, sp.layer_start])

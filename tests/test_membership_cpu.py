@@ -160,3 +160,46 @@ def test_scale_replicas_up_and_down():
     assert out["single"][1] == expect
     m = next(iter(out["topo"]["models"].values()))
     assert m["complete"] and list(m["replicas"]) == out["left"]
+
+
+def test_unreachable_worker_gets_no_stage():
+    """A worker whose advertised control endpoint does not answer the coordinator registers,
+    is reported unreachable, gets no stage in a plan and is never a spare; a reachable
+    worker's round trip is recorded."""
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = []
+        try:
+            for i in range(2):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=1.0,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            ghost = Identity.generate("ghost")
+            rep = await core.register({"worker_id": "ghost", "fingerprint": ghost.fingerprint,
+                                       "ring_endpoint": "127.0.0.1:9", "control_endpoint": "127.0.0.1:9",
+                                       "capabilities": {}})
+            plan = core.plan({"preset": "tiny-llama-cpu", "seed": 0}, 2)
+            topo = core.topology()
+            hb = await core.heartbeat({"worker_id": "ghost", "fingerprint": ghost.fingerprint})
+            return rep, plan, topo, hb, core.deployer.excluded
+        finally:
+            for w in ws:
+                await w.stop()
+            await rpc.stop()
+
+    rep, plan, topo, hb, excluded = asyncio.run(go())
+    assert rep["accepted"] and rep["reachable"] is False
+    assert {p["worker_id"] for p in plan} == {"w0", "w1"}
+    by = {w["worker_id"]: w for w in topo["workers"]}
+    assert by["ghost"]["reachable"] is False and by["w0"]["reachable"] is True
+    assert by["w0"]["link"] is not None and by["w0"]["link"]["rtt_ms"] > 0
+    assert hb["ok"] and "ghost" in excluded
