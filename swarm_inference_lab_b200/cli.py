@@ -440,7 +440,10 @@ def coordinator_command(state: str = typer.Option(STATE, "--state-dir"),
 
 
 @app.command("submit")
-def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids"),
+def submit_command(model: str, prompt_ids: str = typer.Option(None, "--prompt-ids"),
+                   prompt: str = typer.Option(None, "--prompt",
+                                              help="text, tokenized by the coordinator with the "
+                                                   "deployed checkpoint's tokenizer"),
                    max_tokens: int = typer.Option(16, "--max-tokens"),
                    state: str = typer.Option(STATE, "--state-dir"),
                    return_logits: bool = typer.Option(False, "--return-logits"),
@@ -451,12 +454,15 @@ def submit_command(model: str, prompt_ids: str = typer.Option(..., "--prompt-ids
     """Stream one request of an already deployed MODEL through the coordinator (NDJSON); it
     ends after MAX_TOKENS, the model's EOS token or a --stop token (each emitted)."""
     from .cluster.control import coordinator_client
-    ids = [int(x) for x in prompt_ids.split(",") if x.strip()]
+    if (prompt_ids is None) == (prompt is None):
+        raise typer.BadParameter("give exactly one of --prompt-ids and --prompt")
+    ids = None if prompt_ids is None else [int(x) for x in prompt_ids.split(",") if x.strip()]
 
     async def go():
         cli = coordinator_client(_store(state))
         try:
             async for ev in cli.submit_stream(model, ids, max_tokens, return_logits=return_logits,
+                                              prompt=prompt,
                                               speculate_k=speculate, ignore_eos=ignore_eos,
                                               stop_token_ids=[int(x) for x in stop.split(",")
                                                               if x.strip()]):

@@ -125,6 +125,7 @@ class ActiveModel:
     topology_id: str
     scheduler: object = None
     eos_token_ids: tuple = ()
+    tokenizer: object = None       # the checkpoint's tokenizer, when it carries one
 
     @property
     def deployment(self) -> Deployment:
@@ -338,9 +339,13 @@ class CoordinatorCore:
             cap = int(req.get("capacity") or 8)
             routes = [ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0)
                       for rid, d in deployed.items()]
+            tok = None
+            if "checkpoint" in model:
+                from ..model_io.loader import load_tokenizer
+                tok = load_tokenizer(model["checkpoint"])
             m = ActiveModel(name, model, rev, deployed, plan[-1]["layer_end"], topology,
                             ReplicaScheduler(AtomicRouteAllocator(routes)),
-                            _model_config(model).eos_token_ids)
+                            _model_config(model).eos_token_ids, tok)
             self.models[name] = m
             self.events.append({"event": "model_deployed", "model": name, "replicas": len(deployed),
                                 "generation": m.deployment.generation, "at": time.time()})
@@ -500,6 +505,14 @@ class CoordinatorCore:
             yield {"event": "failed", "error": f"model {name} is not deployed"}
             return
         rid = req.get("request_id") or uuid.uuid4().hex[:12]
+        if req.get("prompt_ids") is None:
+            # text prompts are tokenized here, with the checkpoint's own tokenizer
+            if m.tokenizer is None or req.get("prompt") is None:
+                yield {"event": "failed", "request_id": rid,
+                       "error": "send prompt_ids: this model has no tokenizer" if m.tokenizer is None
+                       else "a request needs prompt_ids or prompt"}
+                return
+            req = dict(req, prompt_ids=list(m.tokenizer.encode(req["prompt"])))
         prompt = [int(t) for t in req["prompt_ids"]]
         rec = RequestRecord(rid, prompt, model=name, started_at=time.time())
         self.requests[rid] = rec
@@ -564,9 +577,12 @@ class CoordinatorCore:
                 await agen.aclose()
                 await ctl.cancel_current(finished=True)   # every stage closes the session
             rec.state = "COMPLETED"
-            yield {"event": "completed", "request_id": rid, "tokens": rec.tokens,
-                   "generations": rec.generations, "seconds": time.perf_counter() - t0,
-                   "stop_reason": stop_reason}
+            done = {"event": "completed", "request_id": rid, "tokens": rec.tokens,
+                    "generations": rec.generations, "seconds": time.perf_counter() - t0,
+                    "stop_reason": stop_reason, "prompt_tokens": len(prompt)}
+            if m.tokenizer is not None:
+                done["text"] = m.tokenizer.decode(rec.tokens)
+            yield done
         except Exception as exc:  # noqa: BLE001 - reported to the caller as an event
             rec.state = "FAILED"
             rec.error = self.last_error = f"{type(exc).__name__}: {exc}"
@@ -895,12 +911,16 @@ class CoordinatorClient:
     async def pairing_uri(self, ttl_s: float = 600.0) -> str:
         return (await self._call("PairingCreate", "PairingRequest", {"ttl_s": ttl_s}))["uri"]
 
-    async def submit_stream(self, model: str, prompt_ids: list[int], max_tokens: int, *,
+    async def submit_stream(self, model: str, prompt_ids: list[int] | None, max_tokens: int, *,
                             return_logits: bool = False, request_id: str | None = None,
-                            speculate_k: int = 0, stop_token_ids=(), ignore_eos: bool = False):
+                            speculate_k: int = 0, stop_token_ids=(), ignore_eos: bool = False,
+                            prompt: str | None = None):
+        """``prompt_ids``, or None with a text ``prompt`` the coordinator tokenizes with the
+        deployed checkpoint's tokenizer (the ``completed`` event then carries ``text``)."""
         async for _, ev in self.client.call_stream(
                 COORDINATOR_SERVICE, "SubmitStream", "SubmitRequest",
-                {"model": model, "prompt_ids": list(prompt_ids), "max_tokens": max_tokens,
+                {"model": model, "prompt_ids": None if prompt_ids is None else list(prompt_ids),
+                 "prompt": prompt, "max_tokens": max_tokens,
                  "return_logits": return_logits, "request_id": request_id,
                  "speculate_k": speculate_k, "stop_token_ids": list(stop_token_ids),
                  "ignore_eos": ignore_eos}):
