@@ -322,13 +322,29 @@ def cluster_revoke(node: str, state: str = typer.Option(STATE, "--state-dir")):
 
 
 @cluster_app.command("topology")
-def cluster_topology(state: str = typer.Option(STATE, "--state-dir")):
-    """The running coordinator's view: workers (health, draining, link class) and, per
-    deployed model and replica, which worker covers which layers and whether coverage is
-    complete; exits 1 when a deployed model has a gap or a stage on a dead worker."""
-    rep = _with_coordinator(state, lambda c: c.topology())
+def cluster_topology(state: str = typer.Option(STATE, "--state-dir"),
+                     wait: float = typer.Option(0.0, "--wait",
+                                                help="seconds to wait for complete coverage"),
+                     model: str = typer.Option(None, "--model",
+                                               help="with --wait: a model that must be deployed")):
+    """The running coordinator's view: workers (health, draining, reachability, link class)
+    and, per deployed model and replica, which worker covers which layers and whether
+    coverage is complete; exits 1 when a deployed model has a gap or a stage on a dead or
+    unreachable worker.  --wait polls until coverage is complete (and --model is deployed)."""
+    def complete(rep):
+        return (all(m["complete"] for m in rep["models"].values())
+                and (model is None or model in rep["models"]))
+
+    async def poll(c):
+        t0 = time.time()
+        while True:
+            rep = await c.topology()
+            if complete(rep) or time.time() - t0 >= wait:
+                return rep
+            await asyncio.sleep(0.25)
+    rep = _with_coordinator(state, poll)
     typer.echo(json.dumps(rep, indent=1))
-    if not all(m["complete"] for m in rep["models"].values()):
+    if not complete(rep):
         raise typer.Exit(1)
 
 

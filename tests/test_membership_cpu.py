@@ -203,3 +203,39 @@ def test_unreachable_worker_gets_no_stage():
     assert by["ghost"]["reachable"] is False and by["w0"]["reachable"] is True
     assert by["w0"]["link"] is not None and by["w0"]["link"]["rtt_ms"] > 0
     assert hb["ok"] and "ghost" in excluded
+
+
+def test_cluster_topology_wait_polls_until_coverage(monkeypatch):
+    """``cluster topology --wait`` polls the coordinator until every deployed model (and the
+    named one) is covered; without coverage in time it exits 1."""
+    import json
+
+    from typer.testing import CliRunner
+
+    import swarm_inference_lab_b200.cli as cli
+
+    class Fake:
+        def __init__(self, complete_after):
+            self.calls, self.after = 0, complete_after
+
+        async def topology(self):
+            self.calls += 1
+            ok = self.calls > self.after
+            return {"workers": [], "departed": [], "draining": [],
+                    "models": {"m": {"layers": 4, "replicas": {}, "complete": ok}} if ok or self.calls > 1 else {}}
+
+    def with_fake(fake):
+        def run(state, fn):
+            import asyncio
+            return asyncio.run(fn(fake))
+        return run
+
+    fake = Fake(complete_after=3)
+    monkeypatch.setattr(cli, "_with_coordinator", with_fake(fake))
+    r = CliRunner().invoke(cli.app, ["cluster", "topology", "--wait", "10", "--model", "m"])
+    assert r.exit_code == 0, r.output
+    assert fake.calls == 4 and json.loads(r.output)["models"]["m"]["complete"]
+    slow = Fake(complete_after=10 ** 6)
+    monkeypatch.setattr(cli, "_with_coordinator", with_fake(slow))
+    r = CliRunner().invoke(cli.app, ["cluster", "topology", "--wait", "0.6", "--model", "m"])
+    assert r.exit_code == 1 and slow.calls >= 2
