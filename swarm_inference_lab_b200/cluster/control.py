@@ -99,6 +99,8 @@ async def serve_coordinator(store: ClusterStateStore, *, heartbeat_timeout_s: fl
     rpc = CoordinatorRpcServer(core, host=host, port=int(port) + CONTROL_PORT_OFFSET,
                                credentials=server_credentials(ca, crt, key))
     cport = await rpc.start()
+    # models deployed before a restart come back once their workers have re-registered
+    restoring = asyncio.get_running_loop().create_task(core.restore())
     rt = store.runtime()
     rt["coordinator"] = {"pid": os.getpid(), "pairing": doc["coordinator_endpoint"],
                          "control": f"{host}:{cport}", "started": time.time()}
@@ -115,6 +117,7 @@ async def serve_coordinator(store: ClusterStateStore, *, heartbeat_timeout_s: fl
     try:
         await stop.wait()
     finally:
+        restoring.cancel()
         await rpc.stop()
         await pm.close()
         rt = store.runtime()

@@ -347,9 +347,44 @@ class CoordinatorCore:
                             ReplicaScheduler(AtomicRouteAllocator(routes)),
                             _model_config(model).eos_token_ids, tok)
             self.models[name] = m
+            if self.state is not None:
+                self.state.record_model(name, {"model": model, "stages": len(m.deployment.stages),
+                                               "replicas": len(deployed), "capacity": cap})
             self.events.append({"event": "model_deployed", "model": name, "replicas": len(deployed),
                                 "generation": m.deployment.generation, "at": time.time()})
             return self._model_status(m)
+
+    async def restore(self, *, timeout_s: float = 120.0, poll_s: float = 0.5) -> dict:
+        """After a restart: redeploys every model the durable state records (same name,
+        stage count and replicas) once enough free, healthy, reachable workers have
+        registered again; returns ``{name: "restored" | error}``."""
+        if self.state is None:
+            return {}
+        out = {}
+        t0 = time.time()
+        for name, desc in self.state.models().items():
+            if name in self.models:
+                out[name] = "restored"
+                continue
+            need = int(desc["stages"]) * int(desc.get("replicas", 1))
+            while True:
+                busy = {sp.worker_id for m in self.models.values() for d in m.replicas.values()
+                        for sp in d.stages}
+                free = [w for w in self.registry.healthy() if w.worker_id not in busy
+                        and w.worker_id not in self.draining and w.worker_id not in self.unreachable]
+                if len(free) >= need or time.time() - t0 > timeout_s:
+                    break
+                await asyncio.sleep(poll_s)
+            try:
+                await self.deploy({"model": desc["model"], "name": name, "stages": desc["stages"],
+                                   "replicas": desc.get("replicas", 1),
+                                   "capacity": desc.get("capacity")})
+                out[name] = "restored"
+                self.events.append({"event": "model_restored", "model": name, "at": time.time()})
+            except Exception as exc:  # noqa: BLE001 - reported per model
+                out[name] = f"{type(exc).__name__}: {exc}"
+                self.last_error = f"restore {name}: {out[name]}"
+        return out
 
     async def _deploy_replicas(self, model: dict, rev: str, by_rep: dict[str, list[dict]],
                                topology: str) -> dict[str, Deployment]:
@@ -404,6 +439,7 @@ class CoordinatorCore:
                 for rid, d in added.items():
                     m.replicas[rid] = d
                     alloc.add_route(ReplicaRoute(rid, [sp.worker_id for sp in d.stages], cap, 1.0))
+                self._record_scale(m)
                 self.events.append({"event": "model_scaled", "model": name, "replicas": want,
                                     "added": sorted(added), "at": time.time()})
                 return {"ok": True, "replicas": len(m.replicas), "added": sorted(added)}
@@ -417,10 +453,17 @@ class CoordinatorCore:
                 for rid in removed:
                     alloc.remove_route(rid)
                     await self.deployer.unload(m.replicas.pop(rid).deployment_id)
+                self._record_scale(m)
                 self.events.append({"event": "model_scaled", "model": name, "replicas": want,
                                     "removed": removed, "at": time.time()})
                 return {"ok": True, "replicas": len(m.replicas), "removed": removed}
             return {"ok": True, "replicas": cur}
+
+    def _record_scale(self, m: ActiveModel) -> None:
+        if self.state is not None:
+            desc = self.state.models().get(m.name)
+            if desc is not None:
+                self.state.record_model(m.name, dict(desc, replicas=len(m.replicas)))
 
     def _model_status(self, m: ActiveModel) -> dict:
         d = m.deployment
@@ -442,6 +485,8 @@ class CoordinatorCore:
                 return {"unloaded": False}
             for d in m.replicas.values():
                 await self.deployer.unload(d.deployment_id)
+            if self.state is not None:
+                self.state.drop_model(m.name)
             return {"unloaded": True}
 
     def _route(self, m: ActiveModel, d: Deployment | None = None) -> Route:

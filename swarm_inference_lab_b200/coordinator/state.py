@@ -73,6 +73,21 @@ class DurableState:
             self.data["audit"].append({"event": event, "ts": time.time(), **fields})
             self._save()
 
+    def record_model(self, name: str, desc: dict) -> None:
+        """A deployed model's description (model, stages, replicas, capacity), redeployed by
+        a restarted coordinator."""
+        with self._lock:
+            self.data.setdefault("models", {})[name] = desc
+            self._save()
+
+    def drop_model(self, name: str) -> None:
+        with self._lock:
+            if self.data.setdefault("models", {}).pop(name, None) is not None:
+                self._save()
+
+    def models(self) -> dict:
+        return dict(self.data.get("models", {}))
+
     def mark_restart_boundaries(self) -> list[str]:
         """After a restart: running requests become 'replay_required'."""
         with self._lock:

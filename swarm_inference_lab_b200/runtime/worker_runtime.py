@@ -170,6 +170,9 @@ class WorkerRuntime:
                     self.registered = False
                     return
                 if rep.get("reregister"):
+                    # the coordinator restarted (or forgot this worker): reservations made
+                    # for its earlier deployments are void
+                    self.reservations.clear()
                     await self.register()
             except asyncio.CancelledError:
                 raise

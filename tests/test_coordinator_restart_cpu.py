@@ -1,0 +1,71 @@
+"""A coordinator restart (CPU, in-process): the deployed model is recorded in the durable
+state; a new coordinator on the same state directory and port is told nothing, the workers
+re-register through their heartbeats (their reservations for the old deployment are void),
+``restore`` redeploys the model under its name with a new generation, and a request then
+produces the reference tokens.  An unloaded model is not restored."""
+import asyncio
+
+import torch
+
+PROMPT = list(range(3, 15))
+
+
+def test_restart_restores_deployed_models(tmp_path):
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.models.config import preset
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(preset("tiny-llama-cpu"), random_source(0)).greedy_generate(PROMPT, 5)[0]
+
+    async def tokens(core, name):
+        return [ev["token"] async for ev in core.submit_stream(
+            {"model": name, "prompt_ids": PROMPT, "max_tokens": 5}) if ev["event"] == "token"]
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, state_dir=tmp_path, require_member=False,
+                               heartbeat_timeout_s=30.0, heartbeat_s=0.2)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = []
+        try:
+            for i in range(2):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=0.2,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2,
+                                     "name": "tiny"})
+            gen0 = dep["generation"]
+            before = await tokens(core, "tiny")
+            await rpc.stop()                                   # the coordinator goes away
+            core2 = CoordinatorCore(ident, state_dir=tmp_path, require_member=False,
+                                    heartbeat_timeout_s=30.0, heartbeat_s=0.2)
+            rpc2 = CoordinatorRpcServer(core2, host="127.0.0.1", port=port)
+            await rpc2.start()
+            try:
+                restored = await asyncio.wait_for(core2.restore(timeout_s=30.0, poll_s=0.1), 60)
+                st = core2.status()["models"]["tiny"]
+                after = await tokens(core2, "tiny")
+                await core2.unload({"model": "tiny"})
+                core3 = CoordinatorCore(ident, state_dir=tmp_path, require_member=False)
+                nothing = await core3.restore(timeout_s=1.0)
+                await core3.close()
+            finally:
+                await rpc2.stop()
+            return before, restored, st, gen0, after, nothing
+        finally:
+            for w in ws:
+                await w.stop()
+
+    before, restored, st, gen0, after, nothing = asyncio.run(go())
+    assert before == expect
+    assert restored == {"tiny": "restored"}
+    assert st["phase"] == "READY" and st["generation"] > gen0
+    assert len(st["stages"]) == 2
+    assert after == expect
+    assert nothing == {}
