@@ -360,6 +360,10 @@ class CoordinatorCore:
         registered again; returns ``{name: "restored" | error}``."""
         if self.state is None:
             return {}
+        interrupted = self.state.mark_restart_boundaries()   # their streams ended with us
+        if interrupted:
+            self.events.append({"event": "requests_interrupted", "requests": interrupted,
+                                "at": time.time()})
         out = {}
         t0 = time.time()
         for name, desc in self.state.models().items():

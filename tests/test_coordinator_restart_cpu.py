@@ -2,7 +2,8 @@
 state; a new coordinator on the same state directory and port is told nothing, the workers
 re-register through their heartbeats (their reservations for the old deployment are void),
 ``restore`` redeploys the model under its name with a new generation, and a request then
-produces the reference tokens.  An unloaded model is not restored."""
+produces the reference tokens.  A request that was running is marked ``replay_required``;
+an unloaded model is not restored."""
 import asyncio
 
 import torch
@@ -42,6 +43,7 @@ def test_restart_restores_deployed_models(tmp_path):
                                      "name": "tiny"})
             gen0 = dep["generation"]
             before = await tokens(core, "tiny")
+            core.state.record_request("cut-off", PROMPT, {"max_tokens": 5})   # still running
             await rpc.stop()                                   # the coordinator goes away
             core2 = CoordinatorCore(ident, state_dir=tmp_path, require_member=False,
                                     heartbeat_timeout_s=30.0, heartbeat_s=0.2)
@@ -49,6 +51,7 @@ def test_restart_restores_deployed_models(tmp_path):
             await rpc2.start()
             try:
                 restored = await asyncio.wait_for(core2.restore(timeout_s=30.0, poll_s=0.1), 60)
+                cut = core2.state.data["requests"]["cut-off"]["state"]
                 st = core2.status()["models"]["tiny"]
                 after = await tokens(core2, "tiny")
                 await core2.unload({"model": "tiny"})
@@ -57,12 +60,13 @@ def test_restart_restores_deployed_models(tmp_path):
                 await core3.close()
             finally:
                 await rpc2.stop()
-            return before, restored, st, gen0, after, nothing
+            return before, restored, st, gen0, after, nothing, cut
         finally:
             for w in ws:
                 await w.stop()
 
-    before, restored, st, gen0, after, nothing = asyncio.run(go())
+    before, restored, st, gen0, after, nothing, cut = asyncio.run(go())
+    assert cut == "replay_required"
     assert before == expect
     assert restored == {"tiny": "restored"}
     assert st["phase"] == "READY" and st["generation"] > gen0
