@@ -115,7 +115,11 @@ class DeploymentManager:
         self.state = state
         self.ttl = lease_ttl_s
         self.deployments: dict[str, Deployment] = {}
-        self._generation = int(time.time())  # monotonic across coordinator restarts
+        # Route generations fence stale routes, so they never repeat: a restarted coordinator
+        # continues above the last one it handed out (kept in the durable state), and above
+        # the wall clock in seconds when it has no state.
+        last = int(state.data.get("last_generation", 0)) if state is not None else 0
+        self._generation = max(int(time.time()), last)
         self.excluded: set[str] = set()       # draining workers: never a replacement
 
     # ------------------------------------------------------------ helpers
@@ -128,6 +132,8 @@ class DeploymentManager:
 
     def _next_generation(self) -> int:
         self._generation += 1
+        if self.state is not None:
+            self.state.set_last_generation(self._generation)
         return self._generation
 
     def _lease(self, d: Deployment) -> dict:

@@ -73,6 +73,12 @@ class DurableState:
             self.data["audit"].append({"event": event, "ts": time.time(), **fields})
             self._save()
 
+    def set_last_generation(self, generation: int) -> None:
+        with self._lock:
+            self.data["last_generation"] = max(int(generation),
+                                               int(self.data.get("last_generation", 0)))
+            self._save()
+
     def record_model(self, name: str, desc: dict) -> None:
         """A deployed model's description (model, stages, replicas, capacity), redeployed by
         a restarted coordinator."""

@@ -73,3 +73,22 @@ def test_restart_restores_deployed_models(tmp_path):
     assert len(st["stages"]) == 2
     assert after == expect
     assert nothing == {}
+
+
+def test_route_generations_never_repeat_across_restarts(tmp_path):
+    """Generations fence stale routes: a coordinator restarted within the same second (or
+    with a clock set back) continues above the last generation it handed out."""
+    from swarm_inference_lab_b200.coordinator.deployment import DeploymentManager
+    from swarm_inference_lab_b200.coordinator.state import DurableState, WorkerRegistry
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    ident = Identity.generate("c")
+    path = tmp_path / "coordinator_state.json"
+    a = DeploymentManager(WorkerRegistry(), {}, ident, DurableState(path))
+    seen = [a._next_generation() for _ in range(3)]
+    b = DeploymentManager(WorkerRegistry(), {}, ident, DurableState(path))
+    assert b._next_generation() > max(seen)
+    st = DurableState(path)
+    st.set_last_generation(10 ** 12)                  # as if the clock had been far ahead
+    c = DeploymentManager(WorkerRegistry(), {}, ident, DurableState(path))
+    assert c._next_generation() == 10 ** 12 + 1
