@@ -488,6 +488,23 @@ def submit_command(model: str, prompt_ids: str = typer.Option(None, "--prompt-id
     asyncio.run(go())
 
 
+@app.command("metrics")
+def metrics_command(state: str = typer.Option(STATE, "--state-dir"),
+                    workers: bool = typer.Option(False, "--workers",
+                                                 help="add every worker's stage view and metrics"),
+                    prometheus: bool = typer.Option(False, "--prometheus")):
+    """The running coordinator's counters, gauges and latency summaries (registrations,
+    heartbeats, requests, tokens, TTFT / TPOT, recoveries, transport errors), as JSON or
+    Prometheus text; --workers adds each worker's stage (frames, rejections, forward time)
+    and metrics."""
+    rep = _with_coordinator(state, lambda c: c.metrics(workers=workers))
+    if prometheus:
+        typer.echo(rep["prometheus"])
+    else:
+        typer.echo(json.dumps({k: v for k, v in rep.items() if k != "prometheus"}, indent=1,
+                              default=str))
+
+
 @app.command("status")
 def status_command(state: str = typer.Option(STATE, "--state-dir"),
                    json_output: bool = typer.Option(False, "--json")):

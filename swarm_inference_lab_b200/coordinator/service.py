@@ -739,6 +739,20 @@ class CoordinatorCore:
             await self._drop(wid, "worker_removed")
         return {"ok": True, "moved": moved}
 
+    async def worker_metrics(self, timeout_s: float = 2.0) -> dict:
+        """Every registered worker's own view (its Health call): the stage it hosts
+        (layers, generation, sessions, frames, rejections, tokens, forward time) and its
+        metrics snapshot; an unanswered worker shows the error."""
+        async def one(wid, ag):
+            try:
+                h = await asyncio.wait_for(ag.health(), timeout_s)
+                return wid, {"stage": {k: v for k, v in h.items() if k != "metrics"},
+                             "metrics": h.get("metrics", {})}
+            except Exception as exc:  # noqa: BLE001 - reported per worker
+                return wid, {"error": f"{type(exc).__name__}: {exc}"}
+        pairs = await asyncio.gather(*(one(w, a) for w, a in sorted(self.agents.items())))
+        return dict(pairs)
+
     def topology(self) -> dict:
         """Workers (health, draining, measured link class) and, per deployed model and
         replica, which worker covers which layers and whether coverage is complete: every
@@ -853,7 +867,10 @@ class CoordinatorRpcServer:
             return core.status()
 
         async def metrics(obj):
-            return {"snapshot": METRICS.snapshot(), "prometheus": METRICS.prometheus()}
+            rep = {"snapshot": METRICS.snapshot(), "prometheus": METRICS.prometheus()}
+            if obj.get("workers"):
+                rep["workers"] = await core.worker_metrics()
+            return rep
 
         async def plan(obj):
             return {"plan": core.plan(obj["model"], obj.get("stages"), int(obj.get("replicas") or 1))}
@@ -941,8 +958,8 @@ class CoordinatorClient:
     async def plan(self, model: dict, stages: int | None = None) -> list[dict]:
         return (await self._call("PlanModel", "PlanRequest", {"model": model, "stages": stages}))["plan"]
 
-    async def metrics(self) -> dict:
-        return await self._call("Metrics", "MetricsRequest", {})
+    async def metrics(self, *, workers: bool = False) -> dict:
+        return await self._call("Metrics", "MetricsRequest", {"workers": workers})
 
     async def topology(self) -> dict:
         return await self._call("Topology", "TopologyRequest", {})

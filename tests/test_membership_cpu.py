@@ -239,3 +239,49 @@ def test_cluster_topology_wait_polls_until_coverage(monkeypatch):
     monkeypatch.setattr(cli, "_with_coordinator", with_fake(slow))
     r = CliRunner().invoke(cli.app, ["cluster", "topology", "--wait", "0.6", "--model", "m"])
     assert r.exit_code == 1 and slow.calls >= 2
+
+
+def test_worker_metrics_through_the_coordinator():
+    """``Metrics`` with ``workers``: every worker's stage view (layers, frames, tokens) and
+    metrics snapshot, gathered by the coordinator after a request."""
+    from swarm_inference_lab_b200.coordinator.service import (CoordinatorClient, CoordinatorCore,
+                                                              CoordinatorRpcServer)
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = []
+        try:
+            for i in range(2):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=1.0,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2})
+            _ = [ev async for ev in core.submit_stream(
+                {"model": dep["model"], "prompt_ids": PROMPT, "max_tokens": 3})]
+            cli = CoordinatorClient(f"127.0.0.1:{port}")
+            try:
+                rep = await cli.metrics(workers=True)
+                plain = await cli.metrics()
+            finally:
+                await cli.close()
+            return rep, plain
+        finally:
+            for w in ws:
+                await w.stop()
+            await rpc.stop()
+
+    rep, plain = asyncio.run(go())
+    assert "workers" not in plain and "coordinator_tokens" in str(plain["snapshot"])
+    ws = rep["workers"]
+    assert set(ws) == {"w0", "w1"}
+    layers = sorted(tuple(w["stage"]["layers"]) for w in ws.values())
+    assert layers == [(0, 2), (2, 4)]
+    assert all(w["stage"]["frames"] > 0 for w in ws.values())
+    assert all(isinstance(w["metrics"], dict) for w in ws.values())
