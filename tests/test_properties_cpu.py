@@ -81,3 +81,35 @@ def test_generations_never_repeat_over_restarts(tmp_path_factory, steps):
         dm = DeploymentManager(WorkerRegistry(), {}, ident, DurableState(path))
         seen += [dm._next_generation() for _ in range(n)]
     assert seen == sorted(seen) and len(seen) == len(set(seen))
+
+
+_text = st.text(alphabet=st.characters(min_codepoint=33, max_codepoint=0x2FF), min_size=1, max_size=24)
+
+
+@settings(max_examples=80, deadline=None)
+@given(op=st.integers(1, 13), seq=st.integers(0, 2 ** 40), pos=st.integers(-1, 2 ** 31 - 1),
+       src=st.integers(-1, 63), dst=st.integers(-1, 63), stage=st.integers(0, 63),
+       lo=st.integers(0, 500), n=st.integers(1, 100), sid=_text, rid=_text, rev=_text,
+       payload=st.binary(max_size=512),
+       attrs=st.dictionaries(st.text(min_size=1, max_size=8),
+                             st.one_of(st.integers(-10 ** 9, 10 ** 9), st.booleans(), st.text(max_size=8)),
+                             max_size=4))
+def test_stage_ring_frames_roundtrip_in_both_codecs(op, seq, pos, src, dst, stage, lo, n, sid, rid,
+                                                    rev, payload, attrs):
+    """Any valid frame survives encode -> decode unchanged, and the C++ codec writes the same
+    bytes and reads back the same fields (when the native library is built)."""
+    from swarm_inference_lab_b200.protocol import stage_ring as sr
+    m = sr.StageMessage(operation=sr.Operation(op), model_revision=rev, tokenizer_revision="tok",
+                        topology_id="topo", stage_id=stage, layer_start=lo, layer_end=lo + n,
+                        session_id=sid, request_id=rid, sequence_number=seq, token_position=pos,
+                        source_stage=src, destination_stage=dst, payload=payload, attributes=attrs)
+    f = sr.encode(m)
+    assert sr.decode(f) == m
+    try:
+        import torch  # noqa: F401 - the native library links against torch's runtime
+        from swarm_inference_lab_b200 import _native
+    except ImportError:
+        return
+    meta = sr.canonical_json(m.metadata())
+    assert _native.ring_encode(op, 0, seq, pos, src, dst, meta, payload) == f
+    assert _native.ring_decode(f) == (op, 0, seq, pos, src, dst, meta, payload)
