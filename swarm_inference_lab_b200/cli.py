@@ -422,8 +422,9 @@ def cluster_start(state: str = typer.Option(STATE, "--state-dir"),
 
 
 @cluster_app.command("stop")
-def cluster_stop(state: str = typer.Option(STATE, "--state-dir"), wait_s: float = 10.0):
-    """Stop the coordinator process started by ``cluster start``."""
+def cluster_stop(state: str = typer.Option(STATE, "--state-dir"), wait_s: float = 45.0):
+    """Stop the coordinator process started by ``cluster start``: it admits no new request
+    and lets the running ones finish (up to 30 s) before it exits."""
     import signal as _signal
     st = _store(state)
     rec = st.runtime().get("coordinator")

@@ -80,8 +80,10 @@ def coordinator_client(store: ClusterStateStore, timeout: float = 600.0):
 
 
 async def serve_coordinator(store: ClusterStateStore, *, heartbeat_timeout_s: float = 5.0,
-                            heartbeat_s: float = 1.0, ready_file: str | None = None) -> None:
-    """The coordinator process: pairing + gRPC control plane until SIGTERM / SIGINT."""
+                            heartbeat_s: float = 1.0, ready_file: str | None = None,
+                            drain_s: float = 30.0) -> None:
+    """The coordinator process: pairing + gRPC control plane until SIGTERM / SIGINT; on the
+    signal it stops admitting requests and lets running ones finish (at most ``drain_s``)."""
     from ..coordinator.service import CoordinatorCore, CoordinatorRpcServer
     from .pairing import PairingManager
     doc = store.load_cluster()
@@ -116,6 +118,7 @@ async def serve_coordinator(store: ClusterStateStore, *, heartbeat_timeout_s: fl
             pass
     try:
         await stop.wait()
+        await core.drain(drain_s)
     finally:
         restoring.cancel()
         await rpc.stop()

@@ -183,6 +183,7 @@ class CoordinatorCore:
         self.draining: set[str] = set()      # leaving: no new stages, never a spare
         self.unreachable: set[str] = set()   # advertised control endpoint does not answer
         self.departed: set[str] = set()      # left or removed: heartbeats refused
+        self.accepting = True                # False while draining for a shutdown
         self._sweeper: asyncio.Task | None = None
         self._lock = asyncio.Lock()
 
@@ -554,6 +555,9 @@ class CoordinatorCore:
             yield {"event": "failed", "error": f"model {name} is not deployed"}
             return
         rid = req.get("request_id") or uuid.uuid4().hex[:12]
+        if not self.accepting:
+            yield {"event": "failed", "request_id": rid, "error": "the coordinator is shutting down"}
+            return
         if req.get("prompt_ids") is None:
             # text prompts are tokenized here, with the checkpoint's own tokenizer
             if m.tokenizer is None or req.get("prompt") is None:
@@ -833,6 +837,19 @@ class CoordinatorCore:
                                  "generations": r.generations, "started_at": r.started_at,
                                  "error": r.error}
                              for k, r in self.requests.items()}}
+
+    async def drain(self, timeout_s: float = 30.0, poll_s: float = 0.05) -> int:
+        """Stops admitting requests and waits up to ``timeout_s`` for the running ones to
+        finish; returns how many were still running."""
+        self.accepting = False
+        t0 = time.time()
+        while True:
+            running = sum(r.state == "RUNNING" for r in self.requests.values())
+            if running == 0 or time.time() - t0 >= timeout_s:
+                break
+            await asyncio.sleep(poll_s)
+        self.events.append({"event": "drained", "still_running": running, "at": time.time()})
+        return running
 
     async def close(self) -> None:
         if self._sweeper is not None:

@@ -285,3 +285,50 @@ def test_worker_metrics_through_the_coordinator():
     assert layers == [(0, 2), (2, 4)]
     assert all(w["stage"]["frames"] > 0 for w in ws.values())
     assert all(isinstance(w["metrics"], dict) for w in ws.values())
+
+
+def test_drain_lets_running_requests_finish():
+    """``drain`` (the coordinator's shutdown): a request already streaming runs to completion,
+    a new one is refused, and drain returns once nothing runs."""
+    from swarm_inference_lab_b200.coordinator.service import CoordinatorCore, CoordinatorRpcServer
+    from swarm_inference_lab_b200.models.config import preset
+    from swarm_inference_lab_b200.models.reference import ReferenceDecoder, random_source
+    from swarm_inference_lab_b200.runtime.worker_runtime import WorkerRuntime
+    from swarm_inference_lab_b200.security.identity import Identity
+
+    torch.set_num_threads(2)
+    expect = ReferenceDecoder(preset("tiny-llama-cpu"), random_source(0)).greedy_generate(PROMPT, 6)[0]
+
+    async def go():
+        ident = Identity.generate("coordinator")
+        core = CoordinatorCore(ident, require_member=False, heartbeat_timeout_s=30.0)
+        rpc = CoordinatorRpcServer(core, host="127.0.0.1", port=0)
+        port = await rpc.start()
+        ws = []
+        try:
+            for i in range(2):
+                w = WorkerRuntime(f"w{i}", Identity.generate(f"w{i}"), f"127.0.0.1:{port}",
+                                  coordinator_fingerprint=ident.fingerprint, heartbeat_s=1.0,
+                                  device="cpu")
+                await w.start()
+                ws.append(w)
+            dep = await core.deploy({"model": {"preset": "tiny-llama-cpu", "seed": 0}, "stages": 2})
+            agen = core.submit_stream({"model": dep["model"], "prompt_ids": PROMPT, "max_tokens": 6})
+            first = [await agen.__anext__(), await agen.__anext__()]        # accepted, token 0
+            drain = asyncio.get_running_loop().create_task(core.drain(30.0))
+            await asyncio.sleep(0.05)
+            refused = [ev async for ev in core.submit_stream(
+                {"model": dep["model"], "prompt_ids": PROMPT, "max_tokens": 2})]
+            rest = [ev async for ev in agen]
+            left = await drain
+            return first + rest, refused, left
+        finally:
+            for w in ws:
+                await w.stop()
+            await rpc.stop()
+
+    evs, refused, left = asyncio.run(go())
+    assert evs[-1]["event"] == "completed"
+    assert [e["token"] for e in evs if e["event"] == "token"] == expect
+    assert refused[-1]["event"] == "failed" and "shutting down" in refused[-1]["error"]
+    assert left == 0
