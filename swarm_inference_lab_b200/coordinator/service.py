@@ -831,6 +831,10 @@ class CoordinatorCore:
                 "throughput_tokens_s": tokens / uptime if uptime > 0 else 0.0,
                 "recoveries": sum(max(0, len(r.generations) - 1) for r in self.requests.values()),
                 "last_error": self.last_error,
+                "accepting": self.accepting,
+                "draining_workers": sorted(self.draining),
+                "unreachable_workers": sorted(self.unreachable),
+                "departed_workers": sorted(self.departed),
                 "models": {k: self._model_status(v) for k, v in self.models.items()},
                 "requests": {k: {"state": r.state, "model": r.model, "prompt_tokens": len(r.prompt),
                                  "tokens": len(r.tokens), "published": len(r.published),
