@@ -145,6 +145,7 @@ class RequestRecord:
     error: str | None = None
     cancel_requested: bool = False
     replica: str | None = None
+    stop_reason: str | None = None
 
 
 def _model_config(model: dict):
@@ -630,6 +631,7 @@ class CoordinatorCore:
                 await agen.aclose()
                 await ctl.cancel_current(finished=True)   # every stage closes the session
             rec.state = "COMPLETED"
+            rec.stop_reason = stop_reason
             done = {"event": "completed", "request_id": rid, "tokens": rec.tokens,
                     "generations": rec.generations, "seconds": time.perf_counter() - t0,
                     "stop_reason": stop_reason, "prompt_tokens": len(prompt)}
@@ -839,6 +841,7 @@ class CoordinatorCore:
                 "requests": {k: {"state": r.state, "model": r.model, "prompt_tokens": len(r.prompt),
                                  "tokens": len(r.tokens), "published": len(r.published),
                                  "generations": r.generations, "started_at": r.started_at,
+                                 "replica": r.replica, "stop_reason": r.stop_reason,
                                  "error": r.error}
                              for k, r in self.requests.items()}}
 

@@ -60,13 +60,15 @@ def test_coordinator_stream_ends_at_a_stop_token():
             core.models[name].eos_token_ids = (stop,)
             eos = await run(core, name)
             full = await run(core, name, ignore_eos=True)
-            return stopped, stats, eos, full, [w.owner.stats.errors for w in ws]
+            reasons = sorted(r["stop_reason"] for r in core.status()["requests"].values())
+            return stopped, stats, eos, full, [w.owner.stats.errors for w in ws], reasons
         finally:
             for w in ws:
                 await w.stop()
             await rpc.stop()
 
-    stopped, stats, eos, full, errors = asyncio.run(go())
+    stopped, stats, eos, full, errors, reasons = asyncio.run(go())
+    assert reasons == ["length", "stop_token", "stop_token"]
     assert stopped[0] == expect[:cut] and stopped[1]["stop_reason"] == "stop_token"
     assert stopped[1]["event"] == "completed"
     assert stats == [(1, 1), (1, 1)]
