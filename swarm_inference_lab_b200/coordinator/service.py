@@ -289,7 +289,10 @@ class CoordinatorCore:
             out.append({"worker_id": w.worker_id, "fingerprint": w.fingerprint,
                         "ring_endpoint": w.endpoint, "healthy": w.healthy,
                         "last_heartbeat": w.last_heartbeat,
-                        "control_endpoint": w.capabilities.get("control_endpoint")})
+                        "control_endpoint": w.capabilities.get("control_endpoint"),
+                        "reachable": w.worker_id not in self.unreachable,
+                        "rtt_ms": w.capabilities.get("rtt_ms"),
+                        "draining": w.worker_id in self.draining})
         return sorted(out, key=lambda d: d["worker_id"])
 
     # ------------------------------------------------------------ planning / deployment

@@ -190,6 +190,8 @@ def test_unreachable_worker_gets_no_stage():
             plan = core.plan({"preset": "tiny-llama-cpu", "seed": 0}, 2)
             topo = core.topology()
             hb = await core.heartbeat({"worker_id": "ghost", "fingerprint": ghost.fingerprint})
+            listed = {w["worker_id"]: w for w in core.workers()}
+            assert listed["ghost"]["reachable"] is False and listed["w1"]["rtt_ms"] > 0
             return rep, plan, topo, hb, core.deployer.excluded
         finally:
             for w in ws:
