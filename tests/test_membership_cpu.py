@@ -334,3 +334,41 @@ def test_drain_lets_running_requests_finish():
     assert [e["token"] for e in evs if e["event"] == "token"] == expect
     assert refused[-1]["event"] == "failed" and "shutting down" in refused[-1]["error"]
     assert left == 0
+
+
+def test_cli_scale_and_metrics_commands(monkeypatch):
+    """``model scale`` exits 1 when the coordinator cannot make the change; ``metrics
+    --prometheus`` prints the text exposition and ``--workers`` asks for the worker views."""
+    import json
+
+    from typer.testing import CliRunner
+
+    import swarm_inference_lab_b200.cli as cli
+
+    calls = []
+
+    class Fake:
+        async def scale(self, name, replicas):
+            calls.append(("scale", name, replicas))
+            return {"ok": replicas <= 2, "replicas": min(replicas, 2)}
+
+        async def metrics(self, *, workers=False):
+            calls.append(("metrics", workers))
+            rep = {"snapshot": {"coordinator_tokens": 5}, "prometheus": "coordinator_tokens 5\n"}
+            if workers:
+                rep["workers"] = {"w0": {"stage": {"frames": 3}, "metrics": {}}}
+            return rep
+
+    def run_with(state, fn):
+        import asyncio
+        return asyncio.run(fn(Fake()))
+
+    monkeypatch.setattr(cli, "_with_coordinator", run_with)
+    invoke = CliRunner().invoke
+    assert invoke(cli.app, ["model", "scale", "m", "--replicas", "2"]).exit_code == 0
+    assert invoke(cli.app, ["model", "scale", "m", "--replicas", "5"]).exit_code == 1
+    r = invoke(cli.app, ["metrics", "--prometheus"])
+    assert r.exit_code == 0 and r.output.startswith("coordinator_tokens 5")
+    r = invoke(cli.app, ["metrics", "--workers"])
+    assert json.loads(r.output)["workers"]["w0"]["stage"]["frames"] == 3
+    assert calls == [("scale", "m", 2), ("scale", "m", 5), ("metrics", False), ("metrics", True)]
