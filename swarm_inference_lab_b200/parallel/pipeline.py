@@ -55,17 +55,28 @@ class PipelineStage:
     """Runs one stage of a micro-batched forward step."""
 
     def __init__(self, pg: PipeGroup, stage_fn: Callable[[int, torch.Tensor], torch.Tensor],
-                 hidden: int, dtype=torch.bfloat16, device="cpu"):
+                 hidden: int, dtype=torch.bfloat16, device="cpu", monitor=None):
         self.pg = pg
         self.fn = stage_fn
         self.hidden = hidden
         self.dtype = dtype
         self.device = torch.device(device)
+        # optional ``parallel.rank_health.RankMonitor``: peers that failed, left or went
+        # silent are reported before a step's first send / receive, and a transfer broken by
+        # a dead peer raises ``RankFailure`` naming it
+        self.monitor = monitor
 
     def step(self, inputs: list[torch.Tensor] | None, mb_sizes: list[int]) -> list[torch.Tensor] | None:
         """``inputs``: per-micro-batch token ids on the first stage (None elsewhere).
         Returns per-micro-batch outputs of the last stage's ``stage_fn`` on stage 0 (the
         tokens travel back), the last stage's own outputs on the last stage, None elsewhere."""
+        if self.monitor is None:
+            return self._step(inputs, mb_sizes)
+        self.monitor.check()
+        with self.monitor.guard():
+            return self._step(inputs, mb_sizes)
+
+    def _step(self, inputs, mb_sizes):
         pg = self.pg
         M = len(mb_sizes)
         recv_bufs, recv_reqs = [None] * M, [None] * M

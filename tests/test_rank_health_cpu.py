@@ -116,3 +116,61 @@ def test_a_rank_that_never_joins_is_reported():
     out = _run("never", ranks=(0, 1), world=3)
     for r in (0, 1):
         assert out[r] == [("failure", {2: "never joined"})], out
+
+
+def _pipe_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from swarm_inference_lab_b200.parallel.pipeline import PipeGroup, PipelineStage
+    from swarm_inference_lab_b200.parallel.rank_health import RankFailure, RankMonitor
+    store = dist.TCPStore("127.0.0.1", port, world_size=None, is_master=(rank == 0),
+                          timeout=timedelta(seconds=30), wait_for_workers=False)
+    mon = RankMonitor("127.0.0.1", port, rank, world, interval_s=0.1, timeout_s=1.0).start(3.0)
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=5))
+    H = 8
+
+    def fn(m, x):
+        if rank == 0:
+            return torch.ones(x.shape[0], H) * x.float().sum()
+        return x.sum(dim=0, keepdim=True)[:, :1].to(torch.int64)
+
+    stage = PipelineStage(PipeGroup(rank, world, list(range(world))), fn, H, dtype=torch.float32,
+                          monitor=mon)
+    stage.result_shape = lambda n: (1, 1)
+    try:
+        for step in range(6):
+            stage.step([torch.tensor([1, 2, 3])] if rank == 0 else None, [3])
+            if rank == 1 and step == 1:
+                os._exit(0)                           # the last stage dies between steps
+        q.put((rank, "finished", None))
+    except RankFailure as f:
+        q.put((rank, "failure", f.ranks))
+    finally:
+        mon.stop()
+        import time
+        time.sleep(1.0)
+
+
+@pytest.mark.timeout(180)
+def test_pipeline_stage_names_a_dead_next_stage():
+    """A 2-stage gloo pipeline with a monitor: when the last stage dies between steps, the
+    first stage's next step ends with ``RankFailure`` naming it instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_pipe_rank, args=(r, 2, port, q)) for r in (0, 1)]
+    for p in procs:
+        p.start()
+    try:
+        for p in procs:
+            p.join(timeout=90)
+        got = [q.get(timeout=10)]
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+    (rank, kind, ranks), = got
+    assert rank == 0 and kind == "failure" and list(ranks) == [1] and "silent" in ranks[1]
