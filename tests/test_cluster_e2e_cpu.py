@@ -172,6 +172,45 @@ def test_cluster_create_join_and_run_distributed(tmp_path, single_process):
         _swarm("cluster", "stop", "--state-dir", str(coord), check=False)
 
 
+def test_coordinator_restart_restores_the_deployment(tmp_path, single_process):
+    """``cluster stop`` / ``cluster start`` with a model deployed: the restarted coordinator
+    finds its deployment in the durable state, the agents re-register over mutual TLS, the
+    model comes back under its name (``cluster topology --wait``) and a request through
+    ``submit`` returns the single-process tokens."""
+    toks_ref, _ = single_process
+    port = _free_pair()
+    coord, n1, n2 = tmp_path / "coord", tmp_path / "n1", tmp_path / "n2"
+    _swarm("cluster", "create", "restart", "--host", "127.0.0.1", "--port", str(port),
+           "--state-dir", str(coord), "--json")
+    agents = []
+    try:
+        _swarm("cluster", "start", "--state-dir", str(coord))
+        for name, st in (("n1", n1), ("n2", n2)):
+            uri = _swarm("cluster", "pair", "--state-dir", str(coord)).stdout.strip().splitlines()[-1]
+            _swarm("node", "join", uri, "--name", name, "--state-dir", str(st))
+        for st in (n1, n2):
+            ready = tmp_path / f"{st.name}.ready"
+            agents.append(_start_agent(st, ready))
+            _wait_file(ready, agents[-1])
+        dep = json.loads(_swarm("model", "deploy", "tiny-llama-cpu", "--stages", "2", "--name", "tiny",
+                                "--state-dir", str(coord)).stdout)
+        assert dep["model"] == "tiny"
+        _swarm("cluster", "stop", "--state-dir", str(coord))
+        _swarm("cluster", "start", "--state-dir", str(coord))
+        topo = json.loads(_swarm("cluster", "topology", "--wait", "60", "--model", "tiny",
+                                 "--state-dir", str(coord), timeout=120).stdout)
+        assert topo["models"]["tiny"]["complete"]
+        rep = next(iter(topo["models"]["tiny"]["replicas"].values()))
+        assert rep["generation"] > dep["generation"]
+        out = _swarm("submit", "tiny", "--prompt-ids", ",".join(map(str, PROMPT)),
+                     "--max-tokens", str(NEW), "--state-dir", str(coord), timeout=300).stdout
+        events = [json.loads(l) for l in out.strip().splitlines()]
+        assert events[-1]["event"] == "completed" and events[-1]["tokens"] == toks_ref
+    finally:
+        _stop(agents)
+        _swarm("cluster", "stop", "--state-dir", str(coord), check=False)
+
+
 def test_worker_killed_mid_decode_recovers_on_a_spare(tmp_path, single_process):
     """The coordinator runs in this process so the test can pause the stream between two
     tokens; the three nodes are separate processes."""
